@@ -1,0 +1,84 @@
+"""ctypes binding of ``libdee_b200.so`` (the C ABI in ``include/dee_b200.h``).
+
+The library is built in-tree by ``dee_b200.build``.  Loading fails loudly
+when it is missing: there is no CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libdee_b200.so")
+
+DEE_OK = 0
+DEE_ERR_INVALID = -1
+DEE_ERR_CUDA = -2
+DEE_ERR_RANGE = -3
+DEE_ERR_UNSUPPORTED = -4
+DEE_ERR_DEVICE = -5
+DEE_ERR_NO_BANK = -6
+
+# Every symbol include/dee_b200.h declares, with (restype, argtypes).
+P = ctypes.c_void_p
+SZ = ctypes.c_size_t
+I = ctypes.c_int
+U32P = ctypes.POINTER(ctypes.c_uint32)
+
+
+class DeeConfig(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_int),
+        ("inter", ctypes.c_int),
+        ("num_experts", ctypes.c_int),
+        ("topk", ctypes.c_int),
+        ("num_layers", ctypes.c_int),
+        ("device_id", ctypes.c_int),
+        ("swiglu_limit", ctypes.c_float),
+        ("max_tokens", ctypes.c_int),
+    ]
+
+
+SIGNATURES = {
+    "dee_abi_config_size": (SZ, []),
+    "dee_abi_version": (I, []),
+    "dee_engine_create": (I, [ctypes.POINTER(DeeConfig), ctypes.POINTER(P)]),
+    "dee_engine_destroy": (None, [P]),
+    "dee_last_error": (ctypes.c_char_p, [P]),
+    "dee_expert_bank_attach": (I, [P, I, P, I, SZ, P]),
+    "dee_expert_bank_set_slots": (I, [P, I, P, P]),
+    "dee_route_topk_device": (I, [P, P, I, P, P, P]),
+    "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),
+    "dee_moe_forward_combined_device": (I, [P, I, P, I, P, I, P, P, P, P]),
+    "dee_moe_forward_device": (I, [P, I, P, I, P, P, I, P, P, P, P]),
+    "dee_engine_sync_status": (I, [P, P, U32P]),
+    "dee_journal_ids_host": (I, [P, P, I]),
+    "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),
+    "dee_fp4_quantize_device": (I, [P, SZ, SZ, P, P, P]),
+    "dee_engine_launch_count": (ctypes.c_uint64, [P]),
+}
+
+_lib = None
+
+
+def load(build_if_missing: bool = False) -> ctypes.CDLL:
+    """Load the CUDA library; raise if it is absent (no fallback path)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        if build_if_missing:
+            from . import build
+            build.build()
+        else:
+            raise RuntimeError(
+                f"dee_b200 CUDA library not built ({LIB_PATH}); run `python -m dee_b200.build`")
+    lib = ctypes.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if lib.dee_abi_config_size() != ctypes.sizeof(DeeConfig):
+        raise ImportError("dee_b200 ABI mismatch: dee_config size differs; rebuild the library")
+    _lib = lib
+    return lib

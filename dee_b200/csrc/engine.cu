@@ -1,0 +1,562 @@
+// engine.cu -- host orchestration behind the C ABI in include/dee_b200.h.
+//
+// The engine replaces the per-expert host loop of the reference
+// (Engine::moe_forward_batch_device_impl, reference
+// dee.cpp/src/engine.cpp:776-1190: host grouping, one D2D copy per gathered
+// row, three dequant launches, three cuBLAS calls and one D2D copy per
+// scattered row for every active expert) with a fixed sequence of launches
+// independent of how many experts are active:
+//
+//   permute (1 CTA)  -> gather (token rows into grouped order)
+//   -> gate/up grouped GEMM (tcgen05, SwiGLU epilogue)
+//   -> down grouped GEMM (tcgen05, scatter epilogue)
+//   -> combine (optional)
+#include "../../include/dee_b200.h"
+#include "kernels.h"
+
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+namespace dee {
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+struct RecordLayout {
+    size_t w1, w3, w2, s1, s3, s2, bytes;
+};
+
+RecordLayout record_layout(int hidden, int inter) {
+    const size_t ih = static_cast<size_t>(hidden) * inter;
+    RecordLayout L{};
+    L.w1 = 0;
+    L.w3 = ih / 2;
+    L.w2 = ih;
+    L.s1 = ih + ih / 2;
+    L.s3 = L.s1 + ih / 32;
+    L.s2 = L.s3 + ih / 32;
+    L.bytes = L.s2 + ih / 32;
+    return L;
+}
+
+struct Bank {
+    bool attached = false;
+    const uint8_t* records = nullptr;
+    int n_slots = 0;
+    size_t record_bytes = 0;
+    int32_t* d_slot_of = nullptr;  // [E]
+    CUtensorMap w1, w3, w2, s1, s3, s2;
+};
+
+template <class T>
+cudaError_t dev_alloc(T** p, size_t n) {
+    return cudaMalloc(reinterpret_cast<void**>(p), n * sizeof(T) + 16);
+}
+
+}  // namespace
+}  // namespace dee
+
+struct dee_engine {
+    dee_config cfg{};
+    std::string last_error;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;  // the engine's own stream (synchronous API)
+    uint32_t* d_status = nullptr;
+    uint32_t* h_status = nullptr;  // pinned
+    std::vector<dee::Bank> banks;
+    // workspaces, capacity in selections (tokens * topk)
+    size_t cap_sel = 0;
+    int32_t* d_ids = nullptr;
+    float* d_weights = nullptr;
+    int32_t* d_perm = nullptr;
+    int32_t* d_row_of = nullptr;
+    int32_t* d_counts = nullptr;
+    int32_t* d_offsets = nullptr;
+    dee::TileDesc* d_tiles = nullptr;
+    int32_t* d_n_tiles = nullptr;
+    int max_tiles = 0;
+    __half* d_xperm = nullptr;
+    __half* d_act = nullptr;
+    float* d_raw = nullptr;
+    int32_t* h_ids = nullptr;  // pinned staging of the consumed ids
+    size_t h_ids_count = 0;
+    CUtensorMap map_xperm, map_act;
+    uint64_t launches = 0;
+};
+
+namespace dee {
+namespace {
+
+int fail(dee_engine* e, int code, const std::string& msg) {
+    if (e) e->last_error = msg;
+    return code;
+}
+
+int cuda_fail(dee_engine* e, cudaError_t err, const char* what) {
+    return fail(e, DEE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+bool encode(dee_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+            const cuuint64_t* dims, const cuuint64_t* strides, const cuuint32_t* box,
+            CUtensorMapSwizzle swz, const char* what) {
+    auto fn = get_encode_fn();
+    if (!fn) {
+        e->last_error = "cuTensorMapEncodeTiled unavailable (driver entry point)";
+        return false;
+    }
+    cuuint32_t elem[5] = {1, 1, 1, 1, 1};
+    const CUresult r = fn(map, dt, rank, const_cast<void*>(base), dims, strides, box, elem,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        e->last_error = std::string("cuTensorMapEncodeTiled failed for ") + what + " (code " +
+                        std::to_string(static_cast<int>(r)) + ")";
+        return false;
+    }
+    return true;
+}
+
+void free_workspace(dee_engine* e) {
+    cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
+    cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
+    cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw);
+    if (e->h_ids) cudaFreeHost(e->h_ids);
+    e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
+    e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
+    e->d_xperm = nullptr; e->d_act = nullptr; e->d_raw = nullptr; e->h_ids = nullptr;
+    e->cap_sel = 0;
+}
+
+// Grow the workspaces to hold `sel` selections.  Growth synchronises
+// `stream` first so no queued kernel still reads the old buffers (the
+// reference grows its batch buffers the same way, engine.cpp:827-884).
+int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
+    if (sel <= e->cap_sel) return DEE_OK;
+    cudaError_t err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "cudaStreamSynchronize(workspace growth)");
+    free_workspace(e);
+    const size_t cap = ((sel + 255) / 256) * 256;
+    const int H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
+    const int max_tiles = E + static_cast<int>(cap / 16) + 1;
+    if ((err = dev_alloc(&e->d_ids, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_weights, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_perm, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_row_of, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_counts, static_cast<size_t>(E))) != cudaSuccess ||
+        (err = dev_alloc(&e->d_offsets, static_cast<size_t>(E) + 1)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_tiles, static_cast<size_t>(max_tiles))) != cudaSuccess ||
+        (err = dev_alloc(&e->d_n_tiles, 1)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_xperm, cap * H)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_act, cap * I)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_raw, cap * H)) != cudaSuccess ||
+        (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
+                             cudaHostAllocDefault)) != cudaSuccess) {
+        free_workspace(e);
+        return cuda_fail(e, err, "workspace allocation");
+    }
+    e->cap_sel = cap;
+    e->max_tiles = max_tiles;
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), cap};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 2};
+        const cuuint32_t box[2] = {64, 16};
+        if (!encode(e, &e->map_xperm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_xperm, dims, strides,
+                    box, CU_TENSOR_MAP_SWIZZLE_128B, "X_perm"))
+            return DEE_ERR_CUDA;
+    }
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(I), cap};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(I) * 2};
+        const cuuint32_t box[2] = {64, 16};
+        if (!encode(e, &e->map_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
+                    box, CU_TENSOR_MAP_SWIZZLE_128B, "act"))
+            return DEE_ERR_CUDA;
+    }
+    return DEE_OK;
+}
+
+int check_engine(dee_engine* e) {
+    if (!e) return DEE_ERR_INVALID;
+    cudaError_t err = cudaSetDevice(e->cfg.device_id);
+    if (err != cudaSuccess) return cuda_fail(e, err, "cudaSetDevice");
+    return DEE_OK;
+}
+
+bool host_ids_valid(dee_engine* e, const int32_t* ids, size_t n) {
+    for (size_t i = 0; i < n; ++i) {
+        if (ids[i] < 0 || ids[i] >= e->cfg.num_experts) {
+            e->last_error = "expert id " + std::to_string(ids[i]) + " at selection " +
+                            std::to_string(i) + " is outside [0," +
+                            std::to_string(e->cfg.num_experts) + ")";
+            return false;
+        }
+    }
+    return true;
+}
+
+// The launch sequence shared by every forward entry point.  d_ids32 holds
+// validated-or-device-checked int32 ids [T, K]; raw receives [T*K, H] FP32.
+int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
+                float* raw, cudaStream_t stream) {
+    if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
+        return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
+    const dee::Bank& bank = e->banks[layer];
+    const int K = e->cfg.topk, H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
+    const size_t sel = static_cast<size_t>(tokens) * K;
+    const bool large = tokens > 64;
+    const int n_max = gemm_n_max(large);
+
+    PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles};
+    cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
+                                     stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H,
+                             e->d_xperm, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "gather launch");
+
+    GemmArgs a{};
+    a.hidden = H;
+    a.inter = I;
+    a.topk = K;
+    a.swiglu_limit = e->cfg.swiglu_limit;
+    a.tiles = e->d_tiles;
+    a.n_tiles = e->d_n_tiles;
+    a.slot_of = bank.d_slot_of;
+    a.num_slots = bank.n_slots;
+    a.num_experts = E;
+    a.perm = e->d_perm;
+    a.act = e->d_act;
+    a.raw = raw;
+    a.status = e->d_status;
+
+    GemmMaps gm{};
+    gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3; gm.b = e->map_xperm;
+    a.k_total = H;
+    a.m_tiles = I / 64;
+    err = launch_moe_gemm(true, large, gm, a, e->num_sms, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
+
+    gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2; gm.b = e->map_act;
+    a.k_total = I;
+    a.m_tiles = H / 128;
+    err = launch_moe_gemm(false, large, gm, a, e->num_sms, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "down GEMM launch");
+    e->launches += 4;
+    return DEE_OK;
+}
+
+}  // namespace
+}  // namespace dee
+
+using namespace dee;
+
+extern "C" {
+
+size_t dee_abi_config_size(void) { return sizeof(dee_config); }
+int dee_abi_version(void) { return DEE_B200_ABI_VERSION; }
+
+int dee_engine_create(const dee_config* cfg, dee_engine** out) {
+    if (!cfg || !out) return DEE_ERR_INVALID;
+    *out = nullptr;
+    const int H = cfg->hidden, I = cfg->inter;
+    if (H <= 0 || I <= 0 || H % 512 != 0 || I % 512 != 0 || cfg->num_experts <= 0 ||
+        cfg->num_experts > 256 || cfg->topk <= 0 || cfg->topk > 32 ||
+        cfg->topk > cfg->num_experts || cfg->num_layers <= 0)
+        return DEE_ERR_UNSUPPORTED;
+    auto* e = new dee_engine();
+    e->cfg = *cfg;
+    if (e->cfg.max_tokens <= 0) e->cfg.max_tokens = 64;
+    cudaError_t err = cudaSetDevice(cfg->device_id);
+    if (err == cudaSuccess)
+        err = cudaDeviceGetAttribute(&e->num_sms, cudaDevAttrMultiProcessorCount, cfg->device_id);
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&e->d_status), 16);
+    if (err == cudaSuccess) err = cudaMemset(e->d_status, 0, 16);
+    if (err == cudaSuccess)
+        err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_status), 16, cudaHostAllocDefault);
+    if (err != cudaSuccess) {
+        dee_engine_destroy(e);
+        return DEE_ERR_CUDA;
+    }
+    e->banks.resize(static_cast<size_t>(cfg->num_layers));
+    const int rc = ensure_capacity(e, static_cast<size_t>(e->cfg.max_tokens) * cfg->topk, e->stream);
+    if (rc != DEE_OK) {
+        dee_engine_destroy(e);
+        return rc;
+    }
+    *out = e;
+    return DEE_OK;
+}
+
+void dee_engine_destroy(dee_engine* e) {
+    if (!e) return;
+    cudaSetDevice(e->cfg.device_id);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    free_workspace(e);
+    for (auto& b : e->banks) cudaFree(b.d_slot_of);
+    cudaFree(e->d_status);
+    if (e->h_status) cudaFreeHost(e->h_status);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+}
+
+const char* dee_last_error(const dee_engine* e) { return e ? e->last_error.c_str() : "null engine"; }
+
+int dee_expert_bank_attach(dee_engine* e, int layer, const void* d_records, int n_slots,
+                           size_t record_bytes, const int32_t* h_slot_of_expert) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    if (layer < 0 || layer >= e->cfg.num_layers || !d_records || n_slots <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid bank arguments");
+    const int H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
+    const RecordLayout L = record_layout(H, I);
+    if (record_bytes < L.bytes || record_bytes % 16 != 0 ||
+        (reinterpret_cast<uintptr_t>(d_records) & 15) != 0)
+        return fail(e, DEE_ERR_INVALID, "record_bytes must be >= " + std::to_string(L.bytes) +
+                                            " and 16-byte aligned");
+    std::vector<int32_t> slots(static_cast<size_t>(E));
+    for (int i = 0; i < E; ++i) {
+        slots[i] = h_slot_of_expert ? h_slot_of_expert[i] : (i < n_slots ? i : -1);
+        if (slots[i] >= n_slots) return fail(e, DEE_ERR_INVALID, "slot index beyond n_slots");
+    }
+    Bank& b = e->banks[layer];
+    if (!b.d_slot_of) {
+        cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&b.d_slot_of), sizeof(int32_t) * E);
+        if (err != cudaSuccess) return cuda_fail(e, err, "slot table allocation");
+    }
+    cudaError_t err = cudaMemcpy(b.d_slot_of, slots.data(), sizeof(int32_t) * E,
+                                 cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return cuda_fail(e, err, "slot table upload");
+    const uint8_t* base = static_cast<const uint8_t*>(d_records);
+    const cuuint64_t ns = static_cast<cuuint64_t>(n_slots);
+    const cuuint64_t rb = static_cast<cuuint64_t>(record_bytes);
+    {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(H / 2), static_cast<cuuint64_t>(I), ns};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(H / 2), rb};
+        const cuuint32_t box[3] = {128, 64, 1};
+        if (!encode(e, &b.w1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.w1, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "w1") ||
+            !encode(e, &b.w3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.w3, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "w3"))
+            return DEE_ERR_CUDA;
+    }
+    {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(I / 2), static_cast<cuuint64_t>(H), ns};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(I / 2), rb};
+        const cuuint32_t box[3] = {128, 128, 1};
+        if (!encode(e, &b.w2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.w2, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "w2"))
+            return DEE_ERR_CUDA;
+    }
+    {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(H / 32), static_cast<cuuint64_t>(I), ns};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(H / 32), rb};
+        const cuuint32_t box[3] = {16, 64, 1};
+        if (!encode(e, &b.s1, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.s1, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, "w1.scale") ||
+            !encode(e, &b.s3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.s3, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, "w3.scale"))
+            return DEE_ERR_CUDA;
+    }
+    {
+        const cuuint64_t dims[3] = {static_cast<cuuint64_t>(I / 32), static_cast<cuuint64_t>(H), ns};
+        const cuuint64_t strides[2] = {static_cast<cuuint64_t>(I / 32), rb};
+        const cuuint32_t box[3] = {16, 128, 1};
+        if (!encode(e, &b.s2, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base + L.s2, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE, "w2.scale"))
+            return DEE_ERR_CUDA;
+    }
+    b.records = base;
+    b.n_slots = n_slots;
+    b.record_bytes = record_bytes;
+    b.attached = true;
+    return DEE_OK;
+}
+
+int dee_expert_bank_set_slots(dee_engine* e, int layer, const int32_t* h_slot_of_expert,
+                              void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (layer < 0 || layer >= e->cfg.num_layers || !e->banks[layer].attached || !h_slot_of_expert)
+        return fail(e, DEE_ERR_NO_BANK, "no bank attached for layer");
+    Bank& b = e->banks[layer];
+    for (int i = 0; i < e->cfg.num_experts; ++i)
+        if (h_slot_of_expert[i] >= b.n_slots)
+            return fail(e, DEE_ERR_INVALID, "slot index beyond n_slots");
+    cudaError_t err = cudaMemcpyAsync(b.d_slot_of, h_slot_of_expert,
+                                      sizeof(int32_t) * e->cfg.num_experts, cudaMemcpyHostToDevice,
+                                      static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(e, err, "slot table update");
+    return DEE_OK;
+}
+
+int dee_route_topk_device(dee_engine* e, const float* d_logits, int tokens, int32_t* d_ids,
+                          float* d_weights, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_logits || !d_ids || !d_weights || tokens <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid router arguments");
+    cudaError_t err = launch_route_topk(d_logits, tokens, e->cfg.num_experts, e->cfg.topk, d_ids,
+                                        d_weights, e->d_status, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(e, err, "router launch");
+    e->launches += 1;
+    return DEE_OK;
+}
+
+int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int tokens,
+                           const int32_t* d_ids, const int32_t* h_ids, int topk,
+                           const float* d_weights, float* d_out_f32, float* d_raw, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_x_f16 || tokens <= 0 || topk != e->cfg.topk || (!d_ids && !h_ids) ||
+        (!d_out_f32 && !d_raw) || (d_out_f32 && !d_weights))
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_device arguments");
+    const size_t sel = static_cast<size_t>(tokens) * topk;
+    if (h_ids && !host_ids_valid(e, h_ids, sel)) return DEE_ERR_RANGE;
+    if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    const int32_t* ids32 = d_ids;
+    cudaError_t err;
+    if (h_ids) {
+        std::memcpy(e->h_ids, h_ids, sel * sizeof(int32_t));
+        err = cudaMemcpyAsync(e->d_ids, e->h_ids, sel * sizeof(int32_t), cudaMemcpyHostToDevice,
+                              stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "ids H2D");
+        ids32 = e->d_ids;
+    } else {
+        err = cudaMemcpyAsync(e->h_ids, d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                              stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
+    }
+    e->h_ids_count = sel;
+    float* raw = d_raw ? d_raw : e->d_raw;
+    if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, ids32, raw,
+                          stream)) != DEE_OK)
+        return rc;
+    if (d_out_f32) {
+        err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
+        e->launches += 1;
+    }
+    return DEE_OK;
+}
+
+int dee_moe_forward_batch_device(dee_engine* e, int layer, const void* d_h_in, int tokens,
+                                 const int32_t* h_expert_ids, int topk, void* d_experts_out) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_h_in || !h_expert_ids || !d_experts_out || tokens <= 0 || topk != e->cfg.topk)
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_batch_device arguments");
+    cudaError_t err = cudaMemsetAsync(e->d_status, 0, 4, e->stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "status reset");
+    rc = dee_moe_forward_device(e, layer, d_h_in, tokens, nullptr, h_expert_ids, topk, nullptr,
+                                nullptr, static_cast<float*>(d_experts_out), e->stream);
+    if (rc != DEE_OK) return rc;
+    uint32_t st = 0;
+    return dee_engine_sync_status(e, e->stream, &st);
+}
+
+int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in, int tokens,
+                                    const int64_t* d_expert_ids, int topk,
+                                    const float* d_weights_f32, void* d_output_f16,
+                                    void* d_raw_trace_out, void* external_stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(external_stream);
+    if (!d_h_in || !d_expert_ids || !d_weights_f32 || !d_output_f16 || tokens <= 0 ||
+        topk != e->cfg.topk)
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_combined_device arguments");
+    const size_t sel = static_cast<size_t>(tokens) * topk;
+    if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    cudaError_t err = launch_ids_i64_to_i32(d_expert_ids, static_cast<int>(sel),
+                                            e->cfg.num_experts, e->d_ids, e->d_status, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "id conversion launch");
+    err = cudaMemcpyAsync(e->h_ids, e->d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
+    e->h_ids_count = sel;
+    float* raw = d_raw_trace_out ? static_cast<float*>(d_raw_trace_out) : e->d_raw;
+    if ((rc = run_experts(e, layer, static_cast<const __half*>(d_h_in), tokens, e->d_ids, raw,
+                          stream)) != DEE_OK)
+        return rc;
+    err = launch_combine_f16(raw, d_weights_f32, d_expert_ids, tokens, topk, e->cfg.hidden,
+                             static_cast<__half*>(d_output_f16), stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "FP16 combine launch");
+    e->launches += 2;
+    return DEE_OK;
+}
+
+int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaMemcpyAsync(e->h_status, e->d_status, 4, cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return cuda_fail(e, err, "status readback");
+    const uint32_t st = *e->h_status;
+    if (status_out) *status_out = st;
+    if (st != 0) {
+        cudaMemsetAsync(e->d_status, 0, 4, s);
+        cudaStreamSynchronize(s);
+        char buf[160];
+        std::snprintf(buf, sizeof(buf),
+                      "device status 0x%08x (bit0-3: pipeline wait timeout, bit4: expert id out "
+                      "of range or not resident, bit5: tile overflow, bit7: router failure)",
+                      st);
+        e->last_error = buf;
+        return DEE_ERR_DEVICE;
+    }
+    return DEE_OK;
+}
+
+int dee_journal_ids_host(dee_engine* e, int32_t* h_out, int max_ids) {
+    if (!e || !h_out || max_ids < 0) return DEE_ERR_INVALID;
+    const size_t n = e->h_ids_count < static_cast<size_t>(max_ids) ? e->h_ids_count
+                                                                   : static_cast<size_t>(max_ids);
+    if (n) std::memcpy(h_out, e->h_ids, n * sizeof(int32_t));
+    return static_cast<int>(n);
+}
+
+int dee_fp4_decode_device(const uint8_t* d_packed, const uint8_t* d_scale, void* d_dst_f16,
+                          size_t out, size_t in, void* stream) {
+    if (!d_packed || !d_scale || !d_dst_f16 || out == 0 || in % 64 != 0) return DEE_ERR_INVALID;
+    return launch_fp4_decode(d_packed, d_scale, static_cast<__half*>(d_dst_f16), out, in,
+                             static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? DEE_OK
+               : DEE_ERR_CUDA;
+}
+
+int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_packed,
+                            uint8_t* d_scale, void* stream) {
+    if (!d_w || !d_packed || !d_scale || out == 0 || in % 32 != 0) return DEE_ERR_INVALID;
+    return launch_fp4_quantize(d_w, out, in, d_packed, d_scale,
+                               static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? DEE_OK
+               : DEE_ERR_CUDA;
+}
+
+uint64_t dee_engine_launch_count(const dee_engine* e) { return e ? e->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,70 @@
+// kernels.h -- launchers shared between the kernel files and the engine.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "moe_gemm.cuh"
+
+namespace dee {
+
+struct GemmMaps {
+    CUtensorMap w0, w1, s0, s1, b;
+};
+
+// Largest N (rows per expert tile) of the small / large GEMM configuration.
+int gemm_n_max(bool large);
+
+cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, const GemmArgs& args,
+                            int grid, cudaStream_t stream);
+
+// Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
+cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
+                              int32_t* ids, float* weights, uint32_t* status, cudaStream_t stream);
+
+// Group-by-expert permutation (one CTA): counts/offsets per expert, grouped
+// row -> position table, position -> row table, and the GEMM tile list.
+struct PermuteOut {
+    int32_t* counts;    // [E]
+    int32_t* offsets;   // [E + 1]
+    int32_t* perm;      // [T*K] grouped row -> position
+    int32_t* row_of;    // [T*K] position -> grouped row
+    TileDesc* tiles;    // [max_tiles]
+    int32_t* n_tiles;   // [1]
+};
+cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
+                           int max_tiles, const PermuteOut& out, uint32_t* status,
+                           cudaStream_t stream);
+
+// X_perm[row] = X[perm[row] / topk] (FP16 rows of H elements).
+cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,
+                               int max_rows, int topk, int hidden, __half* x_perm,
+                               cudaStream_t stream);
+
+// Live combine: out[t] = sum_r w[t, r] * raw[t, r] in rank order, FP32.
+cudaError_t launch_combine_f32(const float* raw, const float* weights, int tokens, int topk,
+                               int hidden, float* out, cudaStream_t stream);
+// Exact eager-FP16 combine in stable ascending-expert order.
+cudaError_t launch_combine_f16(const float* raw, const float* weights, const int64_t* ids64,
+                               int tokens, int topk, int hidden, __half* out,
+                               cudaStream_t stream);
+// Same as combine_f16 with int32 expert ids.
+cudaError_t launch_combine_f16_i32(const float* raw, const float* weights, const int32_t* ids,
+                                   int tokens, int topk, int hidden, __half* out,
+                                   cudaStream_t stream);
+
+// Standalone FP4 -> FP16 decode of one [out, in] projection.
+cudaError_t launch_fp4_decode(const uint8_t* packed, const uint8_t* scale, __half* dst,
+                              size_t out, size_t in, cudaStream_t stream);
+
+// N(0, std)-shaped FP32 weights [out, in] -> packed FP4 + UE8M0 scales.
+cudaError_t launch_fp4_quantize(const float* w, size_t out, size_t in, uint8_t* packed,
+                                uint8_t* scale, cudaStream_t stream);
+
+// Convert int64 ids to int32 (validating range into status).
+cudaError_t launch_ids_i64_to_i32(const int64_t* src, int n, int experts, int32_t* dst,
+                                  uint32_t* status, cudaStream_t stream);
+
+}  // namespace dee

@@ -1,0 +1,404 @@
+// routing.cu -- router top-k, group-by-expert permutation, token gather and
+// the route-weighted combines.
+#include "kernels.h"
+
+namespace dee {
+namespace {
+
+using sm100::kStatusBadExpert;
+using sm100::kStatusBadShape;
+
+constexpr uint32_t kStatusBadRouter = 1u << 7;
+constexpr int kRouteMaxPerLane = 16;  // experts <= 512
+
+struct Cand {
+    float p;
+    int id;
+};
+
+// Probability-descending, then lower expert id: the partial_sort comparator
+// of Engine::route_topk_batch (reference dee.cpp/src/engine.cpp:2755-2760).
+__device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
+    if (a.p != b.p) return a.p > b.p;
+    return a.id < b.id;
+}
+
+// One warp per token.  Softmax follows engine.cpp:2739-2754: the maximum
+// logit, exp of (logit - max) rounded to FP32, a double-precision
+// denominator summed in expert order, an FP32 inverse, FP32 probabilities.
+// exp is evaluated in double and rounded once to FP32 (correctly rounded in
+// practice), which the reference's libm expf matches except for rare
+// last-bit cases.
+__global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, int experts,
+                                  int topk, int32_t* __restrict__ ids, float* __restrict__ weights,
+                                  uint32_t* status) {
+    extern __shared__ float route_smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    float* sp = route_smem + warp * experts;
+    const float* l = logits + static_cast<size_t>(t) * experts;
+    const int nper = (experts + 31) >> 5;
+
+    float v[kRouteMaxPerLane];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+        const int e = lane + 32 * j;
+        v[j] = (j < nper && e < experts) ? l[e] : -INFINITY;
+        if (j < nper && e < experts) m = (m < v[j]) ? v[j] : m;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float other = __shfl_xor_sync(0xffffffffu, m, o);
+        m = (m < other) ? other : m;
+    }
+#pragma unroll
+    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+        const int e = lane + 32 * j;
+        if (j < nper && e < experts) {
+            const float d = __fsub_rn(v[j], m);
+            v[j] = static_cast<float>(exp(static_cast<double>(d)));
+            sp[e] = v[j];
+        }
+    }
+    __syncwarp();
+    double den = 0.0;
+    if (lane == 0)
+        for (int e = 0; e < experts; ++e) den += static_cast<double>(sp[e]);
+    den = __shfl_sync(0xffffffffu, den, 0);
+    const bool bad = !(den > 0.0) || !isfinite(den);
+    const float inv = static_cast<float>(1.0 / den);
+    Cand mine[kRouteMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+        const int e = lane + 32 * j;
+        mine[j].p = (j < nper && e < experts) ? __fmul_rn(v[j], inv) : -INFINITY;
+        mine[j].id = (j < nper && e < experts) ? e : 0x7fffffff;
+    }
+    float sel_p[32];
+    int sel_id[32];
+    for (int k = 0; k < topk; ++k) {
+        Cand best{-INFINITY, 0x7fffffff};
+        int best_j = -1;
+#pragma unroll
+        for (int j = 0; j < kRouteMaxPerLane; ++j) {
+            if (mine[j].id != 0x7fffffff && (best_j < 0 || better(mine[j], best))) {
+                best = mine[j];
+                best_j = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            Cand other;
+            other.p = __shfl_xor_sync(0xffffffffu, best.p, o);
+            other.id = __shfl_xor_sync(0xffffffffu, best.id, o);
+            if (other.id != 0x7fffffff && (best.id == 0x7fffffff || better(other, best))) best = other;
+        }
+        sel_p[k] = best.p;
+        sel_id[k] = best.id;
+        // the owning lane retires the winner
+#pragma unroll
+        for (int j = 0; j < kRouteMaxPerLane; ++j)
+            if (mine[j].id == best.id) mine[j].id = 0x7fffffff;
+    }
+    if (lane == 0) {
+        float sum = 0.0f;
+        for (int k = 0; k < topk; ++k) sum = __fadd_rn(sum, sel_p[k]);
+        const bool bad_sum = !(sum > 0.0f);
+        if (bad || bad_sum) atomicOr(status, kStatusBadRouter);
+        for (int k = 0; k < topk; ++k) {
+            const bool ok = !(bad || bad_sum) && sel_id[k] >= 0 && sel_id[k] < experts;
+            ids[static_cast<size_t>(t) * topk + k] = ok ? sel_id[k] : 0;
+            weights[static_cast<size_t>(t) * topk + k] = ok ? __fdiv_rn(sel_p[k], sum) : 0.0f;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Permutation.  Selections are enumerated in the reference's grouping order
+// j = rank * T + token (engine.cpp:812-823: for each expert, rank-major then
+// token) and placed with a stable counting sort by expert id, so the rows of
+// one expert keep (rank, token) order and experts appear by ascending id.
+// ---------------------------------------------------------------------------
+constexpr int kPermThreads = 1024;
+constexpr int kPermMaxExperts = 256;
+
+__global__ void __launch_bounds__(kPermThreads, 1)
+    permute_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts,
+                   int n_tile_max, int max_tiles, PermuteOut out, uint32_t* status) {
+    __shared__ int cnt[kPermMaxExperts];
+    __shared__ int off[kPermMaxExperts + 1];
+    __shared__ int cursor[kPermMaxExperts];
+    __shared__ int ntile_off[kPermMaxExperts + 1];
+    __shared__ int wcnt[32][kPermMaxExperts];  // per-warp group sizes, zero when unused
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int sel = tokens * topk;
+
+    for (int e = tid; e < experts; e += kPermThreads) { cnt[e] = 0; cursor[e] = 0; }
+    for (int i = tid; i < 32 * kPermMaxExperts; i += kPermThreads) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    for (int p = tid; p < sel; p += kPermThreads) {
+        const int e = ids[p];
+        if (e < 0 || e >= experts) {
+            atomicOr(status, kStatusBadExpert);
+            out.row_of[p] = -1;
+        } else {
+            atomicAdd(&cnt[e], 1);
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scan of counts and of per-expert tile counts
+        const int per = (experts + 31) / 32;
+        int s = 0, st = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < experts) {
+                s += cnt[e];
+                st += cnt[e] > 0 ? (cnt[e] + n_tile_max - 1) / n_tile_max : 0;
+            }
+        }
+        int incl = s, incl_t = st;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xffffffffu, incl, o);
+            const int b = __shfl_up_sync(0xffffffffu, incl_t, o);
+            if (lane >= o) { incl += a; incl_t += b; }
+        }
+        int run = incl - s, run_t = incl_t - st;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < experts) {
+                off[e] = run;
+                ntile_off[e] = run_t;
+                run += cnt[e];
+                run_t += cnt[e] > 0 ? (cnt[e] + n_tile_max - 1) / n_tile_max : 0;
+            }
+        }
+        if (lane == 31) { off[experts] = incl; ntile_off[experts] = incl_t; }
+    }
+    __syncthreads();
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (int base = 0; base < sel; base += kPermThreads) {
+        const int j = base + tid;
+        int key = -1 - lane;  // unique per lane when not a valid selection
+        int p = -1;
+        if (j < sel) {
+            const int r = j / tokens;
+            const int t = j - r * tokens;
+            p = t * topk + r;
+            const int e = ids[p];
+            if (e >= 0 && e < experts) key = e;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const int rank_w = __popc(peers & lt_mask);
+        const bool leader = rank_w == 0;
+        if (key >= 0 && leader) wcnt[warp][key] = __popc(peers);
+        __syncthreads();
+        if (key >= 0) {
+            int pre = 0;
+            for (int w = 0; w < warp; ++w) pre += wcnt[w][key];
+            const int row = off[key] + cursor[key] + pre + rank_w;
+            out.perm[row] = p;
+            out.row_of[p] = row;
+        }
+        __syncthreads();
+        if (key >= 0 && leader) {
+            atomicAdd(&cursor[key], __popc(peers));
+            wcnt[warp][key] = 0;
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < experts; e += kPermThreads) {
+        out.counts[e] = cnt[e];
+        out.offsets[e] = off[e];
+        const int c = cnt[e];
+        if (c == 0) continue;
+        const int nt = (c + n_tile_max - 1) / n_tile_max;
+        const int sz = (c + nt - 1) / nt;
+        for (int i = 0; i < nt; ++i) {
+            const int slot = ntile_off[e] + i;
+            if (slot >= max_tiles) { atomicOr(status, kStatusBadShape); break; }
+            const int start = i * sz;
+            const int n = min(sz, c - start);
+            TileDesc td;
+            td.expert = e;
+            td.row_start = off[e] + start;
+            td.n_rows = n;
+            td.n_pad = (n + 15) & ~15;
+            out.tiles[slot] = td;
+        }
+    }
+    if (tid == 0) {
+        out.offsets[experts] = off[experts];
+        *out.n_tiles = min(ntile_off[experts], max_tiles);
+    }
+}
+
+__global__ void gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
+                                   const int32_t* __restrict__ total_rows_dev, int max_rows,
+                                   int topk, int hidden, __half* __restrict__ x_perm) {
+    const int rows = min(*total_rows_dev, max_rows);
+    const int warps_total = gridDim.x * (blockDim.x >> 5);
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int vec = hidden / 8;  // uint4 per row
+    for (int row = w; row < rows; row += warps_total) {
+        const int t = perm[row] / topk;
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * hidden);
+        uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<size_t>(row) * hidden);
+        for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
+    }
+}
+
+// Live DeepSeek combine (deepseek_v4_layer_candidate.py:616-629): out = 0,
+// then for each rank in order out += w * raw, each multiply and add rounded
+// to FP32 separately.
+__global__ void combine_f32_kernel(const float* __restrict__ raw, const float* __restrict__ w,
+                                   int tokens, int topk, int hidden, float* __restrict__ out) {
+    const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = (i * 4) / hidden;
+        const size_t h = i * 4 - t * hidden;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < topk; ++r) {
+            const size_t s = t * topk + r;
+            const float wr = w[s];
+            const float4 v = *reinterpret_cast<const float4*>(raw + s * hidden + h);
+            acc.x = __fadd_rn(acc.x, __fmul_rn(wr, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(wr, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(wr, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(wr, v.w));
+        }
+        *reinterpret_cast<float4*>(out + t * hidden + h) = acc;
+    }
+}
+
+// Exact eager-FP16 combine (weighted_combine_fp16_kernel,
+// reference swiglu_cuda.cu:69-116): ranks visited in stable ascending expert
+// order; raw, product and running sum each rounded to FP16.
+template <class IdT>
+__global__ void combine_f16_kernel(const float* __restrict__ raw, const float* __restrict__ w,
+                                   const IdT* __restrict__ ids, int tokens, int topk, int hidden,
+                                   __half* __restrict__ out) {
+    const size_t n = static_cast<size_t>(tokens) * hidden;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = i / hidden;
+        const size_t h = i - t * hidden;
+        const IdT* te = ids + t * topk;
+        __half acc = __float2half_rn(0.0f);
+        bool ok = true;
+        for (int rank = 0; rank < topk && ok; ++rank) {
+            int pos = -1;
+            for (int p = 0; p < topk && pos < 0; ++p) {
+                int sr = 0;
+                for (int o = 0; o < topk; ++o)
+                    if (te[o] < te[p] || (te[o] == te[p] && o < p)) ++sr;
+                if (sr == rank) pos = p;
+            }
+            if (pos < 0) { ok = false; break; }
+            const size_t s = t * topk + pos;
+            const __half rv = __float2half_rn(raw[s * hidden + h]);
+            const __half wv = __float2half_rn(__fmul_rn(__half2float(rv), w[s]));
+            acc = __float2half_rn(__fadd_rn(__half2float(acc), __half2float(wv)));
+        }
+        if (ok) out[i] = acc;
+    }
+}
+
+__global__ void ids_i64_to_i32_kernel(const int64_t* __restrict__ src, int n, int experts,
+                                      int32_t* __restrict__ dst, uint32_t* status) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int64_t e = src[i];
+        if (e < 0 || e >= experts) {
+            atomicOr(status, kStatusBadExpert);
+            dst[i] = -1;
+        } else {
+            dst[i] = static_cast<int32_t>(e);
+        }
+    }
+}
+
+int grid_for(size_t n, int threads, int cap) {
+    size_t g = (n + threads - 1) / threads;
+    if (g < 1) g = 1;
+    if (g > static_cast<size_t>(cap)) g = cap;
+    return static_cast<int>(g);
+}
+
+}  // namespace
+
+cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
+                              int32_t* ids, float* weights, uint32_t* status,
+                              cudaStream_t stream) {
+    if (tokens <= 0 || experts <= 0 || experts > 32 * kRouteMaxPerLane || topk <= 0 ||
+        topk > 32 || topk > experts)
+        return cudaErrorInvalidValue;
+    const int warps = 4;
+    const int grid = (tokens + warps - 1) / warps;
+    const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
+    route_topk_kernel<<<grid, warps * 32, smem, stream>>>(logits, tokens, experts, topk, ids,
+                                                           weights, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
+                           int max_tiles, const PermuteOut& out, uint32_t* status,
+                           cudaStream_t stream) {
+    if (experts <= 0 || experts > kPermMaxExperts || tokens <= 0 || topk <= 0 || n_tile_max < 16)
+        return cudaErrorInvalidValue;
+    permute_kernel<<<1, kPermThreads, 0, stream>>>(ids, tokens, topk, experts, n_tile_max,
+                                                   max_tiles, out, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,
+                               int max_rows, int topk, int hidden, __half* x_perm,
+                               cudaStream_t stream) {
+    if (hidden % 8 != 0) return cudaErrorInvalidValue;
+    const int grid = grid_for(static_cast<size_t>(max_rows) * 32, 256, 148 * 8);
+    gather_rows_kernel<<<grid, 256, 0, stream>>>(x, perm, total_rows_dev, max_rows, topk, hidden,
+                                                 x_perm);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine_f32(const float* raw, const float* weights, int tokens, int topk,
+                               int hidden, float* out, cudaStream_t stream) {
+    if (hidden % 4 != 0) return cudaErrorInvalidValue;
+    const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
+    combine_f32_kernel<<<grid_for(n4, 256, 148 * 16), 256, 0, stream>>>(raw, weights, tokens, topk,
+                                                                         hidden, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine_f16(const float* raw, const float* weights, const int64_t* ids64,
+                               int tokens, int topk, int hidden, __half* out,
+                               cudaStream_t stream) {
+    const size_t n = static_cast<size_t>(tokens) * hidden;
+    combine_f16_kernel<int64_t><<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
+        raw, weights, ids64, tokens, topk, hidden, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_combine_f16_i32(const float* raw, const float* weights, const int32_t* ids,
+                                   int tokens, int topk, int hidden, __half* out,
+                                   cudaStream_t stream) {
+    const size_t n = static_cast<size_t>(tokens) * hidden;
+    combine_f16_kernel<int32_t><<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
+        raw, weights, ids, tokens, topk, hidden, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ids_i64_to_i32(const int64_t* src, int n, int experts, int32_t* dst,
+                                  uint32_t* status, cudaStream_t stream) {
+    ids_i64_to_i32_kernel<<<grid_for(n, 256, 1024), 256, 0, stream>>>(src, n, experts, dst, status);
+    return cudaGetLastError();
+}
+
+}  // namespace dee

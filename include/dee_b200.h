@@ -1,0 +1,149 @@
+/*
+ * dee_b200.h -- C ABI of the B200-native routed-expert MoE layer.
+ *
+ * Drop-in boundary for the routed-expert FFN of so-nerdyy/dee.  Each entry
+ * point names the reference interface it replaces (paths relative to the
+ * reference project root).  Conventions follow the reference engine:
+ *   - the caller owns every input/output buffer; the engine owns expert
+ *     banks' descriptors, workspaces and its compute stream
+ *     (dee.cpp/include/dee/engine.h:302-326);
+ *   - failures return a negative status and record a message readable with
+ *     dee_last_error() (Engine::last_error_message, engine.h:434-436);
+ *   - one engine per CUDA device, driven from one host thread at a time.
+ * No torch types cross this boundary: device pointers, host pointers,
+ * sizes and CUDA stream handles (cudaStream_t passed as void*; NULL is the
+ * legacy default stream, as in engine.cpp:2011-2013).
+ */
+#ifndef DEE_B200_H
+#define DEE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DEE_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define DEE_API __attribute__((visibility("default")))
+#else
+#define DEE_API
+#endif
+
+/* Status codes. */
+#define DEE_OK 0
+#define DEE_ERR_INVALID (-1)     /* bad argument or shape                     */
+#define DEE_ERR_CUDA (-2)        /* CUDA runtime/driver error                 */
+#define DEE_ERR_RANGE (-3)       /* expert id outside [0, num_experts)        */
+#define DEE_ERR_UNSUPPORTED (-4) /* configuration this build does not cover   */
+#define DEE_ERR_DEVICE (-5)      /* a kernel reported a failure (status word) */
+#define DEE_ERR_NO_BANK (-6)     /* no expert bank attached for the layer     */
+
+typedef struct dee_engine dee_engine;
+
+/* Mirrors the EngineConfig fields the routed-expert path reads
+ * (dee.cpp/include/dee/engine.h:84-156). */
+typedef struct dee_config {
+    int hidden;          /* EngineConfig::hidden                             */
+    int inter;           /* EngineConfig::inter                              */
+    int num_experts;     /* EngineConfig::num_experts                        */
+    int topk;            /* EngineConfig::topk                               */
+    int num_layers;      /* EngineConfig::num_layers (bank slots)            */
+    int device_id;       /* EngineConfig::device_id                          */
+    float swiglu_limit;  /* EngineConfig::swiglu_limit, 0 disables the clamp */
+    int max_tokens;      /* initial workspace capacity; grows on demand      */
+} dee_config;
+
+/* sizeof(dee_config) of this build; replaces engine_abi_size()
+ * (engine.h:771-774) as the guard a binding checks before use. */
+DEE_API size_t dee_abi_config_size(void);
+DEE_API int dee_abi_version(void);
+
+/* Engine::init (engine.h:237).  Returns DEE_OK and *out on success. */
+DEE_API int dee_engine_create(const dee_config* cfg, dee_engine** out);
+DEE_API void dee_engine_destroy(dee_engine* engine);
+
+/* Engine::last_error_message (engine.h:434-436, pydee.cpp:768-772). */
+DEE_API const char* dee_last_error(const dee_engine* engine);
+
+/* Attach the packed expert records of one layer.  d_records points at
+ * n_slots records of record_bytes each in the DEE4 layout
+ * [w1][w3][w2][w1.scale][w3.scale][w2.scale]
+ * (dee.cpp/include/dee/expert_store.h:28-46; VramCacheManager::data,
+ * vram_cache.h:166-215 supplies the same per-expert device pointer).
+ * h_slot_of_expert (host, num_experts entries, may be NULL for identity)
+ * maps an expert id to its slot, -1 for "not resident". */
+DEE_API int dee_expert_bank_attach(dee_engine* engine, int layer, const void* d_records, int n_slots,
+                           size_t record_bytes, const int32_t* h_slot_of_expert);
+
+/* Update the slot table of an attached bank (offload tier residency). */
+DEE_API int dee_expert_bank_set_slots(dee_engine* engine, int layer, const int32_t* h_slot_of_expert,
+                              void* stream);
+
+/* Softmax top-k with renormalised weights on device logits [T, E] FP32 ->
+ * ids [T, K] int32 in rank order and weights [T, K] FP32.
+ * Engine::route_topk_batch (engine.cpp:2604-2771). */
+DEE_API int dee_route_topk_device(dee_engine* engine, const float* d_logits, int tokens,
+                          int32_t* d_ids, float* d_weights, void* stream);
+
+/* Engine::moe_forward_batch_device (engine.h:312-314, pydee.cpp:430-467):
+ * FP16 hidden [T, H] on device, host int32 ids [T, K] (validated on the
+ * host, fail closed), FP32 raw expert outputs [T, K, H] on device.
+ * Runs on the engine's stream and synchronises it before returning. */
+DEE_API int dee_moe_forward_batch_device(dee_engine* engine, int layer, const void* d_h_in, int tokens,
+                                 const int32_t* h_expert_ids, int topk, void* d_experts_out);
+
+/* Engine::moe_forward_combined_device (engine.h:322-326,
+ * pydee.cpp:468-509): device int64 ids, FP32 weights, FP16 output combined
+ * in stable expert order with FP16 rounding (swiglu_cuda.cu:69-116),
+ * optional FP32 raw trace [T, K, H].  Work is queued on external_stream
+ * without a host synchronisation; invalid ids are reported through
+ * dee_engine_sync_status. */
+DEE_API int dee_moe_forward_combined_device(dee_engine* engine, int layer, const void* d_h_in, int tokens,
+                                    const int64_t* d_expert_ids, int topk,
+                                    const float* d_weights_f32, void* d_output_f16,
+                                    void* d_raw_trace_out, void* external_stream);
+
+/* The live DeepSeek layer in one call: ids from device (d_ids) or host
+ * (h_ids, validated), raw expert rows and the rank-order FP32 combine
+ * out[t] = sum_r w[t, r] * raw[t, r] of
+ * dee.cpp/scripts/deepseek_v4_layer_candidate.py:616-629.  d_out_f32 and
+ * d_raw may each be NULL (not both).  Queued on `stream`, no host sync. */
+DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_x_f16, int tokens,
+                           const int32_t* d_ids, const int32_t* h_ids, int topk,
+                           const float* d_weights, float* d_out_f32, float* d_raw, void* stream);
+
+/* Synchronise `stream`, read and clear the engine's device status word.
+ * Returns DEE_ERR_DEVICE (and *status_out != 0) when a kernel flagged an
+ * invalid expert id, a router failure or a pipeline timeout. */
+DEE_API int dee_engine_sync_status(dee_engine* engine, void* stream, uint32_t* status_out);
+
+/* Host copy of the int32 [T, K] route ids the last forward consumed -- the
+ * buffer the route journal records (deepseek_v4_native_generate.py
+ * :2196-2216).  Valid after the forward's stream has been synchronised.
+ * Returns the number of ids written. */
+DEE_API int dee_journal_ids_host(dee_engine* engine, int32_t* h_out, int max_ids);
+
+/* fp4_e2m1_to_f16_cuda (dee.cpp/include/dee/cuda_convert.h:104-134,
+ * cuda_convert.cu:252-288): packed [out, in/2] + scales [out, in/32] ->
+ * FP16 [out, in]; in must be a multiple of 64. */
+DEE_API int dee_fp4_decode_device(const uint8_t* d_packed, const uint8_t* d_scale, void* d_dst_f16,
+                          size_t out, size_t in, void* stream);
+
+/* Pack FP32 [out, in] weights as E2M1 + per-32 UE8M0 scales (the layout the
+ * reference's repacker writes, repack_to_dee4.py:42-55); used to build
+ * synthetic expert banks on the device. */
+DEE_API int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_packed,
+                            uint8_t* d_scale, void* stream);
+
+/* Kernel launches issued by this engine since creation (for the bench's
+ * launch accounting). */
+DEE_API uint64_t dee_engine_launch_count(const dee_engine* engine);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DEE_B200_H */

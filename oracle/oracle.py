@@ -1,0 +1,297 @@
+"""Parity oracle for the routed-expert MoE path (TEST INFRASTRUCTURE ONLY).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` leg of
+``bench.py`` import this module.  It is the checker, never the measured or
+shipped path.
+
+It wraps two shared libraries built by ``oracle/Makefile``:
+
+* ``oracle/libdee_oracle.so`` -- the C restatement in ``dee_oracle.c``
+  (decode, router, grouping, FP16 expert chain, combines; each function
+  cites the reference line it follows).
+* ``oracle/_ref/libdee_ref.so`` -- the reference project's own CPU code
+  (``dee.cpp/src/weight_mmap.cpp`` FP4 decode and the KT-bridge
+  ``ReferenceCpuExecutor``), compiled from the reference sources.
+
+and adds numpy restatements used to build synthetic inputs:
+
+* ``quantize_fp4`` -- the published MXFP4 recipe the reference's
+  quantisation helpers follow (``dee.cpp/scripts/deepseek_v4_layer_common.py``
+  ``fast_log2_ceil``/``fast_round_scale`` :160-178 and ``round_e2m1_grid``
+  :181-211): per 32-element block, scale = 2^ceil(log2(amax / 6)) as a
+  UE8M0 byte, values divided by the scale, clamped to +-6 and rounded to the
+  E2M1 grid with ties to the even grid entry.
+* ``build_record`` -- the DEE4 record layout ``[w1][w3][w2][s1][s3][s2]``
+  (``dee.cpp/include/dee/expert_store.h:28-46``,
+  ``dee.cpp/kaggle/deepseek-v4-flash-0731/repack_to_dee4.py:42-55``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+_REF = None
+
+E2M1_TABLE = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                       0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=np.float32)
+
+
+def build_libs(with_ref: bool = False) -> None:
+    """Compile the oracle (and optionally the reference shim) in place."""
+    import subprocess
+    targets = ["all"] + (["ref"] if with_ref else [])
+    subprocess.run(["make", "-s", "-C", _HERE] + targets, check=True)
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "libdee_oracle.so")
+        if not os.path.exists(path):
+            build_libs(False)
+        L = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        L.dee_ref_f32_to_f16.restype = ctypes.c_uint16
+        L.dee_ref_f32_to_f16.argtypes = [ctypes.c_float]
+        L.dee_ref_f16_to_f32.restype = ctypes.c_float
+        L.dee_ref_f16_to_f32.argtypes = [ctypes.c_uint16]
+        L.dee_ref_scale_device.restype = ctypes.c_float
+        L.dee_ref_scale_device.argtypes = [ctypes.c_uint8]
+        L.dee_ref_scale_host.restype = ctypes.c_float
+        L.dee_ref_scale_host.argtypes = [ctypes.c_uint8]
+        L.dee_ref_fp4_decode_f16.argtypes = [P, P, P, ctypes.c_size_t, ctypes.c_size_t]
+        L.dee_ref_fp4_dequant_f32.argtypes = [P, P, ctypes.c_size_t, ctypes.c_size_t, P]
+        L.dee_ref_route_topk.restype = ctypes.c_int
+        L.dee_ref_route_topk.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P]
+        L.dee_ref_group.restype = ctypes.c_int
+        L.dee_ref_group.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P, P]
+        L.dee_ref_record_bytes.restype = ctypes.c_size_t
+        L.dee_ref_record_bytes.argtypes = [ctypes.c_int, ctypes.c_int]
+        L.dee_ref_expert_f16.argtypes = [P, ctypes.c_int, ctypes.c_int, P, ctypes.c_int, ctypes.c_float, P]
+        L.dee_ref_moe_layer.restype = ctypes.c_int
+        L.dee_ref_moe_layer.argtypes = [P, ctypes.c_size_t, P, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                        ctypes.c_int, P, ctypes.c_int, P, ctypes.c_float, ctypes.c_int, P]
+        L.dee_ref_combine_f32.argtypes = [P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+        L.dee_ref_combine_f16.argtypes = [P, P, P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P]
+        L.dee_ref_num_threads.restype = ctypes.c_int
+        _LIB = L
+    return _LIB
+
+
+def ref_lib() -> ctypes.CDLL | None:
+    """The reference's own CPU code, or None when oracle/_ref was not built."""
+    global _REF
+    if _REF is None:
+        path = os.path.join(_HERE, "_ref", "libdee_ref.so")
+        if not os.path.exists(path):
+            return None
+        L = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        L.dee_refimpl_fp4_dequantize.argtypes = [P, P, ctypes.c_size_t, ctypes.c_size_t, P]
+        L.dee_refimpl_expert.restype = ctypes.c_int
+        L.dee_refimpl_expert.argtypes = [P, ctypes.c_size_t, ctypes.c_size_t, P, ctypes.c_float,
+                                         ctypes.c_float, P]
+        L.dee_refimpl_moe_layer.restype = ctypes.c_int
+        L.dee_refimpl_moe_layer.argtypes = [P, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                            ctypes.c_int, P, ctypes.c_int, P, P, ctypes.c_float,
+                                            ctypes.c_int, P]
+        _REF = L
+    return _REF
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+# ---------------------------------------------------------------------------
+# Record layout and synthetic experts
+# ---------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class Layout:
+    hidden: int
+    inter: int
+
+    @property
+    def ih(self) -> int:
+        return self.hidden * self.inter
+
+    @property
+    def w1(self) -> int: return 0
+    @property
+    def w3(self) -> int: return self.ih // 2
+    @property
+    def w2(self) -> int: return self.ih
+    @property
+    def s1(self) -> int: return self.ih + self.ih // 2
+    @property
+    def s3(self) -> int: return self.s1 + self.ih // 32
+    @property
+    def s2(self) -> int: return self.s3 + self.ih // 32
+    @property
+    def bytes(self) -> int: return self.s2 + self.ih // 32
+
+
+def quantize_fp4(w: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """FP32 [out, in] -> (packed uint8 [out, in/2], scale uint8 [out, in/32])."""
+    w = np.asarray(w, dtype=np.float32)
+    out, n = w.shape
+    blk = w.reshape(out, n // 32, 32)
+    amax = np.abs(blk).max(axis=-1)
+    amax = np.maximum(amax, np.float32(6.0 * 2.0 ** -126))
+    v = (amax * np.float32(1.0 / 6.0)).astype(np.float32)
+    bits = v.view(np.int32)
+    e = ((bits >> 23) & 0xFF) - 127 + ((bits & 0x7FFFFF) != 0).astype(np.int32)
+    s = ((e + 127).astype(np.int64) << 23).astype(np.int32).view(np.float32)
+    q = np.clip(blk / s[..., None], -6.0, 6.0).astype(np.float32)
+    a = np.abs(q)
+    mag_idx = np.select(
+        [a <= 0.25, a < 0.75, a <= 1.25, a < 1.75, a <= 2.5, a < 3.5, a <= 5.0],
+        [0, 1, 2, 3, 4, 5, 6], default=7).astype(np.uint8)
+    nib = mag_idx | np.where((q < 0) & (mag_idx != 0), 8, 0).astype(np.uint8)
+    nib = nib.reshape(out, n)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).astype(np.uint8)
+    scale = (e + 127).astype(np.uint8)
+    return np.ascontiguousarray(packed), np.ascontiguousarray(scale)
+
+
+def build_record(layout: Layout, w1p, w1s, w3p, w3s, w2p, w2s) -> np.ndarray:
+    rec = np.empty(layout.bytes, dtype=np.uint8)
+    for off, arr in ((layout.w1, w1p), (layout.w3, w3p), (layout.w2, w2p),
+                     (layout.s1, w1s), (layout.s3, w3s), (layout.s2, w2s)):
+        a = np.ascontiguousarray(arr, dtype=np.uint8).reshape(-1)
+        rec[off:off + a.size] = a
+    return rec
+
+
+def split_record(layout: Layout, rec: np.ndarray) -> dict[str, np.ndarray]:
+    H, I = layout.hidden, layout.inter
+    return {
+        "w1.weight": rec[layout.w1:layout.w1 + I * H // 2].reshape(I, H // 2),
+        "w3.weight": rec[layout.w3:layout.w3 + I * H // 2].reshape(I, H // 2),
+        "w2.weight": rec[layout.w2:layout.w2 + I * H // 2].reshape(H, I // 2),
+        "w1.scale": rec[layout.s1:layout.s1 + I * H // 32].reshape(I, H // 32),
+        "w3.scale": rec[layout.s3:layout.s3 + I * H // 32].reshape(I, H // 32),
+        "w2.scale": rec[layout.s2:layout.s2 + I * H // 32].reshape(H, I // 32),
+    }
+
+
+def synthetic_records(layout: Layout, experts: int, seed: int, std: float = 0.02,
+                      kind: str = "normal") -> np.ndarray:
+    """[experts, record_bytes] uint8.  kind="normal": N(0, std) weights through
+    quantize_fp4.  kind="bytes": uniform random nibbles with scale bytes in
+    [0x7D, 0x83) (the reference's realistic range,
+    dee.cpp/scripts/deepseek_v4_expert_reference.py:433-436)."""
+    rng = np.random.default_rng(seed)
+    H, I = layout.hidden, layout.inter
+    recs = np.empty((experts, layout.bytes), dtype=np.uint8)
+    for e in range(experts):
+        if kind == "normal":
+            parts = []
+            for shape in ((I, H), (I, H), (H, I)):
+                w = rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
+                parts.append(quantize_fp4(w))
+            (p1, s1), (p3, s3), (p2, s2) = parts
+        else:
+            p1 = rng.integers(0, 256, (I, H // 2), dtype=np.uint8)
+            p3 = rng.integers(0, 256, (I, H // 2), dtype=np.uint8)
+            p2 = rng.integers(0, 256, (H, I // 2), dtype=np.uint8)
+            s1 = rng.integers(0x7D, 0x83, (I, H // 32), dtype=np.uint8)
+            s3 = rng.integers(0x7D, 0x83, (I, H // 32), dtype=np.uint8)
+            s2 = rng.integers(0x7D, 0x83, (H, I // 32), dtype=np.uint8)
+        recs[e] = build_record(layout, p1, s1, p3, s3, p2, s2)
+    return recs
+
+
+# ---------------------------------------------------------------------------
+# Wrappers over the C restatement
+# ---------------------------------------------------------------------------
+
+def f16_bits(x: np.ndarray) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(x, dtype=np.float32).astype(np.float16).view(np.uint16))
+
+
+def fp4_decode_f16(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    out, half_in = packed.shape
+    dst = np.empty((out, half_in * 2), dtype=np.uint16)
+    lib().dee_ref_fp4_decode_f16(_p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scale)),
+                                 _p(dst), out, half_in * 2)
+    return dst
+
+
+def fp4_dequant_f32(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    out, half_in = packed.shape
+    dst = np.empty((out, half_in * 2), dtype=np.float32)
+    lib().dee_ref_fp4_dequant_f32(_p(np.ascontiguousarray(packed)), _p(np.ascontiguousarray(scale)),
+                                  out, half_in * 2, _p(dst))
+    return dst
+
+
+def route_topk(logits: np.ndarray, topk: int) -> tuple[np.ndarray, np.ndarray]:
+    logits = np.ascontiguousarray(logits, dtype=np.float32)
+    T, E = logits.shape
+    ids = np.empty((T, topk), dtype=np.int32)
+    w = np.empty((T, topk), dtype=np.float32)
+    rc = lib().dee_ref_route_topk(_p(logits), T, E, topk, _p(ids), _p(w))
+    if rc != 0:
+        raise ValueError("router denominator or selected sum not positive and finite")
+    return ids, w
+
+
+def group(ids: np.ndarray, experts: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, K = ids.shape
+    counts = np.empty(experts, dtype=np.int32)
+    offsets = np.empty(experts + 1, dtype=np.int32)
+    perm = np.empty(T * K, dtype=np.int32)
+    if lib().dee_ref_group(_p(ids), T, K, experts, _p(counts), _p(offsets), _p(perm)) != 0:
+        raise ValueError("expert id out of range")
+    return counts, offsets, perm
+
+
+def moe_layer_raw(records: np.ndarray, layout: Layout, x_f16: np.ndarray, ids: np.ndarray,
+                  swiglu_limit: float = 0.0, threads: int = 0) -> np.ndarray:
+    """Raw FP32 [T, K, H] expert outputs under the live FP16 chain."""
+    records = np.ascontiguousarray(records, dtype=np.uint8)
+    x_f16 = np.ascontiguousarray(x_f16, dtype=np.uint16)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, K = ids.shape
+    E = records.shape[0]
+    raw = np.zeros((T, K, layout.hidden), dtype=np.float32)
+    rc = lib().dee_ref_moe_layer(_p(records), records.shape[1], None, layout.hidden, layout.inter,
+                                 E, K, _p(x_f16), T, _p(ids), swiglu_limit, threads, _p(raw))
+    if rc != 0:
+        raise ValueError("expert id out of range")
+    return raw
+
+
+def combine_f32(raw: np.ndarray, weights: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.float32)
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    T, K, H = raw.shape
+    out = np.empty((T, H), dtype=np.float32)
+    lib().dee_ref_combine_f32(_p(raw), _p(weights), T, K, H, _p(out))
+    return out
+
+
+def combine_f16(raw: np.ndarray, weights: np.ndarray, ids: np.ndarray) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.float32)
+    weights = np.ascontiguousarray(weights, dtype=np.float32)
+    ids64 = np.ascontiguousarray(ids, dtype=np.int64)
+    T, K, H = raw.shape
+    out = np.zeros((T, H), dtype=np.uint16)
+    lib().dee_ref_combine_f16(_p(raw), _p(weights), _p(ids64), T, K, H, _p(out))
+    return out
+
+
+def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.asarray(a, dtype=np.float64)
+    b = np.asarray(b, dtype=np.float64)
+    den = np.linalg.norm(b.ravel())
+    return float(np.linalg.norm((a - b).ravel()) / (den if den > 0 else 1.0))

@@ -1,0 +1,233 @@
+"""GPU parity: the CUDA path through the C ABI against the CPU oracle.
+
+Bars (stated per test): bit-exact for decode, quantise, routing ids, the
+combines given identical raw rows and the permutation; relative L2 <= 2e-3
+for expert outputs against the oracle's restatement of the reference
+dequant + cuBLAS FP16 chain.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL_REL_L2 = 2e-3
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    major, minor = torch.cuda.get_device_capability()
+    assert (major, minor) == (10, 0), f"needs sm_100 (B200), got sm_{major}{minor}"
+    from dee_b200 import build
+    build.build()
+    return torch
+
+
+@pytest.fixture(scope="module")
+def lib(torch_cuda):
+    from dee_b200 import _native
+    return _native.load()
+
+
+def _engine(H, I, E, K, layers=1, limit=0.0, max_tokens=64):
+    import dee_b200
+    return dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
+                                                     num_layers=layers, swiglu_limit=limit,
+                                                     max_tokens=max_tokens))
+
+
+def _rand_ids(rng, T, E, K, allow_dup=False):
+    if allow_dup:
+        return rng.integers(0, E, (T, K)).astype(np.int32)
+    return np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+
+
+def test_fp4_decode_bitexact(torch_cuda, lib, oracle_mod):
+    torch = torch_cuda
+    rng = np.random.default_rng(1)
+    out, n = 256, 512
+    packed = rng.integers(0, 256, (out, n // 2), dtype=np.uint8)
+    scale = np.tile(np.arange(256, dtype=np.uint8), out * (n // 32) // 256 + 1)[: out * (n // 32)]
+    scale = scale.reshape(out, n // 32)
+    dp = torch.from_numpy(packed).cuda()
+    ds = torch.from_numpy(scale).cuda()
+    dst = torch.empty((out, n), dtype=torch.float16, device="cuda")
+    assert lib.dee_fp4_decode_device(dp.data_ptr(), ds.data_ptr(), dst.data_ptr(), out, n, None) == 0
+    torch.cuda.synchronize()
+    got = dst.cpu().numpy().view(np.uint16)
+    want = oracle_mod.fp4_decode_f16(packed, scale)
+    assert np.array_equal(got, want)
+
+
+def test_fp4_quantize_matches_oracle(torch_cuda, lib, oracle_mod):
+    torch = torch_cuda
+    rng = np.random.default_rng(2)
+    w = (rng.standard_normal((128, 1024)) * 0.02).astype(np.float32)
+    w[0, :32] = 0
+    w[1, 5] = 3.0
+    dw = torch.from_numpy(w).cuda()
+    p = torch.empty((128, 512), dtype=torch.uint8, device="cuda")
+    s = torch.empty((128, 32), dtype=torch.uint8, device="cuda")
+    assert lib.dee_fp4_quantize_device(dw.data_ptr(), 128, 1024, p.data_ptr(), s.data_ptr(), None) == 0
+    torch.cuda.synchronize()
+    wp, ws = oracle_mod.quantize_fp4(w)
+    assert np.array_equal(p.cpu().numpy(), wp)
+    assert np.array_equal(s.cpu().numpy(), ws)
+
+
+@pytest.mark.parametrize("T,E,K", [(2, 3, 2), (1000, 256, 6), (37, 16, 6)])
+def test_route_topk_matches_oracle(torch_cuda, oracle_mod, T, E, K):
+    torch = torch_cuda
+    if (T, E, K) == (2, 3, 2):
+        logits = np.array([[1, 2, 3], [-1, 4, 2]], np.float32)  # test_real_router.cpp:91-116
+    else:
+        logits = (np.random.default_rng(T).standard_normal((T, E)) * 3).astype(np.float32)
+        logits[0, :8] = 1.25  # exact ties
+    eng = _engine(512, 512, E, K)
+    dl = torch.from_numpy(logits).cuda()
+    ids = torch.empty((T, K), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, K), dtype=torch.float32, device="cuda")
+    eng.route_topk_device(dl.data_ptr(), T, ids.data_ptr(), w.data_ptr())
+    assert eng.sync_status() == 0
+    ids_ref, w_ref = oracle_mod.route_topk(logits, K)
+    assert np.array_equal(ids.cpu().numpy(), ids_ref)
+    ulp = np.abs(w.cpu().numpy().view(np.int32) - w_ref.view(np.int32))
+    assert ulp.max() <= 2
+    if (T, E, K) == (2, 3, 2):
+        np.testing.assert_allclose(w.cpu().numpy(), [[0.7310586, 0.2689414], [0.8807971, 0.1192029]],
+                                   atol=1e-5)
+
+
+def _run_layer(torch, eng, bank_dev, x16, ids, weights, layer=0, raw_out=True):
+    T, K = ids.shape
+    H = eng.cfg.hidden
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    raw = torch.zeros((T, K, H), dtype=torch.float32, device="cuda")
+    assert eng.moe_forward_batch_device(layer, dx.data_ptr(), T, ids, K, raw.data_ptr()), \
+        eng.last_error_message()
+    return raw.cpu().numpy()
+
+
+@pytest.mark.parametrize("T,dup", [(1, False), (5, True), (8, False), (33, False), (300, False)])
+def test_moe_raw_small_shape(torch_cuda, oracle_mod, T, dup):
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=31 + T, kind="normal")
+    rng = np.random.default_rng(T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _rand_ids(rng, T, E, K, allow_dup=dup)
+    eng = _engine(H, I, E, K)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    raw = _run_layer(torch, eng, bank, x16, ids, None)
+    want = orc.moe_layer_raw(recs, layout, x16, ids)
+    assert np.isfinite(raw).all()
+    assert orc.rel_l2(raw, want) <= TOL_REL_L2
+    # per selection as well: no row may be silently wrong
+    per = [orc.rel_l2(raw[t, r], want[t, r]) for t in range(T) for r in range(K)]
+    assert max(per) <= 5 * TOL_REL_L2
+    assert np.array_equal(eng.journal_ids(T), ids)
+
+
+def test_combines_bitexact_given_raw(torch_cuda, oracle_mod):
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K, T = 512, 512, 16, 6, 9
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=77, kind="normal")
+    rng = np.random.default_rng(78)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _rand_ids(rng, T, E, K)
+    w = rng.random((T, K)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    eng = _engine(H, I, E, K)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    dids = torch.from_numpy(ids).cuda()
+    dids64 = dids.long()
+    dw = torch.from_numpy(w).cuda()
+    out32 = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    raw = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+    eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=dw.data_ptr(),
+                           d_out_ptr=out32.data_ptr(), d_raw_ptr=raw.data_ptr())
+    assert eng.sync_status() == 0
+    raw_np = raw.cpu().numpy()
+    assert np.array_equal(out32.cpu().numpy(), orc.combine_f32(raw_np, w))
+    out16 = torch.empty((T, H), dtype=torch.float16, device="cuda")
+    raw2 = torch.empty_like(raw)
+    stream = torch.cuda.current_stream()
+    assert eng.moe_forward_combined_device(0, dx.data_ptr(), T, dids64.data_ptr(), K, dw.data_ptr(),
+                                           out16.data_ptr(), raw2.data_ptr(), stream.cuda_stream)
+    assert eng.sync_status(stream) == 0
+    assert np.array_equal(raw2.cpu().numpy(), raw_np)  # deterministic across calls
+    assert np.array_equal(out16.cpu().numpy().view(np.uint16), orc.combine_f16(raw_np, w, ids))
+
+
+def test_rows_independent_of_batch_composition(torch_cuda, oracle_mod):
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=90, kind="normal")
+    rng = np.random.default_rng(91)
+    x16 = orc.f16_bits(rng.standard_normal((20, H)))
+    ids = _rand_ids(rng, 20, E, K)
+    eng = _engine(H, I, E, K, max_tokens=128)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    full = _run_layer(torch, eng, bank, x16, ids, None)
+    for t in (0, 7, 19):
+        alone = _run_layer(torch, eng, bank, x16[t:t + 1].copy(), ids[t:t + 1].copy(), None)
+        assert np.array_equal(alone[0], full[t])
+
+
+def test_bad_host_ids_fail_closed(torch_cuda):
+    torch = torch_cuda
+    eng = _engine(512, 512, 16, 6)
+    eng.attach_bank(0, torch.zeros((16, 417792), dtype=torch.uint8, device="cuda"))
+    dx = torch.zeros((2, 512), dtype=torch.float16, device="cuda")
+    raw = torch.zeros((2, 6, 512), dtype=torch.float32, device="cuda")
+    ids = np.array([[0, 1, 2, 3, 4, 5], [0, 1, 2, 3, 4, 16]], np.int32)
+    assert not eng.moe_forward_batch_device(0, dx.data_ptr(), 2, ids, 6, raw.data_ptr())
+    assert "outside" in eng.last_error_message()
+
+
+def test_bad_device_ids_reported(torch_cuda):
+    torch = torch_cuda
+    eng = _engine(512, 512, 16, 6)
+    eng.attach_bank(0, torch.zeros((16, 417792), dtype=torch.uint8, device="cuda"))
+    dx = torch.zeros((2, 512), dtype=torch.float16, device="cuda")
+    ids = torch.tensor([[0, 1, 2, 3, 4, 5], [0, 1, 2, 3, 4, 99]], dtype=torch.int64, device="cuda")
+    w = torch.full((2, 6), 1 / 6, dtype=torch.float32, device="cuda")
+    out = torch.empty((2, 512), dtype=torch.float16, device="cuda")
+    s = torch.cuda.current_stream()
+    assert eng.moe_forward_combined_device(0, dx.data_ptr(), 2, ids.data_ptr(), 6, w.data_ptr(),
+                                           out.data_ptr(), 0, s.cuda_stream)
+    assert eng.sync_status(s) & (1 << 4)
+
+
+@pytest.mark.parametrize("T", [8, 64])
+def test_full_shape_decode(torch_cuda, oracle_mod, T):
+    """DeepSeek-V4 shapes (H=4096, I=2048, E=256, K=6), device-built bank."""
+    torch = torch_cuda
+    orc = oracle_mod
+    from dee_b200.records import RecordLayout, synthetic_bank
+    H, I, E, K = 4096, 2048, 256, 6
+    bank = synthetic_bank(RecordLayout(H, I), E, seed=5)
+    rng = np.random.default_rng(500 + T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _rand_ids(rng, T, E, K)
+    eng = _engine(H, I, E, K)
+    eng.attach_bank(0, bank)
+    raw = _run_layer(torch, eng, bank, x16, ids, None)
+    used = np.unique(ids)
+    recs = np.zeros((E, bank.shape[1]), np.uint8)
+    recs[used] = bank[torch.from_numpy(used).cuda().long()].cpu().numpy()
+    want = orc.moe_layer_raw(recs, orc.Layout(H, I), x16, ids)
+    assert orc.rel_l2(raw, want) <= TOL_REL_L2
