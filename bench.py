@@ -1,0 +1,495 @@
+"""Benchmark of the routed-expert MoE layer (DeepSeek-V4 shapes) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dee|reference]
+
+Workload (decode): one MoE layer, H=4096,
+I=2048, 256 FP4 experts resident in HBM, top-6 softmax routing with
+renormalised weights, b=8 tokens per step (hidden ~N(0,1) drawn as bf16 and
+handed over as FP16, router W_r [4096,256] ~N(0,0.02), expert weights
+~N(0,0.02) packed E2M1 + UE8M0/32).  A step = route the step's logits, group,
+gate/up + SwiGLU, down, rank-order combine.  Each step uses a different token
+batch, and L2 is flushed (a 256 MiB write) before every timed step, outside
+its CUDA events.  The b=1 and b=64 decode points and the 4096-token prefill
+(configs[2], Zipf(1.1) expert bias) are measured in the same run and
+reported under "sweep".
+
+Multi-GPU (torchrun, one rank per GPU): each rank runs its own decode layer
+on its own token batches over the full expert bank (replicas, weak scaling);
+value = all ranks' tokens / max-over-ranks time.
+
+--impl reference times the reference's own CPU routed-expert executor
+(oracle/_ref, compiled from the reference sources) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, I, E, K = 4096, 2048, 256, 6
+RECORD_BYTES = 13_369_344
+GATE_UP_BYTES_PER_EXPERT = 2 * (H * I // 2) + 2 * (H * I // 32)   # w1, w3 + scales
+DOWN_BYTES_PER_EXPERT = H * I // 2 + H * I // 32                    # w2 + scales
+METRIC = "MoE-layer tokens/s (decode b=8, one DSv4-shaped FP4 layer)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="dee", choices=["dee", "reference"])
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload construction (device)
+# ---------------------------------------------------------------------------
+
+def make_inputs(torch, n_batches: int, b: int, seed: int, zipf: bool = False):
+    """Token batches: X ~ N(0,1) as bf16 handed over as FP16, logits = X W_r."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    w_r = torch.randn((H, E), generator=g, device="cuda", dtype=torch.float32) * 0.02
+    bias = None
+    if zipf:
+        # Zipf(s=1.1) expert popularity over a seeded permutation of experts
+        perm = torch.randperm(E, generator=g, device="cuda")
+        rank = torch.empty(E, device="cuda", dtype=torch.float32)
+        rank[perm] = torch.arange(1, E + 1, device="cuda", dtype=torch.float32)
+        p = rank.pow(-1.1)
+        bias = torch.log(p / p.sum())
+    xs, logits = [], []
+    for _ in range(n_batches):
+        x = torch.randn((b, H), generator=g, device="cuda", dtype=torch.float32).to(torch.bfloat16)
+        l = x.float() @ w_r
+        if bias is not None:
+            l = l + bias
+        xs.append(x.to(torch.float16).contiguous())
+        logits.append(l.contiguous())
+    return xs, logits
+
+
+def build_engine(torch, bank, max_tokens):
+    import dee_b200
+    eng = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
+                                                    max_tokens=max_tokens,
+                                                    device_id=torch.cuda.current_device()))
+    eng.attach_bank(0, bank)
+    return eng
+
+
+class Layer:
+    """One step of the path on device-resident inputs."""
+
+    def __init__(self, torch, eng, b):
+        self.torch = torch
+        self.eng = eng
+        self.b = b
+        self.ids = torch.empty((b, K), dtype=torch.int32, device="cuda")
+        self.w = torch.empty((b, K), dtype=torch.float32, device="cuda")
+        self.out = torch.empty((b, H), dtype=torch.float32, device="cuda")
+
+    def __call__(self, x, logits, stream):
+        self.eng.route_topk_device(logits.data_ptr(), self.b, self.ids.data_ptr(), self.w.data_ptr(),
+                                   stream)
+        self.eng.moe_forward_device(0, x.data_ptr(), self.b, d_ids_ptr=self.ids.data_ptr(),
+                                    d_weights_ptr=self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),
+                                    stream=stream)
+
+
+def time_steps(torch, fn, n_steps, flush, stream, warmup):
+    """Per-step CUDA-event times (ms) with an L2 flush before each step."""
+    torch.cuda.synchronize()  # inputs were produced on the default stream
+    for i in range(warmup):
+        fn(i, stream)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_steps)]
+    for i in range(n_steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        evs[i][0].record(stream)
+        fn(i, stream)
+        evs[i][1].record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def unique_experts(torch, ids_list):
+    return [int(torch.unique(ids).numel()) for ids in ids_list]
+
+
+def decode_point(torch, eng, b, n_steps, warmup, flush, stream, seed, profile=True):
+    xs, logits = make_inputs(torch, max(n_steps, warmup, 1), b, seed)
+    layer = Layer(torch, eng, b)
+    ids_seen = []
+
+    def fn(i, s):
+        layer(xs[i % len(xs)], logits[i % len(xs)], s)
+
+    times = time_steps(torch, fn, n_steps, flush, stream, warmup)
+    # unique experts per step (same routing as the timed steps)
+    for i in range(n_steps):
+        layer(xs[i % len(xs)], logits[i % len(xs)], stream)
+        with torch.cuda.stream(stream):
+            ids_seen.append(layer.ids.clone())
+    torch.cuda.synchronize()
+    uniq = unique_experts(torch, ids_seen)
+    stages = None
+    if profile:
+        eng.set_profiling(True)
+        acc = {}
+        for i in range(n_steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            layer(xs[i % len(xs)], logits[i % len(xs)], stream)
+            for k, v in eng.stage_ms().items():
+                acc.setdefault(k, []).append(v)
+        eng.set_profiling(False)
+        stages = {k: statistics.mean(v) for k, v in acc.items()}
+    status = eng.sync_status(stream)
+    if status:
+        raise RuntimeError(f"device status {status:#x}: {eng.last_error_message()}")
+    return times, uniq, stages
+
+
+def layer_bytes(b, u):
+    return u * RECORD_BYTES + b * H * 2 + b * H * 4 + b * E * 4 + b * K * 8
+
+
+def e2e_point(torch, eng, b, n_steps, warmup, flush, stream, seed):
+    """Same metric through the public C-ABI calls with host buffers: H2D of
+    the step's hidden states and logits from pinned memory, the layer, D2H
+    of the FP32 output into pinned memory, all inside the timed region."""
+    xs, logits = make_inputs(torch, max(n_steps, warmup, 1), b, seed)
+    hx = [x.cpu().pin_memory() for x in xs]
+    hl = [l.cpu().pin_memory() for l in logits]
+    dx = torch.empty((b, H), dtype=torch.float16, device="cuda")
+    dl = torch.empty((b, E), dtype=torch.float32, device="cuda")
+    hout = torch.empty((b, H), dtype=torch.float32).pin_memory()
+    layer = Layer(torch, eng, b)
+
+    def fn(i, s):
+        j = i % len(hx)
+        with torch.cuda.stream(s):
+            dx.copy_(hx[j], non_blocking=True)
+            dl.copy_(hl[j], non_blocking=True)
+        layer(dx, dl, s)
+        with torch.cuda.stream(s):
+            hout.copy_(layer.out, non_blocking=True)
+
+    times = time_steps(torch, fn, n_steps, flush, stream, warmup)
+    h2d = b * H * 2 + b * E * 4
+    d2h = b * H * 4
+    return times, h2d, d2h
+
+
+def prefill_point(torch, eng, n_steps, warmup, flush, stream, seed):
+    T = 4096
+    xs, logits = make_inputs(torch, max(min(n_steps, 4), 1), T, seed, zipf=True)
+    layer = Layer(torch, eng, T)
+
+    def fn(i, s):
+        layer(xs[i % len(xs)], logits[i % len(xs)], s)
+
+    times = time_steps(torch, fn, n_steps, flush, stream, warmup)
+    eng.set_profiling(True)
+    with torch.cuda.stream(stream):
+        flush.zero_()
+    fn(0, stream)
+    stages = eng.stage_ms()
+    eng.set_profiling(False)
+    torch.cuda.synchronize()
+    counts = torch.bincount(layer.ids.flatten().long(), minlength=E)
+    return times, stages, counts
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's own FP32 routed-expert executor
+# ---------------------------------------------------------------------------
+
+def cpu_reference_sample(b, seed, min_seconds=8.0, max_reps=50):
+    """Time dee_refimpl_moe_layer (ReferenceCpuExecutor fanned out over every
+    host thread) on one b-token decode layer.  Records are random-byte FP4
+    with scale bytes in [0x7D, 0x83): the executor's cost does not depend on
+    the values.  Returns (tokens/s, threads, reps, seconds)."""
+    import numpy as np
+    from oracle import oracle as orc
+    ref = orc.ref_lib()
+    if ref is None:
+        return None
+    rng = np.random.default_rng(seed)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(b)]).astype(np.int32)
+    used, remap = np.unique(ids, return_inverse=True)
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, len(used), seed=seed, kind="bytes")
+    ids_local = remap.reshape(ids.shape).astype(np.int32)
+    x = rng.standard_normal((b, H)).astype(np.float16).astype(np.float32)
+    w = rng.random((b, K)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    out = np.empty((b, H), np.float32)
+    threads = len(os.sched_getaffinity(0))
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        rc = ref.dee_refimpl_moe_layer(recs.ctypes.data, recs.shape[1], H, I, K, x.ctypes.data, b,
+                                       ids_local.ctypes.data, w.ctypes.data, 0.0, threads,
+                                       out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(f"reference executor error {rc}")
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds or reps >= max_reps:
+            break
+    return b * reps / el, threads, reps, el
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    b = args.batch
+    cpu_model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu_model = next((ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")), "")
+    except OSError:
+        pass
+    res = cpu_reference_sample(b, seed=7, min_seconds=1.0, max_reps=1)
+    if res is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built"}))
+        return
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, threads, reps, el = cpu_reference_sample(b, seed=7 + i, min_seconds=0.0, max_reps=1)
+        if i >= args.warmup:
+            vals.append((v, el))
+    total_tokens = b * len(vals)
+    total_s = sum(el for _, el in vals)
+    value = total_tokens / total_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000 * total_s / len(vals), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"cfg1-decode-b{b}", "hidden": H, "inter": I, "experts": E, "topk": K,
+                   "tokens_per_step": b},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"one b={b} decode layer per step ({b * K} token-expert selections) "
+                                   f"through the reference ReferenceCpuExecutor on {threads} threads; "
+                                   f"random-byte FP4 records", "cpu": cpu_model},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+# ---------------------------------------------------------------------------
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from dee_b200.records import RecordLayout, synthetic_bank
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    hbm_peak, tc_peak, peak_kind = load_peaks()
+    b = args.batch
+    bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
+    eng = build_engine(torch, bank, max_tokens=max(b, 64))
+    stream = torch.cuda.Stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    launches0 = eng.launch_count()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- timed region: the headline decode point ----
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        times, uniq, stages = decode_point(torch, eng, b, args.steps, args.warmup, flush, stream,
+                                           seed=1000 + rank, profile=False)
+    torch.cuda.synchronize()
+    barrier()
+    # route + permute + gather + gate/up + down + combine, counted by the engine
+    per_step_launches = (eng.launch_count() - launches0) / (args.steps * 2 + args.warmup)
+    total_ms = sum(times)
+    if world > 1:
+        t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * b * args.steps / (total_ms / 1000.0)
+
+    # ---- roofline pass (stage events on the launch stream) ----
+    _, uniq_p, stages = decode_point(torch, eng, b, min(args.steps, 20), 1, flush, stream,
+                                     seed=1000 + rank, profile=True)
+    u_mean = statistics.mean(uniq_p)
+    gu_bytes = u_mean * GATE_UP_BYTES_PER_EXPERT + b * K * H * 2 + b * K * I * 2
+    gu_ms = stages.get("gate_up", float("nan"))
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+    layer_ms = statistics.mean(times)
+    layer_gbs = statistics.mean(layer_bytes(b, u) for u in uniq) / (layer_ms / 1000.0) / 1e9
+
+    result = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": layer_ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic",
+        "config": {"workload": f"cfg1-decode-b{b}", "hidden": H, "inter": I, "experts": E, "topk": K,
+                   "tokens_per_step": b, "experts_resident": E, "weights": "fp4-e2m1+ue8m0/32",
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "unique_experts_per_step": statistics.mean(uniq)},
+        "hbm_gbs_layer": layer_gbs,
+        "hbm_frac_layer": layer_gbs / hbm_peak,
+        "stage_ms": stages,
+        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel<gate_up>", "achieved": achieved,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
+                     "algorithmic_bytes_per_launch": gu_bytes},
+        "gpu_launches": int(round(per_step_launches * args.steps)),
+        "gpu_launches_per_step": per_step_launches,
+    }
+    result["clocks"] = clk.summary()
+
+    # ---- e2e through the C ABI with host buffers ----
+    e_times, h2d, d2h = e2e_point(torch, eng, b, args.steps, args.warmup, flush, stream, seed=2000 + rank)
+    e_ms = sum(e_times)
+    if world > 1:
+        t = torch.tensor([e_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    result["e2e"] = {"value": world * b * args.steps / (e_ms / 1000.0), "unit": "tokens/s",
+                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    # ---- sweep: b = 1, 64 and the 4096-token prefill ----
+    if not args.no_sweep:
+        sweep = {}
+        for bb in (1, 64):
+            if bb == b:
+                continue
+            st, uq, sg = decode_point(torch, eng, bb, max(10, args.steps // 2), 3, flush, stream,
+                                      seed=3000 + bb + rank, profile=True)
+            ms = statistics.mean(st)
+            gbs = statistics.mean(layer_bytes(bb, u) for u in uq) / (ms / 1000.0) / 1e9
+            sweep[f"decode_b{bb}"] = {"tokens_per_s": bb / (ms / 1000.0), "ms": ms,
+                                      "unique_experts": statistics.mean(uq), "hbm_gbs": gbs,
+                                      "hbm_frac": gbs / hbm_peak, "stage_ms": sg}
+        pt, psg, counts = prefill_point(torch, eng, 5, 2, flush, stream, seed=4000 + rank)
+        pms = statistics.mean(pt)
+        flops = 6 * 4096 * 3 * 2 * H * I
+        gemm_ms = psg.get("gate_up", 0) + psg.get("down", 0)
+        sweep["prefill_t4096"] = {"tokens_per_s": 4096 / (pms / 1000.0), "ms": pms,
+                                  "tflops_layer": flops / (pms / 1000.0) / 1e12,
+                                  "tc_frac_layer": flops / (pms / 1000.0) / 1e12 / tc_peak,
+                                  "tflops_gemms": flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None,
+                                  "stage_ms": psg, "max_expert_rows": int(counts.max()),
+                                  "active_experts": int((counts > 0).sum())}
+        result["sweep"] = sweep
+
+    # ---- CPU baseline (rank 0, N=1): the reference executor on host cores ----
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res = cpu_reference_sample(b, seed=7)
+        if res is not None:
+            v, threads, reps, el = res
+            result["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": threads,
+                                      "kind": "reference",
+                                      "sample": f"{reps} x one b={b} decode layer ({b * K} selections) "
+                                                f"through ReferenceCpuExecutor, {el:.1f} s"}
+    if world > 1:
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
+if __name__ == "__main__":
+    main()

@@ -102,6 +102,18 @@ class Engine:
     def launch_count(self) -> int:
         return int(self._lib.dee_engine_launch_count(self._h))
 
+    def set_profiling(self, enable: bool) -> None:
+        self._check(self._lib.dee_engine_set_profiling(self._h, int(bool(enable))),
+                    "dee_engine_set_profiling")
+
+    def stage_ms(self) -> dict[str, float]:
+        """Per-stage milliseconds of the most recent profiled forward."""
+        buf = (ctypes.c_float * len(_native.STAGES))()
+        n = self._lib.dee_engine_stage_ms(self._h, buf, len(_native.STAGES))
+        if n < 0:
+            self._check(n, "dee_engine_stage_ms")
+        return {name: float(buf[i]) for i, name in enumerate(_native.STAGES) if buf[i] >= 0}
+
     # -- expert residency ------------------------------------------------
     def attach_bank(self, layer: int, records, slot_of_expert: np.ndarray | None = None) -> None:
         """records: device uint8 tensor [n_slots, record_bytes] (DEE4 layout)."""
@@ -155,6 +167,16 @@ class Engine:
                                              ctypes.c_void_p(d_ids_ptr), ctypes.c_void_p(d_weights_ptr),
                                              ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_route_topk_device")
+
+    def route_dsv4_device(self, d_logits_ptr: int, tokens: int, d_ids_ptr: int, d_weights_ptr: int, *,
+                          d_bias_ptr: int = 0, d_tid2eid_ptr: int = 0, d_input_ids_ptr: int = 0,
+                          route_scale: float = 1.5, stream=None) -> None:
+        rc = self._lib.dee_route_dsv4_device(
+            self._h, ctypes.c_void_p(d_logits_ptr), ctypes.c_void_p(d_bias_ptr or 0),
+            ctypes.c_void_p(d_tid2eid_ptr or 0), ctypes.c_void_p(d_input_ids_ptr or 0), tokens,
+            float(route_scale), ctypes.c_void_p(d_ids_ptr), ctypes.c_void_p(d_weights_ptr),
+            ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_route_dsv4_device")
 
     def moe_forward_device(self, layer: int, d_x_ptr: int, tokens: int, *, d_ids_ptr: int = 0,
                            h_ids: np.ndarray | None = None, d_weights_ptr: int = 0,

@@ -48,6 +48,7 @@ SIGNATURES = {
     "dee_expert_bank_attach": (I, [P, I, P, I, SZ, P]),
     "dee_expert_bank_set_slots": (I, [P, I, P, P]),
     "dee_route_topk_device": (I, [P, P, I, P, P, P]),
+    "dee_route_dsv4_device": (I, [P, P, P, P, P, I, ctypes.c_float, P, P, P]),
     "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),
     "dee_moe_forward_combined_device": (I, [P, I, P, I, P, I, P, P, P, P]),
     "dee_moe_forward_device": (I, [P, I, P, I, P, P, I, P, P, P, P]),
@@ -56,7 +57,11 @@ SIGNATURES = {
     "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),
     "dee_fp4_quantize_device": (I, [P, SZ, SZ, P, P, P]),
     "dee_engine_launch_count": (ctypes.c_uint64, [P]),
+    "dee_engine_set_profiling": (I, [P, I]),
+    "dee_engine_stage_ms": (I, [P, P, I]),
 }
+
+STAGES = ("route", "permute", "gather", "gate_up", "down", "combine")
 
 _lib = None
 

@@ -59,6 +59,9 @@ RecordLayout record_layout(int hidden, int inter) {
     return L;
 }
 
+enum Stage : int { kStageRoute = 0, kStagePermute, kStageGather, kStageGateUp, kStageDown,
+                   kStageCombine, kStageCount };
+
 struct Bank {
     bool attached = false;
     const uint8_t* records = nullptr;
@@ -102,6 +105,13 @@ struct dee_engine {
     size_t h_ids_count = 0;
     CUtensorMap map_xperm, map_act;
     uint64_t launches = 0;
+    // Opt-in stage timing (the role of the reference's StageProfiler,
+    // dee.cpp/include/dee/profiling.h:31-46): events recorded on the launch
+    // stream around each stage of the most recent forward.
+    bool profile = false;
+    cudaEvent_t ev_start[dee::kStageCount] = {};
+    cudaEvent_t ev_end[dee::kStageCount] = {};
+    bool ev_used[dee::kStageCount] = {};
 };
 
 namespace dee {
@@ -110,6 +120,19 @@ namespace {
 int fail(dee_engine* e, int code, const std::string& msg) {
     if (e) e->last_error = msg;
     return code;
+}
+
+// Stage timing: when profiling is on, each stage of a forward is bracketed
+// by two events recorded on the stream the stage is launched on.
+void stage_begin(dee_engine* e, int st, cudaStream_t stream) {
+    if (!e->profile) return;
+    cudaEventRecord(e->ev_start[st], stream);
+}
+
+void stage_end(dee_engine* e, int st, cudaStream_t stream) {
+    if (!e->profile) return;
+    cudaEventRecord(e->ev_end[st], stream);
+    e->ev_used[st] = true;
 }
 
 int cuda_fail(dee_engine* e, cudaError_t err, const char* what) {
@@ -227,12 +250,16 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     const int n_max = gemm_n_max(large);
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles};
+    stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    stage_end(e, kStagePermute, stream);
+    stage_begin(e, kStageGather, stream);
     err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H,
                              e->d_xperm, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gather launch");
+    stage_end(e, kStageGather, stream);
 
     GemmArgs a{};
     a.hidden = H;
@@ -253,14 +280,18 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3; gm.b = e->map_xperm;
     a.k_total = H;
     a.m_tiles = I / 64;
+    stage_begin(e, kStageGateUp, stream);
     err = launch_moe_gemm(true, large, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
+    stage_end(e, kStageGateUp, stream);
 
     gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2; gm.b = e->map_act;
     a.k_total = I;
     a.m_tiles = H / 128;
+    stage_begin(e, kStageDown, stream);
     err = launch_moe_gemm(false, large, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "down GEMM launch");
+    stage_end(e, kStageDown, stream);
     e->launches += 4;
     return DEE_OK;
 }
@@ -314,6 +345,10 @@ void dee_engine_destroy(dee_engine* e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     free_workspace(e);
     for (auto& b : e->banks) cudaFree(b.d_slot_of);
+    for (int i = 0; i < kStageCount; ++i) {
+        if (e->ev_start[i]) cudaEventDestroy(e->ev_start[i]);
+        if (e->ev_end[i]) cudaEventDestroy(e->ev_end[i]);
+    }
     cudaFree(e->d_status);
     if (e->h_status) cudaFreeHost(e->h_status);
     if (e->stream) cudaStreamDestroy(e->stream);
@@ -417,9 +452,28 @@ int dee_route_topk_device(dee_engine* e, const float* d_logits, int tokens, int3
     if (rc != DEE_OK) return rc;
     if (!d_logits || !d_ids || !d_weights || tokens <= 0)
         return fail(e, DEE_ERR_INVALID, "invalid router arguments");
+    stage_begin(e, kStageRoute, static_cast<cudaStream_t>(stream));
     cudaError_t err = launch_route_topk(d_logits, tokens, e->cfg.num_experts, e->cfg.topk, d_ids,
                                         d_weights, e->d_status, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(e, err, "router launch");
+    stage_end(e, kStageRoute, static_cast<cudaStream_t>(stream));
+    e->launches += 1;
+    return DEE_OK;
+}
+
+int dee_route_dsv4_device(dee_engine* e, const float* d_logits, const float* d_bias,
+                          const int64_t* d_tid2eid, const int64_t* d_input_ids, int tokens,
+                          float route_scale, int32_t* d_ids, float* d_weights, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_logits || !d_ids || !d_weights || tokens <= 0 || (d_tid2eid && !d_input_ids))
+        return fail(e, DEE_ERR_INVALID, "invalid DSv4 router arguments");
+    stage_begin(e, kStageRoute, static_cast<cudaStream_t>(stream));
+    cudaError_t err = launch_route_dsv4(d_logits, d_bias, d_tid2eid, d_input_ids, tokens,
+                                        e->cfg.num_experts, e->cfg.topk, route_scale, d_ids,
+                                        d_weights, e->d_status, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(e, err, "DSv4 router launch");
+    stage_end(e, kStageRoute, static_cast<cudaStream_t>(stream));
     e->launches += 1;
     return DEE_OK;
 }
@@ -456,8 +510,10 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
                           stream)) != DEE_OK)
         return rc;
     if (d_out_f32) {
+        stage_begin(e, kStageCombine, stream);
         err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
+        stage_end(e, kStageCombine, stream);
         e->launches += 1;
     }
     return DEE_OK;
@@ -501,9 +557,11 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_h_in), tokens, e->d_ids, raw,
                           stream)) != DEE_OK)
         return rc;
+    stage_begin(e, kStageCombine, stream);
     err = launch_combine_f16(raw, d_weights_f32, d_expert_ids, tokens, topk, e->cfg.hidden,
                              static_cast<__half*>(d_output_f16), stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "FP16 combine launch");
+    stage_end(e, kStageCombine, stream);
     e->launches += 2;
     return DEE_OK;
 }
@@ -558,5 +616,35 @@ int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_
 }
 
 uint64_t dee_engine_launch_count(const dee_engine* e) { return e ? e->launches : 0; }
+
+int dee_engine_set_profiling(dee_engine* e, int enable) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (enable && !e->ev_start[0]) {
+        for (int i = 0; i < kStageCount; ++i) {
+            cudaError_t err = cudaEventCreate(&e->ev_start[i]);
+            if (err == cudaSuccess) err = cudaEventCreate(&e->ev_end[i]);
+            if (err != cudaSuccess) return cuda_fail(e, err, "profiling event creation");
+        }
+    }
+    e->profile = enable != 0;
+    for (int i = 0; i < kStageCount; ++i) e->ev_used[i] = false;
+    return DEE_OK;
+}
+
+int dee_engine_stage_ms(dee_engine* e, float* out_ms, int n) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!out_ms || n < 0) return DEE_ERR_INVALID;
+    const int m = n < kStageCount ? n : kStageCount;
+    for (int i = 0; i < m; ++i) {
+        out_ms[i] = -1.0f;
+        if (!e->profile || !e->ev_used[i]) continue;
+        cudaError_t err = cudaEventSynchronize(e->ev_end[i]);
+        if (err == cudaSuccess) err = cudaEventElapsedTime(&out_ms[i], e->ev_start[i], e->ev_end[i]);
+        if (err != cudaSuccess) return cuda_fail(e, err, "stage timing readback");
+    }
+    return m;
+}
 
 }  // extern "C"

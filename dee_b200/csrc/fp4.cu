@@ -38,11 +38,14 @@ __global__ void fp4_decode_kernel(const uint8_t* __restrict__ packed,
         const size_t c = i - o * half_in;  // byte column: elements 2c, 2c+1
         const uint32_t byte = packed[i];
         const float s = scale_value(scale[o * (in >> 5) + ((2 * c) >> 5)]);
-        const uint32_t pair = cvt_e2m1x2(byte);
+        // nibble 8 decodes to -0 in E2M1 but the reference table holds +0
+        // there (cuda_convert.cu:212-215): clear that sign before scaling.
+        uint32_t pair = cvt_e2m1x2(byte);
+        if ((pair & 0xFFFFu) == 0x8000u) pair &= 0xFFFF0000u;
+        if ((pair >> 16) == 0x8000u) pair &= 0x0000FFFFu;
         const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&pair));
-        // +0.0f turns the decoded -0 of nibble 8 into the table's +0
-        const __half lo = __float2half_rn(__fadd_rn(__fmul_rn(v.x, s), 0.0f));
-        const __half hi = __float2half_rn(__fadd_rn(__fmul_rn(v.y, s), 0.0f));
+        const __half lo = __float2half_rn(__fmul_rn(v.x, s));
+        const __half hi = __float2half_rn(__fmul_rn(v.y, s));
         reinterpret_cast<__half2*>(dst)[i] = __halves2half2(lo, hi);
     }
 }

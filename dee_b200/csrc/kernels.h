@@ -24,6 +24,13 @@ cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, cons
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
                               int32_t* ids, float* weights, uint32_t* status, cudaStream_t stream);
 
+// DeepSeek-V4 router: sqrt(softplus) scores, bias for selection only (may be
+// null), hash selection from tid2eid[input_ids] when tid2eid is non-null.
+cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int64_t* tid2eid,
+                              const int64_t* input_ids, int tokens, int experts, int topk,
+                              float route_scale, int32_t* ids, float* weights, uint32_t* status,
+                              cudaStream_t stream);
+
 // Group-by-expert permutation (one CTA): counts/offsets per expert, grouped
 // row -> position table, position -> row table, and the GEMM tile list.
 struct PermuteOut {

@@ -116,6 +116,91 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, 
     }
 }
 
+// DeepSeek-V4 router (Gate.forward as restated by the reference,
+// dee.cpp/scripts/deepseek_v4_layer_common.py:349-403 and
+// deepseek_v4_expert_reference.py:132-163): score = sqrt(softplus(logit))
+// (softplus threshold 20), the bias shifts only the selection, top-k by the
+// biased score (ties -> lower expert id), weights = unbiased scores of the
+// selected experts / their sum, times route_scale.  Hash layers select
+// tid2eid[input_id] instead of top-k.  One warp per token.
+__global__ void route_dsv4_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                                  const int64_t* __restrict__ tid2eid,
+                                  const int64_t* __restrict__ input_ids, int tokens, int experts,
+                                  int topk, float route_scale, int32_t* __restrict__ ids,
+                                  float* __restrict__ weights, uint32_t* status) {
+    extern __shared__ float dsv4_smem[];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    float* sc = dsv4_smem + warp * experts;  // unbiased scores
+    const float* l = logits + static_cast<size_t>(t) * experts;
+    const int nper = (experts + 31) >> 5;
+    Cand mine[kRouteMaxPerLane];
+#pragma unroll
+    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+        const int e = lane + 32 * j;
+        if (j < nper && e < experts) {
+            const float x = l[e];
+            const float sp = x > 20.0f ? x : log1pf(expf(x));
+            const float s = sqrtf(sp);
+            sc[e] = s;
+            mine[j].p = bias ? __fadd_rn(s, bias[e]) : s;
+            mine[j].id = e;
+        } else {
+            mine[j].p = -INFINITY;
+            mine[j].id = 0x7fffffff;
+        }
+    }
+    __syncwarp();
+    int sel_id[32];
+    if (tid2eid) {
+        const int64_t tok = input_ids[t];
+        for (int k = 0; k < topk; ++k) {
+            const int64_t e = tid2eid[tok * topk + k];
+            sel_id[k] = (e >= 0 && e < experts) ? static_cast<int>(e) : -1;
+        }
+    } else {
+        for (int k = 0; k < topk; ++k) {
+            Cand best{-INFINITY, 0x7fffffff};
+            int best_j = -1;
+#pragma unroll
+            for (int j = 0; j < kRouteMaxPerLane; ++j) {
+                if (mine[j].id != 0x7fffffff && (best_j < 0 || better(mine[j], best))) {
+                    best = mine[j];
+                    best_j = j;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                Cand other;
+                other.p = __shfl_xor_sync(0xffffffffu, best.p, o);
+                other.id = __shfl_xor_sync(0xffffffffu, best.id, o);
+                if (other.id != 0x7fffffff && (best.id == 0x7fffffff || better(other, best))) best = other;
+            }
+            sel_id[k] = best.id;
+#pragma unroll
+            for (int j = 0; j < kRouteMaxPerLane; ++j)
+                if (mine[j].id == best.id) mine[j].id = 0x7fffffff;
+        }
+    }
+    if (lane == 0) {
+        float sum = 0.0f;
+        bool ok = true;
+        for (int k = 0; k < topk; ++k) {
+            if (sel_id[k] < 0 || sel_id[k] >= experts) { ok = false; break; }
+            sum = __fadd_rn(sum, sc[sel_id[k]]);
+        }
+        if (!ok || !(sum > 0.0f)) atomicOr(status, kStatusBadRouter);
+        for (int k = 0; k < topk; ++k) {
+            const bool good = ok && sum > 0.0f;
+            ids[static_cast<size_t>(t) * topk + k] = good ? sel_id[k] : 0;
+            weights[static_cast<size_t>(t) * topk + k] =
+                good ? __fmul_rn(__fdiv_rn(sc[sel_id[k]], sum), route_scale) : 0.0f;
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Permutation.  Selections are enumerated in the reference's grouping order
 // j = rank * T + token (engine.cpp:812-823: for each expert, rank-major then
@@ -345,6 +430,22 @@ cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int 
     const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
     route_topk_kernel<<<grid, warps * 32, smem, stream>>>(logits, tokens, experts, topk, ids,
                                                            weights, status);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int64_t* tid2eid,
+                              const int64_t* input_ids, int tokens, int experts, int topk,
+                              float route_scale, int32_t* ids, float* weights, uint32_t* status,
+                              cudaStream_t stream) {
+    if (tokens <= 0 || experts <= 0 || experts > 32 * kRouteMaxPerLane || topk <= 0 ||
+        topk > 32 || topk > experts || (tid2eid && !input_ids))
+        return cudaErrorInvalidValue;
+    const int warps = 4;
+    const int grid = (tokens + warps - 1) / warps;
+    const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
+    route_dsv4_kernel<<<grid, warps * 32, smem, stream>>>(logits, bias, tid2eid, input_ids, tokens,
+                                                          experts, topk, route_scale, ids, weights,
+                                                          status);
     return cudaGetLastError();
 }
 

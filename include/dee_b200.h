@@ -88,6 +88,18 @@ DEE_API int dee_expert_bank_set_slots(dee_engine* engine, int layer, const int32
 DEE_API int dee_route_topk_device(dee_engine* engine, const float* d_logits, int tokens,
                           int32_t* d_ids, float* d_weights, void* stream);
 
+/* DeepSeek-V4 router on device logits [T, E] (x . W_gate^T, FP32):
+ * score = sqrt(softplus(logit)); d_bias (E floats, may be NULL) shifts only
+ * the selection; top-k by biased score, ties to the lower id; weights =
+ * selected unbiased scores / their sum * route_scale.  With d_tid2eid
+ * ([vocab, K] int64) and d_input_ids ([T] int64) the selection is the hash
+ * table row instead (hash layers).  Replaces the torch router of
+ * dee.cpp/scripts/deepseek_v4_layer_candidate.py:99-120
+ * (deepseek_v4_layer_common.py:349-403). */
+DEE_API int dee_route_dsv4_device(dee_engine* engine, const float* d_logits, const float* d_bias,
+                                  const int64_t* d_tid2eid, const int64_t* d_input_ids, int tokens,
+                                  float route_scale, int32_t* d_ids, float* d_weights, void* stream);
+
 /* Engine::moe_forward_batch_device (engine.h:312-314, pydee.cpp:430-467):
  * FP16 hidden [T, H] on device, host int32 ids [T, K] (validated on the
  * host, fail closed), FP32 raw expert outputs [T, K, H] on device.
@@ -141,6 +153,18 @@ DEE_API int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uin
 /* Kernel launches issued by this engine since creation (for the bench's
  * launch accounting). */
 DEE_API uint64_t dee_engine_launch_count(const dee_engine* engine);
+
+/* Opt-in stage timing, the role of the reference's StageProfiler
+ * (dee.cpp/include/dee/profiling.h:31-46, GpuStage): when enabled every
+ * stage of a forward is bracketed by CUDA events on its launch stream.
+ * Stages: 0 route, 1 permute, 2 gather, 3 gate/up GEMM, 4 down GEMM,
+ * 5 combine. */
+DEE_API int dee_engine_set_profiling(dee_engine* engine, int enable);
+
+/* Milliseconds of each stage of the most recent profiled forward (-1 for a
+ * stage that did not run).  Waits for the stage events.  Returns the number
+ * of entries written. */
+DEE_API int dee_engine_stage_ms(dee_engine* engine, float* out_ms, int n);
 
 #ifdef __cplusplus
 }

@@ -244,6 +244,33 @@ def route_topk(logits: np.ndarray, topk: int) -> tuple[np.ndarray, np.ndarray]:
     return ids, w
 
 
+def route_dsv4(logits: np.ndarray, topk: int, bias: np.ndarray | None = None,
+               route_scale: float = 1.5, tid2eid: np.ndarray | None = None,
+               input_ids: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """DeepSeek-V4 Gate.forward restated in numpy FP32
+    (dee.cpp/scripts/deepseek_v4_layer_common.py:349-403): scores =
+    sqrt(softplus(logits)) with softplus threshold 20; bias shifts only the
+    selection; top-k by biased score with ties to the lower id (hash layers:
+    tid2eid[input_ids]); weights = selected unbiased scores / their sum *
+    route_scale.  Returns (ids int32, weights f32, unbiased scores f32)."""
+    x = np.ascontiguousarray(logits, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        sp = np.where(x > 20.0, x, np.log1p(np.exp(x.astype(np.float64))).astype(np.float32))
+    scores = np.sqrt(sp.astype(np.float32)).astype(np.float32)
+    T, E = scores.shape
+    if tid2eid is not None:
+        ids = np.asarray(tid2eid)[np.asarray(input_ids)].astype(np.int32)
+    else:
+        sel = scores + (bias.astype(np.float32) if bias is not None else np.float32(0))
+        ids = np.lexsort((np.tile(np.arange(E), (T, 1)), -sel), axis=1)[:, :topk].astype(np.int32)
+    w = np.take_along_axis(scores, ids, 1)
+    s = np.zeros(T, np.float32)
+    for k in range(topk):
+        s = (s + w[:, k]).astype(np.float32)
+    w = ((w / s[:, None]).astype(np.float32) * np.float32(route_scale)).astype(np.float32)
+    return ids, w, scores
+
+
 def group(ids: np.ndarray, experts: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
     ids = np.ascontiguousarray(ids, dtype=np.int32)
     T, K = ids.shape

@@ -109,8 +109,18 @@ def make_moe_layer() -> None:
     res = moe.moe_layer_forward(torch.from_numpy(x), torch.from_numpy(gate_w), torch.from_numpy(bias),
                                 routed, None, topk=6, route_scale=1.5, score_func="sqrtsoftplus",
                                 swiglu_limit=10.0)
+    # the router's logits by the reference's own expression (router_scores :146)
+    logits = (torch.from_numpy(x).float() @ torch.from_numpy(gate_w).float().transpose(0, 1)).numpy()
+    # a hash layer (router_select with tid2eid, layer_common.py:387-392)
+    tid2eid = np.stack([rng.choice(E, 6, replace=False) for _ in range(50)]).astype(np.int64)
+    input_ids = rng.integers(0, 50, 7).astype(np.int64)
+    _, h_idx, h_w = common.router_select(torch.from_numpy(x), torch.from_numpy(gate_w), None,
+                                         tid2eid=torch.from_numpy(tid2eid),
+                                         input_ids=torch.from_numpy(input_ids), topk=6,
+                                         route_scale=1.5, score_func="sqrtsoftplus")
     np.savez_compressed(HERE / "moe_layer.npz", records_seed=404, records_sha256=_sha(recs), x=x,
-                        gate_w=gate_w, bias=bias,
+                        gate_w=gate_w, bias=bias, logits=logits, tid2eid=tid2eid,
+                        input_ids=input_ids, hash_ids=h_idx.numpy(), hash_weights=h_w.numpy(),
                         scores=res["scores"].numpy(), expert_ids=res["expert_ids"].numpy(),
                         routing_weights=res["routing_weights"].numpy(),
                         moe_output=res["moe_output"].numpy())

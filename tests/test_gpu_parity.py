@@ -231,3 +231,47 @@ def test_full_shape_decode(torch_cuda, oracle_mod, T):
     recs[used] = bank[torch.from_numpy(used).cuda().long()].cpu().numpy()
     want = orc.moe_layer_raw(recs, orc.Layout(H, I), x16, ids)
     assert orc.rel_l2(raw, want) <= TOL_REL_L2
+
+
+@pytest.mark.parametrize("hashed", [False, True])
+def test_dsv4_router_matches_reference_fixture(torch_cuda, oracle_mod, hashed):
+    """Selection ids exact against the reference's own torch router outputs;
+    weights within 1e-6 relative (device expf/log1pf vs torch CPU)."""
+    import os
+    torch = torch_cuda
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "moe_layer.npz"))
+    T, E = g["logits"].shape
+    eng = _engine(512, 512, E, 6)
+    dl = torch.from_numpy(g["logits"]).cuda()
+    ids = torch.empty((T, 6), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, 6), dtype=torch.float32, device="cuda")
+    if hashed:
+        t2e = torch.from_numpy(g["tid2eid"]).cuda()
+        inp = torch.from_numpy(g["input_ids"]).cuda()
+        eng.route_dsv4_device(dl.data_ptr(), T, ids.data_ptr(), w.data_ptr(), d_tid2eid_ptr=t2e.data_ptr(),
+                              d_input_ids_ptr=inp.data_ptr())
+        want_ids, want_w = g["hash_ids"], g["hash_weights"]
+    else:
+        db = torch.from_numpy(g["bias"]).cuda()
+        eng.route_dsv4_device(dl.data_ptr(), T, ids.data_ptr(), w.data_ptr(), d_bias_ptr=db.data_ptr())
+        want_ids, want_w = g["expert_ids"], g["routing_weights"]
+    assert eng.sync_status() == 0
+    assert np.array_equal(ids.cpu().numpy(), want_ids.astype(np.int32))
+    np.testing.assert_allclose(w.cpu().numpy(), want_w, rtol=1e-6)
+
+
+def test_dsv4_router_large_matches_oracle(torch_cuda, oracle_mod):
+    torch = torch_cuda
+    rng = np.random.default_rng(17)
+    T, E = 2048, 256
+    logits = (rng.standard_normal((T, E)) * 2).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.05).astype(np.float32)
+    eng = _engine(512, 512, E, 6)
+    ids = torch.empty((T, 6), dtype=torch.int32, device="cuda")
+    w = torch.empty((T, 6), dtype=torch.float32, device="cuda")
+    dl, db = torch.from_numpy(logits).cuda(), torch.from_numpy(bias).cuda()
+    eng.route_dsv4_device(dl.data_ptr(), T, ids.data_ptr(), w.data_ptr(), d_bias_ptr=db.data_ptr())
+    assert eng.sync_status() == 0
+    want_ids, want_w, _ = oracle_mod.route_dsv4(logits, 6, bias=bias)
+    assert np.array_equal(ids.cpu().numpy(), want_ids)
+    np.testing.assert_allclose(w.cpu().numpy(), want_w, rtol=2e-6)

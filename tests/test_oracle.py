@@ -246,3 +246,21 @@ def test_moe_layer_raw_layout(oracle_mod):
             L.dee_ref_expert_f16(recs[ids[t, r]].ctypes.data, 512, 512, x[t:t + 1].ctypes.data, 1, 0.0,
                                  y.ctypes.data)
             assert np.array_equal(y[0], raw[t, r])
+
+
+# --- DeepSeek-V4 router: deepseek_v4_layer_common.py:349-403 ---
+
+def test_dsv4_router_matches_reference(oracle_mod):
+    g = _load("moe_layer.npz")
+    ids, w, scores = oracle_mod.route_dsv4(g["logits"], 6, bias=g["bias"])
+    assert np.array_equal(ids, g["expert_ids"].astype(np.int32))
+    np.testing.assert_allclose(scores + g["bias"], g["scores"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(w, g["routing_weights"], rtol=1e-6)
+    assert abs(float(w.sum(1).mean()) - 1.5) < 1e-5
+
+
+def test_dsv4_hash_router_matches_reference(oracle_mod):
+    g = _load("moe_layer.npz")
+    ids, w, _ = oracle_mod.route_dsv4(g["logits"], 6, tid2eid=g["tid2eid"], input_ids=g["input_ids"])
+    assert np.array_equal(ids, g["hash_ids"].astype(np.int32))
+    np.testing.assert_allclose(w, g["hash_weights"], rtol=1e-6)
