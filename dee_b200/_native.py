@@ -18,6 +18,7 @@ DEE_ERR_RANGE = -3
 DEE_ERR_UNSUPPORTED = -4
 DEE_ERR_DEVICE = -5
 DEE_ERR_NO_BANK = -6
+DEE_ERR_SCRATCH_LIMIT = -7
 
 # Every symbol include/dee_b200.h declares, with (restype, argtypes).
 P = ctypes.c_void_p
@@ -57,6 +58,7 @@ SIGNATURES = {
     "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),
     "dee_fp4_quantize_device": (I, [P, SZ, SZ, P, P, P]),
     "dee_engine_launch_count": (ctypes.c_uint64, [P]),
+    "dee_moe_forward_noalloc": (I, [ctypes.POINTER(DeeConfig), P, SZ, I, P, I, P, P, P, P, P]),
     "dee_engine_set_profiling": (I, [P, I]),
     "dee_engine_stage_ms": (I, [P, P, I]),
 }

@@ -40,6 +40,7 @@ extern "C" {
 #define DEE_ERR_UNSUPPORTED (-4) /* configuration this build does not cover   */
 #define DEE_ERR_DEVICE (-5)      /* a kernel reported a failure (status word) */
 #define DEE_ERR_NO_BANK (-6)     /* no expert bank attached for the layer     */
+#define DEE_ERR_SCRATCH_LIMIT (-7) /* request larger than the static scratch  */
 
 typedef struct dee_engine dee_engine;
 
@@ -149,6 +150,25 @@ DEE_API int dee_fp4_decode_device(const uint8_t* d_packed, const uint8_t* d_scal
  * synthetic expert banks on the device. */
 DEE_API int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_packed,
                             uint8_t* d_scale, void* stream);
+
+/* The layer forward for callers that cannot allocate device memory (code
+ * inside an allocator or memory-pool callback, or a host whose device memory
+ * is entirely owned by its own caching allocator).  No counterpart in the
+ * reference: it has no engine handle and allocates nothing.  Same kernels
+ * and results as dee_moe_forward_device with device ids and the FP32
+ * rank-order combine; every scratch buffer lives in a 4 MiB static device
+ * array that the library reserves on each GPU it is loaded on (145
+ * selections at H=4096, I=2048, i.e. 24 tokens at top-6).  Larger requests
+ * return DEE_ERR_SCRATCH_LIMIT.  d_records holds n_slots records in expert
+ * order (slot e = expert e).  d_status_out (may be NULL) receives the
+ * kernels' status word (0 = ok).  All calls share the static array: calls
+ * that overlap on the GPU race, so serialise them.  The first call on a
+ * device resolves the array's device address; make it before any stream
+ * capture. */
+DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void* d_records,
+                                    size_t record_bytes, int n_slots, const void* d_x_f16,
+                                    int tokens, const int32_t* d_ids, const float* d_weights,
+                                    float* d_out_f32, uint32_t* d_status_out, void* stream);
 
 /* Kernel launches issued by this engine since creation (for the bench's
  * launch accounting). */
