@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=E,
+                    help="experts in the bank (smaller values only for profiling captures)")
     return ap.parse_args()
 
 
@@ -382,6 +384,8 @@ def main():
                                 device_id=torch.device("cuda", local))
     hbm_peak, tc_peak, peak_kind = load_peaks()
     b = args.batch
+    global E
+    E = args.experts
     bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
     eng = build_engine(torch, bank, max_tokens=max(b, 64))
     stream = torch.cuda.Stream()
@@ -432,7 +436,7 @@ def main():
         "hbm_gbs_layer": layer_gbs,
         "hbm_frac_layer": layer_gbs / hbm_peak,
         "stage_ms": stages,
-        "roofline": {"bound": "hbm", "kernel": "moe_gemm_kernel<gate_up>", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "moe_decode_kernel<gate_up>", "achieved": achieved,
                      "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
                      "algorithmic_bytes_per_launch": gu_bytes},

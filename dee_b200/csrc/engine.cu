@@ -11,7 +11,7 @@
 //   -> gate/up grouped GEMM (tcgen05, SwiGLU epilogue)
 //   -> down grouped GEMM (tcgen05, scatter epilogue)
 //   -> combine (optional)
-#include "../../include/dee_b200.h"
+#include "dee_b200.h"
 #include "kernels.h"
 
 #include <cstdio>
@@ -103,7 +103,8 @@ struct dee_engine {
     float* d_raw = nullptr;
     int32_t* h_ids = nullptr;  // pinned staging of the consumed ids
     size_t h_ids_count = 0;
-    CUtensorMap map_xperm, map_act;
+    CUtensorMap map_xperm, map_act;      // 16-row token boxes (tcgen05 kernel)
+    CUtensorMap map_xperm8, map_act8;    // 8-row token boxes (decode kernel)
     uint64_t launches = 0;
     // Opt-in stage timing (the role of the reference's StageProfiler,
     // dee.cpp/include/dee/profiling.h:31-46): events recorded on the launch
@@ -180,7 +181,7 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
     free_workspace(e);
     const size_t cap = ((sel + 255) / 256) * 256;
     const int H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
-    const int max_tiles = E + static_cast<int>(cap / 16) + 1;
+    const int max_tiles = E + static_cast<int>(cap / 8) + 1;
     if ((err = dev_alloc(&e->d_ids, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_weights, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm, cap)) != cudaSuccess ||
@@ -214,6 +215,18 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         if (!encode(e, &e->map_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
                     box, CU_TENSOR_MAP_SWIZZLE_128B, "act"))
             return DEE_ERR_CUDA;
+        const cuuint32_t box8[2] = {64, 8};
+        if (!encode(e, &e->map_act8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
+                    box8, CU_TENSOR_MAP_SWIZZLE_128B, "act/8"))
+            return DEE_ERR_CUDA;
+    }
+    {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), cap};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 2};
+        const cuuint32_t box8[2] = {64, 8};
+        if (!encode(e, &e->map_xperm8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_xperm, dims,
+                    strides, box8, CU_TENSOR_MAP_SWIZZLE_128B, "X_perm/8"))
+            return DEE_ERR_CUDA;
     }
     return DEE_OK;
 }
@@ -246,8 +259,11 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     const dee::Bank& bank = e->banks[layer];
     const int K = e->cfg.topk, H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
     const size_t sel = static_cast<size_t>(tokens) * K;
-    const bool large = tokens > 64;
-    const int n_max = gemm_n_max(large);
+    // Decode-sized calls use the register-dequant kernel (tiles of <= 8 token
+    // rows); larger calls the tcgen05 kernel (tiles of <= 128 rows).
+    const bool decode = tokens <= kDecodeMaxTokens;
+    const bool large = !decode;
+    const int n_max = decode ? kDecodeTileRows : gemm_n_max(large);
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles};
     stage_begin(e, kStagePermute, stream);
@@ -277,19 +293,23 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.status = e->d_status;
 
     GemmMaps gm{};
-    gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3; gm.b = e->map_xperm;
+    gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3;
+    gm.b = decode ? e->map_xperm8 : e->map_xperm;
     a.k_total = H;
     a.m_tiles = I / 64;
     stage_begin(e, kStageGateUp, stream);
-    err = launch_moe_gemm(true, large, gm, a, e->num_sms, stream);
+    err = decode ? launch_moe_decode(true, gm, a, e->num_sms, stream)
+                 : launch_moe_gemm(true, large, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
     stage_end(e, kStageGateUp, stream);
 
-    gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2; gm.b = e->map_act;
+    gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
+    gm.b = decode ? e->map_act8 : e->map_act;
     a.k_total = I;
     a.m_tiles = H / 128;
     stage_begin(e, kStageDown, stream);
-    err = launch_moe_gemm(false, large, gm, a, e->num_sms, stream);
+    err = decode ? launch_moe_decode(false, gm, a, e->num_sms, stream)
+                 : launch_moe_gemm(false, large, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "down GEMM launch");
     stage_end(e, kStageDown, stream);
     e->launches += 4;
@@ -499,10 +519,6 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
                               stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "ids H2D");
         ids32 = e->d_ids;
-    } else {
-        err = cudaMemcpyAsync(e->h_ids, d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                              stream);
-        if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
     }
     e->h_ids_count = sel;
     float* raw = d_raw ? d_raw : e->d_raw;
@@ -515,6 +531,13 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
         stage_end(e, kStageCombine, stream);
         e->launches += 1;
+    }
+    if (!h_ids) {
+        // the journal's copy of the ids; queued last so the kernels of the
+        // layer stay back to back on the stream
+        err = cudaMemcpyAsync(e->h_ids, d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                              stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
     }
     return DEE_OK;
 }
@@ -550,8 +573,6 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     cudaError_t err = launch_ids_i64_to_i32(d_expert_ids, static_cast<int>(sel),
                                             e->cfg.num_experts, e->d_ids, e->d_status, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "id conversion launch");
-    err = cudaMemcpyAsync(e->h_ids, e->d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
-    if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
     e->h_ids_count = sel;
     float* raw = d_raw_trace_out ? static_cast<float*>(d_raw_trace_out) : e->d_raw;
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_h_in), tokens, e->d_ids, raw,
@@ -563,6 +584,8 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     if (err != cudaSuccess) return cuda_fail(e, err, "FP16 combine launch");
     stage_end(e, kStageCombine, stream);
     e->launches += 2;
+    err = cudaMemcpyAsync(e->h_ids, e->d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
     return DEE_OK;
 }
 

@@ -10,6 +10,23 @@
 
 namespace dee {
 
+// Launch with programmatic stream serialisation (see sm100::pdl_wait).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 struct GemmMaps {
     CUtensorMap w0, w1, s0, s1, b;
 };
@@ -19,6 +36,13 @@ int gemm_n_max(bool large);
 
 cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, const GemmArgs& args,
                             int grid, cudaStream_t stream);
+
+// Decode-sized groups (tiles of at most kDecodeTileRows token rows): register
+// dequant + mma.sync kernel of moe_decode.cu.  maps.b must use 8-row boxes.
+constexpr int kDecodeTileRows = 8;
+constexpr int kDecodeMaxTokens = 64;
+cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
+                              cudaStream_t stream);
 
 // Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,

@@ -1,0 +1,389 @@
+// moe_decode.cu -- grouped W4A16 GEMM for decode-sized expert groups.
+//
+// For groups of at most 8 token rows per expert (decode), every packed
+// weight byte is used by only a handful of tokens, so the kernel is bound
+// by how fast weights can be streamed and turned into tensor-core operands.
+// Measured on B200, the tensor-memory A path of moe_gemm.cu pays about 110
+// cycles per 128x16 A slice whatever N is, and staging dequantised weights in
+// shared memory would need ~5 bytes of shared-memory traffic per weight.
+// Here the dequantised weights never leave registers:
+//
+//   warp 0       TMA producer: per 512-wide K stage, the packed FP4 rows
+//                (128 rows x 256 B), their UE8M0 scales and the stage's token
+//                rows (8 rows x 1 KB, 128-byte swizzled), plus L2 prefetch of
+//                later stages
+//   warps 1-8    consumers: each owns 16 weight rows of the 128-row work item,
+//                reads its packed bytes from shared memory, converts them
+//                (cvt.rn.f16x2.e2m1x2) into mma.sync.m16n8k16 A fragments and
+//                accumulates FP32 in registers, applying each 32-wide block's
+//                power-of-two scale to the block's partial sum
+//
+// Gate/up items pair 8 gate rows with the same 8 up rows in each 16-row MMA
+// tile, so one thread holds the gate and up accumulators of the same
+// (feature, token) and applies the reference's FP16 SwiGLU chain in
+// registers (swiglu_cuda.cu:46-59).  Down items scatter FP32 rows to
+// raw[token * K + rank] (engine.cpp:1080-1113).
+#include "kernels.h"
+
+namespace dee {
+namespace {
+
+using namespace sm100;
+
+constexpr int kDecThreads = 288;          // 9 warps
+constexpr int kDecStages = 5;
+constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 512)
+constexpr int kDecScBytes = 2048;          // 128 rows x 16 scale bytes
+constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
+constexpr int kDecStageBytes = kDecPkBytes + kDecScBytes + kDecBBytes;
+constexpr int kDecPrefetch = 4;
+constexpr int kDecSmem = 1024 + kDecStages * kDecStageBytes + 256;
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ float scale_value(uint32_t b) {
+    const int e = static_cast<int>(b) - 127;
+    if (e >= 127) return __int_as_float(0x7F7FFFFF);
+    if (e <= -127) return 0.0f;
+    return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+// Block scale for the FP16-rounded dequant path: FP16(value * 2^(s-127)).
+struct Scale {
+    uint32_t h2;   // f16x2 scale when 2^(s-127) is an exact binary16
+    float f;       // FP32 scale otherwise
+    bool fast;
+};
+
+__device__ __forceinline__ Scale make_scale(uint32_t sbyte) {
+    Scale s;
+    s.fast = sbyte >= 103u && sbyte <= 142u;
+    const int e = static_cast<int>(sbyte) - 127;
+    const uint32_t sh = s.fast ? (e >= -14 ? static_cast<uint32_t>(e + 15) << 10 : 1u << (e + 24)) : 0u;
+    s.h2 = sh | (sh << 16);
+    s.f = scale_value(sbyte);
+    return s;
+}
+
+// Four packed bytes -> four f16x2 (unscaled E2M1 values, exact in FP16).
+__device__ __forceinline__ void cvt_e2m1x8(uint32_t w, uint32_t& o0, uint32_t& o1, uint32_t& o2,
+                                           uint32_t& o3) {
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
+        : "r"(w));
+}
+
+// f16x2 of unscaled E2M1 values -> FP16(value * 2^(s-127)), as the reference
+// dequant kernel rounds them (cuda_convert.cu:245).
+__device__ __forceinline__ uint32_t dequant_f16(uint32_t r, const Scale& s) {
+    if (s.fast) return hmul2(r, s.h2);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&r));
+    const __half lo = __float2half_rn(f.x * s.f);
+    const __half hi = __float2half_rn(f.y * s.f);
+    return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+}
+
+__device__ __forceinline__ void mma_16816_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_16816_zero(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                               uint32_t a3, uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
+        : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
+}
+
+__device__ __forceinline__ float silu_ref(float g) {
+    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+}
+
+struct DecItem {
+    int m;
+    TileDesc td;
+    int slot;
+    bool valid;
+};
+
+__device__ __forceinline__ DecItem dec_item(const GemmArgs& a, int item) {
+    DecItem d;
+    const int tile = item / a.m_tiles;
+    d.m = item - tile * a.m_tiles;
+    d.td = a.tiles[tile];
+    const int e = d.td.expert;
+    int slot = -1;
+    if (e >= 0 && e < a.num_experts) slot = a.slot_of[e];
+    d.valid = slot >= 0 && slot < a.num_slots && d.td.n_rows > 0 && d.td.n_rows <= 8;
+    d.slot = (slot < 0 || slot >= a.num_slots) ? 0 : slot;
+    return d;
+}
+
+template <GemmMode MODE>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
+                      const __grid_constant__ CUtensorMap map_s0, const __grid_constant__ CUtensorMap map_s1,
+                      const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+    constexpr bool kGU = MODE == GemmMode::kGateUp;
+    if (kGU) pdl_wait();
+    const int n_items = *args.n_tiles * args.m_tiles;
+    if (static_cast<int>(blockIdx.x) >= n_items) {
+        if (!kGU) pdl_wait();
+        pdl_trigger();
+        return;
+    }
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
+    uint64_t* empty = full + kDecStages;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecStages; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 8);
+        }
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&map_w0);
+        prefetch_tmap(&map_s0);
+        prefetch_tmap(&map_b);
+        if (kGU) { prefetch_tmap(&map_w1); prefetch_tmap(&map_s1); }
+    }
+    __syncthreads();
+    if (!kGU && warp != 0) pdl_wait();
+    pdl_trigger();
+    const int k_stages = args.k_total / kKStage;
+    uint32_t* status = args.status;
+
+    if (warp == 0) {
+        if (lane != 0) return;
+        const uint64_t pol_w = policy_evict_first();
+        const uint64_t pol_b = policy_evict_last();
+        int pf_item = blockIdx.x, pf_s = 0;
+        DecItem pf{};
+        bool pf_valid = false;
+        auto pf_advance = [&]() {
+            if (pf_valid && ++pf_s < k_stages) return;
+            if (pf_valid) pf_item += gridDim.x;
+            pf_s = 0;
+            pf_valid = pf_item < n_items;
+            if (pf_valid) pf = dec_item(args, pf_item);
+        };
+        auto pf_issue = [&]() {
+            if (!pf_valid) return;
+            const int xk = pf_s * (kKStage / 2);
+            const int row = kGU ? pf.m * 64 : pf.m * 128;
+            tma_prefetch_3d(&map_w0, xk, row, pf.slot);
+            tma_prefetch_3d(&map_w0, xk + 128, row, pf.slot);
+            if (kGU) {
+                tma_prefetch_3d(&map_w1, xk, row, pf.slot);
+                tma_prefetch_3d(&map_w1, xk + 128, row, pf.slot);
+            }
+        };
+        pf_advance();
+        for (int i = 0; i < kDecStages + kDecPrefetch && pf_valid; ++i) {
+            pf_issue();
+            pf_advance();
+        }
+        // the down GEMM's token operand is the gate/up output: weights may be
+        // prefetched early, the stage loads wait for the predecessor
+        if (!kGU) pdl_wait();
+        int st = 0;
+        uint32_t ph = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            const DecItem it = dec_item(args, item);
+            if (!it.valid) atomicOr(status, kStatusBadExpert);
+            for (int s = 0; s < k_stages; ++s) {
+                pf_issue();
+                pf_advance();
+                if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
+                mbar_arrive_expect_tx(&full[st], kDecStageBytes);
+                uint8_t* pk = smem + st * kDecStageBytes;
+                uint8_t* sc = pk + kDecPkBytes;
+                uint8_t* bt = sc + kDecScBytes;
+                const int xk = s * (kKStage / 2);
+                if (kGU) {
+                    const int row = it.m * 64;
+                    tma_load_3d(pk, &map_w0, &full[st], xk, row, it.slot, pol_w);
+                    tma_load_3d(pk + 8192, &map_w1, &full[st], xk, row, it.slot, pol_w);
+                    tma_load_3d(pk + 16384, &map_w0, &full[st], xk + 128, row, it.slot, pol_w);
+                    tma_load_3d(pk + 24576, &map_w1, &full[st], xk + 128, row, it.slot, pol_w);
+                    tma_load_3d(sc, &map_s0, &full[st], s * 16, row, it.slot, pol_w);
+                    tma_load_3d(sc + 1024, &map_s1, &full[st], s * 16, row, it.slot, pol_w);
+                } else {
+                    const int row = it.m * 128;
+                    tma_load_3d(pk, &map_w0, &full[st], xk, row, it.slot, pol_w);
+                    tma_load_3d(pk + 16384, &map_w0, &full[st], xk + 128, row, it.slot, pol_w);
+                    tma_load_3d(sc, &map_s0, &full[st], s * 16, row, it.slot, pol_w);
+                }
+                for (int j = 0; j < 8; ++j)
+                    tma_load_2d(bt + j * 1024, &map_b, &full[st], s * kKStage + j * 64,
+                                it.td.row_start, pol_b);
+                if (++st == kDecStages) { st = 0; ph ^= 1; }
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    // K inside each 32-wide scale block is assigned so that thread q owns
+    // packed bytes 4q..4q+3 (K 8q..8q+7): its A fragments come from one
+    // 32-bit word per row and its token fragments for both k16 steps from
+    // one 16-byte slice of the token row.  A and B use the same assignment,
+    // so the MMA's sum is unchanged.  Each block is accumulated into a zeroed
+    // temporary and added with the row's power-of-two scale in FP32; blocks
+    // whose scale is not an exact binary16 take the FP16-rounded path of the
+    // reference dequant instead.
+    const int cw = warp - 1;        // 0..7: 16-row MMA tile of the item
+    const int g = lane >> 2;        // fragment row within 8 / token column
+    const int q = lane & 3;
+    const int row_lo = kGU ? (8 * cw + g) : (16 * cw + g);
+    const int row_hi = kGU ? (64 + 8 * cw + g) : (16 * cw + 8 + g);
+    const int sw_lo = row_lo & 7, sw_hi = row_hi & 7;
+    int st = 0;
+    uint32_t ph = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+        const DecItem it = dec_item(args, item);
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        bool ok = true;
+        for (int s = 0; s < k_stages; ++s) {
+            ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
+            if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+            const uint8_t* pk = smem + st * kDecStageBytes;
+            const uint8_t* sc = pk + kDecPkBytes;
+            const uint8_t* bt = sc + kDecScBytes;
+            const uint4 slo = *reinterpret_cast<const uint4*>(sc + row_lo * 16);
+            const uint4 shi = *reinterpret_cast<const uint4*>(sc + row_hi * 16);
+            const uint32_t slw[4] = {slo.x, slo.y, slo.z, slo.w};
+            const uint32_t shw[4] = {shi.x, shi.y, shi.z, shi.w};
+            // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
+            // finite binary16, so scaling the block's FP32 partial sum equals
+            // summing the reference's FP16-rounded weights.  Byte 103 rounds
+            // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.
+            bool in_range = true;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const uint32_t x = (slw[i] >> (8 * b)) & 0xFFu, y = (shw[i] >> (8 * b)) & 0xFFu;
+                    in_range = in_range && x >= 104u && x <= 140u && y >= 104u && y <= 140u;
+                }
+            }
+            const bool fast = __all_sync(0xffffffffu, in_range);
+#pragma unroll
+            for (int blk = 0; blk < 16; ++blk) {
+                const int half = blk >> 3;
+                const int chunk = blk & 7;
+                const uint32_t wlo = *reinterpret_cast<const uint32_t*>(
+                    pk + half * 16384 + row_lo * 128 + ((chunk ^ sw_lo) << 4) + q * 4);
+                const uint32_t whi = *reinterpret_cast<const uint32_t*>(
+                    pk + half * 16384 + row_hi * 128 + ((chunk ^ sw_hi) << 4) + q * 4);
+                const int cb = (blk & 1) * 4 + q;  // 16-byte chunk of the token row in box blk/2
+                const uint4 bv = *reinterpret_cast<const uint4*>(bt + (blk >> 1) * 1024 + g * 128 +
+                                                                  ((cb ^ g) << 4));
+                const uint32_t sb_lo = (slw[blk >> 2] >> ((blk & 3) * 8)) & 0xFFu;
+                const uint32_t sb_hi = (shw[blk >> 2] >> ((blk & 3) * 8)) & 0xFFu;
+                uint32_t a[8];  // [lo b0, lo b1, lo b2, lo b3, hi b0..b3] as f16x2
+                cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
+                cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
+                if (fast) {
+                    float t[4];
+                    mma_16816_zero(t, a[0], a[4], a[1], a[5], bv.x, bv.y);
+                    mma_16816_acc(t, a[2], a[6], a[3], a[7], bv.z, bv.w);
+                    const float flo = __uint_as_float((sb_lo) << 23);
+                    const float fhi = __uint_as_float((sb_hi) << 23);
+                    c[0] = fmaf(flo, t[0], c[0]);
+                    c[1] = fmaf(flo, t[1], c[1]);
+                    c[2] = fmaf(fhi, t[2], c[2]);
+                    c[3] = fmaf(fhi, t[3], c[3]);
+                } else {
+                    const Scale s_lo = make_scale(sb_lo), s_hi = make_scale(sb_hi);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        a[i] = dequant_f16(a[i], s_lo);
+                        a[4 + i] = dequant_f16(a[4 + i], s_hi);
+                    }
+                    mma_16816_acc(c, a[0], a[4], a[1], a[5], bv.x, bv.y);
+                    mma_16816_acc(c, a[2], a[6], a[3], a[7], bv.z, bv.w);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+            if (++st == kDecStages) { st = 0; ph ^= 1; }
+        }
+        if (!ok) break;
+        if (!it.valid) continue;
+        const int n_rows = it.td.n_rows;
+        const int n0 = 2 * q, n1 = 2 * q + 1;
+        if (kGU) {
+            const int feat = it.m * 64 + 8 * cw + g;
+            const float lim = args.swiglu_limit;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int n = h ? n1 : n0;
+                if (n >= n_rows) continue;
+                float gv = __half2float(__float2half_rn(c[h]));
+                float uv = __half2float(__float2half_rn(c[2 + h]));
+                if (lim > 0.0f) {
+                    gv = fminf(gv, lim);
+                    uv = fminf(fmaxf(uv, -lim), lim);
+                }
+                const __half sv = __float2half_rn(silu_ref(gv));
+                args.act[static_cast<size_t>(it.td.row_start + n) * args.inter + feat] =
+                    __float2half_rn(__fmul_rn(__half2float(sv), uv));
+            }
+        } else {
+            const int f_lo = it.m * 128 + 16 * cw + g;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int n = h ? n1 : n0;
+                if (n >= n_rows) continue;
+                const size_t pos = static_cast<size_t>(args.perm[it.td.row_start + n]);
+                args.raw[pos * args.hidden + f_lo] = c[h];
+                args.raw[pos * args.hidden + f_lo + 8] = c[2 + h];
+            }
+        }
+    }
+}
+
+template <GemmMode MODE>
+cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
+    auto kern = moe_decode_kernel<MODE>;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), kDecSmem, stream, maps.w0, maps.w1, maps.s0,
+                      maps.s1, maps.b, args);
+}
+
+}  // namespace
+
+cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
+                              cudaStream_t stream) {
+    return gate_up ? launch_dec<GemmMode::kGateUp>(maps, args, grid, stream)
+                   : launch_dec<GemmMode::kDown>(maps, args, grid, stream);
+}
+
+}  // namespace dee

@@ -106,9 +106,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr int AS = Cfg::kA;
     constexpr bool kGU = MODE == GemmMode::kGateUp;
 
+    // The gate/up GEMM follows the kernels that write its tile list and
+    // token rows, so it waits before reading anything.  The down GEMM
+    // follows the gate/up GEMM, which triggers only after its own wait, so
+    // the tile list (written two kernels back) is complete when the down
+    // GEMM starts: its weight producer streams W2 at once, every other role
+    // waits for the gate/up results first.
+    if (kGU) pdl_wait();
     const int n_tiles = *args.n_tiles;
     const int n_items = n_tiles * args.m_tiles;
-    if (static_cast<int>(blockIdx.x) >= n_items) return;  // uniform per CTA
+    if (static_cast<int>(blockIdx.x) >= n_items) {  // uniform per CTA
+        if (!kGU) pdl_wait();
+        pdl_trigger();
+        return;
+    }
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -131,7 +142,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < PK; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 4); }
+        for (int i = 0; i < PK; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 8); }
         for (int i = 0; i < BS; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
         for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
@@ -155,6 +166,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int k_stages = args.k_total / kKStage;
     const int k_blocks = args.k_total / kKBlock;
     uint32_t* status = args.status;
+    if (!kGU && warp != 0) pdl_wait();
+    pdl_trigger();
 
     if (warp == 0) {
         // ---------------- packed weight + scale producer ----------------
@@ -163,11 +176,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int ps = 0;
             uint32_t pphase = 0;
             bool ok = true;
+            // L2 prefetch cursor: runs Cfg::kPrefetch stages ahead of the loads
+            int pf_item = blockIdx.x, pf_s = 0, pf_slot = 0, pf_m = 0;
+            bool pf_valid = false;
+            auto pf_advance = [&]() {
+                if (pf_valid && ++pf_s < k_stages) return;
+                if (pf_valid) pf_item += gridDim.x;
+                pf_s = 0;
+                pf_valid = pf_item < n_items;
+                if (pf_valid) {
+                    ItemInfo pit;
+                    load_item(args, pf_item, pit);
+                    pf_slot = (pit.slot < 0 || pit.slot >= args.num_slots) ? 0 : pit.slot;
+                    pf_m = pit.m;
+                }
+            };
+            auto pf_issue = [&]() {
+                if (!pf_valid) return;
+                const int xk = pf_s * (kKStage / 2);
+                if (kGU) {
+                    tma_prefetch_3d(&map_w0, xk, pf_m * 64, pf_slot);
+                    tma_prefetch_3d(&map_w1, xk, pf_m * 64, pf_slot);
+                    tma_prefetch_3d(&map_w0, xk + 128, pf_m * 64, pf_slot);
+                    tma_prefetch_3d(&map_w1, xk + 128, pf_m * 64, pf_slot);
+                } else {
+                    tma_prefetch_3d(&map_w0, xk, pf_m * 128, pf_slot);
+                    tma_prefetch_3d(&map_w0, xk + 128, pf_m * 128, pf_slot);
+                }
+            };
+            if (Cfg::kPrefetch > 0) {
+                pf_advance();
+                for (int i = 0; i < PK + Cfg::kPrefetch && pf_valid; ++i) {
+                    pf_issue();
+                    pf_advance();
+                }
+            }
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 ItemInfo it;
                 if (!load_item(args, item, it)) { atomicOr(status, kStatusBadExpert); }
                 const int slot = (it.slot < 0 || it.slot >= args.num_slots) ? 0 : it.slot;
                 for (int s = 0; s < k_stages; ++s) {
+                    if (Cfg::kPrefetch > 0) {
+                        pf_issue();
+                        pf_advance();
+                    }
                     if (!mbar_wait(&pk_empty[ps], pphase ^ 1, status, kStatusTimeoutTma)) { ok = false; break; }
                     mbar_arrive_expect_tx(&pk_full[ps], kPkStageBytes + kScStageBytes);
                     uint8_t* dst = pk_smem + ps * kPkStageBytes;
@@ -202,13 +254,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 ItemInfo it;
                 load_item(args, item, it);
                 const int n_pad = min(it.td.n_pad, NMAX);
-                for (int kb = 0; kb < k_blocks; ++kb) {
+                for (int kb0 = 0; kb0 < k_blocks; kb0 += Cfg::kBKb) {
                     if (!mbar_wait(&b_empty[bs], bphase ^ 1, status, kStatusTimeoutTma)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&b_full[bs], n_pad * 128);
+                    mbar_arrive_expect_tx(&b_full[bs], n_pad * 128 * Cfg::kBKb);
                     uint8_t* dst = b_smem + bs * Cfg::kBStageBytes;
-                    for (int r = 0; r < n_pad; r += 16)
-                        tma_load_2d(dst + r * 128, &map_b, &b_full[bs], kb * kKBlock,
-                                    it.td.row_start + r, pol);
+                    for (int j = 0; j < Cfg::kBKb; ++j)
+                        for (int r = 0; r < n_pad; r += 16)
+                            tma_load_2d(dst + j * (NMAX * 128) + r * 128, &map_b, &b_full[bs],
+                                        (kb0 + j) * kKBlock, it.td.row_start + r, pol);
                     if (++bs == BS) { bs = 0; bphase ^= 1; }
                 }
             }
@@ -231,27 +284,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint32_t d_tmem = tmem_base + Cfg::kAccBase + acc * NMAX;
                 const uint32_t idesc = idesc_f16_f32(128, n_pad);
                 for (int kb = 0; kb < k_blocks; ++kb) {
+                    const int j = kb % Cfg::kBKb;  // K step within the token-operand stage
                     if (!mbar_wait(&a_full[as], aphase, status, kStatusTimeoutMma) ||
-                        !mbar_wait(&b_full[bs], bphase, status, kStatusTimeoutMma)) { ok = false; break; }
+                        (j == 0 && !mbar_wait(&b_full[bs], bphase, status, kStatusTimeoutMma))) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_tmem = tmem_base + as * 32;
-                    const uint32_t b_addr = smem_u32(b_smem + bs * Cfg::kBStageBytes);
+                    const uint32_t b_addr = smem_u32(b_smem + bs * Cfg::kBStageBytes + j * (NMAX * 128));
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         mma_f16_ts(d_tmem, a_tmem + q * 8, smem_desc_k128(b_addr + q * 32), idesc,
                                    (kb | q) != 0 ? 1u : 0u);
                     }
                     mma_commit(&a_empty[as]);
-                    mma_commit(&b_empty[bs]);
                     if (++as == AS) { as = 0; aphase ^= 1; }
-                    if (++bs == BS) { bs = 0; bphase ^= 1; }
+                    if (j == Cfg::kBKb - 1) {
+                        mma_commit(&b_empty[bs]);
+                        if (++bs == BS) { bs = 0; bphase ^= 1; }
+                    }
                 }
                 if (!ok) break;
                 mma_commit(&acc_full[acc]);
             }
         }
-    } else if (warp <= 6) {
+    } else if (warp <= 10) {
         // ---------------- dequantisers (TMEM lane = thread's weight row) ----------------
+        // Two warpgroups split the eight 64-wide K steps of a packed stage
+        // (even steps: warps 3-6, odd steps: warps 7-10); each thread owns
+        // one weight row, i.e. one TMEM lane.
+        const int wg = (warp - 3) >> 2;
         const int quad = warp & 3;
         const int L = quad * 32 + lane;  // TMEM lane / A row
         int srow;
@@ -261,9 +324,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
             srow = L;
         }
+        const int sw = srow & 7;
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
-        int ps = 0, as = 0;
-        uint32_t pphase = 0, aphase = 0;
+        int ps = 0;
+        uint32_t pphase = 0;
+        uint32_t g = 0;  // K steps issued so far by this CTA (both warpgroups)
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             for (int s = 0; s < k_stages && ok; ++s) {
@@ -272,29 +337,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 const uint8_t* st = pk_smem + ps * kPkStageBytes;
                 const uint4 sc = *reinterpret_cast<const uint4*>(sc_smem + ps * kScStageBytes + srow * 16);
                 const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll 1
-                for (int j = 0; j < 8; ++j) {
-                    const int half = j >> 2;
+                const uint32_t sshift = 16u * static_cast<uint32_t>(wg);
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = 2 * jj + wg;  // K step within the stage
                     const int c0 = (j & 3) * 2;
-                    const uint8_t* rowp = st + half * 16384 + srow * 128;
-                    const int sw = srow & 7;
+                    const uint8_t* rowp = st + (jj >> 1) * 16384 + srow * 128;
                     const uint4 q0 = *reinterpret_cast<const uint4*>(rowp + ((c0 ^ sw) << 4));
                     const uint4 q1 = *reinterpret_cast<const uint4*>(rowp + (((c0 + 1) ^ sw) << 4));
-                    const uint32_t sb0 = (scw[(2 * j) >> 2] >> (((2 * j) & 3) * 8)) & 0xFFu;
-                    const uint32_t sb1 = (scw[(2 * j + 1) >> 2] >> (((2 * j + 1) & 3) * 8)) & 0xFFu;
+                    const uint32_t sb0 = (scw[jj] >> sshift) & 0xFFu;
+                    const uint32_t sb1 = (scw[jj] >> (sshift + 8)) & 0xFFu;
                     uint32_t v[32];
                     dequant_block32(q0, sb0, v);
                     dequant_block32(q1, sb1, v + 16);
-                    ok = mbar_wait(&a_empty[as], aphase ^ 1, status, kStatusTimeoutDequant);
-                    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+                    const uint32_t gi = g + static_cast<uint32_t>(j);
+                    const int as = static_cast<int>(gi % AS);
+                    const uint32_t aphase = (gi / AS) & 1u;
+                    const bool got = mbar_wait(&a_empty[as], aphase ^ 1, status, kStatusTimeoutDequant);
+                    if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                     tc_fence_after();
                     tmem_st_32x32b_x32(tmem_base + lane_addr + as * 32, v);
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&a_full[as]);
-                    if (++as == AS) { as = 0; aphase ^= 1; }
                 }
+                g += 8;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&pk_empty[ps]);
                 if (++ps == PK) { ps = 0; pphase ^= 1; }
@@ -380,15 +448,15 @@ cudaError_t launch_one(const GemmMaps& maps, const GemmArgs& args, int grid, cud
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    kern<<<grid, kGemmThreads, Cfg::kSmemBytes, stream>>>(maps.w0, maps.w1, maps.s0, maps.s1,
-                                                          maps.b, args);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, maps.w0,
+                      maps.w1, maps.s0, maps.s1, maps.b, args);
 }
 
-// Decode-sized tiles (<= 32 rows per expert tile) keep deep packed-weight
-// pipelines; prefill-sized tiles trade pipeline depth for wide N.
-using CfgSmall = GemmConfig<32, 5, 12, 8>;
-using CfgLarge = GemmConfig<128, 3, 6, 4>;
+// Decode-sized tiles: token rows for a whole 512-wide K stage per load (the
+// token operand then costs one TMA round trip per eight K steps) and packed
+// weights prefetched into L2 four stages beyond the shared-memory ring.
+using CfgSmall = GemmConfig<16, 4, 4, 8, 8, 4>;
+using CfgLarge = GemmConfig<128, 3, 6, 1, 4, 2>;
 
 }  // namespace
 

@@ -13,10 +13,11 @@
 //   warp 0      TMA producer of packed FP4 weight tiles + UE8M0 scale tiles
 //   warp 1      TMA producer of the token operand (X_perm or act) tiles
 //   warp 2      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 3-6   dequantisers: each thread owns one weight row (one TMEM lane),
-//               turns 64 packed nibbles into 64 FP16 weights per step and
-//               writes them to a tensor-memory A buffer with tcgen05.st
-//   warps 7-10  epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
+//   warps 3-10  dequantisers, two warpgroups taking alternate 64-wide K steps:
+//               each thread owns one weight row (one TMEM lane), turns 64
+//               packed nibbles into 64 FP16 weights per step and writes them
+//               to a tensor-memory A buffer with tcgen05.st
+//   warps 11-14 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
 //               scatter, global stores
 //
 // The MMA is tcgen05.mma.kind::f16 with A (weights, M = 128 rows) read from
@@ -62,23 +63,30 @@ struct GemmArgs {
     uint32_t* status;        // device status word (sm100::StatusBits)
 };
 
-constexpr int kGemmThreads = 352;     // 11 warps
+constexpr int kGemmThreads = 480;     // 15 warps
 constexpr int kPkStageBytes = 32768;  // 128 rows x 256 packed bytes (K = 512)
 constexpr int kScStageBytes = 2048;   // 128 rows x 16 scale bytes
 constexpr int kKStage = 512;          // K elements per packed stage
 constexpr int kKBlock = 64;           // K elements per A/B step (one 128B row of FP16)
 
-template <int N_MAX, int PK_STAGES, int B_STAGES, int A_STAGES>
+// N_MAX: largest MMA N (token rows per tile); PK_STAGES: packed-weight
+// stages in shared memory; B_STAGES x B_KB: token-operand stages, each
+// covering B_KB 64-wide K steps; A_STAGES: tensor-memory A buffers;
+// PREFETCH: packed stages prefetched into L2 ahead of the shared-memory ring.
+template <int N_MAX, int PK_STAGES, int B_STAGES, int B_KB, int A_STAGES, int PREFETCH>
 struct GemmConfig {
     static constexpr int kNMax = N_MAX;
     static constexpr int kPk = PK_STAGES;
     static constexpr int kB = B_STAGES;
+    static constexpr int kBKb = B_KB;
     static constexpr int kA = A_STAGES;
-    static constexpr int kBStageBytes = N_MAX * 128;
+    static constexpr int kPrefetch = PREFETCH;
+    static constexpr int kBStageBytes = N_MAX * 128 * B_KB;
     static constexpr int kAccBase = A_STAGES * 32;
     static constexpr int kTmemCols = 512;
     static_assert(N_MAX % 16 == 0 && N_MAX <= 256, "N_MAX");
     static_assert(kAccBase + 2 * N_MAX <= kTmemCols, "tensor memory budget");
+    static_assert(A_STAGES % 2 == 0, "each A stage must belong to one dequantiser warpgroup");
     static constexpr int kSmemBytes = 1024 /*align slack*/ + PK_STAGES * kPkStageBytes +
                                       B_STAGES * kBStageBytes + PK_STAGES * kScStageBytes +
                                       1024 /*barriers*/;

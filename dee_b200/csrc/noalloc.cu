@@ -23,7 +23,7 @@
 //   * The first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current).  Make
 //     that first call before any stream capture begins.
-#include "../../include/dee_b200.h"
+#include "dee_b200.h"
 #include "kernels.h"
 
 #include <cstdio>
@@ -73,7 +73,7 @@ ScratchPlan plan(int H, int I, int E, size_t sel) {
     p.n_tiles = o; o = align256(o + sizeof(int32_t));
     p.perm = o; o = align256(o + sizeof(int32_t) * sel);
     p.row_of = o; o = align256(o + sizeof(int32_t) * sel);
-    p.max_tiles = E + static_cast<int>(sel / 16) + 1;
+    p.max_tiles = E + static_cast<int>(sel / 8) + 1;
     p.tiles = o; o = align256(o + sizeof(TileDesc) * p.max_tiles);
     p.xperm = o; o = align256(o + sel * H * sizeof(__half));
     p.act = o; o = align256(o + sel * I * sizeof(__half));
@@ -165,6 +165,7 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     auto* status = reinterpret_cast<uint32_t*>(base + sp.status);
     auto* slots = reinterpret_cast<int32_t*>(base + sp.slots);
 
+    const bool decode = tokens <= kDecodeMaxTokens;
     // Tensor maps over the caller's records and the scratch rows (host work).
     const uint8_t* rec = static_cast<const uint8_t*>(d_records);
     const cuuint64_t ns = static_cast<cuuint64_t>(n_slots), rb = record_bytes;
@@ -203,14 +204,14 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     {
         const cuuint64_t d[2] = {static_cast<cuuint64_t>(H), sel};
         const cuuint64_t st[1] = {static_cast<cuuint64_t>(H) * 2};
-        const cuuint32_t box[2] = {64, 16};
+        const cuuint32_t box[2] = {64, decode ? 8u : 16u};
         ok = ok && enc(&gu.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base + sp.xperm, d, st, box,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     }
     {
         const cuuint64_t d[2] = {static_cast<cuuint64_t>(I), sel};
         const cuuint64_t st[1] = {static_cast<cuuint64_t>(I) * 2};
-        const cuuint32_t box[2] = {64, 16};
+        const cuuint32_t box[2] = {64, decode ? 8u : 16u};
         ok = ok && enc(&dn.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base + sp.act, d, st, box,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     }
@@ -222,14 +223,15 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     identity_slots_kernel<<<1, 256, 0, stream>>>(slots, E);
     if ((err = cudaGetLastError()) != cudaSuccess) return report(DEE_ERR_CUDA, cudaGetErrorString(err));
 
-    const bool large = tokens > 64;
+    const bool large = !decode;
     PermuteOut po{reinterpret_cast<int32_t*>(base + sp.counts),
                   reinterpret_cast<int32_t*>(base + sp.offsets),
                   reinterpret_cast<int32_t*>(base + sp.perm),
                   reinterpret_cast<int32_t*>(base + sp.row_of),
                   reinterpret_cast<TileDesc*>(base + sp.tiles),
                   reinterpret_cast<int32_t*>(base + sp.n_tiles)};
-    err = launch_permute(d_ids, tokens, K, E, gemm_n_max(large), sp.max_tiles, po, status, stream);
+    err = launch_permute(d_ids, tokens, K, E, decode ? kDecodeTileRows : gemm_n_max(large),
+                         sp.max_tiles, po, status, stream);
     if (err == cudaSuccess)
         err = launch_gather_rows(static_cast<const __half*>(d_x_f16), po.perm, po.offsets + E,
                                  static_cast<int>(sel), K, H,
@@ -254,11 +256,13 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     a.status = status;
     a.k_total = H;
     a.m_tiles = I / 64;
-    err = launch_moe_gemm(true, large, gu, a, num_sms, stream);
+    err = decode ? launch_moe_decode(true, gu, a, num_sms, stream)
+                 : launch_moe_gemm(true, large, gu, a, num_sms, stream);
     if (err == cudaSuccess) {
         a.k_total = I;
         a.m_tiles = H / 128;
-        err = launch_moe_gemm(false, large, dn, a, num_sms, stream);
+        err = decode ? launch_moe_decode(false, dn, a, num_sms, stream)
+                     : launch_moe_gemm(false, large, dn, a, num_sms, stream);
     }
     if (err == cudaSuccess)
         err = launch_combine_f32(a.raw, d_weights, tokens, K, H, d_out_f32, stream);

@@ -33,6 +33,8 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, 
                                   int topk, int32_t* __restrict__ ids, float* __restrict__ weights,
                                   uint32_t* status) {
     extern __shared__ float route_smem[];
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -129,6 +131,8 @@ __global__ void route_dsv4_kernel(const float* __restrict__ logits, const float*
                                   int topk, float route_scale, int32_t* __restrict__ ids,
                                   float* __restrict__ weights, uint32_t* status) {
     extern __shared__ float dsv4_smem[];
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -223,6 +227,8 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     const int lane = tid & 31;
     const int sel = tokens * topk;
 
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     for (int e = tid; e < experts; e += kPermThreads) { cnt[e] = 0; cursor[e] = 0; }
     for (int i = tid; i < 32 * kPermMaxExperts; i += kPermThreads) (&wcnt[0][0])[i] = 0;
     __syncthreads();
@@ -327,6 +333,8 @@ __global__ void __launch_bounds__(kPermThreads, 1)
 __global__ void gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
                                    const int32_t* __restrict__ total_rows_dev, int max_rows,
                                    int topk, int hidden, __half* __restrict__ x_perm) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     const int rows = min(*total_rows_dev, max_rows);
     const int warps_total = gridDim.x * (blockDim.x >> 5);
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -345,6 +353,8 @@ __global__ void gather_rows_kernel(const __half* __restrict__ x, const int32_t* 
 // to FP32 separately.
 __global__ void combine_f32_kernel(const float* __restrict__ raw, const float* __restrict__ w,
                                    int tokens, int topk, int hidden, float* __restrict__ out) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -371,6 +381,8 @@ template <class IdT>
 __global__ void combine_f16_kernel(const float* __restrict__ raw, const float* __restrict__ w,
                                    const IdT* __restrict__ ids, int tokens, int topk, int hidden,
                                    __half* __restrict__ out) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     const size_t n = static_cast<size_t>(tokens) * hidden;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -399,6 +411,8 @@ __global__ void combine_f16_kernel(const float* __restrict__ raw, const float* _
 
 __global__ void ids_i64_to_i32_kernel(const int64_t* __restrict__ src, int n, int experts,
                                       int32_t* __restrict__ dst, uint32_t* status) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int64_t e = src[i];
         if (e < 0 || e >= experts) {
@@ -428,9 +442,8 @@ cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int 
     const int warps = 4;
     const int grid = (tokens + warps - 1) / warps;
     const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
-    route_topk_kernel<<<grid, warps * 32, smem, stream>>>(logits, tokens, experts, topk, ids,
-                                                           weights, status);
-    return cudaGetLastError();
+    return launch_pdl(route_topk_kernel, dim3(grid), dim3(warps * 32), smem, stream, logits, tokens,
+                      experts, topk, ids, weights, status);
 }
 
 cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int64_t* tid2eid,
@@ -443,20 +456,17 @@ cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int6
     const int warps = 4;
     const int grid = (tokens + warps - 1) / warps;
     const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
-    route_dsv4_kernel<<<grid, warps * 32, smem, stream>>>(logits, bias, tid2eid, input_ids, tokens,
-                                                          experts, topk, route_scale, ids, weights,
-                                                          status);
-    return cudaGetLastError();
+    return launch_pdl(route_dsv4_kernel, dim3(grid), dim3(warps * 32), smem, stream, logits, bias,
+                      tid2eid, input_ids, tokens, experts, topk, route_scale, ids, weights, status);
 }
 
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
                            cudaStream_t stream) {
-    if (experts <= 0 || experts > kPermMaxExperts || tokens <= 0 || topk <= 0 || n_tile_max < 16)
+    if (experts <= 0 || experts > kPermMaxExperts || tokens <= 0 || topk <= 0 || n_tile_max < 8)
         return cudaErrorInvalidValue;
-    permute_kernel<<<1, kPermThreads, 0, stream>>>(ids, tokens, topk, experts, n_tile_max,
-                                                   max_tiles, out, status);
-    return cudaGetLastError();
+    return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), 0, stream, ids, tokens, topk,
+                      experts, n_tile_max, max_tiles, out, status);
 }
 
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,
@@ -464,42 +474,38 @@ cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32
                                cudaStream_t stream) {
     if (hidden % 8 != 0) return cudaErrorInvalidValue;
     const int grid = grid_for(static_cast<size_t>(max_rows) * 32, 256, 148 * 8);
-    gather_rows_kernel<<<grid, 256, 0, stream>>>(x, perm, total_rows_dev, max_rows, topk, hidden,
-                                                 x_perm);
-    return cudaGetLastError();
+    return launch_pdl(gather_rows_kernel, dim3(grid), dim3(256), 0, stream, x, perm, total_rows_dev,
+                      max_rows, topk, hidden, x_perm);
 }
 
 cudaError_t launch_combine_f32(const float* raw, const float* weights, int tokens, int topk,
                                int hidden, float* out, cudaStream_t stream) {
     if (hidden % 4 != 0) return cudaErrorInvalidValue;
     const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
-    combine_f32_kernel<<<grid_for(n4, 256, 148 * 16), 256, 0, stream>>>(raw, weights, tokens, topk,
-                                                                         hidden, out);
-    return cudaGetLastError();
+    return launch_pdl(combine_f32_kernel, dim3(grid_for(n4, 256, 148 * 16)), dim3(256), 0, stream,
+                      raw, weights, tokens, topk, hidden, out);
 }
 
 cudaError_t launch_combine_f16(const float* raw, const float* weights, const int64_t* ids64,
                                int tokens, int topk, int hidden, __half* out,
                                cudaStream_t stream) {
     const size_t n = static_cast<size_t>(tokens) * hidden;
-    combine_f16_kernel<int64_t><<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
-        raw, weights, ids64, tokens, topk, hidden, out);
-    return cudaGetLastError();
+    return launch_pdl(combine_f16_kernel<int64_t>, dim3(grid_for(n, 256, 148 * 16)), dim3(256), 0,
+                      stream, raw, weights, ids64, tokens, topk, hidden, out);
 }
 
 cudaError_t launch_combine_f16_i32(const float* raw, const float* weights, const int32_t* ids,
                                    int tokens, int topk, int hidden, __half* out,
                                    cudaStream_t stream) {
     const size_t n = static_cast<size_t>(tokens) * hidden;
-    combine_f16_kernel<int32_t><<<grid_for(n, 256, 148 * 16), 256, 0, stream>>>(
-        raw, weights, ids, tokens, topk, hidden, out);
-    return cudaGetLastError();
+    return launch_pdl(combine_f16_kernel<int32_t>, dim3(grid_for(n, 256, 148 * 16)), dim3(256), 0,
+                      stream, raw, weights, ids, tokens, topk, hidden, out);
 }
 
 cudaError_t launch_ids_i64_to_i32(const int64_t* src, int n, int experts, int32_t* dst,
                                   uint32_t* status, cudaStream_t stream) {
-    ids_i64_to_i32_kernel<<<grid_for(n, 256, 1024), 256, 0, stream>>>(src, n, experts, dst, status);
-    return cudaGetLastError();
+    return launch_pdl(ids_i64_to_i32_kernel, dim3(grid_for(n, 256, 1024)), dim3(256), 0, stream, src,
+                      n, experts, dst, status);
 }
 
 }  // namespace dee

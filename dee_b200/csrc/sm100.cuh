@@ -82,6 +82,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// is suspended (up to the hint) instead of spinning, so waiting roles do not
+// take issue slots from the warps doing the work.
+constexpr uint32_t kSuspendHintNs = 20000;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (and
 // sets `code` in *status) when the limit expires.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
@@ -89,13 +106,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (;;) {
-        for (int i = 0; i < 64; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+        for (int i = 0; i < 16; ++i)
+            if (mbar_try_wait_sleep(bar, parity)) return true;
         if (global_ns() - t0 > kWaitLimitNs) {
             atomicOr(status, code);
             return false;
         }
     }
+}
+
+// ---------------------------------------------------------------- PDL
+
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialisation may start while its predecessor in the stream still runs;
+// pdl_wait() blocks until the predecessor has completed and its writes are
+// visible, pdl_trigger() lets the successor launch.  Every kernel here calls
+// pdl_wait() before touching data a predecessor produces and pdl_trigger()
+// only after that wait, so a kernel that starts early can rely on the kernel
+// two places back having completed.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- TMA
@@ -135,6 +167,15 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z),
         "l"(policy)
         : "memory");
+}
+
+// Prefetch a 3-D tile into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t x, int32_t y,
+                                                int32_t z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05

@@ -135,6 +135,63 @@ def test_moe_raw_small_shape(torch_cuda, oracle_mod, T, dup):
     assert np.array_equal(eng.journal_ids(T), ids)
 
 
+def _plant_edge_rows(layout, recs, rng, experts, frac=0.25):
+    """Give a fraction of the W2 rows of `experts` one scale byte for the
+    whole row, drawn from the limits of the exact-FP16 dequant range: 60, 100
+    and 103 underflow or round in FP16, 104 and 140 are the last exact bytes,
+    141 and 142 overflow for |value| >= 2 (their rows keep only nibbles of
+    magnitude <= 1.5).  Returns {expert: (rows, bytes)}."""
+    H, I = layout.hidden, layout.inter
+    edge = np.array([60, 100, 103, 104, 140, 141, 142], dtype=np.uint8)
+    planted = {}
+    for e in experts:
+        rec = recs[e]
+        sc = rec[layout.s2:layout.s2 + H * I // 32].reshape(H, I // 32)
+        pk = rec[layout.w2:layout.w2 + H * I // 2].reshape(H, I // 2)
+        rows = np.flatnonzero(rng.random(H) < frac)
+        vals = rng.choice(edge, size=rows.size)
+        sc[rows] = vals[:, None]
+        big = rows[vals >= 141]
+        pk[big] &= np.uint8(0xBB)  # keep the sign and the two low code bits of each nibble
+        planted[e] = (rows, vals)
+    return planted
+
+
+@pytest.mark.parametrize("T", [8, 100])
+def test_moe_raw_edge_scales(torch_cuda, oracle_mod, T):
+    """Scale bytes outside the exact-FP16 range take the FP16-rounded dequant
+    path; rows without them take the fast one.  Every output feature is
+    compared at its own magnitude.  T=8 runs the decode kernel, T=100 the
+    tensor-memory grouped GEMM; both projections share the dequant code."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=404, kind="normal")
+    rng = np.random.default_rng(405)
+    _plant_edge_rows(layout, recs, rng, experts=range(E))
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _rand_ids(rng, T, E, K)
+    eng = _engine(H, I, E, K, max_tokens=128)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    raw = _run_layer(torch, eng, bank, x16, ids, None).reshape(T * K, H)
+    want = orc.moe_layer_raw(recs, layout, x16, ids).reshape(T * K, H)
+    assert np.isfinite(want).all() and np.isfinite(raw).all()
+    flat = ids.reshape(-1)
+    n_zero, worst = 0, 0.0
+    for e in np.unique(flat):
+        w, r = want[flat == e], raw[flat == e]
+        den = np.linalg.norm(w.astype(np.float64), axis=0)
+        num = np.linalg.norm((r - w).astype(np.float64), axis=0)
+        zero = den == 0
+        assert not r[:, zero].any()  # rows whose weights dequantise to zeros (byte 60)
+        n_zero += int(zero.sum())
+        worst = max(worst, float((num[~zero] / den[~zero]).max()))
+    assert n_zero > 0
+    assert worst <= 5 * TOL_REL_L2, worst
+
+
 def test_combines_bitexact_given_raw(torch_cuda, oracle_mod):
     torch = torch_cuda
     orc = oracle_mod
