@@ -12,11 +12,16 @@
 //                (128 rows x 256 B), their UE8M0 scales and the stage's token
 //                rows (8 rows x 1 KB, 128-byte swizzled), plus L2 prefetch of
 //                later stages
-//   warps 1-8    consumers: each owns 16 weight rows of the 128-row work item,
-//                reads its packed bytes from shared memory, converts them
-//                (cvt.rn.f16x2.e2m1x2) into mma.sync.m16n8k16 A fragments and
-//                accumulates FP32 in registers, applying each 32-wide block's
-//                power-of-two scale to the block's partial sum
+//   warps 1-16   consumers: warp w owns the 16 weight rows (w-1)%8 of the
+//                128-row work item over one half of each stage's K (warps
+//                1-8 the first 256, warps 9-16 the second), reads its packed
+//                bytes from shared memory, converts them (cvt.rn.f16x2.e2m1x2)
+//                into mma.sync.m16n8k16 A fragments and accumulates FP32 in
+//                registers, applying each 32-wide block's power-of-two scale to
+//                the block's partial sum.  At the end of an item the second
+//                warp of each pair hands its sums to the first through shared
+//                memory (one fixed two-term add), and the first runs the
+//                epilogue.
 //
 // Gate/up items pair 8 gate rows with the same 8 up rows in each 16-row MMA
 // tile, so one thread holds the gate and up accumulators of the same
@@ -30,14 +35,17 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kDecThreads = 288;          // 9 warps
+constexpr int kDecThreads = 544;          // 17 warps: producer + 8 pairs of consumers
 constexpr int kDecStages = 5;
 constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 512)
 constexpr int kDecScBytes = 2048;          // 128 rows x 16 scale bytes
 constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
 constexpr int kDecStageBytes = kDecPkBytes + kDecScBytes + kDecBBytes;
 constexpr int kDecPrefetch = 4;
-constexpr int kDecSmem = 1024 + kDecStages * kDecStageBytes + 256;
+constexpr int kDecBarBytes = 256;
+constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
+constexpr int kDecSmem = 1024 + kDecStages * kDecStageBytes + kDecBarBytes + kDecRedBytes;
+static_assert(kDecSmem <= 232448, "shared memory budget");
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -111,6 +119,25 @@ __device__ __forceinline__ void mma_16816_zero(float (&c)[4], uint32_t a0, uint3
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
 }
 
+__device__ __forceinline__ void named_bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Both halves of a block's scale bytes within the exact range (see below).
+__device__ __forceinline__ bool scales_exact(uint32_t w) {
+    bool ok = true;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        const uint32_t x = (w >> (8 * b)) & 0xFFu;
+        ok = ok && x >= 104u && x <= 140u;
+    }
+    return ok;
+}
+
 __device__ __forceinline__ float silu_ref(float g) {
     return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
 }
@@ -158,7 +185,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecStages; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 8);
+            mbar_init(&empty[i], 16);
         }
         fence_barrier_init();
     }
@@ -249,17 +276,32 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // packed bytes 4q..4q+3 (K 8q..8q+7): its A fragments come from one
     // 32-bit word per row and its token fragments for both k16 steps from
     // one 16-byte slice of the token row.  A and B use the same assignment,
-    // so the MMA's sum is unchanged.  Each block is accumulated into a zeroed
-    // temporary and added with the row's power-of-two scale in FP32; blocks
-    // whose scale is not an exact binary16 take the FP16-rounded path of the
-    // reference dequant instead.
-    const int cw = warp - 1;        // 0..7: 16-row MMA tile of the item
-    const int g = lane >> 2;        // fragment row within 8 / token column
+    // so the MMA's sum is unchanged.  MMA column n reads token row
+    // pi(n) = 4*(n&1) + n/2 of the stage, which puts the two lane groups of
+    // each 128-bit shared-memory phase in opposite halves of the swizzle.
+    //
+    // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
+    // finite binary16, so scaling the block's FP32 partial sum equals summing
+    // the reference's FP16-rounded weights.  Byte 103 rounds 0.5 x 2^-24 and
+    // bytes >= 141 overflow in the reference dequant: a stage with any such
+    // block in the warp's rows takes the FP16-rounded path instead.
+    const int cw = (warp - 1) & 7;  // 16-row MMA tile of the item
+    const int kh = (warp - 1) >> 3;  // half of each stage's K
+    const int g = lane >> 2;        // fragment row within 8 / MMA column
     const int q = lane & 3;
     const int row_lo = kGU ? (8 * cw + g) : (16 * cw + g);
     const int row_hi = kGU ? (64 + 8 * cw + g) : (16 * cw + 8 + g);
-    const int sw_lo = row_lo & 7, sw_hi = row_hi & 7;
-    int st = 0;
+    const int brow = ((g & 1) << 2) | (g >> 1);
+    // byte offsets within a stage; rows are 128 B and row & 7 == g, so the
+    // 128-byte swizzle of chunk j of either weight row is j ^ g
+    const int off_lo = kh * 16384 + row_lo * 128 + q * 4;
+    const int off_hi = kh * 16384 + row_hi * 128 + q * 4;
+    const int off_sc = kDecPkBytes + kh * 8;
+    const int off_b = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128;
+    const int xb0 = (q ^ brow) << 4, xb1 = ((4 + q) ^ brow) << 4;
+    float* red = reinterpret_cast<float*>(smem + kDecStages * kDecStageBytes + kDecBarBytes);
+    int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
+    int st = 0, parity = 0;
     uint32_t ph = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const DecItem it = dec_item(args, item);
@@ -268,55 +310,47 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int s = 0; s < k_stages; ++s) {
             ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-            const uint8_t* pk = smem + st * kDecStageBytes;
-            const uint8_t* sc = pk + kDecPkBytes;
-            const uint8_t* bt = sc + kDecScBytes;
-            const uint4 slo = *reinterpret_cast<const uint4*>(sc + row_lo * 16);
-            const uint4 shi = *reinterpret_cast<const uint4*>(sc + row_hi * 16);
-            const uint32_t slw[4] = {slo.x, slo.y, slo.z, slo.w};
-            const uint32_t shw[4] = {shi.x, shi.y, shi.z, shi.w};
-            // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
-            // finite binary16, so scaling the block's FP32 partial sum equals
-            // summing the reference's FP16-rounded weights.  Byte 103 rounds
-            // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.
-            bool in_range = true;
+            const uint8_t* base = smem + st * kDecStageBytes;
+            const uint2 slo = *reinterpret_cast<const uint2*>(base + off_sc + row_lo * 16);
+            const uint2 shi = *reinterpret_cast<const uint2*>(base + off_sc + row_hi * 16);
+            const bool fast = __all_sync(0xffffffffu, scales_exact(slo.x) && scales_exact(slo.y) &&
+                                                          scales_exact(shi.x) && scales_exact(shi.y));
+            if (fast) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-#pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const uint32_t x = (slw[i] >> (8 * b)) & 0xFFu, y = (shw[i] >> (8 * b)) & 0xFFu;
-                    in_range = in_range && x >= 104u && x <= 140u && y >= 104u && y <= 140u;
-                }
-            }
-            const bool fast = __all_sync(0xffffffffu, in_range);
-#pragma unroll
-            for (int blk = 0; blk < 16; ++blk) {
-                const int half = blk >> 3;
-                const int chunk = blk & 7;
-                const uint32_t wlo = *reinterpret_cast<const uint32_t*>(
-                    pk + half * 16384 + row_lo * 128 + ((chunk ^ sw_lo) << 4) + q * 4);
-                const uint32_t whi = *reinterpret_cast<const uint32_t*>(
-                    pk + half * 16384 + row_hi * 128 + ((chunk ^ sw_hi) << 4) + q * 4);
-                const int cb = (blk & 1) * 4 + q;  // 16-byte chunk of the token row in box blk/2
-                const uint4 bv = *reinterpret_cast<const uint4*>(bt + (blk >> 1) * 1024 + g * 128 +
-                                                                  ((cb ^ g) << 4));
-                const uint32_t sb_lo = (slw[blk >> 2] >> ((blk & 3) * 8)) & 0xFFu;
-                const uint32_t sb_hi = (shw[blk >> 2] >> ((blk & 3) * 8)) & 0xFFu;
-                uint32_t a[8];  // [lo b0, lo b1, lo b2, lo b3, hi b0..b3] as f16x2
-                cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
-                cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
-                if (fast) {
+                for (int j = 0; j < 8; ++j) {
+                    const int xw = (j ^ g) << 4;
+                    const uint32_t wlo = *reinterpret_cast<const uint32_t*>(base + off_lo + xw);
+                    const uint32_t whi = *reinterpret_cast<const uint32_t*>(base + off_hi + xw);
+                    const uint4 bv = *reinterpret_cast<const uint4*>(base + off_b + (j >> 1) * 1024 +
+                                                                      ((j & 1) ? xb1 : xb0));
+                    uint32_t a[8];  // [lo b0..b3, hi b0..b3] as f16x2
+                    cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
+                    cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
                     float t[4];
                     mma_16816_zero(t, a[0], a[4], a[1], a[5], bv.x, bv.y);
                     mma_16816_acc(t, a[2], a[6], a[3], a[7], bv.z, bv.w);
-                    const float flo = __uint_as_float((sb_lo) << 23);
-                    const float fhi = __uint_as_float((sb_hi) << 23);
+                    const uint32_t sl = ((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu;
+                    const uint32_t sh = ((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu;
+                    const float flo = __uint_as_float(sl << 23);
+                    const float fhi = __uint_as_float(sh << 23);
                     c[0] = fmaf(flo, t[0], c[0]);
                     c[1] = fmaf(flo, t[1], c[1]);
                     c[2] = fmaf(fhi, t[2], c[2]);
                     c[3] = fmaf(fhi, t[3], c[3]);
-                } else {
-                    const Scale s_lo = make_scale(sb_lo), s_hi = make_scale(sb_hi);
+                }
+            } else {
+#pragma unroll 1
+                for (int j = 0; j < 8; ++j) {
+                    const int xw = (j ^ g) << 4;
+                    const uint32_t wlo = *reinterpret_cast<const uint32_t*>(base + off_lo + xw);
+                    const uint32_t whi = *reinterpret_cast<const uint32_t*>(base + off_hi + xw);
+                    const uint4 bv = *reinterpret_cast<const uint4*>(base + off_b + (j >> 1) * 1024 +
+                                                                      ((j & 1) ? xb1 : xb0));
+                    const Scale s_lo = make_scale(((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu);
+                    const Scale s_hi = make_scale(((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu);
+                    uint32_t a[8];
+                    cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
+                    cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         a[i] = dequant_f16(a[i], s_lo);
@@ -330,10 +364,32 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (lane == 0) mbar_arrive(&empty[st]);
             if (++st == kDecStages) { st = 0; ph ^= 1; }
         }
-        if (!ok) break;
+        // Pair reduction.  The slot is double buffered by item parity: the
+        // second warp can only write it again after passing the next item's
+        // barrier, which the first warp reaches after reading this one.  The
+        // flag carries a timeout of the second warp, so neither warp waits on
+        // a partner that has left.
+        float* slot = red + ((parity * 8 + cw) * 32 + lane) * 4;
+        if (kh == 1) {
+            *reinterpret_cast<float4*>(slot) = make_float4(c[0], c[1], c[2], c[3]);
+            if (lane == 0) red_ok[parity * 8 + cw] = ok ? 1 : 0;
+            named_bar_arrive(1 + cw, 64);
+            parity ^= 1;
+            if (!ok) break;
+            continue;
+        }
+        named_bar_sync(1 + cw, 64);
+        const float4 o = *reinterpret_cast<const float4*>(slot);
+        const bool ok_pair = red_ok[parity * 8 + cw] != 0;
+        parity ^= 1;
+        if (!ok || !ok_pair) break;
+        c[0] += o.x;
+        c[1] += o.y;
+        c[2] += o.z;
+        c[3] += o.w;
         if (!it.valid) continue;
         const int n_rows = it.td.n_rows;
-        const int n0 = 2 * q, n1 = 2 * q + 1;
+        const int n0 = q, n1 = 4 + q;  // tokens of MMA columns 2q and 2q+1
         if (kGU) {
             const int feat = it.m * 64 + 8 * cw + g;
             const float lim = args.swiglu_limit;
