@@ -187,6 +187,9 @@ def time_steps(torch, fn, n_steps, flush, stream, warmup):
     torch.cuda.synchronize()
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_steps)]
+    # profiler range (a no-op without a profiler): `ncu --profile-from-start off`
+    # captures exactly the timed steps
+    torch.cuda.profiler.start()
     for i in range(n_steps):
         with torch.cuda.stream(stream):
             flush.zero_()
@@ -194,6 +197,7 @@ def time_steps(torch, fn, n_steps, flush, stream, warmup):
         fn(i, stream)
         evs[i][1].record(stream)
     torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
     return [a.elapsed_time(b) for a, b in evs]
 
 

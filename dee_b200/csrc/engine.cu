@@ -286,6 +286,8 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.n_tiles = e->d_n_tiles;
     a.slot_of = bank.d_slot_of;
     a.num_slots = bank.n_slots;
+    a.records = bank.records;
+    a.record_bytes = bank.record_bytes;
     a.num_experts = E;
     a.perm = e->d_perm;
     a.act = e->d_act;

@@ -10,8 +10,9 @@
 //
 //   warp 0       TMA producer: per 512-wide K stage, the packed FP4 rows
 //                (128 rows x 256 B), their UE8M0 scales and the stage's token
-//                rows (8 rows x 1 KB, 128-byte swizzled), plus L2 prefetch of
-//                later stages
+//                rows (8 rows x 1 KB, 128-byte swizzled)
+//   warp 17      scale checker: decides per stage whether every block scale
+//                allows the exact FP32 scaling below
 //   warps 1-16   consumers: warp w owns the 16 weight rows (w-1)%8 of the
 //                128-row work item over one half of each stage's K (warps
 //                1-8 the first 256, warps 9-16 the second), reads its packed
@@ -35,14 +36,16 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kDecThreads = 544;          // 17 warps: producer + 8 pairs of consumers
+constexpr int kDecConsumerWarps = 16;
+constexpr int kDecCheckerWarp = 1 + kDecConsumerWarps;
+constexpr int kDecThreads = 32 * (kDecCheckerWarp + 1);  // producer, 8 pairs of consumers, checker
 constexpr int kDecStages = 5;
 constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 512)
 constexpr int kDecScBytes = 2048;          // 128 rows x 16 scale bytes
 constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
 constexpr int kDecStageBytes = kDecPkBytes + kDecScBytes + kDecBBytes;
-constexpr int kDecPrefetch = 4;
-constexpr int kDecBarBytes = 256;
+constexpr int kDecBarBytes = 256;  // full, ready, empty barriers + per-stage fast flags
+static_assert(kDecStages * (3 * 8 + 4) <= kDecBarBytes, "barrier area");
 constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
 constexpr int kDecSmem = 1024 + kDecStages * kDecStageBytes + kDecBarBytes + kDecRedBytes;
 static_assert(kDecSmem <= 232448, "shared memory budget");
@@ -127,15 +130,33 @@ __device__ __forceinline__ void named_bar_arrive(int id, int threads) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-// Both halves of a block's scale bytes within the exact range (see below).
-__device__ __forceinline__ bool scales_exact(uint32_t w) {
-    bool ok = true;
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-        const uint32_t x = (w >> (8 * b)) & 0xFFu;
-        ok = ok && x >= 104u && x <= 140u;
-    }
-    return ok;
+// Per byte of w: bit 7 of the result is set iff the byte lies in [104, 140]
+// (SWAR: add 24 to every byte without carries between bytes, then the byte
+// must read 128..164).
+__device__ __forceinline__ uint32_t scale_bytes_exact(uint32_t w) {
+    const uint32_t y = ((w & 0x7F7F7F7Fu) + 0x18181818u) ^ (w & 0x80808080u);
+    const uint32_t z = (y & 0x7F7F7F7Fu) + 0x5B5B5B5Bu;
+    return y & ~z & 0x80808080u;
+}
+
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr));
+    return v;
 }
 
 __device__ __forceinline__ float silu_ref(float g) {
@@ -179,13 +200,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
-    uint64_t* empty = full + kDecStages;
+    uint64_t* ready = full + kDecStages;
+    uint64_t* empty = ready + kDecStages;
+    volatile int* fast_flag = reinterpret_cast<volatile int*>(empty + kDecStages);
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecStages; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 16);
+            mbar_init(&ready[i], 1);
+            mbar_init(&empty[i], kDecConsumerWarps);
         }
         fence_barrier_init();
     }
@@ -200,39 +224,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     pdl_trigger();
     const int k_stages = args.k_total / kKStage;
     uint32_t* status = args.status;
+    const uint32_t smem_base = smem_u32(smem);
 
     if (warp == 0) {
+        // ---------------- producer ----------------
         if (lane != 0) return;
         const uint64_t pol_w = policy_evict_first();
         const uint64_t pol_b = policy_evict_last();
-        int pf_item = blockIdx.x, pf_s = 0;
-        DecItem pf{};
-        bool pf_valid = false;
-        auto pf_advance = [&]() {
-            if (pf_valid && ++pf_s < k_stages) return;
-            if (pf_valid) pf_item += gridDim.x;
-            pf_s = 0;
-            pf_valid = pf_item < n_items;
-            if (pf_valid) pf = dec_item(args, pf_item);
-        };
-        auto pf_issue = [&]() {
-            if (!pf_valid) return;
-            const int xk = pf_s * (kKStage / 2);
-            const int row = kGU ? pf.m * 64 : pf.m * 128;
-            tma_prefetch_3d(&map_w0, xk, row, pf.slot);
-            tma_prefetch_3d(&map_w0, xk + 128, row, pf.slot);
-            if (kGU) {
-                tma_prefetch_3d(&map_w1, xk, row, pf.slot);
-                tma_prefetch_3d(&map_w1, xk + 128, row, pf.slot);
-            }
-        };
-        pf_advance();
-        for (int i = 0; i < kDecStages + kDecPrefetch && pf_valid; ++i) {
-            pf_issue();
-            pf_advance();
-        }
-        // the down GEMM's token operand is the gate/up output: weights may be
-        // prefetched early, the stage loads wait for the predecessor
+        // the down GEMM's token operand is the gate/up output
         if (!kGU) pdl_wait();
         int st = 0;
         uint32_t ph = 0;
@@ -240,8 +239,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             const DecItem it = dec_item(args, item);
             if (!it.valid) atomicOr(status, kStatusBadExpert);
             for (int s = 0; s < k_stages; ++s) {
-                pf_issue();
-                pf_advance();
                 if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
                 mbar_arrive_expect_tx(&full[st], kDecStageBytes);
                 uint8_t* pk = smem + st * kDecStageBytes;
@@ -271,6 +268,40 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         return;
     }
 
+    if (warp == kDecCheckerWarp) {
+        // ---------------- scale checker ----------------
+        // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
+        // finite binary16, so scaling a block's FP32 partial sum equals
+        // summing the reference's FP16-rounded weights.  Byte 103 rounds
+        // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.  The
+        // checker reads each stage's 2 KB of scale bytes once and publishes
+        // whether all of them are in range; the consumers start the stage
+        // only after that.
+        int st = 0;
+        uint32_t ph = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            for (int s = 0; s < k_stages; ++s) {
+                const bool ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
+                if (!__all_sync(0xffffffffu, ok)) return;
+                const uint32_t sc = smem_base + st * kDecStageBytes + kDecPkBytes + lane * 64;
+                uint32_t acc = 0x80808080u;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 v = lds_v4(sc + i * 16);
+                    acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
+                           scale_bytes_exact(v.w);
+                }
+                const bool fast = __all_sync(0xffffffffu, acc == 0x80808080u);
+                if (lane == 0) {
+                    fast_flag[st] = fast ? 1 : 0;
+                    mbar_arrive(&ready[st]);
+                }
+                if (++st == kDecStages) { st = 0; ph ^= 1; }
+            }
+        }
+        return;
+    }
+
     // ---------------- consumers ----------------
     // K inside each 32-wide scale block is assigned so that thread q owns
     // packed bytes 4q..4q+3 (K 8q..8q+7): its A fragments come from one
@@ -279,26 +310,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // so the MMA's sum is unchanged.  MMA column n reads token row
     // pi(n) = 4*(n&1) + n/2 of the stage, which puts the two lane groups of
     // each 128-bit shared-memory phase in opposite halves of the swizzle.
-    //
-    // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
-    // finite binary16, so scaling the block's FP32 partial sum equals summing
-    // the reference's FP16-rounded weights.  Byte 103 rounds 0.5 x 2^-24 and
-    // bytes >= 141 overflow in the reference dequant: a stage with any such
-    // block in the warp's rows takes the FP16-rounded path instead.
     const int cw = (warp - 1) & 7;  // 16-row MMA tile of the item
     const int kh = (warp - 1) >> 3;  // half of each stage's K
     const int g = lane >> 2;        // fragment row within 8 / MMA column
     const int q = lane & 3;
     const int row_lo = kGU ? (8 * cw + g) : (16 * cw + g);
-    const int row_hi = kGU ? (64 + 8 * cw + g) : (16 * cw + 8 + g);
+    constexpr uint32_t kHi = kGU ? 64 * 128 : 8 * 128;  // byte distance of the hi row
     const int brow = ((g & 1) << 2) | (g >> 1);
-    // byte offsets within a stage; rows are 128 B and row & 7 == g, so the
-    // 128-byte swizzle of chunk j of either weight row is j ^ g
-    const int off_lo = kh * 16384 + row_lo * 128 + q * 4;
-    const int off_hi = kh * 16384 + row_hi * 128 + q * 4;
-    const int off_sc = kDecPkBytes + kh * 8;
-    const int off_b = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128;
-    const int xb0 = (q ^ brow) << 4, xb1 = ((4 + q) ^ brow) << 4;
+    // Stage-relative byte offsets.  Rows are 128 B and row & 7 == g, so chunk
+    // j of a weight row sits at (j ^ g) * 16: with g * 16 folded into w_off
+    // (whose bits 4-6 are otherwise zero) the address of chunk j is
+    // (stage + w_off) ^ (j * 16), for the lo and hi rows alike.
+    const uint32_t w_off = kh * 16384 + row_lo * 128 + (g << 4) + q * 4;
+    const uint32_t s_off = kDecPkBytes + row_lo * 16 + kh * 8;
+    const uint32_t b_off0 = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
+    const uint32_t b_off1 = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
     float* red = reinterpret_cast<float*>(smem + kDecStages * kDecStageBytes + kDecBarBytes);
     int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
     int st = 0, parity = 0;
@@ -308,21 +334,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         float c[4] = {0.f, 0.f, 0.f, 0.f};
         bool ok = true;
         for (int s = 0; s < k_stages; ++s) {
-            ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
+            ok = mbar_wait(&ready[st], ph, status, kStatusTimeoutDequant);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-            const uint8_t* base = smem + st * kDecStageBytes;
-            const uint2 slo = *reinterpret_cast<const uint2*>(base + off_sc + row_lo * 16);
-            const uint2 shi = *reinterpret_cast<const uint2*>(base + off_sc + row_hi * 16);
-            const bool fast = __all_sync(0xffffffffu, scales_exact(slo.x) && scales_exact(slo.y) &&
-                                                          scales_exact(shi.x) && scales_exact(shi.y));
+            const uint32_t sb = smem_base + st * kDecStageBytes;
+            const bool fast = fast_flag[st] != 0;
+            const uint2 slo = lds_v2(sb + s_off);
+            const uint2 shi = lds_v2(sb + s_off + kHi / 8);
+            const uint32_t wb = sb + w_off;
+            const uint32_t bb0 = sb + b_off0, bb1 = sb + b_off1;
             if (fast) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
-                    const int xw = (j ^ g) << 4;
-                    const uint32_t wlo = *reinterpret_cast<const uint32_t*>(base + off_lo + xw);
-                    const uint32_t whi = *reinterpret_cast<const uint32_t*>(base + off_hi + xw);
-                    const uint4 bv = *reinterpret_cast<const uint4*>(base + off_b + (j >> 1) * 1024 +
-                                                                      ((j & 1) ? xb1 : xb0));
+                    const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
+                    const uint32_t wlo = lds_u32(wa);
+                    const uint32_t whi = lds_u32(wa + kHi);
+                    const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
                     uint32_t a[8];  // [lo b0..b3, hi b0..b3] as f16x2
                     cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
                     cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
@@ -341,11 +367,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             } else {
 #pragma unroll 1
                 for (int j = 0; j < 8; ++j) {
-                    const int xw = (j ^ g) << 4;
-                    const uint32_t wlo = *reinterpret_cast<const uint32_t*>(base + off_lo + xw);
-                    const uint32_t whi = *reinterpret_cast<const uint32_t*>(base + off_hi + xw);
-                    const uint4 bv = *reinterpret_cast<const uint4*>(base + off_b + (j >> 1) * 1024 +
-                                                                      ((j & 1) ? xb1 : xb0));
+                    const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
+                    const uint32_t wlo = lds_u32(wa);
+                    const uint32_t whi = lds_u32(wa + kHi);
+                    const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
                     const Scale s_lo = make_scale(((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu);
                     const Scale s_hi = make_scale(((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu);
                     uint32_t a[8];

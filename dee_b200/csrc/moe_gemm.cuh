@@ -56,6 +56,8 @@ struct GemmArgs {
     const int* n_tiles;      // device: number of tiles
     const int* slot_of;      // device: expert -> record slot in the bank
     int num_slots;           // slots in the bank (bounds check)
+    const uint8_t* records;  // bank base: slot s starts at records + s * record_bytes
+    size_t record_bytes;
     int num_experts;
     const int* perm;         // device: grouped row -> position (kDown)
     __half* act;             // kGateUp output [rows, I]

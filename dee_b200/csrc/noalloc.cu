@@ -249,6 +249,8 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     a.n_tiles = po.n_tiles;
     a.slot_of = slots;
     a.num_slots = n_slots;
+    a.records = rec;
+    a.record_bytes = record_bytes;
     a.num_experts = E;
     a.perm = po.perm;
     a.act = reinterpret_cast<__half*>(base + sp.act);

@@ -178,6 +178,12 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t 
                  : "memory");
 }
 
+// Prefetch a contiguous global range into L2 (16-byte aligned address, size a
+// multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---------------------------------------------------------------- tcgen05
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
