@@ -23,11 +23,6 @@
 namespace dee {
 namespace {
 
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 EncodeTiledFn get_encode_fn() {
     static EncodeTiledFn fn = nullptr;
     static std::once_flag once;
@@ -68,7 +63,8 @@ struct Bank {
     int n_slots = 0;
     size_t record_bytes = 0;
     int32_t* d_slot_of = nullptr;  // [E]
-    CUtensorMap w1, w3, w2, s1, s3, s2;
+    CUtensorMap w1, w3, w2, s1, s3, s2;  // tcgen05 kernel
+    GemmMaps dec_gu{}, dec_dn{};         // decode kernel (weight maps)
 };
 
 template <class T>
@@ -104,7 +100,7 @@ struct dee_engine {
     int32_t* h_ids = nullptr;  // pinned staging of the consumed ids
     size_t h_ids_count = 0;
     CUtensorMap map_xperm, map_act;      // 16-row token boxes (tcgen05 kernel)
-    CUtensorMap map_xperm8, map_act8;    // 8-row token boxes (decode kernel)
+    CUtensorMap map_xperm_dec, map_act_dec;  // token rows of the decode kernel
     uint64_t launches = 0;
     // Opt-in stage timing (the role of the reference's StageProfiler,
     // dee.cpp/include/dee/profiling.h:31-46): events recorded on the launch
@@ -215,18 +211,13 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         if (!encode(e, &e->map_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
                     box, CU_TENSOR_MAP_SWIZZLE_128B, "act"))
             return DEE_ERR_CUDA;
-        const cuuint32_t box8[2] = {64, 8};
-        if (!encode(e, &e->map_act8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
-                    box8, CU_TENSOR_MAP_SWIZZLE_128B, "act/8"))
-            return DEE_ERR_CUDA;
     }
-    {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), cap};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 2};
-        const cuuint32_t box8[2] = {64, 8};
-        if (!encode(e, &e->map_xperm8, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_xperm, dims,
-                    strides, box8, CU_TENSOR_MAP_SWIZZLE_128B, "X_perm/8"))
-            return DEE_ERR_CUDA;
+    if (!encode_decode_token_map(get_encode_fn(), e->d_act, static_cast<int>(cap), I,
+                                 &e->map_act_dec) ||
+        !encode_decode_token_map(get_encode_fn(), e->d_xperm, static_cast<int>(cap), H,
+                                 &e->map_xperm_dec)) {
+        e->last_error = "cuTensorMapEncodeTiled failed for the decode token maps";
+        return DEE_ERR_CUDA;
     }
     return DEE_OK;
 }
@@ -295,8 +286,13 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.status = e->d_status;
 
     GemmMaps gm{};
-    gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3;
-    gm.b = decode ? e->map_xperm8 : e->map_xperm;
+    if (decode) {
+        gm = bank.dec_gu;
+        gm.b = e->map_xperm_dec;
+    } else {
+        gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3;
+        gm.b = e->map_xperm;
+    }
     a.k_total = H;
     a.m_tiles = I / 64;
     stage_begin(e, kStageGateUp, stream);
@@ -305,8 +301,13 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
     stage_end(e, kStageGateUp, stream);
 
-    gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
-    gm.b = decode ? e->map_act8 : e->map_act;
+    if (decode) {
+        gm = bank.dec_dn;
+        gm.b = e->map_act_dec;
+    } else {
+        gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
+        gm.b = e->map_act;
+    }
     a.k_total = I;
     a.m_tiles = H / 128;
     stage_begin(e, kStageDown, stream);
@@ -444,6 +445,9 @@ int dee_expert_bank_attach(dee_engine* e, int layer, const void* d_records, int 
                     CU_TENSOR_MAP_SWIZZLE_NONE, "w2.scale"))
             return DEE_ERR_CUDA;
     }
+    if (!encode_decode_weight_maps(get_encode_fn(), base, record_bytes, n_slots, H, I, &b.dec_gu,
+                                   &b.dec_dn))
+        return fail(e, DEE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the decode weight maps");
     b.records = base;
     b.n_slots = n_slots;
     b.record_bytes = record_bytes;

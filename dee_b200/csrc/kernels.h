@@ -38,11 +38,26 @@ cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, cons
                             int grid, cudaStream_t stream);
 
 // Decode-sized groups (tiles of at most kDecodeTileRows token rows): register
-// dequant + mma.sync kernel of moe_decode.cu.  maps.b must use 8-row boxes.
+// dequant + mma.sync kernel of moe_decode.cu.  Its tensor maps come from the
+// two encode_decode_* helpers below (maps.s0 / s1 are not used: scale rows
+// are copied per item straight from the records).
 constexpr int kDecodeTileRows = 8;
 constexpr int kDecodeMaxTokens = 64;
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream);
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Weight maps of the decode kernel over a bank of DEE4 records: W1, W3 (gate
+// and up) into gu->w0 / gu->w1 and W2 into dn->w0 / dn->w1.
+bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t record_bytes,
+                               int n_slots, int hidden, int inter, GemmMaps* gu, GemmMaps* dn);
+// Token-row map of the decode kernel over a [rows, cols] FP16 buffer.
+bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
+                             CUtensorMap* map);
 
 // Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,

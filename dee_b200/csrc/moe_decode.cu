@@ -9,8 +9,9 @@
 // Here the dequantised weights never leave registers:
 //
 //   warp 0       TMA producer: per 512-wide K stage, the packed FP4 rows
-//                (128 rows x 256 B), their UE8M0 scales and the stage's token
-//                rows (8 rows x 1 KB, 128-byte swizzled)
+//                (128 rows x 256 B) and the stage's token rows (8 rows x 1 KB,
+//                128-byte swizzled), one tensor copy per operand; per item,
+//                the rows' UE8M0 scales in one bulk copy per projection
 //   warp 17      scale checker: decides per stage whether every block scale
 //                allows the exact FP32 scaling below
 //   warps 1-16   consumers: warp w owns the 16 weight rows (w-1)%8 of the
@@ -39,16 +40,37 @@ using namespace sm100;
 constexpr int kDecConsumerWarps = 16;
 constexpr int kDecCheckerWarp = 1 + kDecConsumerWarps;
 constexpr int kDecThreads = 32 * (kDecCheckerWarp + 1);  // producer, 8 pairs of consumers, checker
-constexpr int kDecStages = 5;
+constexpr int kDecMaxStages = 4;
 constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 512)
-constexpr int kDecScBytes = 2048;          // 128 rows x 16 scale bytes
 constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
-constexpr int kDecStageBytes = kDecPkBytes + kDecScBytes + kDecBBytes;
-constexpr int kDecBarBytes = 256;  // full, ready, empty barriers + per-stage fast flags
-static_assert(kDecStages * (3 * 8 + 4) <= kDecBarBytes, "barrier area");
+constexpr int kDecStageBytes = kDecPkBytes + kDecBBytes;
+constexpr int kDecBarBytes = 256;  // stage and scale-slot barriers, per-slot flags and item records
 constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
-constexpr int kDecSmem = 1024 + kDecStages * kDecStageBytes + kDecBarBytes + kDecRedBytes;
-static_assert(kDecSmem <= 232448, "shared memory budget");
+constexpr uint32_t kSmemLimit = 232448;
+constexpr int kDecScSlots = 3;  // per-item scale rows: the consumed item, the next, the one after
+
+// Shared-memory plan: a ring of 512-wide K stages (packed weights + token
+// rows), three slots of per-item scale rows (128 rows x K/32 bytes), the
+// barriers and the pair-reduction buffer.  The ring is 4 deep unless the
+// scale rows are too long for that (K > 5120 takes 3).
+struct DecLayout {
+    int stages;
+    uint32_t sc_slot;  // bytes per scale slot
+    uint32_t sc_off, bar_off, red_off, bytes;
+};
+
+__host__ __device__ inline DecLayout dec_layout(int k_total) {
+    DecLayout L;
+    L.sc_slot = (static_cast<uint32_t>(128 * (k_total / 32)) + 1023u) & ~1023u;
+    const uint32_t fixed = 1024 + kDecScSlots * L.sc_slot + kDecBarBytes + kDecRedBytes;
+    const uint32_t room = fixed < kSmemLimit ? (kSmemLimit - fixed) / kDecStageBytes : 0;
+    L.stages = room < kDecMaxStages ? static_cast<int>(room) : kDecMaxStages;
+    L.sc_off = L.stages * kDecStageBytes;
+    L.bar_off = L.sc_off + kDecScSlots * L.sc_slot;
+    L.red_off = L.bar_off + kDecBarBytes;
+    L.bytes = 1024 + L.red_off + kDecRedBytes;
+    return L;
+}
 
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -170,23 +192,34 @@ struct DecItem {
     bool valid;
 };
 
-__device__ __forceinline__ DecItem dec_item(const GemmArgs& a, int item) {
+__device__ __forceinline__ TileDesc load_tile(const GemmArgs& a, int item) {
+    return a.tiles[item / a.m_tiles];
+}
+
+// Completes an item from its tile descriptor: the expert's record slot and
+// whether the item can run (an expert id that is out of range or not
+// resident leaves the item's outputs unwritten and raises kStatusBadExpert).
+__device__ __forceinline__ DecItem finish_item(const GemmArgs& a, int item, const TileDesc& td) {
     DecItem d;
-    const int tile = item / a.m_tiles;
-    d.m = item - tile * a.m_tiles;
-    d.td = a.tiles[tile];
-    const int e = d.td.expert;
+    d.m = item % a.m_tiles;
+    d.td = td;
+    const int e = td.expert;
     int slot = -1;
     if (e >= 0 && e < a.num_experts) slot = a.slot_of[e];
-    d.valid = slot >= 0 && slot < a.num_slots && d.td.n_rows > 0 && d.td.n_rows <= 8;
+    d.valid = slot >= 0 && slot < a.num_slots && td.n_rows > 0 && td.n_rows <= 8;
     d.slot = (slot < 0 || slot >= a.num_slots) ? 0 : slot;
     return d;
 }
 
+// What the consumers need of an item, handed over in shared memory with the
+// item's scale rows.
+struct ItemRec {
+    int m, row_start, n_rows, valid;
+};
+
 template <GemmMode MODE>
 __global__ void __launch_bounds__(kDecThreads, 1)
     moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
-                      const __grid_constant__ CUtensorMap map_s0, const __grid_constant__ CUtensorMap map_s1,
                       const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
     constexpr bool kGU = MODE == GemmMode::kGateUp;
     if (kGU) pdl_wait();
@@ -199,30 +232,40 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
-    uint64_t* ready = full + kDecStages;
-    uint64_t* empty = ready + kDecStages;
-    volatile int* fast_flag = reinterpret_cast<volatile int*>(empty + kDecStages);
+    const DecLayout L = dec_layout(args.k_total);
+    const int n_stages = L.stages;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [stages] TMA landed
+    uint64_t* empty = full + kDecMaxStages;                             // [stages] consumers done
+    uint64_t* sfull = empty + kDecMaxStages;      // [slots] scale rows landed
+    uint64_t* sready = sfull + kDecScSlots;        // [slots] scale rows checked
+    uint64_t* sempty = sready + kDecScSlots;       // [slots] item consumed
+    volatile int* fast_flag = reinterpret_cast<volatile int*>(sempty + kDecScSlots);  // [slots]
+    volatile ItemRec* item_rec = reinterpret_cast<volatile ItemRec*>(smem + L.bar_off + 160);  // [slots]
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kDecStages; ++i) {
+        for (int i = 0; i < n_stages; ++i) {
             mbar_init(&full[i], 1);
-            mbar_init(&ready[i], 1);
             mbar_init(&empty[i], kDecConsumerWarps);
+        }
+        for (int i = 0; i < kDecScSlots; ++i) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&sready[i], 1);
+            mbar_init(&sempty[i], kDecConsumerWarps);
         }
         fence_barrier_init();
     }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&map_w0);
-        prefetch_tmap(&map_s0);
         prefetch_tmap(&map_b);
-        if (kGU) { prefetch_tmap(&map_w1); prefetch_tmap(&map_s1); }
+        if (kGU) prefetch_tmap(&map_w1);
     }
     __syncthreads();
     if (!kGU && warp != 0) pdl_wait();
     pdl_trigger();
     const int k_stages = args.k_total / kKStage;
+    const uint32_t rb = static_cast<uint32_t>(args.k_total / 32);  // scale bytes per weight row
+    const uint32_t sc_item = 128 * rb;                              // scale bytes per item
     uint32_t* status = args.status;
     const uint32_t smem_base = smem_u32(smem);
 
@@ -231,39 +274,72 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (lane != 0) return;
         const uint64_t pol_w = policy_evict_first();
         const uint64_t pol_b = policy_evict_last();
-        // the down GEMM's token operand is the gate/up output
+        const size_t ih = static_cast<size_t>(args.hidden) * args.inter;
+        const size_t off_s1 = ih + ih / 2, off_s3 = off_s1 + ih / 32, off_s2 = off_s3 + ih / 32;
+        // Scale rows of one item are contiguous in the record: one bulk copy
+        // per projection into the item's slot, after the item's record for
+        // the consumers.
+        auto issue_scales = [&](const DecItem& d, int li) -> bool {
+            const int slot = li % kDecScSlots;
+            if (!mbar_wait(&sempty[slot], ((li / kDecScSlots) & 1) ^ 1, status, kStatusTimeoutTma))
+                return false;
+            item_rec[slot].m = d.m;
+            item_rec[slot].row_start = d.td.row_start;
+            item_rec[slot].n_rows = d.td.n_rows;
+            item_rec[slot].valid = d.valid ? 1 : 0;
+            mbar_arrive_expect_tx(&sfull[slot], sc_item);
+            uint8_t* dst = smem + L.sc_off + slot * L.sc_slot;
+            const uint8_t* rec = args.records + static_cast<size_t>(d.slot) * args.record_bytes;
+            if (kGU) {
+                const size_t r0 = static_cast<size_t>(d.m) * 64 * rb;
+                bulk_load(dst, rec + off_s1 + r0, 64 * rb, &sfull[slot]);
+                bulk_load(dst + 64 * rb, rec + off_s3 + r0, 64 * rb, &sfull[slot]);
+            } else {
+                bulk_load(dst, rec + off_s2 + static_cast<size_t>(d.m) * 128 * rb, 128 * rb, &sfull[slot]);
+            }
+            return true;
+        };
+        // The next item's scale rows are issued when an item starts, so they
+        // have a whole item's worth of stage traffic to land behind.  Item
+        // metadata is pipelined so that no dependent global load sits on the
+        // issue path: while item li is issued, the slot of item li+2 and the
+        // tile descriptor of item li+3 are in flight.
+        const int G = gridDim.x;
+        int item = blockIdx.x;
+        DecItem cur = finish_item(args, item, load_tile(args, item));
+        DecItem n1{};
+        if (item + G < n_items) n1 = finish_item(args, item + G, load_tile(args, item + G));
+        TileDesc td2{};
+        if (item + 2 * G < n_items) td2 = load_tile(args, item + 2 * G);
+        // scale rows are weights: the down GEMM fetches its first ones before
+        // waiting for the gate/up output
+        if (!issue_scales(cur, 0)) return;
         if (!kGU) pdl_wait();
         int st = 0;
         uint32_t ph = 0;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            const DecItem it = dec_item(args, item);
-            if (!it.valid) atomicOr(status, kStatusBadExpert);
+        for (int li = 0; item < n_items; item += G, ++li) {
+            if (item + G < n_items && !issue_scales(n1, li + 1)) return;
+            DecItem n2{};
+            if (item + 2 * G < n_items) n2 = finish_item(args, item + 2 * G, td2);
+            if (item + 3 * G < n_items) td2 = load_tile(args, item + 3 * G);
+            if (!cur.valid) atomicOr(status, kStatusBadExpert);
             for (int s = 0; s < k_stages; ++s) {
                 if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
                 mbar_arrive_expect_tx(&full[st], kDecStageBytes);
                 uint8_t* pk = smem + st * kDecStageBytes;
-                uint8_t* sc = pk + kDecPkBytes;
-                uint8_t* bt = sc + kDecScBytes;
-                const int xk = s * (kKStage / 2);
+                // weights: {128 B, rows, two 128-byte K chunks, slot} per
+                // projection; tokens: {64, 8 rows, eight 64-wide K chunks}
                 if (kGU) {
-                    const int row = it.m * 64;
-                    tma_load_3d(pk, &map_w0, &full[st], xk, row, it.slot, pol_w);
-                    tma_load_3d(pk + 8192, &map_w1, &full[st], xk, row, it.slot, pol_w);
-                    tma_load_3d(pk + 16384, &map_w0, &full[st], xk + 128, row, it.slot, pol_w);
-                    tma_load_3d(pk + 24576, &map_w1, &full[st], xk + 128, row, it.slot, pol_w);
-                    tma_load_3d(sc, &map_s0, &full[st], s * 16, row, it.slot, pol_w);
-                    tma_load_3d(sc + 1024, &map_s1, &full[st], s * 16, row, it.slot, pol_w);
+                    tma_load_4d(pk, &map_w0, &full[st], 0, cur.m * 64, 2 * s, cur.slot, pol_w);
+                    tma_load_4d(pk + 16384, &map_w1, &full[st], 0, cur.m * 64, 2 * s, cur.slot, pol_w);
                 } else {
-                    const int row = it.m * 128;
-                    tma_load_3d(pk, &map_w0, &full[st], xk, row, it.slot, pol_w);
-                    tma_load_3d(pk + 16384, &map_w0, &full[st], xk + 128, row, it.slot, pol_w);
-                    tma_load_3d(sc, &map_s0, &full[st], s * 16, row, it.slot, pol_w);
+                    tma_load_4d(pk, &map_w0, &full[st], 0, cur.m * 128, 2 * s, cur.slot, pol_w);
                 }
-                for (int j = 0; j < 8; ++j)
-                    tma_load_2d(bt + j * 1024, &map_b, &full[st], s * kKStage + j * 64,
-                                it.td.row_start, pol_b);
-                if (++st == kDecStages) { st = 0; ph ^= 1; }
+                tma_load_3d(pk + kDecPkBytes, &map_b, &full[st], 0, cur.td.row_start, 8 * s, pol_b);
+                if (++st == n_stages) { st = 0; ph ^= 1; }
             }
+            cur = n1;
+            n1 = n2;
         }
         return;
     }
@@ -274,29 +350,24 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // finite binary16, so scaling a block's FP32 partial sum equals
         // summing the reference's FP16-rounded weights.  Byte 103 rounds
         // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.  The
-        // checker reads each stage's 2 KB of scale bytes once and publishes
-        // whether all of them are in range; the consumers start the stage
-        // only after that.
-        int st = 0;
-        uint32_t ph = 0;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-            for (int s = 0; s < k_stages; ++s) {
-                const bool ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
-                if (!__all_sync(0xffffffffu, ok)) return;
-                const uint32_t sc = smem_base + st * kDecStageBytes + kDecPkBytes + lane * 64;
-                uint32_t acc = 0x80808080u;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint4 v = lds_v4(sc + i * 16);
-                    acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
-                           scale_bytes_exact(v.w);
-                }
-                const bool fast = __all_sync(0xffffffffu, acc == 0x80808080u);
-                if (lane == 0) {
-                    fast_flag[st] = fast ? 1 : 0;
-                    mbar_arrive(&ready[st]);
-                }
-                if (++st == kDecStages) { st = 0; ph ^= 1; }
+        // checker reads each item's scale rows once and publishes whether all
+        // of them are in range; the consumers start the item after that.
+        int li = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
+            const int slot = li % kDecScSlots;
+            const bool ok = mbar_wait(&sfull[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
+            if (!__all_sync(0xffffffffu, ok)) return;
+            const uint32_t sc = smem_base + L.sc_off + slot * L.sc_slot;
+            uint32_t acc = 0x80808080u;
+            for (uint32_t i = lane; i < sc_item / 16; i += 32) {
+                const uint4 v = lds_v4(sc + i * 16);
+                acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
+                       scale_bytes_exact(v.w);
+            }
+            const bool fast = __all_sync(0xffffffffu, acc == 0x80808080u);
+            if (lane == 0) {
+                fast_flag[slot] = fast ? 1 : 0;
+                mbar_arrive(&sready[slot]);
             }
         }
         return;
@@ -315,31 +386,43 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int g = lane >> 2;        // fragment row within 8 / MMA column
     const int q = lane & 3;
     const int row_lo = kGU ? (8 * cw + g) : (16 * cw + g);
-    constexpr uint32_t kHi = kGU ? 64 * 128 : 8 * 128;  // byte distance of the hi row
+    // Stage weights: gate/up as [W1: K half 0 | K half 1][W3: ...], 64 rows
+    // of 128 B each; down as [K half 0 | K half 1] of 128 rows.
+    constexpr uint32_t kHalf = kGU ? 8192 : 16384;     // bytes per K half of one projection
+    constexpr uint32_t kHiRows = kGU ? 64 : 8;         // rows between the lo and hi fragment rows
+    constexpr uint32_t kHi = kGU ? 16384 : 8 * 128;    // their byte distance in a stage
     const int brow = ((g & 1) << 2) | (g >> 1);
     // Stage-relative byte offsets.  Rows are 128 B and row & 7 == g, so chunk
     // j of a weight row sits at (j ^ g) * 16: with g * 16 folded into w_off
     // (whose bits 4-6 are otherwise zero) the address of chunk j is
     // (stage + w_off) ^ (j * 16), for the lo and hi rows alike.
-    const uint32_t w_off = kh * 16384 + row_lo * 128 + (g << 4) + q * 4;
-    const uint32_t s_off = kDecPkBytes + row_lo * 16 + kh * 8;
-    const uint32_t b_off0 = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
-    const uint32_t b_off1 = kDecPkBytes + kDecScBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
-    float* red = reinterpret_cast<float*>(smem + kDecStages * kDecStageBytes + kDecBarBytes);
+    const uint32_t w_off = kh * kHalf + row_lo * 128 + (g << 4) + q * 4;
+    const uint32_t b_off0 = kDecPkBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
+    const uint32_t b_off1 = kDecPkBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
+    // this thread's scale bytes of stage s: row_lo * rb + s * 16 + kh * 8 in the slot
+    const uint32_t s_off = L.sc_off + row_lo * rb + kh * 8;
+    const uint32_t s_hi = kHiRows * rb;
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
     int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
-    int st = 0, parity = 0;
+    int st = 0, parity = 0, li = 0;
     uint32_t ph = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const DecItem it = dec_item(args, item);
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
+        const int slot = li % kDecScSlots;
         float c[4] = {0.f, 0.f, 0.f, 0.f};
-        bool ok = true;
-        for (int s = 0; s < k_stages; ++s) {
-            ok = mbar_wait(&ready[st], ph, status, kStatusTimeoutDequant);
+        bool ok = mbar_wait(&sready[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
+        ok = __all_sync(0xffffffffu, ok);
+        const bool fast = ok && fast_flag[slot] != 0;
+        const int it_m = item_rec[slot].m;
+        const int it_row_start = item_rec[slot].row_start;
+        const int it_n_rows = item_rec[slot].n_rows;
+        const bool it_valid = item_rec[slot].valid != 0;
+        const uint32_t sc_base = smem_base + s_off + slot * L.sc_slot;
+        for (int s = 0; s < k_stages && ok; ++s) {
+            ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
             const uint32_t sb = smem_base + st * kDecStageBytes;
-            const bool fast = fast_flag[st] != 0;
-            const uint2 slo = lds_v2(sb + s_off);
-            const uint2 shi = lds_v2(sb + s_off + kHi / 8);
+            const uint2 slo = lds_v2(sc_base + s * 16);
+            const uint2 shi = lds_v2(sc_base + s * 16 + s_hi);
             const uint32_t wb = sb + w_off;
             const uint32_t bb0 = sb + b_off0, bb1 = sb + b_off1;
             if (fast) {
@@ -387,16 +470,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
-            if (++st == kDecStages) { st = 0; ph ^= 1; }
+            if (++st == n_stages) { st = 0; ph ^= 1; }
         }
-        // Pair reduction.  The slot is double buffered by item parity: the
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sempty[slot]);
+        // Pair reduction.  The buffer is double buffered by item parity: the
         // second warp can only write it again after passing the next item's
         // barrier, which the first warp reaches after reading this one.  The
         // flag carries a timeout of the second warp, so neither warp waits on
         // a partner that has left.
-        float* slot = red + ((parity * 8 + cw) * 32 + lane) * 4;
+        float* rslot = red + ((parity * 8 + cw) * 32 + lane) * 4;
         if (kh == 1) {
-            *reinterpret_cast<float4*>(slot) = make_float4(c[0], c[1], c[2], c[3]);
+            *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
             if (lane == 0) red_ok[parity * 8 + cw] = ok ? 1 : 0;
             named_bar_arrive(1 + cw, 64);
             parity ^= 1;
@@ -404,7 +489,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             continue;
         }
         named_bar_sync(1 + cw, 64);
-        const float4 o = *reinterpret_cast<const float4*>(slot);
+        const float4 o = *reinterpret_cast<const float4*>(rslot);
         const bool ok_pair = red_ok[parity * 8 + cw] != 0;
         parity ^= 1;
         if (!ok || !ok_pair) break;
@@ -412,11 +497,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         c[1] += o.y;
         c[2] += o.z;
         c[3] += o.w;
-        if (!it.valid) continue;
-        const int n_rows = it.td.n_rows;
+        if (!it_valid) continue;
+        const int n_rows = it_n_rows;
         const int n0 = q, n1 = 4 + q;  // tokens of MMA columns 2q and 2q+1
         if (kGU) {
-            const int feat = it.m * 64 + 8 * cw + g;
+            const int feat = it_m * 64 + 8 * cw + g;
             const float lim = args.swiglu_limit;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -429,16 +514,16 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     uv = fminf(fmaxf(uv, -lim), lim);
                 }
                 const __half sv = __float2half_rn(silu_ref(gv));
-                args.act[static_cast<size_t>(it.td.row_start + n) * args.inter + feat] =
+                args.act[static_cast<size_t>(it_row_start + n) * args.inter + feat] =
                     __float2half_rn(__fmul_rn(__half2float(sv), uv));
             }
         } else {
-            const int f_lo = it.m * 128 + 16 * cw + g;
+            const int f_lo = it_m * 128 + 16 * cw + g;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                const size_t pos = static_cast<size_t>(args.perm[it.td.row_start + n]);
+                const size_t pos = static_cast<size_t>(args.perm[it_row_start + n]);
                 args.raw[pos * args.hidden + f_lo] = c[h];
                 args.raw[pos * args.hidden + f_lo + 8] = c[2 + h];
             }
@@ -451,15 +536,62 @@ cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cud
     auto kern = moe_decode_kernel<MODE>;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDecSmem);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmemLimit));
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), kDecSmem, stream, maps.w0, maps.w1, maps.s0,
-                      maps.s1, maps.b, args);
+    const DecLayout L = dec_layout(args.k_total);
+    if (L.stages < 2 || L.bytes > kSmemLimit) return cudaErrorInvalidValue;
+    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps.w0, maps.w1, maps.b,
+                      args);
 }
 
 }  // namespace
+
+// The weight maps view a projection [rows, K/2 bytes] of every record as
+// {128 B, rows, K/256 chunks, slot} with the chunk stride (128 B) below the
+// row stride: one box {128, rows, 2, 1} is a whole 512-wide stage of 64 or
+// 128 rows, landing as [chunk][row][128 B] with the 128-byte swizzle.
+bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t record_bytes,
+                               int n_slots, int hidden, int inter, GemmMaps* gu, GemmMaps* dn) {
+    if (!fn) return false;
+    const uint8_t* rec = static_cast<const uint8_t*>(records);
+    const size_t ih = static_cast<size_t>(hidden) * inter;
+    const cuuint32_t elem[4] = {1, 1, 1, 1};
+    auto enc = [&](CUtensorMap* m, const uint8_t* base, int rows, int k, cuuint32_t box_rows) {
+        const cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(k / 256),
+                                    static_cast<cuuint64_t>(n_slots)};
+        const cuuint64_t strides[3] = {static_cast<cuuint64_t>(k / 2), 128,
+                                       static_cast<cuuint64_t>(record_bytes)};
+        const cuuint32_t box[4] = {128, box_rows, 2, 1};
+        return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<uint8_t*>(base), dims, strides, box,
+                  elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    *gu = GemmMaps{};
+    *dn = GemmMaps{};
+    if (!enc(&gu->w0, rec, inter, hidden, 64) || !enc(&gu->w1, rec + ih / 2, inter, hidden, 64) ||
+        !enc(&dn->w0, rec + ih, hidden, inter, 128))
+        return false;
+    dn->w1 = dn->w0;
+    return true;
+}
+
+// Token rows [rows, cols] FP16 viewed as {64, rows, cols/64 chunks} (chunk
+// stride 128 B): one box {64, 8, 8} is the 8 rows of a tile over a 512-wide
+// stage, landing as [chunk][row][128 B] with the 128-byte swizzle.
+bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
+                             CUtensorMap* map) {
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols / 64)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, 128};
+    const cuuint32_t box[3] = {64, 8, 8};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(rows_base), dims, strides, box,
+              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream) {

@@ -215,6 +215,11 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
         ok = ok && enc(&dn.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base + sp.act, d, st, box,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     }
+    if (decode) {
+        ok = ok && encode_decode_weight_maps(encode_fn(), rec, record_bytes, n_slots, H, I, &gu, &dn);
+        ok = ok && encode_decode_token_map(encode_fn(), base + sp.xperm, static_cast<int>(sel), H, &gu.b);
+        ok = ok && encode_decode_token_map(encode_fn(), base + sp.act, static_cast<int>(sel), I, &dn.b);
+    }
     if (!ok) return report(DEE_ERR_CUDA, "tensor map encoding failed");
 
     // Per-call state that must start from zero: the status word.

@@ -169,6 +169,18 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+// 4-D tiled load (x innermost).
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z, int32_t w,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w),
+        "l"(policy)
+        : "memory");
+}
+
 // Prefetch a 3-D tile into L2 (no shared memory, no barrier).
 __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t x, int32_t y,
                                                 int32_t z) {
@@ -176,6 +188,16 @@ __device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int32_t 
                      reinterpret_cast<uint64_t>(map)),
                  "r"(x), "r"(y), "r"(z)
                  : "memory");
+}
+
+// Contiguous global -> shared copy completing on an mbarrier (16-byte aligned
+// addresses, size a multiple of 16).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // Prefetch a contiguous global range into L2 (16-byte aligned address, size a
