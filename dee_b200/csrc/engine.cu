@@ -97,7 +97,9 @@ struct dee_engine {
     __half* d_xperm = nullptr;
     __half* d_act = nullptr;
     float* d_raw = nullptr;
-    int32_t* h_ids = nullptr;  // pinned staging of the consumed ids
+    int32_t* h_ids = nullptr;      // pinned staging of host-given ids
+    int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
+    cudaStream_t journal_stream = nullptr;
     size_t h_ids_count = 0;
     CUtensorMap map_xperm, map_act;      // 16-row token boxes (tcgen05 kernel)
     CUtensorMap map_xperm_dec, map_act_dec;  // token rows of the decode kernel
@@ -159,11 +161,13 @@ bool encode(dee_engine* e, CUtensorMap* map, CUtensorMapDataType dt, int rank, c
 void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
-    cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw);
+    cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
     e->d_xperm = nullptr; e->d_act = nullptr; e->d_raw = nullptr; e->h_ids = nullptr;
+    e->d_journal = nullptr;
+    e->h_ids_count = 0;
     e->cap_sel = 0;
 }
 
@@ -189,6 +193,7 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_xperm, cap * H)) != cudaSuccess ||
         (err = dev_alloc(&e->d_act, cap * I)) != cudaSuccess ||
         (err = dev_alloc(&e->d_raw, cap * H)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
                              cudaHostAllocDefault)) != cudaSuccess) {
         free_workspace(e);
@@ -256,7 +261,8 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     const bool large = !decode;
     const int n_max = decode ? kDecodeTileRows : gemm_n_max(large);
 
-    PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles};
+    PermuteOut po{e->d_counts, e->d_offsets, e->d_perm,     e->d_row_of,
+                  e->d_tiles,  e->d_n_tiles, e->d_journal};
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream);
@@ -538,13 +544,7 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
         stage_end(e, kStageCombine, stream);
         e->launches += 1;
     }
-    if (!h_ids) {
-        // the journal's copy of the ids; queued last so the kernels of the
-        // layer stay back to back on the stream
-        err = cudaMemcpyAsync(e->h_ids, d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost,
-                              stream);
-        if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
-    }
+    e->journal_stream = stream;
     return DEE_OK;
 }
 
@@ -590,8 +590,7 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     if (err != cudaSuccess) return cuda_fail(e, err, "FP16 combine launch");
     stage_end(e, kStageCombine, stream);
     e->launches += 2;
-    err = cudaMemcpyAsync(e->h_ids, e->d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
-    if (err != cudaSuccess) return cuda_fail(e, err, "journal ids D2H");
+    e->journal_stream = stream;
     return DEE_OK;
 }
 
@@ -618,11 +617,21 @@ int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
     return DEE_OK;
 }
 
+// The permutation kernel copies the ids it consumes into d_journal; reading
+// them waits for the stream of the latest forward.
 int dee_journal_ids_host(dee_engine* e, int32_t* h_out, int max_ids) {
     if (!e || !h_out || max_ids < 0) return DEE_ERR_INVALID;
     const size_t n = e->h_ids_count < static_cast<size_t>(max_ids) ? e->h_ids_count
                                                                    : static_cast<size_t>(max_ids);
-    if (n) std::memcpy(h_out, e->h_ids, n * sizeof(int32_t));
+    if (n == 0) return 0;
+    if (cudaSetDevice(e->cfg.device_id) != cudaSuccess) return DEE_ERR_CUDA;
+    cudaError_t err = cudaStreamSynchronize(e->journal_stream);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(h_out, e->d_journal, n * sizeof(int32_t), cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) {
+        cuda_fail(e, err, "journal ids readback");
+        return DEE_ERR_CUDA;
+    }
     return static_cast<int>(n);
 }
 

@@ -79,6 +79,7 @@ struct PermuteOut {
     int32_t* row_of;    // [T*K] position -> grouped row
     TileDesc* tiles;    // [max_tiles]
     int32_t* n_tiles;   // [1]
+    int32_t* journal;   // [T*K] copy of the consumed ids, or null
 };
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,

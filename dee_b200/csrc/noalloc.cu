@@ -234,7 +234,8 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
                   reinterpret_cast<int32_t*>(base + sp.perm),
                   reinterpret_cast<int32_t*>(base + sp.row_of),
                   reinterpret_cast<TileDesc*>(base + sp.tiles),
-                  reinterpret_cast<int32_t*>(base + sp.n_tiles)};
+                  reinterpret_cast<int32_t*>(base + sp.n_tiles),
+                  nullptr};
     err = launch_permute(d_ids, tokens, K, E, decode ? kDecodeTileRows : gemm_n_max(large),
                          sp.max_tiles, po, status, stream);
     if (err == cudaSuccess)

@@ -29,6 +29,14 @@ __device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
 // exp is evaluated in double and rounded once to FP32 (correctly rounded in
 // practice), which the reference's libm expf matches except for rare
 // last-bit cases.
+//
+// The expert-order double sum is reproduced exactly without running it
+// serially: every term is an FP32 value in [0, 1] and E < 2^b, so when each
+// term is 0 or at least 2^(b-30), every term and every partial sum is a
+// multiple of 2^(b-53) below 2^b, i.e. exactly representable in double, and
+// every addition is exact in any order.  A warp vote checks that; otherwise
+// lane 0 sums in expert order.
+template <int NPER>
 __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, int experts,
                                   int topk, int32_t* __restrict__ ids, float* __restrict__ weights,
                                   uint32_t* status) {
@@ -41,56 +49,70 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, 
     if (t >= tokens) return;
     float* sp = route_smem + warp * experts;
     const float* l = logits + static_cast<size_t>(t) * experts;
-    const int nper = (experts + 31) >> 5;
 
-    float v[kRouteMaxPerLane];
+    float v[NPER];
     float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+    for (int j = 0; j < NPER; ++j) {
         const int e = lane + 32 * j;
-        v[j] = (j < nper && e < experts) ? l[e] : -INFINITY;
-        if (j < nper && e < experts) m = (m < v[j]) ? v[j] : m;
+        v[j] = e < experts ? l[e] : -INFINITY;
+        if (e < experts) m = (m < v[j]) ? v[j] : m;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float other = __shfl_xor_sync(0xffffffffu, m, o);
         m = (m < other) ? other : m;
     }
+    int bits = 0;
+    while ((experts >> bits) != 0) ++bits;  // E < 2^bits
+    const float exact_min = __uint_as_float(static_cast<uint32_t>(127 + bits - 30) << 23);
+    bool exact = true;
+    double part = 0.0;
 #pragma unroll
-    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+    for (int j = 0; j < NPER; ++j) {
         const int e = lane + 32 * j;
-        if (j < nper && e < experts) {
+        if (e < experts) {
             const float d = __fsub_rn(v[j], m);
             v[j] = static_cast<float>(exp(static_cast<double>(d)));
-            sp[e] = v[j];
+            exact = exact && (v[j] == 0.0f || v[j] >= exact_min);
+            part += static_cast<double>(v[j]);
         }
     }
-    __syncwarp();
-    double den = 0.0;
-    if (lane == 0)
-        for (int e = 0; e < experts; ++e) den += static_cast<double>(sp[e]);
-    den = __shfl_sync(0xffffffffu, den, 0);
+    double den;
+    if (__all_sync(0xffffffffu, exact)) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        den = part;
+    } else {
+#pragma unroll
+        for (int j = 0; j < NPER; ++j) {
+            const int e = lane + 32 * j;
+            if (e < experts) sp[e] = v[j];
+        }
+        __syncwarp();
+        den = 0.0;
+        if (lane == 0)
+            for (int e = 0; e < experts; ++e) den += static_cast<double>(sp[e]);
+        den = __shfl_sync(0xffffffffu, den, 0);
+    }
     const bool bad = !(den > 0.0) || !isfinite(den);
     const float inv = static_cast<float>(1.0 / den);
-    Cand mine[kRouteMaxPerLane];
+    Cand mine[NPER];
 #pragma unroll
-    for (int j = 0; j < kRouteMaxPerLane; ++j) {
+    for (int j = 0; j < NPER; ++j) {
         const int e = lane + 32 * j;
-        mine[j].p = (j < nper && e < experts) ? __fmul_rn(v[j], inv) : -INFINITY;
-        mine[j].id = (j < nper && e < experts) ? e : 0x7fffffff;
+        mine[j].p = e < experts ? __fmul_rn(v[j], inv) : -INFINITY;
+        mine[j].id = e < experts ? e : 0x7fffffff;
     }
-    float sel_p[32];
-    int sel_id[32];
+    // K rounds of warp argmax; lane k keeps the k-th winner
+    float my_p = 0.0f;
+    int my_id = 0;
     for (int k = 0; k < topk; ++k) {
-        Cand best{-INFINITY, 0x7fffffff};
-        int best_j = -1;
+        // within a lane ids increase with j, so a strict '>' keeps the lowest id on ties
+        Cand best = mine[0];
 #pragma unroll
-        for (int j = 0; j < kRouteMaxPerLane; ++j) {
-            if (mine[j].id != 0x7fffffff && (best_j < 0 || better(mine[j], best))) {
-                best = mine[j];
-                best_j = j;
-            }
-        }
+        for (int j = 1; j < NPER; ++j)
+            if (mine[j].id != 0x7fffffff && (best.id == 0x7fffffff || mine[j].p > best.p)) best = mine[j];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             Cand other;
@@ -98,33 +120,25 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, 
             other.id = __shfl_xor_sync(0xffffffffu, best.id, o);
             if (other.id != 0x7fffffff && (best.id == 0x7fffffff || better(other, best))) best = other;
         }
-        sel_p[k] = best.p;
-        sel_id[k] = best.id;
+        if (lane == k) { my_p = best.p; my_id = best.id; }
         // the owning lane retires the winner
 #pragma unroll
-        for (int j = 0; j < kRouteMaxPerLane; ++j)
+        for (int j = 0; j < NPER; ++j)
             if (mine[j].id == best.id) mine[j].id = 0x7fffffff;
     }
-    if (lane == 0) {
-        float sum = 0.0f;
-        for (int k = 0; k < topk; ++k) sum = __fadd_rn(sum, sel_p[k]);
-        const bool bad_sum = !(sum > 0.0f);
-        if (bad || bad_sum) atomicOr(status, kStatusBadRouter);
-        for (int k = 0; k < topk; ++k) {
-            const bool ok = !(bad || bad_sum) && sel_id[k] >= 0 && sel_id[k] < experts;
-            ids[static_cast<size_t>(t) * topk + k] = ok ? sel_id[k] : 0;
-            weights[static_cast<size_t>(t) * topk + k] = ok ? __fdiv_rn(sel_p[k], sum) : 0.0f;
-        }
+    // sum of the selected probabilities in rank order (lane 0), then each
+    // rank's weight on its own lane
+    float sum = 0.0f;
+    for (int k = 0; k < topk; ++k) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, my_p, k));
+    const bool bad_sum = !(sum > 0.0f);
+    if (lane == 0 && (bad || bad_sum)) atomicOr(status, kStatusBadRouter);
+    if (lane < topk) {
+        const bool ok = !(bad || bad_sum) && my_id >= 0 && my_id < experts;
+        ids[static_cast<size_t>(t) * topk + lane] = ok ? my_id : 0;
+        weights[static_cast<size_t>(t) * topk + lane] = ok ? __fdiv_rn(my_p, sum) : 0.0f;
     }
 }
 
-// DeepSeek-V4 router (Gate.forward as restated by the reference,
-// dee.cpp/scripts/deepseek_v4_layer_common.py:349-403 and
-// deepseek_v4_expert_reference.py:132-163): score = sqrt(softplus(logit))
-// (softplus threshold 20), the bias shifts only the selection, top-k by the
-// biased score (ties -> lower expert id), weights = unbiased scores of the
-// selected experts / their sum, times route_scale.  Hash layers select
-// tid2eid[input_id] instead of top-k.  One warp per token.
 __global__ void route_dsv4_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
                                   const int64_t* __restrict__ tid2eid,
                                   const int64_t* __restrict__ input_ids, int tokens, int experts,
@@ -234,6 +248,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     __syncthreads();
     for (int p = tid; p < sel; p += kPermThreads) {
         const int e = ids[p];
+        if (out.journal) out.journal[p] = e;
         if (e < 0 || e >= experts) {
             atomicOr(status, kStatusBadExpert);
             out.row_of[p] = -1;
@@ -442,8 +457,11 @@ cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int 
     const int warps = 4;
     const int grid = (tokens + warps - 1) / warps;
     const size_t smem = static_cast<size_t>(warps) * experts * sizeof(float);
-    return launch_pdl(route_topk_kernel, dim3(grid), dim3(warps * 32), smem, stream, logits, tokens,
-                      experts, topk, ids, weights, status);
+    if (experts <= 256)
+        return launch_pdl(route_topk_kernel<8>, dim3(grid), dim3(warps * 32), smem, stream, logits,
+                          tokens, experts, topk, ids, weights, status);
+    return launch_pdl(route_topk_kernel<kRouteMaxPerLane>, dim3(grid), dim3(warps * 32), smem, stream,
+                      logits, tokens, experts, topk, ids, weights, status);
 }
 
 cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int64_t* tid2eid,

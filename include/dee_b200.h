@@ -135,8 +135,8 @@ DEE_API int dee_engine_sync_status(dee_engine* engine, void* stream, uint32_t* s
 
 /* Host copy of the int32 [T, K] route ids the last forward consumed -- the
  * buffer the route journal records (deepseek_v4_native_generate.py
- * :2196-2216).  Valid after the forward's stream has been synchronised.
- * Returns the number of ids written. */
+ * :2196-2216).  Waits for the last forward's stream, then copies.  Returns
+ * the number of ids written, or a negative DEE_ERR_* code. */
 DEE_API int dee_journal_ids_host(dee_engine* engine, int32_t* h_out, int max_ids);
 
 /* fp4_e2m1_to_f16_cuda (dee.cpp/include/dee/cuda_convert.h:104-134,

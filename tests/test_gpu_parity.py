@@ -79,13 +79,17 @@ def test_fp4_quantize_matches_oracle(torch_cuda, lib, oracle_mod):
     assert np.array_equal(s.cpu().numpy(), ws)
 
 
-@pytest.mark.parametrize("T,E,K", [(2, 3, 2), (1000, 256, 6), (37, 16, 6)])
-def test_route_topk_matches_oracle(torch_cuda, oracle_mod, T, E, K):
+# spread 3: some exp terms fall below the exact-tree bound, so the denominator
+# is summed serially; spread 0.5: every term is above it and the warp sums a
+# tree, which must give the identical double
+@pytest.mark.parametrize("T,E,K,spread", [(2, 3, 2, 0), (1000, 256, 6, 3.0), (37, 16, 6, 3.0),
+                                          (500, 256, 6, 0.5), (64, 200, 8, 0.5)])
+def test_route_topk_matches_oracle(torch_cuda, oracle_mod, T, E, K, spread):
     torch = torch_cuda
     if (T, E, K) == (2, 3, 2):
         logits = np.array([[1, 2, 3], [-1, 4, 2]], np.float32)  # test_real_router.cpp:91-116
     else:
-        logits = (np.random.default_rng(T).standard_normal((T, E)) * 3).astype(np.float32)
+        logits = (np.random.default_rng(T).standard_normal((T, E)) * spread).astype(np.float32)
         logits[0, :8] = 1.25  # exact ties
     eng = _engine(512, 512, E, K)
     dl = torch.from_numpy(logits).cuda()
