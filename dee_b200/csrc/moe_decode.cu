@@ -222,10 +222,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
                       const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
     constexpr bool kGU = MODE == GemmMode::kGateUp;
-    if (kGU) pdl_wait();
+    // The tile list comes from the permutation kernel, which has completed
+    // whenever this kernel runs: its predecessor (gather or gate/up) only
+    // signals its dependents after its own griddepcontrol.wait.  Everything
+    // that reads weights or the tile list may therefore start before this
+    // kernel's wait; only the token rows (the predecessor's output) wait.
     const int n_items = *args.n_tiles * args.m_tiles;
     if (static_cast<int>(blockIdx.x) >= n_items) {
-        if (!kGU) pdl_wait();
+        pdl_wait();
         pdl_trigger();
         return;
     }
@@ -261,7 +265,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (kGU) prefetch_tmap(&map_w1);
     }
     __syncthreads();
-    if (!kGU && warp != 0) pdl_wait();
+    if (warp != 0) pdl_wait();
     pdl_trigger();
     const int k_stages = args.k_total / kKStage;
     const uint32_t rb = static_cast<uint32_t>(args.k_total / 32);  // scale bytes per weight row
@@ -299,6 +303,21 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
             return true;
         };
+        // weights: {128 B, rows, two 128-byte K chunks, slot} per projection;
+        // tokens: {64, 8 rows, eight 64-wide K chunks}
+        auto issue_weights = [&](const DecItem& d, int s, int st) {
+            uint8_t* pk = smem + st * kDecStageBytes;
+            if (kGU) {
+                tma_load_4d(pk, &map_w0, &full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
+                tma_load_4d(pk + 16384, &map_w1, &full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
+            } else {
+                tma_load_4d(pk, &map_w0, &full[st], 0, d.m * 128, 2 * s, d.slot, pol_w);
+            }
+        };
+        auto issue_tokens = [&](const DecItem& d, int s, int st) {
+            tma_load_3d(smem + st * kDecStageBytes + kDecPkBytes, &map_b, &full[st], 0, d.td.row_start,
+                        8 * s, pol_b);
+        };
         // The next item's scale rows are issued when an item starts, so they
         // have a whole item's worth of stage traffic to land behind.  Item
         // metadata is pipelined so that no dependent global load sits on the
@@ -311,31 +330,31 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (item + G < n_items) n1 = finish_item(args, item + G, load_tile(args, item + G));
         TileDesc td2{};
         if (item + 2 * G < n_items) td2 = load_tile(args, item + 2 * G);
-        // scale rows are weights: the down GEMM fetches its first ones before
-        // waiting for the gate/up output
+        // Before the wait: the first two items' scale rows and the weights of
+        // the first ring's worth of stages.
         if (!issue_scales(cur, 0)) return;
-        if (!kGU) pdl_wait();
+        if (item + G < n_items && !issue_scales(n1, 1)) return;
+        const int pre = n_stages < k_stages ? n_stages : k_stages;
+        for (int s = 0; s < pre; ++s) {  // first use of ring slots 0..pre-1
+            mbar_arrive_expect_tx(&full[s], kDecStageBytes);
+            issue_weights(cur, s, s);
+        }
+        pdl_wait();
         int st = 0;
         uint32_t ph = 0;
         for (int li = 0; item < n_items; item += G, ++li) {
-            if (item + G < n_items && !issue_scales(n1, li + 1)) return;
+            if (li > 0 && item + G < n_items && !issue_scales(n1, li + 1)) return;
             DecItem n2{};
             if (item + 2 * G < n_items) n2 = finish_item(args, item + 2 * G, td2);
             if (item + 3 * G < n_items) td2 = load_tile(args, item + 3 * G);
             if (!cur.valid) atomicOr(status, kStatusBadExpert);
             for (int s = 0; s < k_stages; ++s) {
-                if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
-                mbar_arrive_expect_tx(&full[st], kDecStageBytes);
-                uint8_t* pk = smem + st * kDecStageBytes;
-                // weights: {128 B, rows, two 128-byte K chunks, slot} per
-                // projection; tokens: {64, 8 rows, eight 64-wide K chunks}
-                if (kGU) {
-                    tma_load_4d(pk, &map_w0, &full[st], 0, cur.m * 64, 2 * s, cur.slot, pol_w);
-                    tma_load_4d(pk + 16384, &map_w1, &full[st], 0, cur.m * 64, 2 * s, cur.slot, pol_w);
-                } else {
-                    tma_load_4d(pk, &map_w0, &full[st], 0, cur.m * 128, 2 * s, cur.slot, pol_w);
+                if (li > 0 || s >= pre) {
+                    if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
+                    mbar_arrive_expect_tx(&full[st], kDecStageBytes);
+                    issue_weights(cur, s, st);
                 }
-                tma_load_3d(pk + kDecPkBytes, &map_b, &full[st], 0, cur.td.row_start, 8 * s, pol_b);
+                issue_tokens(cur, s, st);
                 if (++st == n_stages) { st = 0; ph ^= 1; }
             }
             cur = n1;
@@ -359,6 +378,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (!__all_sync(0xffffffffu, ok)) return;
             const uint32_t sc = smem_base + L.sc_off + slot * L.sc_slot;
             uint32_t acc = 0x80808080u;
+#pragma unroll 4
             for (uint32_t i = lane; i < sc_item / 16; i += 32) {
                 const uint4 v = lds_v4(sc + i * 16);
                 acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
