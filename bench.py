@@ -13,9 +13,13 @@ its CUDA events.  The b=1 and b=64 decode points and the 4096-token prefill
 (configs[2], Zipf(1.1) expert bias) are measured in the same run and
 reported under "sweep".
 
-Multi-GPU (torchrun, one rank per GPU): each rank runs its own decode layer
-on its own token batches over the full expert bank (replicas, weak scaling);
-value = all ranks' tokens / max-over-ranks time.
+Multi-GPU (torchrun, one rank per GPU): expert parallel.  Rank r holds
+experts [r*E/N, (r+1)*E/N) and its own b tokens per step; it routes them,
+packs the selections by owner rank, exchanges rows with NCCL all-to-all,
+runs the grouped GEMMs over the rows it received, returns the FP32 rows and
+combines (dee_b200.ep).  Weak scaling: value = all ranks' tokens / the
+max-over-ranks time; the per-GPU weight traffic shrinks as the union of
+the N*b tokens' experts is spread over N GPUs.
 
 --impl reference times the reference's own CPU routed-expert executor
 (oracle/_ref, compiled from the reference sources) on the same workload.
@@ -179,6 +183,28 @@ class Layer:
                                     stream=stream)
 
 
+class EpLayer:
+    """One rank's expert-parallel step: route this rank's tokens (a router
+    engine over all E experts), then dee_b200.ep.ExpertParallelMoE over the
+    rank's share of the experts (pack, NCCL all-to-all, grouped GEMMs,
+    all-to-all back, combine)."""
+
+    def __init__(self, torch, router, ep, b):
+        self.torch = torch
+        self.router = router
+        self.ep = ep
+        self.b = b
+        self.ids = torch.empty((b, K), dtype=torch.int32, device="cuda")
+        self.w = torch.empty((b, K), dtype=torch.float32, device="cuda")
+        self.out = ep.out
+
+    def __call__(self, x, logits, stream):
+        self.router.route_topk_device(logits.data_ptr(), self.b, self.ids.data_ptr(), self.w.data_ptr(),
+                                      stream)
+        with self.torch.cuda.stream(stream):
+            self.ep.forward(x, self.ids, self.w)
+
+
 def time_steps(torch, fn, n_steps, flush, stream, warmup):
     """Per-step CUDA-event times (ms) with an L2 flush before each step."""
     torch.cuda.synchronize()  # inputs were produced on the default stream
@@ -202,23 +228,26 @@ def time_steps(torch, fn, n_steps, flush, stream, warmup):
 
 
 def unique_experts(torch, ids_list):
-    return [int(torch.unique(ids).numel()) for ids in ids_list]
+    """Distinct experts per step (ids < 0 mark unused expert-parallel rows)."""
+    return [int(torch.unique(ids[ids >= 0]).numel()) for ids in ids_list]
 
 
-def decode_point(torch, eng, b, n_steps, warmup, flush, stream, seed, profile=True):
+def decode_point(torch, eng, b, n_steps, warmup, flush, stream, seed, profile=True, make_layer=None):
     xs, logits = make_inputs(torch, max(n_steps, warmup, 1), b, seed)
-    layer = Layer(torch, eng, b)
+    layer = make_layer(b) if make_layer else Layer(torch, eng, b)
     ids_seen = []
 
     def fn(i, s):
         layer(xs[i % len(xs)], logits[i % len(xs)], s)
 
     times = time_steps(torch, fn, n_steps, flush, stream, warmup)
-    # unique experts per step (same routing as the timed steps)
+    # experts this GPU's grouped GEMMs stream per step (same routing as the
+    # timed steps): the step's own ids on one GPU, the received rows' local
+    # experts under expert parallelism
     for i in range(n_steps):
         layer(xs[i % len(xs)], logits[i % len(xs)], stream)
         with torch.cuda.stream(stream):
-            ids_seen.append(layer.ids.clone())
+            ids_seen.append(layer.ep.recv_expert.clone() if hasattr(layer, "ep") else layer.ids.clone())
     torch.cuda.synchronize()
     uniq = unique_experts(torch, ids_seen)
     stages = None
@@ -243,7 +272,7 @@ def layer_bytes(b, u):
     return u * RECORD_BYTES + b * H * 2 + b * H * 4 + b * E * 4 + b * K * 8
 
 
-def e2e_point(torch, eng, b, n_steps, warmup, flush, stream, seed):
+def e2e_point(torch, eng, b, n_steps, warmup, flush, stream, seed, make_layer=None):
     """Same metric through the public C-ABI calls with host buffers: H2D of
     the step's hidden states and logits from pinned memory, the layer, D2H
     of the FP32 output into pinned memory, all inside the timed region."""
@@ -253,7 +282,7 @@ def e2e_point(torch, eng, b, n_steps, warmup, flush, stream, seed):
     dx = torch.empty((b, H), dtype=torch.float16, device="cuda")
     dl = torch.empty((b, E), dtype=torch.float32, device="cuda")
     hout = torch.empty((b, H), dtype=torch.float32).pin_memory()
-    layer = Layer(torch, eng, b)
+    layer = make_layer(b) if make_layer else Layer(torch, eng, b)
 
     def fn(i, s):
         j = i % len(hx)
@@ -390,8 +419,29 @@ def main():
     b = args.batch
     global E
     E = args.experts
-    bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
-    eng = build_engine(torch, bank, max_tokens=max(b, 64))
+    make_layer = None
+    if world == 1:
+        bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
+        eng = build_engine(torch, bank, max_tokens=max(b, 64))
+    else:
+        # expert parallel: this rank's contiguous share of the experts
+        import dee_b200
+        from dee_b200.ep import ExpertParallelMoE
+        if E % world:
+            raise SystemExit(f"--experts {E} is not divisible by {world} ranks")
+        epr = E // world
+        bank = synthetic_bank(RecordLayout(H, I), epr, seed=11 + rank)
+        eng = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=epr, topk=K,
+                                                        max_tokens=64, device_id=local))
+        eng.attach_bank(0, bank)
+        router = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
+                                                           max_tokens=64, device_id=local))
+        ep_cache = {}
+
+        def make_layer(bb):
+            if bb not in ep_cache:
+                ep_cache[bb] = ExpertParallelMoE(torch, rank, world, epr, bb, K, H, "cuda", engine=eng)
+            return EpLayer(torch, router, ep_cache[bb], bb)
     stream = torch.cuda.Stream()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     launches0 = eng.launch_count()
@@ -405,7 +455,7 @@ def main():
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         times, uniq, stages = decode_point(torch, eng, b, args.steps, args.warmup, flush, stream,
-                                           seed=1000 + rank, profile=False)
+                                           seed=1000 + rank, profile=False, make_layer=make_layer)
     torch.cuda.synchronize()
     barrier()
     # route + permute + gather + gate/up + down + combine, counted by the engine
@@ -419,7 +469,7 @@ def main():
 
     # ---- roofline pass (stage events on the launch stream) ----
     _, uniq_p, stages = decode_point(torch, eng, b, min(args.steps, 20), 1, flush, stream,
-                                     seed=1000 + rank, profile=True)
+                                     seed=1000 + rank, profile=True, make_layer=make_layer)
     u_mean = statistics.mean(uniq_p)
     gu_bytes = u_mean * GATE_UP_BYTES_PER_EXPERT + b * K * H * 2 + b * K * I * 2
     gu_ms = stages.get("gate_up", float("nan"))
@@ -434,7 +484,7 @@ def main():
         "data": "synthetic",
         "config": {"workload": f"cfg1-decode-b{b}", "hidden": H, "inter": I, "experts": E, "topk": K,
                    "tokens_per_step": b, "experts_resident": E, "weights": "fp4-e2m1+ue8m0/32",
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "unique_experts_per_step": statistics.mean(uniq)},
         "hbm_gbs_layer": layer_gbs,
@@ -450,7 +500,8 @@ def main():
     result["clocks"] = clk.summary()
 
     # ---- e2e through the C ABI with host buffers ----
-    e_times, h2d, d2h = e2e_point(torch, eng, b, args.steps, args.warmup, flush, stream, seed=2000 + rank)
+    e_times, h2d, d2h = e2e_point(torch, eng, b, args.steps, args.warmup, flush, stream, seed=2000 + rank,
+                                  make_layer=make_layer)
     e_ms = sum(e_times)
     if world > 1:
         t = torch.tensor([e_ms], device="cuda", dtype=torch.float64)
@@ -460,7 +511,7 @@ def main():
                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
 
     # ---- sweep: b = 1, 64 and the 4096-token prefill ----
-    if not args.no_sweep:
+    if not args.no_sweep and world == 1:
         sweep = {}
         for bb in (1, 64):
             if bb == b:

@@ -191,6 +191,32 @@ class Engine:
             ctypes.c_void_p(d_raw_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_moe_forward_device")
 
+    # -- expert parallelism (see dee_b200.ep for the whole layer) -----------
+    def ep_pack_device(self, d_ids_ptr: int, tokens: int, d_x_ptr: int, ranks: int,
+                       experts_per_rank: int, capacity: int, d_send_rows_ptr: int,
+                       d_send_expert_ptr: int, d_slot_of_pos_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_ep_pack_device(
+            self._h, ctypes.c_void_p(d_ids_ptr), tokens, ctypes.c_void_p(d_x_ptr), ranks,
+            experts_per_rank, capacity, ctypes.c_void_p(d_send_rows_ptr),
+            ctypes.c_void_p(d_send_expert_ptr), ctypes.c_void_p(d_slot_of_pos_ptr),
+            ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_pack_device")
+
+    def moe_forward_rows_device(self, layer: int, d_rows_ptr: int, d_expert_ptr: int, rows: int,
+                                d_raw_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_moe_forward_rows_device(
+            self._h, layer, ctypes.c_void_p(d_rows_ptr), ctypes.c_void_p(d_expert_ptr), rows,
+            ctypes.c_void_p(d_raw_ptr), ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_moe_forward_rows_device")
+
+    def ep_combine_device(self, d_back_ptr: int, d_slot_of_pos_ptr: int, d_weights_ptr: int,
+                          tokens: int, d_out_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_ep_combine_device(
+            self._h, ctypes.c_void_p(d_back_ptr), ctypes.c_void_p(d_slot_of_pos_ptr),
+            ctypes.c_void_p(d_weights_ptr), tokens, ctypes.c_void_p(d_out_ptr),
+            ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_combine_device")
+
     def sync_status(self, stream=None) -> int:
         st = ctypes.c_uint32(0)
         rc = self._lib.dee_engine_sync_status(self._h, ctypes.c_void_p(_stream_handle(stream)),

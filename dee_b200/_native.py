@@ -53,6 +53,9 @@ SIGNATURES = {
     "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),
     "dee_moe_forward_combined_device": (I, [P, I, P, I, P, I, P, P, P, P]),
     "dee_moe_forward_device": (I, [P, I, P, I, P, P, I, P, P, P, P]),
+    "dee_ep_pack_device": (I, [P, P, I, P, I, I, I, P, P, P, P]),
+    "dee_moe_forward_rows_device": (I, [P, I, P, P, I, P, P]),
+    "dee_ep_combine_device": (I, [P, P, P, P, I, P, P]),
     "dee_engine_sync_status": (I, [P, P, U32P]),
     "dee_journal_ids_host": (I, [P, P, I]),
     "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),

@@ -248,24 +248,26 @@ bool host_ids_valid(dee_engine* e, const int32_t* ids, size_t n) {
 
 // The launch sequence shared by every forward entry point.  d_ids32 holds
 // validated-or-device-checked int32 ids [T, K]; raw receives [T*K, H] FP32.
+// The expert-parallel rows entry point runs it with K = 1, one row per
+// selection, and ids of -1 for unused rows (skip_negative).
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
-                float* raw, cudaStream_t stream) {
+                float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
-    const int K = e->cfg.topk, H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
+    const int H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
     const size_t sel = static_cast<size_t>(tokens) * K;
     // Decode-sized calls use the register-dequant kernel (tiles of <= 8 token
     // rows); larger calls the tcgen05 kernel (tiles of <= 128 rows).
-    const bool decode = tokens <= kDecodeMaxTokens;
+    const bool decode = sel <= static_cast<size_t>(kDecodeMaxSelections);
     const bool large = !decode;
     const int n_max = decode ? kDecodeTileRows : gemm_n_max(large);
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm,     e->d_row_of,
-                  e->d_tiles,  e->d_n_tiles, e->d_journal};
+                  e->d_tiles,  e->d_n_tiles, write_journal ? e->d_journal : nullptr};
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
-                                     stream);
+                                     stream, skip_negative);
     if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
     stage_end(e, kStagePermute, stream);
     stage_begin(e, kStageGather, stream);
@@ -535,7 +537,7 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     e->h_ids_count = sel;
     float* raw = d_raw ? d_raw : e->d_raw;
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, ids32, raw,
-                          stream)) != DEE_OK)
+                          stream, topk, false, true)) != DEE_OK)
         return rc;
     if (d_out_f32) {
         stage_begin(e, kStageCombine, stream);
@@ -582,7 +584,7 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     e->h_ids_count = sel;
     float* raw = d_raw_trace_out ? static_cast<float*>(d_raw_trace_out) : e->d_raw;
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_h_in), tokens, e->d_ids, raw,
-                          stream)) != DEE_OK)
+                          stream, topk, false, true)) != DEE_OK)
         return rc;
     stage_begin(e, kStageCombine, stream);
     err = launch_combine_f16(raw, d_weights_f32, d_expert_ids, tokens, topk, e->cfg.hidden,
@@ -591,6 +593,61 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     stage_end(e, kStageCombine, stream);
     e->launches += 2;
     e->journal_stream = stream;
+    return DEE_OK;
+}
+
+int dee_ep_pack_device(dee_engine* e, const int32_t* d_ids, int tokens, const void* d_x_f16,
+                       int ranks, int experts_per_rank, int capacity, void* d_send_rows,
+                       int32_t* d_send_expert, int32_t* d_slot_of_pos, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_ids || !d_x_f16 || !d_send_rows || !d_send_expert || !d_slot_of_pos || tokens <= 0 ||
+        ranks <= 0 || ranks > kEpMaxRanks || capacity <= 0 || experts_per_rank != e->cfg.num_experts)
+        return fail(e, DEE_ERR_INVALID,
+                    "invalid ep_pack arguments (ranks 1..32, capacity > 0, experts_per_rank must "
+                    "equal the engine's num_experts)");
+    const size_t sel = static_cast<size_t>(tokens) * e->cfg.topk;
+    // room for the rows this engine receives next (ranks x capacity), so the
+    // rows forward does not regrow the workspace and drop the journal
+    const size_t recv = static_cast<size_t>(ranks) * capacity;
+    if ((rc = ensure_capacity(e, sel > recv ? sel : recv, stream)) != DEE_OK) return rc;
+    cudaError_t err = launch_ep_pack(d_ids, static_cast<const __half*>(d_x_f16), tokens, e->cfg.topk,
+                                     e->cfg.hidden, ranks, experts_per_rank, capacity,
+                                     static_cast<__half*>(d_send_rows), d_send_expert, d_slot_of_pos,
+                                     e->d_journal, e->d_status, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep pack launch");
+    e->launches += 2;
+    e->h_ids_count = sel;
+    e->journal_stream = stream;
+    return DEE_OK;
+}
+
+int dee_moe_forward_rows_device(dee_engine* e, int layer, const void* d_rows_f16,
+                                const int32_t* d_expert, int rows, float* d_raw, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_rows_f16 || !d_expert || !d_raw || rows <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_rows_device arguments");
+    if ((rc = ensure_capacity(e, static_cast<size_t>(rows), stream)) != DEE_OK) return rc;
+    return run_experts(e, layer, static_cast<const __half*>(d_rows_f16), rows, d_expert, d_raw, stream,
+                       1, true, false);
+}
+
+int dee_ep_combine_device(dee_engine* e, const float* d_back, const int32_t* d_slot_of_pos,
+                          const float* d_weights, int tokens, float* d_out, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    if (!d_back || !d_slot_of_pos || !d_weights || !d_out || tokens <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid ep_combine arguments");
+    cudaError_t err = launch_ep_combine(d_back, d_slot_of_pos, d_weights, tokens, e->cfg.topk,
+                                        e->cfg.hidden, d_out, static_cast<cudaStream_t>(stream_v));
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
+    e->launches += 1;
     return DEE_OK;
 }
 

@@ -43,6 +43,7 @@ cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, cons
 // are copied per item straight from the records).
 constexpr int kDecodeTileRows = 8;
 constexpr int kDecodeMaxTokens = 64;
+constexpr int kDecodeMaxSelections = 384;  // selections (rows) the decode kernel takes
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream);
 
@@ -58,6 +59,18 @@ bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t rec
 // Token-row map of the decode kernel over a [rows, cols] FP16 buffer.
 bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
                              CUtensorMap* map);
+
+// Expert-parallel packing (ep.cu): selections [T, K] of global ids over
+// ranks x experts_per_rank experts -> per destination rank `capacity` slots of
+// FP16 rows and local expert ids (-1 unused), and slot_of_pos [T*K].
+constexpr int kEpMaxRanks = 32;
+cudaError_t launch_ep_pack(const int32_t* ids, const __half* x, int tokens, int topk, int hidden,
+                           int ranks, int epr, int capacity, __half* send_rows, int32_t* send_expert,
+                           int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
+                           cudaStream_t stream);
+// Rank-order FP32 combine of rows returned by the expert owners.
+cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,
+                              int tokens, int topk, int hidden, float* out, cudaStream_t stream);
 
 // Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
@@ -81,9 +94,11 @@ struct PermuteOut {
     int32_t* n_tiles;   // [1]
     int32_t* journal;   // [T*K] copy of the consumed ids, or null
 };
+// skip_negative: ids of -1 mark unused rows (expert-parallel receive
+// buffers) and are left out without raising kStatusBadExpert.
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
-                           cudaStream_t stream);
+                           cudaStream_t stream, bool skip_negative = false);
 
 // X_perm[row] = X[perm[row] / topk] (FP16 rows of H elements).
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,

@@ -165,7 +165,7 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     auto* status = reinterpret_cast<uint32_t*>(base + sp.status);
     auto* slots = reinterpret_cast<int32_t*>(base + sp.slots);
 
-    const bool decode = tokens <= kDecodeMaxTokens;
+    const bool decode = static_cast<size_t>(tokens) * K <= static_cast<size_t>(kDecodeMaxSelections);
     // Tensor maps over the caller's records and the scratch rows (host work).
     const uint8_t* rec = static_cast<const uint8_t*>(d_records);
     const cuuint64_t ns = static_cast<cuuint64_t>(n_slots), rb = record_bytes;

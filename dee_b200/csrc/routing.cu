@@ -230,7 +230,8 @@ constexpr int kPermMaxExperts = 256;
 
 __global__ void __launch_bounds__(kPermThreads, 1)
     permute_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts,
-                   int n_tile_max, int max_tiles, PermuteOut out, uint32_t* status) {
+                   int n_tile_max, int max_tiles, PermuteOut out, uint32_t* status,
+                   bool skip_negative) {
     __shared__ int cnt[kPermMaxExperts];
     __shared__ int off[kPermMaxExperts + 1];
     __shared__ int cursor[kPermMaxExperts];
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kPermThreads, 1)
         const int e = ids[p];
         if (out.journal) out.journal[p] = e;
         if (e < 0 || e >= experts) {
-            atomicOr(status, kStatusBadExpert);
+            if (!(skip_negative && e == -1)) atomicOr(status, kStatusBadExpert);
             out.row_of[p] = -1;
         } else {
             atomicAdd(&cnt[e], 1);
@@ -480,11 +481,11 @@ cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int6
 
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, bool skip_negative) {
     if (experts <= 0 || experts > kPermMaxExperts || tokens <= 0 || topk <= 0 || n_tile_max < 8)
         return cudaErrorInvalidValue;
     return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), 0, stream, ids, tokens, topk,
-                      experts, n_tile_max, max_tiles, out, status);
+                      experts, n_tile_max, max_tiles, out, status, skip_negative);
 }
 
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,

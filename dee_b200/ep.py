@@ -1,0 +1,115 @@
+"""Expert-parallel routed-expert layer: one rank's share, over torch.distributed.
+
+Rank r of `world` owns experts [r*epr, (r+1)*epr) (epr = experts per rank),
+the official DeepSeek-V4 split (benchmark_reports/deepseek-v4-flash-0731-t4/
+official-source/inference/model.py:625-626).  Its engine is configured with
+num_experts = epr and holds those records.  Tokens are routed on their owner
+rank with the same router as one GPU, so the route ids (and the journal) do
+not depend on the GPU count.  A layer call on this rank's T tokens:
+
+  1. pack: selections sorted by owner rank into `capacity` rows per rank
+     (FP16 hidden row + the owner's local expert id, -1 unused);
+  2. all-to-all of the rows and the expert ids (equal blocks, so no host
+     synchronisation and no split sizes);
+  3. the grouped expert GEMMs over the received rows;
+  4. all-to-all of the FP32 output rows back to their tokens' owners;
+  5. the rank-order FP32 combine.
+
+torch.distributed (NCCL on GPUs) is the transport; the packing, GEMMs and
+combine are the engine's kernels (`ops=None`).  Tests pass other `ops` with
+the same contracts to run the choreography on CPU ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Any, Callable
+
+
+@dataclass
+class EpOps:
+    """The three device steps of a layer call.
+
+    pack(ids, x, send_rows, send_expert, slot_of_pos)
+    compute(recv_rows, recv_expert, raw)
+    combine(back, slot_of_pos, weights, out)
+    """
+
+    pack: Callable[..., None]
+    compute: Callable[..., None]
+    combine: Callable[..., None]
+
+
+def engine_ops(engine, layer: int, world: int, experts_per_rank: int, capacity: int,
+               stream_of: Callable[[], Any]) -> EpOps:
+    """EpOps over a dee_b200.Engine (device tensors, the current CUDA stream)."""
+
+    def pack(ids, x, send_rows, send_expert, slot_of_pos):
+        engine.ep_pack_device(ids.data_ptr(), ids.shape[0], x.data_ptr(), world, experts_per_rank,
+                              capacity, send_rows.data_ptr(), send_expert.data_ptr(),
+                              slot_of_pos.data_ptr(), stream_of())
+
+    def compute(recv_rows, recv_expert, raw):
+        engine.moe_forward_rows_device(layer, recv_rows.data_ptr(), recv_expert.data_ptr(),
+                                       recv_rows.shape[0], raw.data_ptr(), stream_of())
+
+    def combine(back, slot_of_pos, weights, out):
+        engine.ep_combine_device(back.data_ptr(), slot_of_pos.data_ptr(), weights.data_ptr(),
+                                 out.shape[0], out.data_ptr(), stream_of())
+
+    return EpOps(pack, compute, combine)
+
+
+class ExpertParallelMoE:
+    """One rank's share of an expert-parallel MoE layer with fixed T tokens per rank.
+
+    All ranks must call forward() together with the same `tokens`; buffers
+    are allocated once.  `capacity` defaults to tokens * topk, which covers
+    any routing (a rank can receive at most all selections of another).
+    """
+
+    def __init__(self, torch_mod, rank: int, world: int, experts_per_rank: int, tokens: int,
+                 topk: int, hidden: int, device, *, engine=None, layer: int = 0,
+                 capacity: int | None = None, group=None, ops: EpOps | None = None):
+        self.torch = torch_mod
+        self.dist = torch_mod.distributed
+        self.rank, self.world, self.epr = rank, world, experts_per_rank
+        self.tokens, self.topk, self.hidden = tokens, topk, hidden
+        self.capacity = capacity if capacity is not None else tokens * topk
+        self.group = group
+        if ops is None:
+            if engine is None:
+                raise ValueError("ExpertParallelMoE needs an engine or explicit ops")
+            cuda = torch_mod.cuda
+            ops = engine_ops(engine, layer, world, experts_per_rank, self.capacity,
+                             lambda: cuda.current_stream())
+        self.ops = ops
+        n = world * self.capacity
+        t = torch_mod
+        self.send_rows = t.empty((n, hidden), dtype=t.float16, device=device)
+        self.send_expert = t.empty((n,), dtype=t.int32, device=device)
+        self.recv_rows = t.empty((n, hidden), dtype=t.float16, device=device)
+        self.recv_expert = t.empty((n,), dtype=t.int32, device=device)
+        self.slot_of_pos = t.empty((tokens * topk,), dtype=t.int32, device=device)
+        self.raw = t.zeros((n, hidden), dtype=t.float32, device=device)
+        self.back = t.empty((n, hidden), dtype=t.float32, device=device)
+        self.out = t.empty((tokens, hidden), dtype=t.float32, device=device)
+
+    def forward(self, x, ids, weights):
+        """x FP16 [T, H], ids int32 [T, K] (global expert ids), weights FP32
+        [T, K] -> FP32 [T, H] (a view of an internal buffer, valid until the
+        next call)."""
+        shapes_ok = (tuple(ids.shape) == (self.tokens, self.topk) and
+                     tuple(x.shape) == (self.tokens, self.hidden))
+        if not shapes_ok:
+            raise ValueError(f"expected x [{self.tokens}, {self.hidden}] and ids [{self.tokens}, "
+                             f"{self.topk}], got {tuple(x.shape)} and {tuple(ids.shape)}")
+        self.ops.pack(ids, x, self.send_rows, self.send_expert, self.slot_of_pos)
+        # FP16 rows travel as int32 pairs: a bitwise view every backend moves
+        i32 = self.torch.int32
+        self.dist.all_to_all_single(self.recv_rows.view(i32), self.send_rows.view(i32),
+                                    group=self.group)
+        self.dist.all_to_all_single(self.recv_expert, self.send_expert, group=self.group)
+        self.ops.compute(self.recv_rows, self.recv_expert, self.raw)
+        self.dist.all_to_all_single(self.back, self.raw, group=self.group)
+        self.ops.combine(self.back, self.slot_of_pos, weights, self.out)
+        return self.out

@@ -133,6 +133,47 @@ DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_
  * invalid expert id, a router failure or a pipeline timeout. */
 DEE_API int dee_engine_sync_status(dee_engine* engine, void* stream, uint32_t* status_out);
 
+/* Expert parallelism over `ranks` GPUs (no counterpart in the reference's
+ * engine, which runs one GPU; the split follows the official DeepSeek-V4
+ * convention that rank r owns experts [r*epr, (r+1)*epr),
+ * benchmark_reports/deepseek-v4-flash-0731-t4/official-source/inference/
+ * model.py:625-626).  The engine of each rank is configured with
+ * num_experts = experts_per_rank and holds that rank's records.  A layer is
+ *   dee_ep_pack_device -> all-to-all of send rows and send experts ->
+ *   dee_moe_forward_rows_device -> all-to-all of the FP32 rows back ->
+ *   dee_ep_combine_device;
+ * the all-to-alls exchange equal blocks of `capacity` rows per rank pair, so
+ * no host synchronisation is needed between the steps. */
+
+/* Pack this rank's selections (device global ids [T, K]) by owner rank:
+ * d_send_rows FP16 [ranks * capacity, H] (the token's hidden row),
+ * d_send_expert int32 [ranks * capacity] (the owner's local expert id, -1 in
+ * unused slots), d_slot_of_pos int32 [T * K] (the send row of selection
+ * t*K + r).  Within a destination the selections keep ascending t*K + r.
+ * capacity must cover the most selections any one rank receives from this
+ * one (T * K always does); overflow raises a device status bit.  The ids
+ * are also the journal's (dee_journal_ids_host). */
+DEE_API int dee_ep_pack_device(dee_engine* engine, const int32_t* d_ids, int tokens,
+                               const void* d_x_f16, int ranks, int experts_per_rank, int capacity,
+                               void* d_send_rows, int32_t* d_send_expert, int32_t* d_slot_of_pos,
+                               void* stream);
+
+/* The grouped expert GEMMs over received rows: row i (FP16 [rows, H]) through
+ * local expert d_expert[i] into d_raw FP32 [rows, H]; rows with expert -1 are
+ * skipped (their output rows are left as they were).  Same kernels and
+ * per-row results as dee_moe_forward_device. */
+DEE_API int dee_moe_forward_rows_device(dee_engine* engine, int layer, const void* d_rows_f16,
+                                        const int32_t* d_expert, int rows, float* d_raw,
+                                        void* stream);
+
+/* out[t] = sum_r w[t, r] * back[slot_of_pos[t*K + r]] in rank order, each
+ * multiply and add rounded to FP32 (the live combine of
+ * dee.cpp/scripts/deepseek_v4_layer_candidate.py:616-629), over the rows that
+ * came back from the expert owners (d_back FP32 [ranks * capacity, H]). */
+DEE_API int dee_ep_combine_device(dee_engine* engine, const float* d_back,
+                                  const int32_t* d_slot_of_pos, const float* d_weights, int tokens,
+                                  float* d_out_f32, void* stream);
+
 /* Host copy of the int32 [T, K] route ids the last forward consumed -- the
  * buffer the route journal records (deepseek_v4_native_generate.py
  * :2196-2216).  Waits for the last forward's stream, then copies.  Returns
