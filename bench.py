@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
+                    help="multi-GPU transport: NVLink peer memory (default) or NCCL all-to-all")
     ap.add_argument("--experts", type=int, default=E,
                     help="experts in the bank (smaller values only for profiling captures)")
     return ap.parse_args()
@@ -189,14 +191,22 @@ class EpLayer:
     rank's share of the experts (pack, NCCL all-to-all, grouped GEMMs,
     all-to-all back, combine)."""
 
-    def __init__(self, torch, router, ep, b):
+    def __init__(self, torch, router, ep, b, rank, world, epr):
         self.torch = torch
         self.router = router
         self.ep = ep
         self.b = b
+        self.rank, self.world, self.epr = rank, world, epr
         self.ids = torch.empty((b, K), dtype=torch.int32, device="cuda")
         self.w = torch.empty((b, K), dtype=torch.float32, device="cuda")
         self.out = ep.out
+
+    def local_ids(self):
+        """This rank's experts selected by any rank's tokens this step (local ids)."""
+        parts = [self.torch.empty_like(self.ids) for _ in range(self.world)]
+        self.torch.distributed.all_gather(parts, self.ids)
+        ids = self.torch.cat(parts).flatten() - self.rank * self.epr
+        return ids[(ids >= 0) & (ids < self.epr)]
 
     def __call__(self, x, logits, stream):
         self.router.route_topk_device(logits.data_ptr(), self.b, self.ids.data_ptr(), self.w.data_ptr(),
@@ -247,7 +257,7 @@ def decode_point(torch, eng, b, n_steps, warmup, flush, stream, seed, profile=Tr
     for i in range(n_steps):
         layer(xs[i % len(xs)], logits[i % len(xs)], stream)
         with torch.cuda.stream(stream):
-            ids_seen.append(layer.ep.recv_expert.clone() if hasattr(layer, "ep") else layer.ids.clone())
+            ids_seen.append(layer.local_ids() if hasattr(layer, "local_ids") else layer.ids.clone())
     torch.cuda.synchronize()
     uniq = unique_experts(torch, ids_seen)
     stages = None
@@ -420,6 +430,7 @@ def main():
     global E
     E = args.experts
     make_layer = None
+    transport = None
     if world == 1:
         bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
         eng = build_engine(torch, bank, max_tokens=max(b, 64))
@@ -437,14 +448,30 @@ def main():
         router = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
                                                            max_tokens=64, device_id=local))
         ep_cache = {}
+        transport = args.ep
 
         def make_layer(bb):
+            nonlocal transport
             if bb not in ep_cache:
-                ep_cache[bb] = ExpertParallelMoE(torch, rank, world, epr, bb, K, H, "cuda", engine=eng)
-            return EpLayer(torch, router, ep_cache[bb], bb)
+                if transport == "p2p" and bb != b:
+                    raise SystemExit("the peer path is set up for one batch size per engine")
+                ep = None
+                if transport == "p2p":
+                    from dee_b200.ep import ExpertParallelPeer
+                    try:
+                        ep = ExpertParallelPeer(torch, eng, rank, world, bb, H)
+                    except Exception as exc:  # no peer access: same layer over NCCL
+                        print(f"rank {rank}: NVLink peer path unavailable ({exc}); using NCCL",
+                              file=sys.stderr)
+                        transport = "nccl"
+                if ep is None:
+                    ep = ExpertParallelMoE(torch, rank, world, epr, bb, K, H, "cuda", engine=eng)
+                ep_cache[bb] = ep
+            return EpLayer(torch, router, ep_cache[bb], bb, rank, world, epr)
     stream = torch.cuda.Stream()
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
-    launches0 = eng.launch_count()
+    engines = [eng] if world == 1 else [eng, router]
+    launches0 = sum(x.launch_count() for x in engines)
 
     def barrier():
         if world > 1:
@@ -459,7 +486,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     # route + permute + gather + gate/up + down + combine, counted by the engine
-    per_step_launches = (eng.launch_count() - launches0) / (args.steps * 2 + args.warmup)
+    per_step_launches = (sum(x.launch_count() for x in engines) - launches0) / (args.steps * 2 + args.warmup)
     total_ms = sum(times)
     if world > 1:
         t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
@@ -484,7 +511,7 @@ def main():
         "data": "synthetic",
         "config": {"workload": f"cfg1-decode-b{b}", "hidden": H, "inter": I, "experts": E, "topk": K,
                    "tokens_per_step": b, "experts_resident": E, "weights": "fp4-e2m1+ue8m0/32",
-                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "parallelism": (f"ep{world}-{transport}" if world > 1 else "single"),
                    "l2": "flushed (256 MiB write) before every timed step",
                    "unique_experts_per_step": statistics.mean(uniq)},
         "hbm_gbs_layer": layer_gbs,
@@ -545,6 +572,9 @@ def main():
                                       "sample": f"{reps} x one b={b} decode layer ({b * K} selections) "
                                                 f"through ReferenceCpuExecutor, {el:.1f} s"}
     if world > 1:
+        # every rank is past its last layer call before any exchange block goes
+        torch.cuda.synchronize()
+        dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))

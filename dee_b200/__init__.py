@@ -217,6 +217,45 @@ class Engine:
             ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_ep_combine_device")
 
+    # -- expert parallelism over NVLink peer memory ---------------------------
+    def ep_p2p_init(self, ranks: int, rank: int, tokens: int) -> tuple[bytes, int]:
+        """Allocate and export this rank's exchange block: (IPC handle, device address)."""
+        handle = ctypes.create_string_buffer(64)
+        block = ctypes.c_uint64(0)
+        rc = self._lib.dee_ep_p2p_init(self._h, ranks, rank, tokens, handle, ctypes.byref(block))
+        self._check(rc, "dee_ep_p2p_init")
+        return handle.raw, block.value
+
+    def ep_p2p_connect(self, handles: list[bytes] | None, blocks: list[int] | None = None) -> None:
+        hbuf = ctypes.create_string_buffer(b"".join(handles)) if handles else None
+        barr = (ctypes.c_uint64 * len(blocks))(*blocks) if blocks else None
+        rc = self._lib.dee_ep_p2p_connect(self._h, hbuf, barr)
+        self._check(rc, "dee_ep_p2p_connect")
+
+    def ep_p2p_dispatch_device(self, d_x_ptr: int, d_ids_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_ep_p2p_dispatch_device(self._h, ctypes.c_void_p(d_x_ptr),
+                                                  ctypes.c_void_p(d_ids_ptr),
+                                                  ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_p2p_dispatch_device")
+
+    def ep_p2p_experts_device(self, layer: int, stream=None) -> None:
+        rc = self._lib.dee_ep_p2p_experts_device(self._h, layer, ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_p2p_experts_device")
+
+    def ep_p2p_combine_device(self, d_weights_ptr: int, d_out_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_ep_p2p_combine_device(self._h, ctypes.c_void_p(d_weights_ptr),
+                                                 ctypes.c_void_p(d_out_ptr),
+                                                 ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_p2p_combine_device")
+
+    def ep_p2p_forward_device(self, layer: int, d_x_ptr: int, d_ids_ptr: int, d_weights_ptr: int,
+                              d_out_ptr: int, stream=None) -> None:
+        rc = self._lib.dee_ep_p2p_forward_device(self._h, layer, ctypes.c_void_p(d_x_ptr),
+                                                 ctypes.c_void_p(d_ids_ptr), ctypes.c_void_p(d_weights_ptr),
+                                                 ctypes.c_void_p(d_out_ptr),
+                                                 ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_ep_p2p_forward_device")
+
     def sync_status(self, stream=None) -> int:
         st = ctypes.c_uint32(0)
         rc = self._lib.dee_engine_sync_status(self._h, ctypes.c_void_p(_stream_handle(stream)),

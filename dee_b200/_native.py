@@ -56,6 +56,12 @@ SIGNATURES = {
     "dee_ep_pack_device": (I, [P, P, I, P, I, I, I, P, P, P, P]),
     "dee_moe_forward_rows_device": (I, [P, I, P, P, I, P, P]),
     "dee_ep_combine_device": (I, [P, P, P, P, I, P, P]),
+    "dee_ep_p2p_init": (I, [P, I, I, I, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "dee_ep_p2p_connect": (I, [P, P, P]),
+    "dee_ep_p2p_dispatch_device": (I, [P, P, P, P]),
+    "dee_ep_p2p_experts_device": (I, [P, I, P]),
+    "dee_ep_p2p_combine_device": (I, [P, P, P, P]),
+    "dee_ep_p2p_forward_device": (I, [P, I, P, P, P, P, P]),
     "dee_engine_sync_status": (I, [P, P, U32P]),
     "dee_journal_ids_host": (I, [P, P, I]),
     "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),

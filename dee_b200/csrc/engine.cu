@@ -75,8 +75,27 @@ cudaError_t dev_alloc(T** p, size_t n) {
 }  // namespace
 }  // namespace dee
 
+namespace dee {
+// Peer (NVLink) expert-parallel state of one rank: its exchange block
+// (exported with CUDA IPC), every rank's buffer pointers and the epoch that
+// numbers layer calls.
+struct EpP2P {
+    int ranks = 0, rank = 0, tokens = 0, capacity = 0;
+    uint8_t* block = nullptr;
+    size_t off_recv_rows = 0, off_recv_expert = 0, off_recv_flag = 0, off_back_rows = 0,
+           off_back_flag = 0, bytes = 0;
+    EpPeers peers{};
+    std::vector<void*> opened;        // peer blocks opened from IPC handles
+    float** d_back_peers = nullptr;   // device copy of peers.back_rows
+    int32_t* d_slot_of_pos = nullptr; // [tokens * K]
+    uint32_t epoch = 0;
+    bool connected = false;
+};
+}  // namespace dee
+
 struct dee_engine {
     dee_config cfg{};
+    dee::EpP2P ep;
     std::string last_error;
     int num_sms = 148;
     cudaStream_t stream = nullptr;  // the engine's own stream (synchronous API)
@@ -250,8 +269,14 @@ bool host_ids_valid(dee_engine* e, const int32_t* ids, size_t n) {
 // validated-or-device-checked int32 ids [T, K]; raw receives [T*K, H] FP32.
 // The expert-parallel rows entry point runs it with K = 1, one row per
 // selection, and ids of -1 for unused rows (skip_negative).
+struct EpReturn {
+    float* const* raw_peers;  // device array [ranks]
+    int capacity, rank;
+};
+
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
-                float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal) {
+                float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
+                const EpReturn* ret = nullptr) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -261,6 +286,9 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     // rows); larger calls the tcgen05 kernel (tiles of <= 128 rows).
     const bool decode = sel <= static_cast<size_t>(kDecodeMaxSelections);
     const bool large = !decode;
+    if (ret && !decode)
+        return fail(e, DEE_ERR_UNSUPPORTED, "the NVLink expert-parallel return needs <= " +
+                                                std::to_string(kDecodeMaxSelections) + " rows per rank");
     const int n_max = decode ? kDecodeTileRows : gemm_n_max(large);
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm,     e->d_row_of,
@@ -292,6 +320,11 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.act = e->d_act;
     a.raw = raw;
     a.status = e->d_status;
+    if (ret) {
+        a.raw_peers = ret->raw_peers;
+        a.ep_capacity = ret->capacity;
+        a.ep_rank = ret->rank;
+    }
 
     GemmMaps gm{};
     if (decode) {
@@ -375,6 +408,10 @@ void dee_engine_destroy(dee_engine* e) {
     cudaSetDevice(e->cfg.device_id);
     if (e->stream) cudaStreamSynchronize(e->stream);
     free_workspace(e);
+    for (void* p : e->ep.opened) cudaIpcCloseMemHandle(p);
+    cudaFree(e->ep.block);
+    cudaFree(e->ep.d_back_peers);
+    cudaFree(e->ep.d_slot_of_pos);
     for (auto& b : e->banks) cudaFree(b.d_slot_of);
     for (int i = 0; i < kStageCount; ++i) {
         if (e->ev_start[i]) cudaEventDestroy(e->ev_start[i]);
@@ -649,6 +686,150 @@ int dee_ep_combine_device(dee_engine* e, const float* d_back, const int32_t* d_s
     if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
     e->launches += 1;
     return DEE_OK;
+}
+
+int dee_ep_p2p_init(dee_engine* e, int ranks, int rank, int tokens, void* ipc_handle_out,
+                    uint64_t* block_out) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    if (ranks <= 0 || ranks > kEpMaxRanks || rank < 0 || rank >= ranks || tokens <= 0 ||
+        !ipc_handle_out || e->ep.block)
+        return fail(e, DEE_ERR_INVALID, "invalid ep_p2p_init arguments (or already initialised)");
+    EpP2P& p = e->ep;
+    const size_t H = static_cast<size_t>(e->cfg.hidden);
+    const int cap = tokens * e->cfg.topk;
+    const size_t n = static_cast<size_t>(ranks) * cap;
+    auto up = [](size_t x) { return (x + 255) & ~static_cast<size_t>(255); };
+    p.off_recv_rows = 0;
+    p.off_recv_expert = up(p.off_recv_rows + n * H * 2);
+    p.off_recv_flag = up(p.off_recv_expert + n * 4);
+    p.off_back_rows = up(p.off_recv_flag + static_cast<size_t>(ranks) * 4);
+    p.off_back_flag = up(p.off_back_rows + n * H * 4);
+    p.bytes = up(p.off_back_flag + static_cast<size_t>(ranks) * 4);
+    cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&p.block), p.bytes);
+    if (err == cudaSuccess) err = cudaMemset(p.block, 0, p.bytes);  // flags start below epoch 1
+    if (err == cudaSuccess)
+        err = cudaMalloc(reinterpret_cast<void**>(&p.d_slot_of_pos), sizeof(int32_t) * cap);
+    if (err == cudaSuccess)
+        err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle_out), p.block);
+    if (err != cudaSuccess) {
+        cudaFree(p.block);
+        cudaFree(p.d_slot_of_pos);
+        p = EpP2P{};
+        return cuda_fail(e, err, "ep_p2p_init");
+    }
+    p.ranks = ranks;
+    p.rank = rank;
+    p.tokens = tokens;
+    p.capacity = cap;
+    if (block_out) *block_out = reinterpret_cast<uint64_t>(p.block);
+    return DEE_OK;
+}
+
+int dee_ep_p2p_connect(dee_engine* e, const void* ipc_handles, const uint64_t* blocks) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    EpP2P& p = e->ep;
+    if (!p.block || p.connected || (!ipc_handles && !blocks))
+        return fail(e, DEE_ERR_INVALID, "ep_p2p_connect needs ep_p2p_init first and handles or blocks");
+    for (int d = 0; d < p.ranks; ++d) {
+        uint8_t* base = nullptr;
+        if (d == p.rank) {
+            base = p.block;
+        } else if (blocks && blocks[d]) {
+            base = reinterpret_cast<uint8_t*>(blocks[d]);  // same process, same device
+        } else {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(ipc_handles) + sizeof(h) * d, sizeof(h));
+            void* q = nullptr;
+            cudaError_t err = cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess);
+            if (err != cudaSuccess)
+                return cuda_fail(e, err, ("cudaIpcOpenMemHandle (peer " + std::to_string(d) + ")").c_str());
+            p.opened.push_back(q);
+            base = static_cast<uint8_t*>(q);
+        }
+        p.peers.recv_rows[d] = reinterpret_cast<__half*>(base + p.off_recv_rows);
+        p.peers.recv_expert[d] = reinterpret_cast<int32_t*>(base + p.off_recv_expert);
+        p.peers.recv_flag[d] = reinterpret_cast<uint32_t*>(base + p.off_recv_flag);
+        p.peers.back_rows[d] = reinterpret_cast<float*>(base + p.off_back_rows);
+        p.peers.back_flag[d] = reinterpret_cast<uint32_t*>(base + p.off_back_flag);
+    }
+    cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&p.d_back_peers), sizeof(float*) * p.ranks);
+    if (err == cudaSuccess)
+        err = cudaMemcpy(p.d_back_peers, p.peers.back_rows, sizeof(float*) * p.ranks,
+                         cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep_p2p_connect");
+    p.connected = true;
+    return DEE_OK;
+}
+
+int dee_ep_p2p_dispatch_device(dee_engine* e, const void* d_x_f16, const int32_t* d_ids, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    EpP2P& p = e->ep;
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!p.connected || !d_x_f16 || !d_ids)
+        return fail(e, DEE_ERR_INVALID, "ep_p2p_dispatch needs a connected engine, x and ids");
+    const size_t sel = static_cast<size_t>(p.tokens) * e->cfg.topk;
+    const size_t recv = static_cast<size_t>(p.ranks) * p.capacity;
+    if ((rc = ensure_capacity(e, sel > recv ? sel : recv, stream)) != DEE_OK) return rc;
+    ++p.epoch;
+    cudaError_t err = launch_ep_peer_dispatch(d_ids, static_cast<const __half*>(d_x_f16), p.tokens,
+                                              e->cfg.topk, e->cfg.hidden, p.ranks, p.rank,
+                                              e->cfg.num_experts, p.capacity, p.peers, p.d_slot_of_pos,
+                                              e->d_journal, e->d_status, p.epoch, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep peer dispatch launch");
+    e->launches += 3;
+    e->h_ids_count = sel;
+    e->journal_stream = stream;
+    return DEE_OK;
+}
+
+int dee_ep_p2p_experts_device(dee_engine* e, int layer, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    EpP2P& p = e->ep;
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!p.connected || p.epoch == 0)
+        return fail(e, DEE_ERR_INVALID, "ep_p2p_experts before any dispatch");
+    cudaError_t err = launch_ep_wait(p.peers.recv_flag[p.rank], p.ranks, p.epoch, e->d_status,
+                                     sm100::kStatusTimeoutFlag, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep wait launch");
+    const EpReturn ret{p.d_back_peers, p.capacity, p.rank};
+    if ((rc = run_experts(e, layer, p.peers.recv_rows[p.rank], p.ranks * p.capacity,
+                          p.peers.recv_expert[p.rank], e->d_raw, stream, 1, true, false, &ret)) != DEE_OK)
+        return rc;
+    err = launch_ep_signal(p.peers, true, p.ranks, p.rank, p.epoch, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep signal launch");
+    e->launches += 2;
+    return DEE_OK;
+}
+
+int dee_ep_p2p_combine_device(dee_engine* e, const float* d_weights, float* d_out_f32, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    EpP2P& p = e->ep;
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!p.connected || p.epoch == 0 || !d_weights || !d_out_f32)
+        return fail(e, DEE_ERR_INVALID, "ep_p2p_combine needs a dispatched layer, weights and out");
+    cudaError_t err = launch_ep_wait(p.peers.back_flag[p.rank], p.ranks, p.epoch, e->d_status,
+                                     sm100::kStatusTimeoutFlag, stream);
+    if (err == cudaSuccess)
+        err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
+                                e->cfg.topk, e->cfg.hidden, d_out_f32, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
+    e->launches += 2;
+    return DEE_OK;
+}
+
+int dee_ep_p2p_forward_device(dee_engine* e, int layer, const void* d_x_f16, const int32_t* d_ids,
+                              const float* d_weights, float* d_out_f32, void* stream) {
+    int rc = dee_ep_p2p_dispatch_device(e, d_x_f16, d_ids, stream);
+    if (rc == DEE_OK) rc = dee_ep_p2p_experts_device(e, layer, stream);
+    if (rc == DEE_OK) rc = dee_ep_p2p_combine_device(e, d_weights, d_out_f32, stream);
+    return rc;
 }
 
 int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {

@@ -1,4 +1,4 @@
-// ep.cu -- expert-parallel dispatch packing and combine.
+// ep.cu -- expert-parallel dispatch packing, peer transfers and combine.
 //
 // With the experts split into contiguous ranges of `experts_per_rank` over
 // `ranks` GPUs (rank r owns experts [r*epr, (r+1)*epr), the official
@@ -23,11 +23,14 @@ constexpr int kPackThreads = 1024;
 // One CTA.  Chunk by chunk of 1024 selections: per destination a warp
 // ballot gives each selection its place among its warp's, a scan over the
 // warps' counts its place in the chunk, and a running base per destination
-// its slot.  Unused slots keep the local expert id -1.
+// its slot.  kPeer = false writes the local send block (ranks x capacity
+// local expert ids, -1 unused); kPeer = true writes this rank's block of every
+// owner's receive buffer over NVLink, including -1 for the unused slots.
+template <bool kPeer>
 __global__ void __launch_bounds__(kPackThreads, 1)
-    ep_pack_index_kernel(const int32_t* __restrict__ ids, int sel, int ranks, int epr, int capacity,
-                         int32_t* __restrict__ send_expert, int32_t* __restrict__ slot_of_pos,
-                         int32_t* __restrict__ journal, uint32_t* status) {
+    ep_index_kernel(const int32_t* __restrict__ ids, int sel, int ranks, int rank, int epr, int capacity,
+                    int32_t* __restrict__ send_expert, EpPeers peers, int32_t* __restrict__ slot_of_pos,
+                    int32_t* __restrict__ journal, uint32_t* status) {
     __shared__ int wc[kEpMaxRanks][32];    // per destination, per warp: selections in the chunk
     __shared__ int wpre[kEpMaxRanks][32];  // exclusive prefix over warps
     __shared__ int chunk_total[kEpMaxRanks];
@@ -36,7 +39,8 @@ __global__ void __launch_bounds__(kPackThreads, 1)
     sm100::pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const unsigned lt = (1u << lane) - 1u;
-    for (int i = tid; i < ranks * capacity; i += kPackThreads) send_expert[i] = -1;
+    if (!kPeer)
+        for (int i = tid; i < ranks * capacity; i += kPackThreads) send_expert[i] = -1;
     if (tid < ranks) base[tid] = 0;
     __syncthreads();
     for (int c0 = 0; c0 < sel; c0 += kPackThreads) {
@@ -76,7 +80,10 @@ __global__ void __launch_bounds__(kPackThreads, 1)
             const int s = base[d] + wpre[d][warp] + my_rank;
             if (s < capacity) {
                 slot_of_pos[p] = d * capacity + s;
-                send_expert[d * capacity + s] = le;
+                if (kPeer)
+                    peers.recv_expert[d][rank * capacity + s] = le;
+                else
+                    send_expert[d * capacity + s] = le;
             } else {
                 atomicOr(status, kStatusBadShape);
                 slot_of_pos[p] = -1;
@@ -86,6 +93,10 @@ __global__ void __launch_bounds__(kPackThreads, 1)
         if (tid < ranks) base[tid] += chunk_total[tid];
         __syncthreads();
     }
+    if (kPeer)  // this rank's unused slots in every owner's block
+        for (int d = 0; d < ranks; ++d)
+            for (int s = base[d] + tid; s < capacity; s += kPackThreads)
+                peers.recv_expert[d][rank * capacity + s] = -1;
 }
 
 // One warp per selection: its token's hidden row into its send slot.
@@ -134,6 +145,66 @@ __global__ void ep_combine_kernel(const float* __restrict__ back, const int32_t*
     }
 }
 
+// ---------------------------------------------------------------- peer path
+//
+// Rows and local expert ids go straight into the owners' receive buffers
+// over NVLink (peer pointers from CUDA IPC); block `rank` of every owner's
+// buffer belongs to this rank.
+
+__global__ void ep_peer_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ slot_of_pos,
+                                    int sel, int topk, int hidden, int rank, int capacity, EpPeers peers) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    const int warps_total = gridDim.x * (blockDim.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int vec = hidden / 8;
+    for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < sel; p += warps_total) {
+        const int s = slot_of_pos[p];
+        if (s < 0) continue;
+        const int d = s / capacity;
+        const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(p / topk) * hidden);
+        uint4* dst = reinterpret_cast<uint4*>(peers.recv_rows[d] +
+                                              static_cast<size_t>(rank * capacity + (s - d * capacity)) * hidden);
+        for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
+    }
+}
+
+// After the kernels before it on the stream have completed: make their
+// stores visible system-wide, then publish `epoch` in slot `rank` of every
+// peer's flag array.
+__global__ void ep_signal_kernel(EpPeers peers, bool back, int ranks, int rank, uint32_t epoch) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    for (int d = 0; d < ranks; ++d) {
+        uint32_t* f = (back ? peers.back_flag[d] : peers.recv_flag[d]) + rank;
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+    }
+}
+
+// Wait (bounded) until every peer has published `epoch` in this rank's flag
+// array; on timeout set `code` in the status word and return, so the context
+// stays usable and the host sees the failure.
+__global__ void ep_wait_kernel(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
+                               uint32_t code) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    const int s = threadIdx.x;
+    if (s >= ranks) return;
+    const uint64_t t0 = sm100::global_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
+        if (static_cast<int32_t>(v - epoch) >= 0) break;
+        if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
+            atomicOr(status, code);
+            break;
+        }
+        __nanosleep(200);
+    }
+}
+
 int grid_cap(size_t work, int per_block, int cap) {
     size_t g = (work + per_block - 1) / per_block;
     if (g < 1) g = 1;
@@ -150,11 +221,42 @@ cudaError_t launch_ep_pack(const int32_t* ids, const __half* x, int tokens, int 
         hidden % 8 != 0)
         return cudaErrorInvalidValue;
     const int sel = tokens * topk;
-    cudaError_t err = launch_pdl(ep_pack_index_kernel, dim3(1), dim3(kPackThreads), 0, stream, ids, sel,
-                                 ranks, epr, capacity, send_expert, slot_of_pos, journal, status);
+    cudaError_t err = launch_pdl(ep_index_kernel<false>, dim3(1), dim3(kPackThreads), 0, stream, ids, sel,
+                                 ranks, 0, epr, capacity, send_expert, EpPeers{}, slot_of_pos, journal,
+                                 status);
     if (err != cudaSuccess) return err;
     return launch_pdl(ep_pack_rows_kernel, dim3(grid_cap(static_cast<size_t>(sel), 8, 148 * 8)), dim3(256), 0,
                       stream, x, static_cast<const int32_t*>(slot_of_pos), sel, topk, hidden, send_rows);
+}
+
+cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tokens, int topk, int hidden,
+                                    int ranks, int rank, int epr, int capacity, const EpPeers& peers,
+                                    int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
+                                    uint32_t epoch, cudaStream_t stream) {
+    if (tokens <= 0 || topk <= 0 || ranks <= 0 || ranks > kEpMaxRanks || rank < 0 || rank >= ranks ||
+        epr <= 0 || capacity <= 0 || hidden % 8 != 0)
+        return cudaErrorInvalidValue;
+    const int sel = tokens * topk;
+    cudaError_t err = launch_pdl(ep_index_kernel<true>, dim3(1), dim3(kPackThreads), 0, stream, ids, sel,
+                                 ranks, rank, epr, capacity, static_cast<int32_t*>(nullptr), peers,
+                                 slot_of_pos, journal, status);
+    if (err != cudaSuccess) return err;
+    err = launch_pdl(ep_peer_rows_kernel, dim3(grid_cap(static_cast<size_t>(sel), 8, 148 * 8)), dim3(256), 0,
+                     stream, x, static_cast<const int32_t*>(slot_of_pos), sel, topk, hidden, rank, capacity,
+                     peers);
+    if (err != cudaSuccess) return err;
+    return launch_ep_signal(peers, false, ranks, rank, epoch, stream);
+}
+
+cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int rank, uint32_t epoch,
+                             cudaStream_t stream) {
+    return launch_pdl(ep_signal_kernel, dim3(1), dim3(32), 0, stream, peers, back, ranks, rank, epoch);
+}
+
+cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
+                           uint32_t code, cudaStream_t stream) {
+    if (ranks <= 0 || ranks > kEpMaxRanks) return cudaErrorInvalidValue;
+    return launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, stream, flags, ranks, epoch, status, code);
 }
 
 cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,

@@ -72,6 +72,30 @@ cudaError_t launch_ep_pack(const int32_t* ids, const __half* x, int tokens, int 
 cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,
                               int tokens, int topk, int hidden, float* out, cudaStream_t stream);
 
+// Peer (NVLink) expert parallelism: every rank's exchange buffers, indexed by
+// rank (this rank's own entries are local pointers).  Block s of rank d's
+// receive buffers holds the rows rank s sent to d; block d of rank s's return
+// buffer holds the output rows d computed for s.
+struct EpPeers {
+    __half* recv_rows[kEpMaxRanks];      // [ranks * capacity, H] FP16
+    int32_t* recv_expert[kEpMaxRanks];   // [ranks * capacity], -1 unused
+    uint32_t* recv_flag[kEpMaxRanks];    // [ranks] dispatch epoch per source
+    float* back_rows[kEpMaxRanks];       // [ranks * capacity, H] FP32
+    uint32_t* back_flag[kEpMaxRanks];    // [ranks] return epoch per expert owner
+};
+// Index + row stores into the owners' receive buffers, then the dispatch flags.
+cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tokens, int topk, int hidden,
+                                    int ranks, int rank, int epr, int capacity, const EpPeers& peers,
+                                    int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
+                                    uint32_t epoch, cudaStream_t stream);
+// Publish `epoch` in slot `rank` of every rank's dispatch (back = false) or
+// return (back = true) flags, after the stream's earlier kernels.
+cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int rank, uint32_t epoch,
+                             cudaStream_t stream);
+// Bounded wait until all `ranks` flags reached `epoch` (timeout: `code` in status).
+cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
+                           uint32_t code, cudaStream_t stream);
+
 // Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
                               int32_t* ids, float* weights, uint32_t* status, cudaStream_t stream);

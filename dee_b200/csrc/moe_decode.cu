@@ -543,9 +543,18 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                const size_t pos = static_cast<size_t>(args.perm[it_row_start + n]);
-                args.raw[pos * args.hidden + f_lo] = c[h];
-                args.raw[pos * args.hidden + f_lo + 8] = c[2 + h];
+                const int pos = args.perm[it_row_start + n];
+                float* dst;
+                if (args.raw_peers) {  // straight into the token owner's return buffer
+                    const int src = pos / args.ep_capacity;
+                    const int slot = pos - src * args.ep_capacity;
+                    dst = args.raw_peers[src] +
+                          static_cast<size_t>(args.ep_rank * args.ep_capacity + slot) * args.hidden;
+                } else {
+                    dst = args.raw + static_cast<size_t>(pos) * args.hidden;
+                }
+                dst[f_lo] = c[h];
+                dst[f_lo + 8] = c[2 + h];
             }
         }
     }

@@ -63,6 +63,13 @@ struct GemmArgs {
     __half* act;             // kGateUp output [rows, I]
     float* raw;              // kDown output [positions, H]
     uint32_t* status;        // device status word (sm100::StatusBits)
+    // Expert-parallel return over NVLink (decode kernel only): when set,
+    // output row i -- received from rank i / ep_capacity into slot
+    // i % ep_capacity -- is stored at raw_peers[rank] + (ep_rank *
+    // ep_capacity + slot) * H, the owner's return buffer, instead of raw.
+    float* const* raw_peers;  // device array [ranks] of peer pointers, or null
+    int ep_capacity;
+    int ep_rank;
 };
 
 constexpr int kGemmThreads = 480;     // 15 warps

@@ -113,3 +113,53 @@ class ExpertParallelMoE:
         self.dist.all_to_all_single(self.back, self.raw, group=self.group)
         self.ops.combine(self.back, self.slot_of_pos, weights, self.out)
         return self.out
+
+
+class ExpertParallelPeer:
+    """The same layer over NVLink peer memory instead of a collective library.
+
+    Every rank's engine exports an exchange block with CUDA IPC; the blocks
+    are mapped once (handles exchanged with all_gather_object).  A layer call
+    is one engine call: the selections are written straight into the expert
+    owners' receive buffers, the down-projection epilogue writes each output
+    row straight back into the token owner's return buffer, and per-source
+    epoch flags (bounded waits) order the phases.  Requires peer access
+    between the ranks' GPUs.
+    """
+
+    def __init__(self, torch_mod, engine, rank: int, world: int, tokens: int, hidden: int, *,
+                 layer: int = 0, group=None):
+        self.torch = torch_mod
+        self.engine = engine
+        self.layer = layer
+        self.tokens = tokens
+        dist = torch_mod.distributed
+        err = None
+        handle = None
+        try:
+            handle, _ = engine.ep_p2p_init(world, rank, tokens)
+        except Exception as exc:
+            err = f"rank {rank}: {exc}"
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=group)
+        if err is None and all(h is not None for h in handles):
+            try:
+                engine.ep_p2p_connect(handles)
+            except Exception as exc:
+                err = f"rank {rank}: {exc}"
+        elif err is None:
+            err = "a peer could not export its exchange block"
+        # every rank takes the same decision
+        errors = [None] * world
+        dist.all_gather_object(errors, err, group=group)
+        failed = [e for e in errors if e]
+        if failed:
+            raise RuntimeError("NVLink peer path unavailable: " + "; ".join(failed))
+        self.out = torch_mod.empty((tokens, hidden), dtype=torch_mod.float32, device="cuda")
+
+    def forward(self, x, ids, weights):
+        """x FP16 [T, H], ids int32 [T, K] (global), weights FP32 [T, K] ->
+        FP32 [T, H] (an internal buffer, valid until the next call)."""
+        self.engine.ep_p2p_forward_device(self.layer, x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
+                                          self.out.data_ptr(), self.torch.cuda.current_stream())
+        return self.out

@@ -174,6 +174,44 @@ DEE_API int dee_ep_combine_device(dee_engine* engine, const float* d_back,
                                   const int32_t* d_slot_of_pos, const float* d_weights, int tokens,
                                   float* d_out_f32, void* stream);
 
+/* Expert parallelism over NVLink peer memory (same split and results as the
+ * all-to-all path above, no collective library).  Each rank's engine owns an
+ * exchange block -- receive rows/experts/flags and return rows/flags -- that
+ * the other ranks write directly:
+ *   dispatch: the rank's selections are packed straight into the owners'
+ *             receive buffers, then a per-source epoch flag is raised;
+ *   experts:  a bounded wait for every source's flag, the grouped GEMMs over
+ *             the received rows, whose down-projection epilogue stores each
+ *             FP32 row straight into the token owner's return buffer, then a
+ *             flag per owner;
+ *   combine:  a bounded wait for every owner's flag, the rank-order combine.
+ * All ranks call the phases the same number of times; waits that run out
+ * (2 s) set bit 6 of the device status word and return. */
+#define DEE_EP_IPC_HANDLE_BYTES 64
+
+/* Allocate this rank's exchange block for `tokens` tokens per layer call and
+ * export it: *ipc_handle_out receives DEE_EP_IPC_HANDLE_BYTES (a CUDA IPC
+ * memory handle), *block_out (may be NULL) the block's device address. */
+DEE_API int dee_ep_p2p_init(dee_engine* engine, int ranks, int rank, int tokens,
+                            void* ipc_handle_out, uint64_t* block_out);
+
+/* Map every rank's block: ipc_handles holds ranks x DEE_EP_IPC_HANDLE_BYTES
+ * (rank order); blocks (may be NULL) gives device addresses for ranks that
+ * live in this process on this device, used instead of their handle. */
+DEE_API int dee_ep_p2p_connect(dee_engine* engine, const void* ipc_handles, const uint64_t* blocks);
+
+/* The three phases (device ids [T, K] of global experts, x FP16 [T, H],
+ * weights FP32 [T, K], out FP32 [T, H]); dee_ep_p2p_forward_device runs them
+ * in order.  The dispatched ids are the journal's. */
+DEE_API int dee_ep_p2p_dispatch_device(dee_engine* engine, const void* d_x_f16, const int32_t* d_ids,
+                                       void* stream);
+DEE_API int dee_ep_p2p_experts_device(dee_engine* engine, int layer, void* stream);
+DEE_API int dee_ep_p2p_combine_device(dee_engine* engine, const float* d_weights, float* d_out_f32,
+                                      void* stream);
+DEE_API int dee_ep_p2p_forward_device(dee_engine* engine, int layer, const void* d_x_f16,
+                                      const int32_t* d_ids, const float* d_weights, float* d_out_f32,
+                                      void* stream);
+
 /* Host copy of the int32 [T, K] route ids the last forward consumed -- the
  * buffer the route journal records (deepseek_v4_native_generate.py
  * :2196-2216).  Waits for the last forward's stream, then copies.  Returns

@@ -113,3 +113,53 @@ def test_ep_pack_rejects_bad_arguments(torch_cuda):
     with pytest.raises(dee_b200.DeeError):
         eng.ep_pack_device(d.data_ptr(), 1, x.data_ptr(), 0, EPR, K, d.data_ptr(), d.data_ptr(),
                            d.data_ptr())
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_expert_parallel_peer_emulated_two_ranks(torch_cuda, oracle_mod, T):
+    """The NVLink path with both ranks in this process on one GPU: the blocks
+    are mapped by address, and the phases of the two ranks are interleaved so
+    that each bounded wait finds its flags already raised by earlier kernels
+    on the stream."""
+    torch = torch_cuda
+    orc = oracle_mod
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=313 + T, kind="normal")
+    full = _engine(E)
+    bank_all = torch.from_numpy(recs).cuda()
+    full.attach_bank(0, bank_all)
+    ranks = []
+    for r in range(WORLD):
+        eng = _engine(EPR)
+        bank = torch.from_numpy(np.ascontiguousarray(recs[r * EPR:(r + 1) * EPR])).cuda()
+        eng.attach_bank(0, bank)
+        rng = np.random.default_rng(1700 + 10 * T + r)
+        x16 = orc.f16_bits(rng.standard_normal((T, H)))
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+        w = rng.random((T, K)).astype(np.float32)
+        w /= w.sum(axis=1, keepdims=True)
+        _, block = eng.ep_p2p_init(WORLD, r, T)
+        ranks.append(dict(eng=eng, bank=bank, x16=x16, ids=ids, w=w, block=block,
+                          dx=torch.from_numpy(x16.view(np.float16)).cuda(),
+                          dids=torch.from_numpy(ids).cuda(), dw=torch.from_numpy(w).cuda(),
+                          out=torch.empty((T, H), dtype=torch.float32, device="cuda")))
+    blocks = [rk["block"] for rk in ranks]
+    for rk in ranks:
+        rk["eng"].ep_p2p_connect(None, blocks)
+    for step in range(2):  # two layer calls: the epoch advances
+        for rk in ranks:
+            rk["eng"].ep_p2p_dispatch_device(rk["dx"].data_ptr(), rk["dids"].data_ptr())
+        for rk in ranks:
+            rk["eng"].ep_p2p_experts_device(0)
+        for rk in ranks:
+            rk["eng"].ep_p2p_combine_device(rk["dw"].data_ptr(), rk["out"].data_ptr())
+        torch.cuda.synchronize()
+        for rk in ranks:
+            assert rk["eng"].sync_status() == 0
+            ref = torch.empty((T, H), dtype=torch.float32, device="cuda")
+            full.moe_forward_device(0, rk["dx"].data_ptr(), T, d_ids_ptr=rk["dids"].data_ptr(),
+                                    d_weights_ptr=rk["dw"].data_ptr(), d_out_ptr=ref.data_ptr())
+            torch.cuda.synchronize()
+            got, want = rk["out"].cpu().numpy(), ref.cpu().numpy()
+            assert np.array_equal(got, want), float(np.abs(got - want).max())
+            assert np.array_equal(rk["eng"].journal_ids(T), rk["ids"])
