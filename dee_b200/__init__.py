@@ -61,6 +61,7 @@ class Engine:
         self._h = ctypes.c_void_p()
         self.cfg: EngineConfig | None = None
         self._banks: dict[int, object] = {}
+        self._shared: dict[int, tuple] = {}
 
     # -- lifecycle -------------------------------------------------------
     def init(self, cfg: EngineConfig) -> bool:
@@ -190,6 +191,28 @@ class Engine:
             ctypes.c_void_p(d_weights_ptr or 0), ctypes.c_void_p(d_out_ptr or 0),
             ctypes.c_void_p(d_raw_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_moe_forward_device")
+
+    # -- official DeepSeek-V4 semantics ---------------------------------------
+    def attach_shared_expert(self, layer: int, w1, w1_scale, w3, w3_scale, w2, w2_scale) -> None:
+        """Device tensors: F8_E4M3 (uint8 view) W1, W3 [inter, H], W2 [H, inter]
+        and their E8M0 scale bytes [ceil(rows/128), ceil(cols/128)].  The
+        tensors must stay alive while the engine uses them."""
+        inter = int(w1.shape[0])
+        rc = self._lib.dee_shared_expert_attach(
+            self._h, layer, ctypes.c_void_p(w1.data_ptr()), ctypes.c_void_p(w1_scale.data_ptr()),
+            ctypes.c_void_p(w3.data_ptr()), ctypes.c_void_p(w3_scale.data_ptr()),
+            ctypes.c_void_p(w2.data_ptr()), ctypes.c_void_p(w2_scale.data_ptr()), inter)
+        self._check(rc, "dee_shared_expert_attach")
+        self._shared[layer] = (w1, w1_scale, w3, w3_scale, w2, w2_scale)  # keep the storage alive
+
+    def moe_forward_official_device(self, layer: int, d_x_ptr: int, tokens: int, d_ids_ptr: int,
+                                    d_weights_ptr: int, d_out_ptr: int, d_shared_out_ptr: int = 0,
+                                    stream=None) -> None:
+        rc = self._lib.dee_moe_forward_official_device(
+            self._h, layer, ctypes.c_void_p(d_x_ptr), tokens, ctypes.c_void_p(d_ids_ptr),
+            ctypes.c_void_p(d_weights_ptr), ctypes.c_void_p(d_out_ptr),
+            ctypes.c_void_p(d_shared_out_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_moe_forward_official_device")
 
     # -- expert parallelism (see dee_b200.ep for the whole layer) -----------
     def ep_pack_device(self, d_ids_ptr: int, tokens: int, d_x_ptr: int, ranks: int,

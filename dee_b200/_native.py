@@ -53,6 +53,8 @@ SIGNATURES = {
     "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),
     "dee_moe_forward_combined_device": (I, [P, I, P, I, P, I, P, P, P, P]),
     "dee_moe_forward_device": (I, [P, I, P, I, P, P, I, P, P, P, P]),
+    "dee_shared_expert_attach": (I, [P, I, P, P, P, P, P, P, I]),
+    "dee_moe_forward_official_device": (I, [P, I, P, I, P, P, P, P, P]),
     "dee_ep_pack_device": (I, [P, P, I, P, I, I, I, P, P, P, P]),
     "dee_moe_forward_rows_device": (I, [P, I, P, P, I, P, P]),
     "dee_ep_combine_device": (I, [P, P, P, P, I, P, P]),

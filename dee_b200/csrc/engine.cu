@@ -65,6 +65,11 @@ struct Bank {
     int32_t* d_slot_of = nullptr;  // [E]
     CUtensorMap w1, w3, w2, s1, s3, s2;  // tcgen05 kernel
     GemmMaps dec_gu{}, dec_dn{};         // decode kernel (weight maps)
+    // the layer's shared expert (F8_E4M3 + E8M0 per 128 x 128), if attached
+    bool shared = false;
+    int shared_inter = 0;
+    const uint8_t *sh_s1 = nullptr, *sh_s3 = nullptr, *sh_s2 = nullptr;
+    CUtensorMap sh_m1, sh_m3, sh_m2;
 };
 
 template <class T>
@@ -118,6 +123,11 @@ struct dee_engine {
     float* d_raw = nullptr;
     int32_t* h_ids = nullptr;      // pinned staging of host-given ids
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
+    // shared-expert workspaces, capacity in tokens
+    size_t cap_sh = 0;
+    int cap_sh_inter = 0;
+    __half* d_sh_act = nullptr;
+    float* d_sh_out = nullptr;
     cudaStream_t journal_stream = nullptr;
     size_t h_ids_count = 0;
     CUtensorMap map_xperm, map_act;      // 16-row token boxes (tcgen05 kernel)
@@ -276,7 +286,7 @@ struct EpReturn {
 
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
-                const EpReturn* ret = nullptr) {
+                const EpReturn* ret = nullptr, const float* official_route_w = nullptr) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -320,6 +330,10 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.act = e->d_act;
     a.raw = raw;
     a.status = e->d_status;
+    if (official_route_w) {
+        a.official = 1;
+        a.route_w = official_route_w;
+    }
     if (ret) {
         a.raw_peers = ret->raw_peers;
         a.ep_capacity = ret->capacity;
@@ -408,6 +422,8 @@ void dee_engine_destroy(dee_engine* e) {
     cudaSetDevice(e->cfg.device_id);
     if (e->stream) cudaStreamSynchronize(e->stream);
     free_workspace(e);
+    cudaFree(e->d_sh_act);
+    cudaFree(e->d_sh_out);
     for (void* p : e->ep.opened) cudaIpcCloseMemHandle(p);
     cudaFree(e->ep.block);
     cudaFree(e->ep.d_back_peers);
@@ -685,6 +701,88 @@ int dee_ep_combine_device(dee_engine* e, const float* d_back, const int32_t* d_s
                                         e->cfg.hidden, d_out, static_cast<cudaStream_t>(stream_v));
     if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
     e->launches += 1;
+    return DEE_OK;
+}
+
+int dee_shared_expert_attach(dee_engine* e, int layer, const void* d_w1, const void* d_w1_scale,
+                             const void* d_w3, const void* d_w3_scale, const void* d_w2,
+                             const void* d_w2_scale, int inter_shared) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    const int H = e->cfg.hidden;
+    if (layer < 0 || layer >= e->cfg.num_layers || !d_w1 || !d_w3 || !d_w2 || !d_w1_scale ||
+        !d_w3_scale || !d_w2_scale || inter_shared <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid shared-expert arguments");
+    if (inter_shared % 256 != 0 || H % 256 != 0)
+        return fail(e, DEE_ERR_UNSUPPORTED, "shared expert needs hidden and inter multiples of 256");
+    for (const void* p : {d_w1, d_w3, d_w2})
+        if (reinterpret_cast<uintptr_t>(p) & 15)
+            return fail(e, DEE_ERR_INVALID, "shared-expert weights must be 16-byte aligned");
+    Bank& b = e->banks[layer];
+    if (!encode_shared_weight_maps(get_encode_fn(), d_w1, d_w3, d_w2, H, inter_shared, &b.sh_m1, &b.sh_m3,
+                                   &b.sh_m2))
+        return fail(e, DEE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the shared expert");
+    b.sh_s1 = static_cast<const uint8_t*>(d_w1_scale);
+    b.sh_s3 = static_cast<const uint8_t*>(d_w3_scale);
+    b.sh_s2 = static_cast<const uint8_t*>(d_w2_scale);
+    b.shared_inter = inter_shared;
+    b.shared = true;
+    return DEE_OK;
+}
+
+int dee_moe_forward_official_device(dee_engine* e, int layer, const void* d_x_f16, int tokens,
+                                    const int32_t* d_ids, const float* d_weights, float* d_out_f32,
+                                    float* d_shared_out, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_x_f16 || tokens <= 0 || !d_ids || !d_weights || !d_out_f32)
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_official_device arguments");
+    if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
+        return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
+    const int K = e->cfg.topk, H = e->cfg.hidden;
+    const size_t sel = static_cast<size_t>(tokens) * K;
+    if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    e->h_ids_count = sel;
+    if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, d_ids, e->d_raw, stream, K,
+                          false, true, nullptr, d_weights)) != DEE_OK)
+        return rc;
+    const Bank& b = e->banks[layer];
+    float* shared_out = nullptr;
+    if (b.shared) {
+        const int Is = b.shared_inter;
+        if (static_cast<size_t>(tokens) > e->cap_sh || Is > e->cap_sh_inter) {
+            cudaError_t err = cudaStreamSynchronize(stream);
+            cudaFree(e->d_sh_act);
+            cudaFree(e->d_sh_out);
+            e->d_sh_act = nullptr;
+            e->d_sh_out = nullptr;
+            e->cap_sh = 0;
+            const size_t cap = ((static_cast<size_t>(tokens) + 63) / 64) * 64;
+            const int ci = Is > e->cap_sh_inter ? Is : e->cap_sh_inter;
+            if (err == cudaSuccess) err = dev_alloc(&e->d_sh_act, cap * ci);
+            if (err == cudaSuccess) err = dev_alloc(&e->d_sh_out, cap * H);
+            if (err != cudaSuccess) return cuda_fail(e, err, "shared-expert workspace");
+            e->cap_sh = cap;
+            e->cap_sh_inter = ci;
+        }
+        CUtensorMap map_x, map_act;
+        if (!encode_decode_token_map(get_encode_fn(), d_x_f16, tokens, H, &map_x, 4) ||
+            !encode_decode_token_map(get_encode_fn(), e->d_sh_act, tokens, Is, &map_act, 4))
+            return fail(e, DEE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the shared-expert tokens");
+        shared_out = d_shared_out ? d_shared_out : e->d_sh_out;
+        cudaError_t err = launch_shared_expert(b.sh_m1, b.sh_m3, b.sh_m2, map_x, map_act, b.sh_s1, b.sh_s3,
+                                               b.sh_s2, tokens, H, Is, e->cfg.swiglu_limit, e->d_sh_act,
+                                               shared_out, e->d_status, e->num_sms, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "shared-expert launch");
+        e->launches += 2;
+    }
+    cudaError_t err = launch_combine_sum(e->d_raw, shared_out, tokens, K, H, d_out_f32, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "official combine launch");
+    e->launches += 1;
+    e->journal_stream = stream;
     return DEE_OK;
 }
 

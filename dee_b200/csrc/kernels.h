@@ -56,9 +56,28 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 // and up) into gu->w0 / gu->w1 and W2 into dn->w0 / dn->w1.
 bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t record_bytes,
                                int n_slots, int hidden, int inter, GemmMaps* gu, GemmMaps* dn);
-// Token-row map of the decode kernel over a [rows, cols] FP16 buffer.
+// Token-row map over a [rows, cols] FP16 buffer: boxes of 8 rows x
+// box_chunks 64-wide column chunks (8 for the decode kernel's 512-wide
+// stages, 4 for the shared expert's 256-wide ones).
 bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
-                             CUtensorMap* map);
+                             CUtensorMap* map, int box_chunks = 8);
+
+// The shared expert (moe_shared.cu): dense F8_E4M3 projections W1, W3
+// [inter, H] and W2 [H, inter] with E8M0 scales per 128 x 128 tile.
+bool encode_shared_weight_maps(EncodeTiledFn fn, const void* w1, const void* w3, const void* w2, int hidden,
+                               int inter, CUtensorMap* m1, CUtensorMap* m3, CUtensorMap* m2);
+// Gate/up + SwiGLU over x (map_x: [T, H], 4-chunk boxes) into act [T, inter],
+// then down (map_act over act) into out [T, H] FP32; official FP32 chain, no
+// routing weight.
+cudaError_t launch_shared_expert(const CUtensorMap& m1, const CUtensorMap& m3, const CUtensorMap& m2,
+                                 const CUtensorMap& map_x, const CUtensorMap& map_act, const uint8_t* s1,
+                                 const uint8_t* s3, const uint8_t* s2, int tokens, int hidden, int inter,
+                                 float swiglu_limit, __half* act, float* out, uint32_t* status, int grid,
+                                 cudaStream_t stream);
+// out[t] = sum_r raw[t*K + r] (rank order, FP32) + shared[t] (if non-null):
+// the official combination of weighted routed outputs and the shared expert.
+cudaError_t launch_combine_sum(const float* raw, const float* shared, int tokens, int topk, int hidden,
+                               float* out, cudaStream_t stream);
 
 // Expert-parallel packing (ep.cu): selections [T, K] of global ids over
 // ranks x experts_per_rank experts -> per destination rank `capacity` slots of

@@ -30,6 +30,7 @@
 // (feature, token) and applies the reference's FP16 SwiGLU chain in
 // registers (swiglu_cuda.cu:46-59).  Down items scatter FP32 rows to
 // raw[token * K + rank] (engine.cpp:1080-1113).
+#include "decode_common.cuh"
 #include "kernels.h"
 
 namespace dee {
@@ -125,33 +126,6 @@ __device__ __forceinline__ uint32_t dequant_f16(uint32_t r, const Scale& s) {
     return static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
 }
 
-__device__ __forceinline__ void mma_16816_acc(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                              uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ void mma_16816_zero(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                               uint32_t a3, uint32_t b0, uint32_t b1) {
-    const float z = 0.0f;
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%10, %10, %10, %10};"
-        : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
-}
-
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ void named_bar_arrive(int id, int threads) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 // Per byte of w: bit 7 of the result is set iff the byte lies in [104, 140]
 // (SWAR: add 24 to every byte without carries between bytes, then the byte
 // must read 128..164).
@@ -159,30 +133,6 @@ __device__ __forceinline__ uint32_t scale_bytes_exact(uint32_t w) {
     const uint32_t y = ((w & 0x7F7F7F7Fu) + 0x18181818u) ^ (w & 0x80808080u);
     const uint32_t z = (y & 0x7F7F7F7Fu) + 0x5B5B5B5Bu;
     return y & ~z & 0x80808080u;
-}
-
-__device__ __forceinline__ uint32_t lds_u32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ uint2 lds_v2(uint32_t addr) {
-    uint2 v;
-    asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ uint4 lds_v4(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(addr));
-    return v;
-}
-
-__device__ __forceinline__ float silu_ref(float g) {
-    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
 }
 
 struct DecItem {
@@ -217,7 +167,7 @@ struct ItemRec {
     int m, row_start, n_rows, valid;
 };
 
-template <GemmMode MODE>
+template <GemmMode MODE, bool kOfficial>
 __global__ void __launch_bounds__(kDecThreads, 1)
     moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
                       const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
@@ -431,7 +381,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         float c[4] = {0.f, 0.f, 0.f, 0.f};
         bool ok = mbar_wait(&sready[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
         ok = __all_sync(0xffffffffu, ok);
-        const bool fast = ok && fast_flag[slot] != 0;
+        // official semantics dequantise in FP32: the scaled FP32 partial sum
+        // is exact for every scale byte
+        const bool fast = ok && (kOfficial || fast_flag[slot] != 0);
         const int it_m = item_rec[slot].m;
         const int it_row_start = item_rec[slot].row_start;
         const int it_n_rows = item_rec[slot].n_rows;
@@ -460,8 +412,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     mma_16816_acc(t, a[2], a[6], a[3], a[7], bv.z, bv.w);
                     const uint32_t sl = ((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu;
                     const uint32_t sh = ((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu;
-                    const float flo = __uint_as_float(sl << 23);
-                    const float fhi = __uint_as_float(sh << 23);
+                    const float flo = kOfficial ? e8m0_value(sl) : __uint_as_float(sl << 23);
+                    const float fhi = kOfficial ? e8m0_value(sh) : __uint_as_float(sh << 23);
                     c[0] = fmaf(flo, t[0], c[0]);
                     c[1] = fmaf(flo, t[1], c[1]);
                     c[2] = fmaf(fhi, t[2], c[2]);
@@ -527,15 +479,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                float gv = __half2float(__float2half_rn(c[h]));
-                float uv = __half2float(__float2half_rn(c[2 + h]));
-                if (lim > 0.0f) {
-                    gv = fminf(gv, lim);
-                    uv = fminf(fmaxf(uv, -lim), lim);
-                }
-                const __half sv = __float2half_rn(silu_ref(gv));
+                const float w = (kOfficial && args.route_w) ? args.route_w[args.perm[it_row_start + n]] : 1.0f;
                 args.act[static_cast<size_t>(it_row_start + n) * args.inter + feat] =
-                    __float2half_rn(__fmul_rn(__half2float(sv), uv));
+                    swiglu_out(c[h], c[2 + h], lim, kOfficial, w);
             }
         } else {
             const int f_lo = it_m * 128 + 16 * cw + g;
@@ -560,9 +506,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
 }
 
-template <GemmMode MODE>
+template <GemmMode MODE, bool kOfficial>
 cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
-    auto kern = moe_decode_kernel<MODE>;
+    auto kern = moe_decode_kernel<MODE, kOfficial>;
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -608,14 +554,14 @@ bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t rec
 }
 
 // Token rows [rows, cols] FP16 viewed as {64, rows, cols/64 chunks} (chunk
-// stride 128 B): one box {64, 8, 8} is the 8 rows of a tile over a 512-wide
+// stride 128 B): one box {64, 8, box_chunks} is the 8 rows of a tile over a
 // stage, landing as [chunk][row][128 B] with the 128-byte swizzle.
 bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
-                             CUtensorMap* map) {
+                             CUtensorMap* map, int box_chunks) {
     if (!fn) return false;
     const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols / 64)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, 128};
-    const cuuint32_t box[3] = {64, 8, 8};
+    const cuuint32_t box[3] = {64, 8, static_cast<cuuint32_t>(box_chunks)};
     const cuuint32_t elem[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(rows_base), dims, strides, box,
               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -624,8 +570,11 @@ bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, 
 
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream) {
-    return gate_up ? launch_dec<GemmMode::kGateUp>(maps, args, grid, stream)
-                   : launch_dec<GemmMode::kDown>(maps, args, grid, stream);
+    if (args.official)
+        return gate_up ? launch_dec<GemmMode::kGateUp, true>(maps, args, grid, stream)
+                       : launch_dec<GemmMode::kDown, true>(maps, args, grid, stream);
+    return gate_up ? launch_dec<GemmMode::kGateUp, false>(maps, args, grid, stream)
+                   : launch_dec<GemmMode::kDown, false>(maps, args, grid, stream);
 }
 
 }  // namespace dee

@@ -1,5 +1,6 @@
 // moe_gemm.cu -- the grouped tcgen05 W4A16 kernels (see moe_gemm.cuh).
 #include "moe_gemm.cuh"
+#include "decode_common.cuh"
 #include "kernels.h"
 
 #include <cstdio>
@@ -69,10 +70,6 @@ __device__ __forceinline__ void dequant_block32(const uint4& q, uint32_t sbyte, 
     }
 }
 
-__device__ __forceinline__ float silu_ref(float g) {
-    // swiglu_activation_batch_fp16_kernel: g / (1 + expf(-g)), IEEE divide.
-    return __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-}
 
 struct ItemInfo {
     int tile;
@@ -402,15 +399,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         if ((i & 1) != (is_gate ? 0 : 1)) continue;
                         const int col = c + i;
                         if (col >= n_rows) continue;
-                        float g = __half2float(__float2half_rn(is_gate ? mine : other));
-                        float u = __half2float(__float2half_rn(is_gate ? other : mine));
-                        if (lim > 0.0f) {
-                            g = fminf(g, lim);
-                            u = fminf(fmaxf(u, -lim), lim);
-                        }
-                        const __half s = __float2half_rn(silu_ref(g));
-                        const __half a = __float2half_rn(__fmul_rn(__half2float(s), u));
-                        args.act[static_cast<size_t>(it.td.row_start + col) * args.inter + feat] = a;
+                        const float w = (args.official && args.route_w)
+                                            ? args.route_w[args.perm[it.td.row_start + col]]
+                                            : 1.0f;
+                        args.act[static_cast<size_t>(it.td.row_start + col) * args.inter + feat] =
+                            swiglu_out(is_gate ? mine : other, is_gate ? other : mine, lim,
+                                       args.official != 0, w);
                     }
                 } else {
                     const int feat = it.m * 128 + L;

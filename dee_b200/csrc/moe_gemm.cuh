@@ -70,6 +70,11 @@ struct GemmArgs {
     float* const* raw_peers;  // device array [ranks] of peer pointers, or null
     int ep_capacity;
     int ep_rank;
+    // Official semantics (deepseek_v4_moe_reference.py:87-110): the gate/up
+    // epilogue keeps the FP32 chain and multiplies by route_w[position]
+    // (route_w null: weight 1, the shared expert); weights dequantise in FP32.
+    int official;
+    const float* route_w;
 };
 
 constexpr int kGemmThreads = 480;     // 15 warps

@@ -425,6 +425,37 @@ __global__ void combine_f16_kernel(const float* __restrict__ raw, const float* _
     }
 }
 
+// The official combination (deepseek_v4_moe_reference.py:186-194): routed
+// outputs already carry their weights; out = their sum, then + the shared
+// expert.  Rank order, FP32.
+__global__ void combine_sum_kernel(const float* __restrict__ raw, const float* __restrict__ shared,
+                                   int tokens, int topk, int hidden, float* __restrict__ out) {
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const size_t t = (i * 4) / hidden;
+        const size_t h = i * 4 - t * hidden;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < topk; ++r) {
+            const float4 v = *reinterpret_cast<const float4*>(raw + (t * topk + r) * hidden + h);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (shared) {
+            const float4 v = *reinterpret_cast<const float4*>(shared + t * hidden + h);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        *reinterpret_cast<float4*>(out + t * hidden + h) = acc;
+    }
+}
+
 __global__ void ids_i64_to_i32_kernel(const int64_t* __restrict__ src, int n, int experts,
                                       int32_t* __restrict__ dst, uint32_t* status) {
     sm100::pdl_wait();
@@ -519,6 +550,14 @@ cudaError_t launch_combine_f16_i32(const float* raw, const float* weights, const
     const size_t n = static_cast<size_t>(tokens) * hidden;
     return launch_pdl(combine_f16_kernel<int32_t>, dim3(grid_for(n, 256, 148 * 16)), dim3(256), 0,
                       stream, raw, weights, ids, tokens, topk, hidden, out);
+}
+
+cudaError_t launch_combine_sum(const float* raw, const float* shared, int tokens, int topk, int hidden,
+                               float* out, cudaStream_t stream) {
+    if (hidden % 4 != 0) return cudaErrorInvalidValue;
+    const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
+    return launch_pdl(combine_sum_kernel, dim3(grid_for(n4, 256, 148 * 4)), dim3(256), 0, stream, raw,
+                      shared, tokens, topk, hidden, out);
 }
 
 cudaError_t launch_ids_i64_to_i32(const int64_t* src, int n, int experts, int32_t* dst,

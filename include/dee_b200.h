@@ -133,6 +133,31 @@ DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_
  * invalid expert id, a router failure or a pipeline timeout. */
 DEE_API int dee_engine_sync_status(dee_engine* engine, void* stream, uint32_t* status_out);
 
+/* The official DeepSeek-V4 MoE FFN semantics
+ * (dee.cpp/scripts/deepseek_v4_moe_reference.py:87-203): each routed expert
+ * runs the FP32 SwiGLU chain (clamp = the engine's swiglu_limit, 10 in the
+ * official model) with the routing weight applied to the intermediate BEFORE
+ * w2; the layer's shared expert (dense F8_E4M3 weights, F8_E8M0 scales per
+ * 128 x 128 tile, no routing weight) is added; the sum is FP32.  The MMA
+ * operands are FP16 (x, the weighted intermediate); weights dequantise
+ * exactly.
+ *
+ * Attach the shared expert of `layer`: device F8_E4M3 W1, W3 [inter, H] and
+ * W2 [H, inter] (row-major, 16-byte aligned) and their E8M0 scale bytes
+ * [ceil(rows/128), ceil(cols/128)] (the official shared_experts tensors;
+ * moe_reference.py:35-84).  inter and H must be multiples of 256. */
+DEE_API int dee_shared_expert_attach(dee_engine* engine, int layer, const void* d_w1,
+                                     const void* d_w1_scale, const void* d_w3, const void* d_w3_scale,
+                                     const void* d_w2, const void* d_w2_scale, int inter_shared);
+
+/* One layer with the official semantics: x FP16 [T, H], device ids [T, K]
+ * (global), routing weights FP32 [T, K] -> d_out_f32 [T, H] = sum of weighted
+ * routed outputs + shared expert.  d_shared_out (may be NULL) receives the
+ * shared expert's FP32 [T, H] output. */
+DEE_API int dee_moe_forward_official_device(dee_engine* engine, int layer, const void* d_x_f16,
+                                            int tokens, const int32_t* d_ids, const float* d_weights,
+                                            float* d_out_f32, float* d_shared_out, void* stream);
+
 /* Expert parallelism over `ranks` GPUs (no counterpart in the reference's
  * engine, which runs one GPU; the split follows the official DeepSeek-V4
  * convention that rank r owns experts [r*epr, (r+1)*epr),

@@ -322,3 +322,94 @@ def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
     b = np.asarray(b, dtype=np.float64)
     den = np.linalg.norm(b.ravel())
     return float(np.linalg.norm((a - b).ravel()) / (den if den > 0 else 1.0))
+
+
+# ---------------------------------------------------------------------------
+# Official DeepSeek-V4 MoE semantics (FP32), numpy restatement of
+# dee.cpp/scripts/deepseek_v4_moe_reference.py:35-203
+# ---------------------------------------------------------------------------
+
+_FP4_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0,
+                        -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0], dtype=np.float32)
+
+
+def e8m0_f32(b: np.ndarray) -> np.ndarray:
+    """2^(b - 127) in FP32 for every byte (decode_e8m0,
+    deepseek_v4_expert_reference.py:49-62)."""
+    with np.errstate(over="ignore"):
+        return np.float32(2.0) ** (np.asarray(b, dtype=np.float32) - np.float32(127.0))
+
+
+def e4m3_table() -> np.ndarray:
+    """The 256 F8_E4M3 (fn) values: 1 sign, 4 exponent (bias 7), 3 mantissa
+    bits, subnormals, 0x7F/0xFF NaN, no infinities."""
+    b = np.arange(256)
+    sign = np.where(b & 0x80, -1.0, 1.0)
+    e = (b >> 3) & 0xF
+    m = b & 7
+    val = np.where(e == 0, m / 8.0 * 2.0 ** -6, (1.0 + m / 8.0) * 2.0 ** (e - 7.0))
+    val = sign * val
+    val[(e == 15) & (m == 7)] = np.nan
+    return val.astype(np.float32)
+
+
+def dequant_fp4_f32(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """Packed E2M1 [out, in/2] (low nibble first) x UE8M0 per 32 -> FP32 [out, in]
+    (dequantize_expert_weight, deepseek_v4_expert_reference.py:85-99)."""
+    p = np.asarray(packed, dtype=np.uint8)
+    vals = np.empty((p.shape[0], p.shape[1] * 2), dtype=np.float32)
+    vals[:, 0::2] = _FP4_VALUES[p & 0x0F]
+    vals[:, 1::2] = _FP4_VALUES[p >> 4]
+    return vals * np.repeat(e8m0_f32(scale), 32, axis=1)
+
+
+def dequant_fp8_f32(w: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """F8_E4M3 [out, in] x E8M0 per 128 x 128 tile -> FP32 (dequantize_fp8_e4m3,
+    deepseek_v4_moe_reference.py:35-58)."""
+    v = e4m3_table()[np.asarray(w, dtype=np.uint8)]
+    s = np.repeat(np.repeat(e8m0_f32(scale), 128, axis=0), 128, axis=1)[: v.shape[0], : v.shape[1]]
+    return v * s
+
+
+def _silu(g: np.ndarray) -> np.ndarray:
+    return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+
+
+def _swiglu_f32(x, w1, w3, limit):
+    gate = x @ w1.T
+    up = x @ w3.T
+    if limit > 0:
+        gate = np.minimum(gate, np.float32(limit))
+        up = np.clip(up, np.float32(-limit), np.float32(limit))
+    return (_silu(gate) * up).astype(np.float32)
+
+
+def official_layer(records: np.ndarray, layout: Layout, x: np.ndarray, ids: np.ndarray,
+                   weights: np.ndarray, shared: dict | None = None,
+                   swiglu_limit: float = 10.0) -> tuple[np.ndarray, np.ndarray]:
+    """FP32 moe_layer_forward (deepseek_v4_moe_reference.py:113-203) given the
+    route: each selection's expert with the weight applied to the
+    intermediate before w2, summed, plus the shared expert (keys w1, s1, w3,
+    s3, w2, s2: F8_E4M3 bytes and E8M0 scales).  Returns (moe, shared_out)."""
+    x = np.asarray(x, dtype=np.float32)
+    T, K = ids.shape
+    moe = np.zeros((T, x.shape[1]), dtype=np.float32)
+    cache = {}
+    for t in range(T):
+        for r in range(K):
+            e = int(ids[t, r])
+            if e not in cache:
+                parts = split_record(layout, records[e])
+                cache[e] = (dequant_fp4_f32(parts["w1.weight"], parts["w1.scale"]),
+                            dequant_fp4_f32(parts["w3.weight"], parts["w3.scale"]),
+                            dequant_fp4_f32(parts["w2.weight"], parts["w2.scale"]))
+            w1, w3, w2 = cache[e]
+            h = _swiglu_f32(x[t:t + 1], w1, w3, swiglu_limit) * np.float32(weights[t, r])
+            moe[t] += (h @ w2.T)[0]
+    sh = np.zeros_like(moe)
+    if shared is not None:
+        w1 = dequant_fp8_f32(shared["w1"], shared["s1"])
+        w3 = dequant_fp8_f32(shared["w3"], shared["s3"])
+        w2 = dequant_fp8_f32(shared["w2"], shared["s2"])
+        sh = (_swiglu_f32(x, w1, w3, swiglu_limit) @ w2.T).astype(np.float32)
+    return (moe + sh).astype(np.float32), sh

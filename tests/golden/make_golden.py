@@ -22,6 +22,9 @@ sha256 before use.
 * ``moe_layer.npz`` -- ``moe_layer_forward`` (deepseek_v4_moe_reference.py
                      :113-203): the official sqrt-softplus router with bias,
                      top-6, weights, and the layer output (no shared expert).
+* ``official.npz`` -- ``moe_layer_forward`` with a shared expert (F8_E4M3
+                     weights, E8M0 scales per 128 x 128 tile): routed outputs
+                     weighted before w2, clamp 10, shared output added.
 * ``journal.jsonl`` -- ``RoutedExpertJournal`` (kaggle/deepseek-v4-flash-0731/
                      deepseek_v4_native_generate.py:452-622) for two forwards
                      of three layers with fixed route ids.
@@ -126,6 +129,37 @@ def make_moe_layer() -> None:
                         moe_output=res["moe_output"].numpy())
 
 
+def make_official() -> None:
+    """The official layer with a shared expert, at shapes the kernels take."""
+    layout = orc.Layout(512, 512)
+    E = 16
+    recs = orc.synthetic_records(layout, E, seed=606, kind="normal")
+    rng = np.random.default_rng(607)
+    g = torch.Generator().manual_seed(608)
+    x = rng.standard_normal((5, 512)).astype(np.float16).astype(np.float32)
+    gate_w = (rng.standard_normal((E, 512)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+    shared = {}
+    for name, (rows, cols) in (("w1", (256, 512)), ("w3", (256, 512)), ("w2", (512, 256))):
+        w8 = (torch.randn(rows, cols, generator=g) * 2.0).to(torch.float8_e4m3fn)
+        sc = torch.randint(0x76, 0x7B, ((rows + 127) // 128, (cols + 127) // 128), generator=g,
+                           dtype=torch.uint8)
+        shared[f"{name}.weight"] = w8
+        shared[f"{name}.scale"] = sc
+    routed = {e: {k: torch.from_numpy(v.copy()) for k, v in orc.split_record(layout, recs[e]).items()}
+              for e in range(E)}
+    res = moe.moe_layer_forward(torch.from_numpy(x), torch.from_numpy(gate_w), torch.from_numpy(bias),
+                                routed, shared, topk=6, route_scale=1.5, score_func="sqrtsoftplus",
+                                swiglu_limit=10.0)
+    np.savez_compressed(
+        HERE / "official.npz", records_seed=606, records_sha256=_sha(recs), x=x,
+        sh_w1=shared["w1.weight"].view(torch.uint8).numpy(), sh_s1=shared["w1.scale"].numpy(),
+        sh_w3=shared["w3.weight"].view(torch.uint8).numpy(), sh_s3=shared["w3.scale"].numpy(),
+        sh_w2=shared["w2.weight"].view(torch.uint8).numpy(), sh_s2=shared["w2.scale"].numpy(),
+        expert_ids=res["expert_ids"].numpy(), routing_weights=res["routing_weights"].numpy(),
+        shared_output=res["shared_output"].numpy(), moe_output=res["moe_output"].numpy())
+
+
 def make_journal() -> None:
     import deepseek_v4_native_generate as gen
     rng = np.random.default_rng(505)
@@ -150,6 +184,7 @@ def main() -> None:
     make_decode()
     make_expert()
     make_moe_layer()
+    make_official()
     make_journal()
     for p in sorted(HERE.iterdir()):
         if p.suffix in (".npz", ".jsonl"):

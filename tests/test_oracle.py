@@ -264,3 +264,26 @@ def test_dsv4_hash_router_matches_reference(oracle_mod):
     ids, w, _ = oracle_mod.route_dsv4(g["logits"], 6, tid2eid=g["tid2eid"], input_ids=g["input_ids"])
     assert np.array_equal(ids, g["hash_ids"].astype(np.int32))
     np.testing.assert_allclose(w, g["hash_weights"], rtol=1e-6)
+
+
+def test_e4m3_table_matches_torch():
+    import torch
+    from oracle import oracle as orc
+    tab = orc.e4m3_table()
+    ref = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(np.isnan(tab), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    assert np.array_equal(tab[ok], ref[ok])
+
+
+def test_official_layer_matches_reference_fixture(oracle_mod):
+    """moe_layer_forward of the reference (FP32, weight before w2, clamp 10,
+    F8_E4M3 shared expert) vs the oracle's restatement, same route."""
+    orc = oracle_mod
+    g = _load("official.npz")
+    layout = orc.Layout(512, 512)
+    recs = _records(orc, layout, 16, g["records_seed"], g["records_sha256"])
+    shared = {k: g["sh_" + k] for k in ("w1", "s1", "w3", "s3", "w2", "s2")}
+    moe, sh = orc.official_layer(recs, layout, g["x"], g["expert_ids"], g["routing_weights"], shared, 10.0)
+    assert orc.rel_l2(sh, g["shared_output"]) < 1e-5
+    assert orc.rel_l2(moe, g["moe_output"]) < 1e-5
