@@ -55,6 +55,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
                     help="multi-GPU transport: NVLink peer memory (default) or NCCL all-to-all")
+    ap.add_argument("--workload", default="layer", choices=["layer", "stack"],
+                    help="layer: the one-layer headline (configs 1-2); stack: the synthetic "
+                         "multi-layer greedy decode (config 3)")
+    ap.add_argument("--layers", type=int, default=43, help="stack layers (--workload stack)")
     ap.add_argument("--experts", type=int, default=E,
                     help="experts in the bank (smaller values only for profiling captures)")
     return ap.parse_args()
@@ -409,10 +413,109 @@ def run_reference(args):
 
 # ---------------------------------------------------------------------------
 
+def run_stack(args):
+    """Config 3: greedy decode of b sequences through the synthetic L-layer
+    stack (dee_b200.stack), expert parallel over the launched ranks.  Times
+    `steps` decode steps (CUDA events, max over ranks), then repeats the same
+    decode with the route ids and tokens logged and reports the sha256 of
+    the route journal and of the tokens, which must not depend on N."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from dee_b200.stack import StackSpec, SyntheticStack, journal_bytes, seed_tokens, sha256
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    b = args.batch
+    if b % world:
+        raise SystemExit(f"batch {b} does not split over {world} ranks")
+    t_local = b // world
+    spec = StackSpec(layers=args.layers, experts=args.experts, hidden=H, inter=I, topk=K)
+    t0 = time.perf_counter()
+    stack = SyntheticStack(torch, spec, tokens=t_local, rank=rank, world=world, transport=args.ep)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    first = torch.from_numpy(seed_tokens(spec, b)[rank * t_local:(rank + 1) * t_local]).cuda()
+    stream = torch.cuda.Stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        stack.decode(first, args.warmup)
+    torch.cuda.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            stack.decode(first, args.steps)
+            ev1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # the same decode again, logged
+    ids_log = torch.empty((args.steps, spec.layers, t_local, K), dtype=torch.int32, device="cuda")
+    tok_log = torch.empty((args.steps, t_local), dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        stack.decode(first, args.steps, ids_log, tok_log)
+    torch.cuda.synchronize()
+    status = stack.engine.sync_status() | stack.router.sync_status()
+    if world > 1:
+        parts_i = [torch.empty_like(ids_log) for _ in range(world)]
+        parts_t = [torch.empty_like(tok_log) for _ in range(world)]
+        dist.all_gather(parts_i, ids_log)
+        dist.all_gather(parts_t, tok_log)
+        ids_all = torch.cat(parts_i, dim=2)
+        toks = torch.cat(parts_t, dim=1)
+        st_t = torch.tensor([status], device="cuda", dtype=torch.int64)
+        dist.all_reduce(st_t, op=dist.ReduceOp.MAX)
+        status = int(st_t.item())
+    else:
+        ids_all, toks = ids_log, tok_log
+    result = None
+    if rank == 0:
+        ids_np = ids_all.cpu().numpy()
+        journal = journal_bytes(ids_np, run_id="dee-b200-stack")
+        result = {
+            "metric": f"stack tokens/s ({spec.layers}-layer synthetic DSv4 MoE stack, greedy decode b={b})",
+            "value": b * args.steps / (ms / 1000.0), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg3-stack{spec.layers}-b{b}", "layers": spec.layers, "hidden": H,
+                       "inter": I, "experts": spec.experts, "topk": K, "vocab": spec.vocab, "batch": b,
+                       "parallelism": f"ep{world}-{stack.transport}" if world > 1 else "single",
+                       "expert_bytes_per_gpu": int(sum(x.numel() for x in stack.banks)),
+                       "build_seconds": build_s},
+            "route_journal_sha256": sha256(journal), "journal_lines": journal.count(b"\n"),
+            "tokens_sha256": sha256(toks.cpu().numpy().tobytes()), "device_status": status,
+            "clocks": clk.summary(),
+        }
+    if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result))
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "stack":
+        run_stack(args)
         return
     import torch
     import torch.distributed as dist
@@ -441,7 +544,7 @@ def main():
         if E % world:
             raise SystemExit(f"--experts {E} is not divisible by {world} ranks")
         epr = E // world
-        bank = synthetic_bank(RecordLayout(H, I), epr, seed=11 + rank)
+        bank = synthetic_bank(RecordLayout(H, I), epr, seed=11, first_expert=rank * epr)
         eng = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=epr, topk=K,
                                                         max_tokens=64, device_id=local))
         eng.attach_bank(0, bank)

@@ -64,6 +64,12 @@ SIGNATURES = {
     "dee_ep_p2p_experts_device": (I, [P, I, P]),
     "dee_ep_p2p_combine_device": (I, [P, P, P, P]),
     "dee_ep_p2p_forward_device": (I, [P, I, P, P, P, P, P]),
+    "dee_stack_embed_device": (I, [P, P, P, I, I, P, P]),
+    "dee_stack_rmsnorm_device": (I, [P, P, P, ctypes.c_float, I, P, P]),
+    "dee_stack_router_logits_device": (I, [P, P, P, I, I, P, P]),
+    "dee_stack_residual_add_device": (I, [P, P, P, I, P]),
+    "dee_stack_lm_head_argmax_device": (I, [P, P, P, I, I, P, P, P]),
+    "dee_records_scramble_device": (I, [P, P, I, SZ, SZ, ctypes.c_uint64, I, P]),
     "dee_engine_sync_status": (I, [P, P, U32P]),
     "dee_journal_ids_host": (I, [P, P, I]),
     "dee_fp4_decode_device": (I, [P, P, P, SZ, SZ, P]),

@@ -930,6 +930,70 @@ int dee_ep_p2p_forward_device(dee_engine* e, int layer, const void* d_x_f16, con
     return rc;
 }
 
+int dee_stack_embed_device(dee_engine* e, const void* d_table_f16, const int32_t* d_ids, int tokens,
+                           int vocab, float* d_x, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_table_f16 || !d_ids || !d_x || tokens <= 0 || vocab <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid stack_embed arguments");
+    cudaError_t err = launch_stack_embed(static_cast<const __half*>(d_table_f16), d_ids, tokens, e->cfg.hidden,
+                                         vocab, d_x, e->d_status, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : cuda_fail(e, err, "stack_embed launch");
+}
+
+int dee_stack_rmsnorm_device(dee_engine* e, const float* d_x, const float* d_w, float eps, int tokens,
+                             void* d_y_f16, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_x || !d_w || !d_y_f16 || tokens <= 0) return fail(e, DEE_ERR_INVALID, "invalid stack_rmsnorm arguments");
+    cudaError_t err = launch_stack_rmsnorm(d_x, d_w, eps, tokens, e->cfg.hidden, static_cast<__half*>(d_y_f16),
+                                           static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : cuda_fail(e, err, "stack_rmsnorm launch");
+}
+
+int dee_stack_router_logits_device(dee_engine* e, const void* d_h_f16, const float* d_wr, int tokens,
+                                   int experts, float* d_logits, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_h_f16 || !d_wr || !d_logits || tokens <= 0 || experts <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid stack_router_logits arguments");
+    cudaError_t err = launch_stack_rowdot_f32(static_cast<const __half*>(d_h_f16), d_wr, tokens, e->cfg.hidden,
+                                              experts, d_logits, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : cuda_fail(e, err, "stack_router_logits launch");
+}
+
+int dee_stack_residual_add_device(dee_engine* e, float* d_x, const float* d_y, int tokens, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_x || !d_y || tokens <= 0) return fail(e, DEE_ERR_INVALID, "invalid stack_residual_add arguments");
+    cudaError_t err = launch_stack_residual_add(d_x, d_y, static_cast<size_t>(tokens) * e->cfg.hidden,
+                                                static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : cuda_fail(e, err, "stack_residual_add launch");
+}
+
+int dee_stack_lm_head_argmax_device(dee_engine* e, const void* d_h_f16, const void* d_w_f16, int tokens,
+                                    int vocab, float* d_logits, int32_t* d_ids_out, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_h_f16 || !d_w_f16 || !d_logits || !d_ids_out || tokens <= 0 || vocab <= 0)
+        return fail(e, DEE_ERR_INVALID, "invalid stack_lm_head_argmax arguments");
+    auto s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = launch_stack_rowdot_f16(static_cast<const __half*>(d_h_f16),
+                                              static_cast<const __half*>(d_w_f16), tokens, e->cfg.hidden, vocab,
+                                              d_logits, s);
+    if (err == cudaSuccess) err = launch_stack_argmax(d_logits, tokens, vocab, d_ids_out, s);
+    return err == cudaSuccess ? DEE_OK : cuda_fail(e, err, "stack_lm_head_argmax launch");
+}
+
+int dee_records_scramble_device(const void* d_src, void* d_dst, int records, size_t record_bytes,
+                                size_t packed_bytes, uint64_t seed, int first_record, void* stream) {
+    if (!d_src || !d_dst || records <= 0 || packed_bytes > record_bytes) return DEE_ERR_INVALID;
+    cudaError_t err = launch_records_scramble(static_cast<const uint8_t*>(d_src), static_cast<uint8_t*>(d_dst),
+                                              records, record_bytes, packed_bytes, seed, first_record,
+                                              static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : DEE_ERR_CUDA;
+}
+
 int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
     int rc = check_engine(e);
     if (rc != DEE_OK) return rc;

@@ -115,6 +115,21 @@ cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int ran
 cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
                            uint32_t code, cudaStream_t stream);
 
+// The synthetic stack's dense glue (stack.cu), every per-token result in a
+// fixed order independent of the batch.
+cudaError_t launch_stack_embed(const __half* table, const int32_t* ids, int tokens, int hidden, int vocab,
+                               float* x, uint32_t* status, cudaStream_t stream);
+cudaError_t launch_stack_rmsnorm(const float* x, const float* w, float eps, int tokens, int hidden, __half* y,
+                                 cudaStream_t stream);
+cudaError_t launch_stack_rowdot_f32(const __half* x, const float* w, int tokens, int hidden, int rows,
+                                    float* out, cudaStream_t stream);
+cudaError_t launch_stack_rowdot_f16(const __half* x, const __half* w, int tokens, int hidden, int rows,
+                                    float* out, cudaStream_t stream);
+cudaError_t launch_stack_residual_add(float* x, const float* y, size_t n, cudaStream_t stream);
+cudaError_t launch_stack_argmax(const float* logits, int tokens, int vocab, int32_t* ids, cudaStream_t stream);
+cudaError_t launch_records_scramble(const uint8_t* src, uint8_t* dst, int records, size_t record_bytes,
+                                    size_t packed_bytes, uint64_t seed, int first_record, cudaStream_t stream);
+
 // Router: logits [T, E] FP32 -> ids [T, K] int32 (rank order), weights [T, K].
 cudaError_t launch_route_topk(const float* logits, int tokens, int experts, int topk,
                               int32_t* ids, float* weights, uint32_t* status, cudaStream_t stream);

@@ -30,7 +30,7 @@ class EpOps:
     """The three device steps of a layer call.
 
     pack(ids, x, send_rows, send_expert, slot_of_pos)
-    compute(recv_rows, recv_expert, raw)
+    compute(recv_rows, recv_expert, raw, layer)
     combine(back, slot_of_pos, weights, out)
     """
 
@@ -39,7 +39,7 @@ class EpOps:
     combine: Callable[..., None]
 
 
-def engine_ops(engine, layer: int, world: int, experts_per_rank: int, capacity: int,
+def engine_ops(engine, world: int, experts_per_rank: int, capacity: int,
                stream_of: Callable[[], Any]) -> EpOps:
     """EpOps over a dee_b200.Engine (device tensors, the current CUDA stream)."""
 
@@ -48,7 +48,7 @@ def engine_ops(engine, layer: int, world: int, experts_per_rank: int, capacity: 
                               capacity, send_rows.data_ptr(), send_expert.data_ptr(),
                               slot_of_pos.data_ptr(), stream_of())
 
-    def compute(recv_rows, recv_expert, raw):
+    def compute(recv_rows, recv_expert, raw, layer):
         engine.moe_forward_rows_device(layer, recv_rows.data_ptr(), recv_expert.data_ptr(),
                                        recv_rows.shape[0], raw.data_ptr(), stream_of())
 
@@ -80,9 +80,10 @@ class ExpertParallelMoE:
             if engine is None:
                 raise ValueError("ExpertParallelMoE needs an engine or explicit ops")
             cuda = torch_mod.cuda
-            ops = engine_ops(engine, layer, world, experts_per_rank, self.capacity,
+            ops = engine_ops(engine, world, experts_per_rank, self.capacity,
                              lambda: cuda.current_stream())
         self.ops = ops
+        self.layer = layer
         n = world * self.capacity
         t = torch_mod
         self.send_rows = t.empty((n, hidden), dtype=t.float16, device=device)
@@ -94,10 +95,11 @@ class ExpertParallelMoE:
         self.back = t.empty((n, hidden), dtype=t.float32, device=device)
         self.out = t.empty((tokens, hidden), dtype=t.float32, device=device)
 
-    def forward(self, x, ids, weights):
+    def forward(self, x, ids, weights, layer: int | None = None):
         """x FP16 [T, H], ids int32 [T, K] (global expert ids), weights FP32
         [T, K] -> FP32 [T, H] (a view of an internal buffer, valid until the
-        next call)."""
+        next call).  `layer` selects the engine's expert bank (default: the
+        constructor's)."""
         shapes_ok = (tuple(ids.shape) == (self.tokens, self.topk) and
                      tuple(x.shape) == (self.tokens, self.hidden))
         if not shapes_ok:
@@ -109,7 +111,7 @@ class ExpertParallelMoE:
         self.dist.all_to_all_single(self.recv_rows.view(i32), self.send_rows.view(i32),
                                     group=self.group)
         self.dist.all_to_all_single(self.recv_expert, self.send_expert, group=self.group)
-        self.ops.compute(self.recv_rows, self.recv_expert, self.raw)
+        self.ops.compute(self.recv_rows, self.recv_expert, self.raw, self.layer if layer is None else layer)
         self.dist.all_to_all_single(self.back, self.raw, group=self.group)
         self.ops.combine(self.back, self.slot_of_pos, weights, self.out)
         return self.out
@@ -157,9 +159,10 @@ class ExpertParallelPeer:
             raise RuntimeError("NVLink peer path unavailable: " + "; ".join(failed))
         self.out = torch_mod.empty((tokens, hidden), dtype=torch_mod.float32, device="cuda")
 
-    def forward(self, x, ids, weights):
+    def forward(self, x, ids, weights, layer: int | None = None):
         """x FP16 [T, H], ids int32 [T, K] (global), weights FP32 [T, K] ->
         FP32 [T, H] (an internal buffer, valid until the next call)."""
-        self.engine.ep_p2p_forward_device(self.layer, x.data_ptr(), ids.data_ptr(), weights.data_ptr(),
-                                          self.out.data_ptr(), self.torch.cuda.current_stream())
+        self.engine.ep_p2p_forward_device(self.layer if layer is None else layer, x.data_ptr(), ids.data_ptr(),
+                                          weights.data_ptr(), self.out.data_ptr(),
+                                          self.torch.cuda.current_stream())
         return self.out

@@ -37,18 +37,20 @@ class RecordLayout:
 
 
 def synthetic_bank(layout: RecordLayout, experts: int, seed: int, std: float = 0.02,
-                   device: str = "cuda"):
-    """[experts, record_bytes] uint8 on the device: N(0, std) weights drawn
-    with torch's seeded generator and packed by the device quantiser."""
+                   device: str = "cuda", first_expert: int = 0):
+    """[experts, record_bytes] uint8 on the device: N(0, std) weights packed by
+    the device quantiser.  Expert first_expert + e draws from its own seeded
+    generator, so a record does not depend on which experts are built with
+    it (a rank of an expert-parallel run builds the same records as one GPU)."""
     import torch
     H, I = layout.hidden, layout.inter
     lib = _native.load()
     bank = torch.empty((experts, layout.bytes), dtype=torch.uint8, device=device)
     gen = torch.Generator(device=device)
-    gen.manual_seed(seed)
     off = layout.offsets
     stream = torch.cuda.current_stream().cuda_stream
     for e in range(experts):
+        gen.manual_seed(seed * 1_000_003 + first_expert + e)
         rec = bank[e]
         for name, (rows, cols) in (("w1", (I, H)), ("w3", (I, H)), ("w2", (H, I))):
             w = torch.randn((rows, cols), generator=gen, device=device, dtype=torch.float32) * std

@@ -237,6 +237,36 @@ DEE_API int dee_ep_p2p_forward_device(dee_engine* engine, int layer, const void*
                                       const int32_t* d_ids, const float* d_weights, float* d_out_f32,
                                       void* stream);
 
+/* The dense glue of the synthetic multi-layer stack that drives the routed
+ * layer end to end (no counterpart in the reference engine; the stack of the
+ * benchmark's configurations 3 and 4: embedding -> [RMSNorm, router, MoE,
+ * residual] x L -> RMSNorm -> LM head argmax).  Every per-token result is
+ * computed in a fixed order independent of the batch, so route ids and
+ * tokens do not depend on how the tokens are spread over GPUs.
+ *   embed:        x FP32 [T, H] = table FP16 [V, H] rows of ids [T]
+ *   rmsnorm:      y FP16 [T, H] = x * rsqrt(mean(x^2) + eps) * w
+ *   router:       logits FP32 [T, E] = y . W_r^T, W_r FP32 [E, H]
+ *   residual_add: x += y (FP32 [T, H])
+ *   lm_head:      ids [T] = argmax_v (y . W^T), W FP16 [V, H], first index on
+ *                 ties; d_logits FP32 [T, V] is scratch */
+DEE_API int dee_stack_embed_device(dee_engine* engine, const void* d_table_f16, const int32_t* d_ids,
+                                   int tokens, int vocab, float* d_x, void* stream);
+DEE_API int dee_stack_rmsnorm_device(dee_engine* engine, const float* d_x, const float* d_w, float eps,
+                                     int tokens, void* d_y_f16, void* stream);
+DEE_API int dee_stack_router_logits_device(dee_engine* engine, const void* d_h_f16, const float* d_wr,
+                                           int tokens, int experts, float* d_logits, void* stream);
+DEE_API int dee_stack_residual_add_device(dee_engine* engine, float* d_x, const float* d_y, int tokens,
+                                          void* stream);
+DEE_API int dee_stack_lm_head_argmax_device(dee_engine* engine, const void* d_h_f16, const void* d_w_f16,
+                                            int tokens, int vocab, float* d_logits, int32_t* d_ids_out,
+                                            void* stream);
+/* Derive a distinct bank: dst record i = src record i with its first
+ * packed_bytes (the packed weights) XORed by a hash of (seed, first_record +
+ * i); scale bytes copied.  Used to give every layer of a synthetic stack its
+ * own experts without quantising each one. */
+DEE_API int dee_records_scramble_device(const void* d_src, void* d_dst, int records, size_t record_bytes,
+                                        size_t packed_bytes, uint64_t seed, int first_record, void* stream);
+
 /* Host copy of the int32 [T, K] route ids the last forward consumed -- the
  * buffer the route journal records (deepseek_v4_native_generate.py
  * :2196-2216).  Waits for the last forward's stream, then copies.  Returns

@@ -52,7 +52,7 @@ def _np_ops(orc, layout, recs_local, capacity):
             sexp[d * capacity + s] = int(e) - d * EPR
             sop[p] = d * capacity + s
 
-    def compute(recv_rows, recv_expert, raw):
+    def compute(recv_rows, recv_expert, raw, layer):
         ex, rw = recv_expert.numpy(), raw.numpy()
         live = np.flatnonzero(ex >= 0)
         if live.size:
