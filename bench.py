@@ -59,6 +59,9 @@ def parse():
                     help="layer: the one-layer headline (configs 1-2); stack: the synthetic "
                          "multi-layer greedy decode (config 3)")
     ap.add_argument("--layers", type=int, default=43, help="stack layers (--workload stack)")
+    ap.add_argument("--offload-gib", type=float, default=0.0,
+                    help="stack with the offload tier (config 4): device pool of this many GiB of expert "
+                         "records, the rest in pinned host memory")
     ap.add_argument("--experts", type=int, default=E,
                     help="experts in the bank (smaller values only for profiling captures)")
     return ap.parse_args()
@@ -436,7 +439,12 @@ def run_stack(args):
     t_local = b // world
     spec = StackSpec(layers=args.layers, experts=args.experts, hidden=H, inter=I, topk=K)
     t0 = time.perf_counter()
-    stack = SyntheticStack(torch, spec, tokens=t_local, rank=rank, world=world, transport=args.ep)
+    slots = 0
+    if args.offload_gib > 0:
+        from dee_b200.records import RecordLayout
+        slots = int(args.offload_gib * (1 << 30)) // RecordLayout(H, I).bytes
+    stack = SyntheticStack(torch, spec, tokens=t_local, rank=rank, world=world, transport=args.ep,
+                           offload_slots=slots)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
     first = torch.from_numpy(seed_tokens(spec, b)[rank * t_local:(rank + 1) * t_local]).cuda()
@@ -451,6 +459,7 @@ def run_stack(args):
     torch.cuda.synchronize()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stats0 = stack.engine.offload_stats() if slots else None
     with ClockSampler(local) as clk:
         with torch.cuda.stream(stream):
             ev0.record(stream)
@@ -459,6 +468,15 @@ def run_stack(args):
         torch.cuda.synchronize()
     barrier()
     ms = ev0.elapsed_time(ev1)
+    offload = None
+    if slots:
+        stats1 = stack.engine.offload_stats()
+        d = {k: stats1[k] - stats0[k] for k in stats1}
+        offload = {"pool_gib": args.offload_gib, "pool_slots": slots,
+                   "host_bytes": int(stack.host.numel()), "cold_reads": d["cold_reads"],
+                   "cold_reads_per_token": d["cold_reads"] / (b * args.steps),
+                   "hit_rate": d["hits"] / max(d["lookups"], 1),
+                   "h2d_gbs": d["bytes"] / (ms / 1000.0) / 1e9, "eviction": "next-use"}
     if world > 1:
         t = torch.tensor([ms], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -492,11 +510,14 @@ def run_stack(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic",
-            "config": {"workload": f"cfg3-stack{spec.layers}-b{b}", "layers": spec.layers, "hidden": H,
+            "config": {"workload": (f"cfg4-offload{args.offload_gib:g}GiB-stack{spec.layers}-b{b}" if slots
+                                    else f"cfg3-stack{spec.layers}-b{b}"),
+                       "layers": spec.layers, "hidden": H,
                        "inter": I, "experts": spec.experts, "topk": K, "vocab": spec.vocab, "batch": b,
                        "parallelism": f"ep{world}-{stack.transport}" if world > 1 else "single",
                        "expert_bytes_per_gpu": int(sum(x.numel() for x in stack.banks)),
                        "build_seconds": build_s},
+            "offload": offload,
             "route_journal_sha256": sha256(journal), "journal_lines": journal.count(b"\n"),
             "tokens_sha256": sha256(toks.cpu().numpy().tobytes()), "device_status": status,
             "clocks": clk.summary(),

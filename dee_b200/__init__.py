@@ -240,6 +240,28 @@ class Engine:
             ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_ep_combine_device")
 
+    # -- offload tier --------------------------------------------------------
+    def offload_attach(self, h_records, layers: int, d_pool, pool_slots: int) -> None:
+        """h_records: pinned host uint8 tensor [layers * E, record_bytes];
+        d_pool: device uint8 tensor [pool_slots, record_bytes]."""
+        rc = self._lib.dee_offload_attach(self._h, ctypes.c_void_p(h_records.data_ptr()),
+                                          int(h_records.shape[-1]), layers, ctypes.c_void_p(d_pool.data_ptr()),
+                                          pool_slots)
+        self._check(rc, "dee_offload_attach")
+        self._offload = (h_records, d_pool)  # keep the storage alive
+
+    def offload_prepare_device(self, layer: int, d_ids_ptr: int, tokens: int, stream=None) -> int:
+        cold = ctypes.c_int(0)
+        rc = self._lib.dee_offload_prepare_device(self._h, layer, ctypes.c_void_p(d_ids_ptr), tokens,
+                                                  ctypes.c_void_p(_stream_handle(stream)), ctypes.byref(cold))
+        self._check(rc, "dee_offload_prepare_device")
+        return cold.value
+
+    def offload_stats(self) -> dict:
+        out = (ctypes.c_uint64 * 4)()
+        self._lib.dee_offload_stats(self._h, out)
+        return {"lookups": out[0], "hits": out[1], "cold_reads": out[2], "bytes": out[3]}
+
     # -- expert parallelism over NVLink peer memory ---------------------------
     def ep_p2p_init(self, ranks: int, rank: int, tokens: int) -> tuple[bytes, int]:
         """Allocate and export this rank's exchange block: (IPC handle, device address)."""

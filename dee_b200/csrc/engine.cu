@@ -19,6 +19,9 @@
 #include <mutex>
 #include <string>
 #include <vector>
+#include <algorithm>
+#include <unordered_map>
+#include <cmath>
 
 namespace dee {
 namespace {
@@ -98,9 +101,73 @@ struct EpP2P {
 };
 }  // namespace dee
 
+namespace dee {
+// Offload tier: every layer's records in pinned host memory, a device pool of
+// slots shared by all layers, and a next-use ranking of the residents.
+//
+// The ranking restates the probabilistic-Belady estimator of the reference
+// (dee.cpp/include/dee/next_use.h:1-160): decode visits the layers in a fixed
+// cycle, an expert of layer L is next needed d = (L - current) mod cycle
+// layer calls from now, and with a per-expert reuse probability p (an
+// exponentially weighted estimate updated at every visit of its layer) its
+// expected next use is d + cycle * (1/p - 1).  The victim is the resident with
+// the largest expectation; experts of the running layer rank below all others.
+struct Offload {
+    bool on = false;
+    const uint8_t* host = nullptr;  // [layers][experts] records, pinned
+    size_t record_bytes = 0;
+    int layers = 0, experts = 0, pool_slots = 0;
+    uint8_t* pool = nullptr;        // device [pool_slots] records
+    std::vector<int64_t> slot_key;  // slot -> layer * experts + expert, -1 free
+    std::vector<int32_t> slot_of;   // [layers * experts] -> slot, -1 absent
+    std::vector<uint32_t> visits;   // per layer
+    struct Stat { double ewma; uint32_t last_visit; };
+    std::unordered_map<int64_t, Stat> stats;
+    std::vector<uint32_t> used_visit;  // per slot: the prepare call that last used it
+    uint32_t calls = 0;
+    int current = 0;
+    double alpha = 0.2, p0 = 0.1, p_floor = 1e-3;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t copied = nullptr;
+    int32_t* h_ids = nullptr;       // pinned staging of a layer's ids
+    size_t h_ids_cap = 0;
+    uint64_t lookups = 0, hits = 0, cold = 0, bytes = 0;
+
+    double probability(int64_t key) const {
+        auto it = stats.find(key);
+        if (it == stats.end()) return p0;
+        const int layer = static_cast<int>(key / experts);
+        int64_t elapsed = static_cast<int64_t>(visits[layer]) - it->second.last_visit;
+        if (layer == current) --elapsed;
+        double p = it->second.ewma;
+        if (elapsed > 0) p *= std::pow(1.0 - alpha, static_cast<double>(elapsed));
+        return std::max(p_floor, std::min(1.0, p));
+    }
+    double victim_rank(int64_t key) const {
+        const int layer = static_cast<int>(key / experts);
+        if (layer == current) return -1.0;  // the running layer leaves last
+        const int d = ((layer - current) % layers + layers) % layers;
+        return d + layers * (1.0 / probability(key) - 1.0);
+    }
+    void on_use(int64_t key) {
+        const int layer = static_cast<int>(key / experts);
+        const uint32_t visit = visits[layer];
+        auto it = stats.find(key);
+        if (it == stats.end()) {
+            stats.emplace(key, Stat{p0 * (1.0 - alpha) + alpha, visit});
+            return;
+        }
+        if (it->second.last_visit == visit) return;
+        it->second.ewma = it->second.ewma * std::pow(1.0 - alpha, visit - it->second.last_visit) + alpha;
+        it->second.last_visit = visit;
+    }
+};
+}  // namespace dee
+
 struct dee_engine {
     dee_config cfg{};
     dee::EpP2P ep;
+    dee::Offload off;
     std::string last_error;
     int num_sms = 148;
     cudaStream_t stream = nullptr;  // the engine's own stream (synchronous API)
@@ -424,6 +491,9 @@ void dee_engine_destroy(dee_engine* e) {
     free_workspace(e);
     cudaFree(e->d_sh_act);
     cudaFree(e->d_sh_out);
+    if (e->off.copy_stream) cudaStreamDestroy(e->off.copy_stream);
+    if (e->off.copied) cudaEventDestroy(e->off.copied);
+    if (e->off.h_ids) cudaFreeHost(e->off.h_ids);
     for (void* p : e->ep.opened) cudaIpcCloseMemHandle(p);
     cudaFree(e->ep.block);
     cudaFree(e->ep.d_back_peers);
@@ -928,6 +998,137 @@ int dee_ep_p2p_forward_device(dee_engine* e, int layer, const void* d_x_f16, con
     if (rc == DEE_OK) rc = dee_ep_p2p_experts_device(e, layer, stream);
     if (rc == DEE_OK) rc = dee_ep_p2p_combine_device(e, d_weights, d_out_f32, stream);
     return rc;
+}
+
+int dee_offload_attach(dee_engine* e, const void* h_records, size_t record_bytes, int layers,
+                       void* d_pool, int pool_slots) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    Offload& o = e->off;
+    const int E = e->cfg.num_experts;
+    if (!h_records || !d_pool || layers <= 0 || layers > e->cfg.num_layers || pool_slots <= 0 || o.on)
+        return fail(e, DEE_ERR_INVALID, "invalid offload_attach arguments (or already attached)");
+    o.host = static_cast<const uint8_t*>(h_records);
+    o.record_bytes = record_bytes;
+    o.layers = layers;
+    o.experts = E;
+    o.pool = static_cast<uint8_t*>(d_pool);
+    o.pool_slots = pool_slots;
+    o.slot_key.assign(static_cast<size_t>(pool_slots), -1);
+    o.used_visit.assign(static_cast<size_t>(pool_slots), 0);
+    o.slot_of.assign(static_cast<size_t>(layers) * E, -1);
+    o.visits.assign(static_cast<size_t>(layers), 0);
+    cudaError_t err = cudaStreamCreateWithFlags(&o.copy_stream, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(&o.copied, cudaEventDisableTiming);
+    if (err != cudaSuccess) return cuda_fail(e, err, "offload streams");
+    for (int l = 0; l < layers; ++l) {
+        std::vector<int32_t> none(static_cast<size_t>(E), -1);
+        if ((rc = dee_expert_bank_attach(e, l, d_pool, pool_slots, record_bytes, none.data())) != DEE_OK)
+            return rc;
+    }
+    o.on = true;
+    return DEE_OK;
+}
+
+int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, int tokens, void* stream_v,
+                               int* cold_out) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    Offload& o = e->off;
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    const int E = o.experts, K = e->cfg.topk;
+    if (!o.on || layer < 0 || layer >= o.layers || !d_ids || tokens <= 0)
+        return fail(e, DEE_ERR_INVALID, "offload_prepare needs an attached offload tier and a layer's ids");
+    const size_t sel = static_cast<size_t>(tokens) * K;
+    if (sel > o.h_ids_cap) {
+        if (o.h_ids) cudaFreeHost(o.h_ids);
+        o.h_ids = nullptr;
+        cudaError_t err = cudaHostAlloc(reinterpret_cast<void**>(&o.h_ids), sel * sizeof(int32_t),
+                                        cudaHostAllocDefault);
+        if (err != cudaSuccess) return cuda_fail(e, err, "offload ids staging");
+        o.h_ids_cap = sel;
+    }
+    // The ids, and with them everything queued before on `stream`: once this
+    // returns, no earlier kernel still reads a slot that is about to be refilled.
+    cudaError_t err = cudaMemcpyAsync(o.h_ids, d_ids, sel * sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "offload ids readback");
+    o.current = layer;
+    const uint32_t visit = ++o.visits[layer];
+    std::vector<int> need;
+    for (size_t i = 0; i < sel; ++i) {
+        const int ex = o.h_ids[i];
+        if (ex < 0 || ex >= E) return fail(e, DEE_ERR_RANGE, "offload_prepare: expert id out of range");
+        if (std::find(need.begin(), need.end(), ex) == need.end()) need.push_back(ex);
+    }
+    const uint32_t stamp = ++o.calls;  // "used by this layer call"
+    std::vector<int> miss;
+    for (int ex : need) {
+        const int64_t key = static_cast<int64_t>(layer) * E + ex;
+        o.on_use(key);
+        ++o.lookups;
+        const int32_t slot = o.slot_of[static_cast<size_t>(key)];
+        if (slot >= 0) {
+            ++o.hits;
+            o.used_visit[static_cast<size_t>(slot)] = stamp;
+        } else {
+            miss.push_back(ex);
+        }
+    }
+    // slots for the misses: free ones first, then the residents with the
+    // largest expected next use (never one this layer call uses)
+    std::vector<int> take;
+    std::vector<std::pair<double, int>> cand;
+    for (int s2 = 0; s2 < o.pool_slots && take.size() < miss.size(); ++s2)
+        if (o.slot_key[static_cast<size_t>(s2)] < 0) take.push_back(s2);
+    if (take.size() < miss.size()) {
+        for (int s2 = 0; s2 < o.pool_slots; ++s2) {
+            const int64_t k2 = o.slot_key[static_cast<size_t>(s2)];
+            if (k2 < 0 || o.used_visit[static_cast<size_t>(s2)] == stamp) continue;
+            cand.emplace_back(o.victim_rank(k2), s2);
+        }
+        const size_t want = miss.size() - take.size();
+        if (cand.size() < want) return fail(e, DEE_ERR_INVALID, "offload pool smaller than one layer's experts");
+        std::nth_element(cand.begin(), cand.begin() + (want - 1), cand.end(),
+                         [](const auto& a, const auto& b) { return a.first > b.first; });
+        for (size_t i = 0; i < want; ++i) take.push_back(cand[i].second);
+    }
+    int cold = 0;
+    for (size_t i = 0; i < miss.size(); ++i) {
+        const int64_t key = static_cast<int64_t>(layer) * E + miss[i];
+        const int victim = take[i];
+        const int64_t old = o.slot_key[static_cast<size_t>(victim)];
+        if (old >= 0) o.slot_of[static_cast<size_t>(old)] = -1;
+        o.slot_key[static_cast<size_t>(victim)] = key;
+        o.slot_of[static_cast<size_t>(key)] = victim;
+        o.used_visit[static_cast<size_t>(victim)] = stamp;
+        err = cudaMemcpyAsync(o.pool + static_cast<size_t>(victim) * o.record_bytes,
+                              o.host + static_cast<size_t>(key) * o.record_bytes, o.record_bytes,
+                              cudaMemcpyHostToDevice, o.copy_stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "offload H2D");
+        ++cold;
+        o.bytes += o.record_bytes;
+    }
+    o.cold += static_cast<uint64_t>(cold);
+    // this layer's slot table, after its records, then the compute stream waits
+    Bank& b = e->banks[layer];
+    err = cudaMemcpyAsync(b.d_slot_of, o.slot_of.data() + static_cast<size_t>(layer) * E, sizeof(int32_t) * E,
+                          cudaMemcpyHostToDevice, o.copy_stream);
+    if (err == cudaSuccess) err = cudaEventRecord(o.copied, o.copy_stream);
+    if (err == cudaSuccess) err = cudaStreamWaitEvent(stream, o.copied, 0);
+    if (err != cudaSuccess) return cuda_fail(e, err, "offload slot table");
+    if (cold_out) *cold_out = cold;
+    return DEE_OK;
+}
+
+int dee_offload_stats(dee_engine* e, uint64_t* out4) {
+    if (!e || !out4) return DEE_ERR_INVALID;
+    out4[0] = e->off.lookups;
+    out4[1] = e->off.hits;
+    out4[2] = e->off.cold;
+    out4[3] = e->off.bytes;
+    return DEE_OK;
 }
 
 int dee_stack_embed_device(dee_engine* e, const void* d_table_f16, const int32_t* d_ids, int tokens,

@@ -43,7 +43,7 @@ class SyntheticStack:
     """One rank's share of the stack (world = 1: the whole stack on one GPU)."""
 
     def __init__(self, torch, spec: StackSpec, *, tokens: int, rank: int = 0, world: int = 1,
-                 transport: str = "p2p"):
+                 transport: str = "p2p", offload_slots: int = 0):
         self.torch, self.spec, self.rank, self.world = torch, spec, rank, world
         self.tokens = tokens  # sequences decoded by this rank
         S = spec
@@ -63,17 +63,40 @@ class SyntheticStack:
         base = synthetic_bank(layout, self.epr, seed=S.seed, first_expert=first)
         packed = S.hidden * S.inter * 3 // 2  # w1, w3, w2 packed bytes lead the record
         stream = torch.cuda.current_stream().cuda_stream
-        self.banks = [base]
-        for layer in range(1, S.layers):
-            b = torch.empty_like(base)
+
+        def layer_bank(layer, out):
+            if layer == 0:
+                out.copy_(base)
+                return
             rc = self._lib.dee_records_scramble_device(ctypes.c_void_p(base.data_ptr()),
-                                                       ctypes.c_void_p(b.data_ptr()), self.epr, layout.bytes,
+                                                       ctypes.c_void_p(out.data_ptr()), self.epr, layout.bytes,
                                                        packed, layer, first, ctypes.c_void_p(stream))
             if rc != 0:
                 raise RuntimeError(f"dee_records_scramble_device failed ({rc})")
-            self.banks.append(b)
-        for layer, b in enumerate(self.banks):
-            self.engine.attach_bank(layer, b)
+
+        self.offload = offload_slots > 0
+        if not self.offload:
+            self.banks = [base]
+            for layer in range(1, S.layers):
+                b = torch.empty_like(base)
+                layer_bank(layer, b)
+                self.banks.append(b)
+            for layer, b in enumerate(self.banks):
+                self.engine.attach_bank(layer, b)
+        else:
+            # every layer's records in pinned host memory, a shared device pool
+            if world > 1:
+                raise ValueError("the offload tier runs on one GPU")
+            self.host = torch.empty((S.layers * self.epr, layout.bytes), dtype=torch.uint8, pin_memory=True)
+            tmp = torch.empty_like(base)
+            for layer in range(S.layers):
+                layer_bank(layer, tmp)
+                self.host[layer * self.epr:(layer + 1) * self.epr].copy_(tmp)
+            del tmp
+            self.pool = torch.empty((offload_slots, layout.bytes), dtype=torch.uint8, device=dev)
+            self.engine.offload_attach(self.host, S.layers, self.pool, offload_slots)
+            self.banks = [self.pool]
+        self.cold_reads = 0
         g = torch.Generator(device=dev)
         g.manual_seed(S.seed)
         self.embed = torch.randn((S.vocab, S.hidden), generator=g, device=dev).to(torch.float16)
@@ -122,6 +145,8 @@ class SyntheticStack:
                                                    S.experts, self._h_ptr(self.logits), st), "router_logits")
             self.router.route_topk_device(self.logits.data_ptr(), T, self.ids.data_ptr(), self.w.data_ptr(),
                                           st.value)
+            if self.offload:
+                self.cold_reads += e.offload_prepare_device(layer, self.ids.data_ptr(), T, st.value)
             if self.ep is None:
                 e.moe_forward_device(layer, self.h.data_ptr(), T, d_ids_ptr=self.ids.data_ptr(),
                                      d_weights_ptr=self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),

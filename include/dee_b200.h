@@ -237,6 +237,30 @@ DEE_API int dee_ep_p2p_forward_device(dee_engine* engine, int layer, const void*
                                       const int32_t* d_ids, const float* d_weights, float* d_out_f32,
                                       void* stream);
 
+/* Offload tier (configuration 4): the reference's VRAM expert cache over a
+ * pinned-host record pool (prepare_fp4_experts -> HostPackCache::get_batch ->
+ * H2D, engine.cpp:3133, async_prefetcher.cpp:691-780) with next-use
+ * eviction (VramCacheManager::evict_until_free, vram_cache.cpp:113, ranked by
+ * NextUseEstimator::victim_rank, include/dee/next_use.h:132-137).  Placement
+ * only: it never changes which experts run, so route ids and outputs equal
+ * the all-resident ones.
+ *
+ * Attach: h_records holds every layer's records [layers][num_experts]
+ * (pinned host memory, the DEE4 layout); d_pool is a device pool of
+ * pool_slots records shared by all layers.  Every layer's bank becomes
+ * (d_pool, pool_slots) with no expert resident. */
+DEE_API int dee_offload_attach(dee_engine* engine, const void* h_records, size_t record_bytes, int layers,
+                               void* d_pool, int pool_slots);
+/* Before a layer's forward: read its ids [T, K] (waits for `stream`), keep the
+ * resident experts, bring the others in from host memory into free slots or
+ * the residents with the largest expected next use (one H2D copy per expert on
+ * the engine's copy stream), update the layer's slot table, and make `stream`
+ * wait for the copies.  *cold_out (may be NULL) = experts copied. */
+DEE_API int dee_offload_prepare_device(dee_engine* engine, int layer, const int32_t* d_ids, int tokens,
+                                       void* stream, int* cold_out);
+/* Totals since attach: out4 = {lookups, hits, cold reads, bytes copied}. */
+DEE_API int dee_offload_stats(dee_engine* engine, uint64_t* out4);
+
 /* The dense glue of the synthetic multi-layer stack that drives the routed
  * layer end to end (no counterpart in the reference engine; the stack of the
  * benchmark's configurations 3 and 4: embedding -> [RMSNorm, router, MoE,

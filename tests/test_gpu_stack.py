@@ -48,3 +48,36 @@ def test_stack_decode_is_batch_invariant(torch_cuda, tmp_path):
     p.write_bytes(j)
     n, _ = verify_chain(p)
     assert n == steps * spec.layers
+
+
+@pytest.mark.parametrize("pool", [20, 48])
+def test_offload_tier_matches_resident_stack(torch_cuda, pool):
+    """Records in pinned host memory, a device pool smaller than the stack
+    (20 slots: experts are evicted and re-read every step; 48 = all 3 layers'
+    experts: after the first touches everything hits): route ids and tokens
+    equal the all-resident run."""
+    torch = torch_cuda
+    from dee_b200.stack import StackSpec, SyntheticStack, seed_tokens
+    spec = StackSpec(layers=3, experts=16, hidden=512, inter=512, topk=6, vocab=1024, seed=9)
+    B, steps = 4, 4
+    first = torch.from_numpy(seed_tokens(spec, B)).cuda()
+
+    def run(**kw):
+        st = SyntheticStack(torch, spec, tokens=B, **kw)
+        ids = torch.empty((steps, spec.layers, B, spec.topk), dtype=torch.int32, device="cuda")
+        tok = torch.empty((steps, B), dtype=torch.int32, device="cuda")
+        st.decode(first, steps, ids, tok)
+        torch.cuda.synchronize()
+        assert st.engine.sync_status() == 0
+        return st, ids.cpu().numpy(), tok.cpu().numpy()
+
+    _, ids_r, tok_r = run()
+    st, ids_o, tok_o = run(offload_slots=pool)
+    assert np.array_equal(ids_o, ids_r) and np.array_equal(tok_o, tok_r)
+    stats = st.engine.offload_stats()
+    assert stats["cold_reads"] == st.cold_reads > 0
+    assert stats["hits"] + stats["cold_reads"] == stats["lookups"]
+    if pool >= spec.layers * spec.experts:
+        assert stats["cold_reads"] <= spec.layers * spec.experts  # every expert read once at most
+    else:
+        assert stats["hits"] < stats["lookups"]
