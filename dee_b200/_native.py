@@ -67,6 +67,8 @@ SIGNATURES = {
     "dee_offload_attach": (I, [P, P, SZ, I, P, I]),
     "dee_offload_prepare_device": (I, [P, I, P, I, P, ctypes.POINTER(ctypes.c_int)]),
     "dee_offload_stats": (I, [P, ctypes.POINTER(ctypes.c_uint64)]),
+    "dee_host_alloc_pinned": (I, [SZ, ctypes.POINTER(P)]),
+    "dee_host_free_pinned": (I, [P]),
     "dee_stack_embed_device": (I, [P, P, P, I, I, P, P]),
     "dee_stack_rmsnorm_device": (I, [P, P, P, ctypes.c_float, I, P, P]),
     "dee_stack_router_logits_device": (I, [P, P, P, I, I, P, P]),

@@ -1122,6 +1122,13 @@ int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, i
     return DEE_OK;
 }
 
+int dee_host_alloc_pinned(size_t bytes, void** out) {
+    if (!out || bytes == 0) return DEE_ERR_INVALID;
+    return cudaHostAlloc(out, bytes, cudaHostAllocDefault) == cudaSuccess ? DEE_OK : DEE_ERR_CUDA;
+}
+
+int dee_host_free_pinned(void* p) { return cudaFreeHost(p) == cudaSuccess ? DEE_OK : DEE_ERR_CUDA; }
+
 int dee_offload_stats(dee_engine* e, uint64_t* out4) {
     if (!e || !out4) return DEE_ERR_INVALID;
     out4[0] = e->off.lookups;

@@ -87,7 +87,7 @@ class SyntheticStack:
             # every layer's records in pinned host memory, a shared device pool
             if world > 1:
                 raise ValueError("the offload tier runs on one GPU")
-            self.host = torch.empty((S.layers * self.epr, layout.bytes), dtype=torch.uint8, pin_memory=True)
+            self.host = pinned_host_tensor(torch, S.layers * self.epr, layout.bytes)
             tmp = torch.empty_like(base)
             for layer in range(S.layers):
                 layer_bank(layer, tmp)
@@ -177,6 +177,32 @@ class SyntheticStack:
                 tok_log[s].copy_(b)
             a, b = b, a
         return a
+
+
+class _PinnedBlock:
+    """Owns an exactly sized pinned host allocation (freed with the object)."""
+
+    def __init__(self, nbytes: int):
+        self._lib = _native.load()
+        self.ptr = ctypes.c_void_p()
+        rc = self._lib.dee_host_alloc_pinned(nbytes, ctypes.byref(self.ptr))
+        if rc != 0:
+            raise MemoryError(f"pinned host allocation of {nbytes} bytes failed ({rc})")
+        self.nbytes = nbytes
+
+    def __del__(self):
+        if getattr(self, "ptr", None) and self.ptr.value:
+            self._lib.dee_host_free_pinned(self.ptr)
+            self.ptr = ctypes.c_void_p()
+
+
+def pinned_host_tensor(torch, rows: int, cols: int):
+    """uint8 CPU tensor [rows, cols] in exactly rows*cols bytes of pinned memory."""
+    block = _PinnedBlock(rows * cols)
+    arr = np.ctypeslib.as_array((ctypes.c_uint8 * (rows * cols)).from_address(block.ptr.value))
+    t = torch.from_numpy(arr).view(rows, cols)
+    t._dee_block = block  # the tensor keeps the allocation alive
+    return t
 
 
 def seed_tokens(spec: StackSpec, batch: int) -> np.ndarray:

@@ -258,6 +258,12 @@ DEE_API int dee_offload_attach(dee_engine* engine, const void* h_records, size_t
  * wait for the copies.  *cold_out (may be NULL) = experts copied. */
 DEE_API int dee_offload_prepare_device(dee_engine* engine, int layer, const int32_t* d_ids, int tokens,
                                        void* stream, int* cold_out);
+/* Exactly `bytes` of pinned host memory (for an offload tier's records;
+ * allocators that round pinned requests up to powers of two cannot hold a
+ * 140 GB stack on a 196 GB host). */
+DEE_API int dee_host_alloc_pinned(size_t bytes, void** out);
+DEE_API int dee_host_free_pinned(void* p);
+
 /* Totals since attach: out4 = {lookups, hits, cold reads, bytes copied}. */
 DEE_API int dee_offload_stats(dee_engine* engine, uint64_t* out4);
 
