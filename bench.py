@@ -62,6 +62,11 @@ def parse():
     ap.add_argument("--offload-gib", type=float, default=0.0,
                     help="stack with the offload tier (config 4): device pool of this many GiB of expert "
                          "records, the rest in pinned host memory")
+    ap.add_argument("--store", default=None,
+                    help="stack: read every layer's expert records from this DEE4 store (resident banks "
+                         "or, with --offload-gib, the offload tier's pinned host block)")
+    ap.add_argument("--export-store", default=None,
+                    help="stack on one GPU: write its synthetic records as a DEE4 segmented store here first")
     ap.add_argument("--experts", type=int, default=E,
                     help="experts in the bank (smaller values only for profiling captures)")
     return ap.parse_args()
@@ -443,10 +448,30 @@ def run_stack(args):
     if args.offload_gib > 0:
         from dee_b200.records import RecordLayout
         slots = int(args.offload_gib * (1 << 30)) // RecordLayout(H, I).bytes
+    export = None
+    if args.export_store:
+        if world > 1:
+            raise SystemExit("--export-store runs on one GPU")
+        src = SyntheticStack(torch, spec, tokens=t_local)
+        t1 = time.perf_counter()
+        src.export_store(args.export_store)
+        export = {"path": args.export_store, "seconds": time.perf_counter() - t1}
+        del src
+        torch.cuda.empty_cache()
+        if args.store is None:
+            args.store = args.export_store
+    t0 = time.perf_counter()
     stack = SyntheticStack(torch, spec, tokens=t_local, rank=rank, world=world, transport=args.ep,
-                           offload_slots=slots)
+                           offload_slots=slots, store=args.store)
     torch.cuda.synchronize()
     build_s = time.perf_counter() - t0
+    store_info = None
+    if stack.store is not None:
+        f = stack.store_fill
+        store_info = {"backend": stack.store.backend, "identity": stack.store.identity,
+                      "fill_target": "pinned host" if slots else "HBM", "bytes": f["bytes_read"],
+                      "seconds": f["seconds"], "gb_per_s": f["gb_per_s"], "pread_calls": f["pread_calls"],
+                      "export": export}
     first = torch.from_numpy(seed_tokens(spec, b)[rank * t_local:(rank + 1) * t_local]).cuda()
     stream = torch.cuda.Stream()
 
@@ -518,6 +543,7 @@ def run_stack(args):
                        "expert_bytes_per_gpu": int(sum(x.numel() for x in stack.banks)),
                        "build_seconds": build_s},
             "offload": offload,
+            "store": store_info,
             "route_journal_sha256": sha256(journal), "journal_lines": journal.count(b"\n"),
             "tokens_sha256": sha256(toks.cpu().numpy().tobytes()), "device_status": status,
             "clocks": clk.summary(),

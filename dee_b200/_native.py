@@ -40,6 +40,37 @@ class DeeConfig(ctypes.Structure):
     ]
 
 
+class DeeStoreInfo(ctypes.Structure):
+    _fields_ = [
+        ("start_layer", ctypes.c_int),
+        ("num_layers", ctypes.c_int),
+        ("experts_per_layer", ctypes.c_int),
+        ("segmented", ctypes.c_int),
+        ("trace_indexed", ctypes.c_int),
+        ("record_bytes", ctypes.c_size_t),
+        ("stored_records", ctypes.c_size_t),
+        ("file_count", ctypes.c_size_t),
+        ("weight_offsets", ctypes.c_size_t * 3),
+        ("weight_nbytes", ctypes.c_size_t * 3),
+        ("weight_out", ctypes.c_size_t * 3),
+        ("weight_stored_in", ctypes.c_size_t * 3),
+        ("scale_offsets", ctypes.c_size_t * 3),
+        ("scale_nbytes", ctypes.c_size_t * 3),
+        ("scale_out", ctypes.c_size_t * 3),
+        ("scale_in", ctypes.c_size_t * 3),
+    ]
+
+
+class DeeStoreReadStats(ctypes.Structure):
+    _fields_ = [
+        ("bytes_read", ctypes.c_uint64),
+        ("pread_calls", ctypes.c_uint64),
+        ("short_reads", ctypes.c_uint64),
+        ("records", ctypes.c_uint64),
+        ("seconds", ctypes.c_double),
+    ]
+
+
 SIGNATURES = {
     "dee_abi_config_size": (SZ, []),
     "dee_abi_version": (I, []),
@@ -83,6 +114,20 @@ SIGNATURES = {
     "dee_moe_forward_noalloc": (I, [ctypes.POINTER(DeeConfig), P, SZ, I, P, I, P, P, P, P, P]),
     "dee_engine_set_profiling": (I, [P, I]),
     "dee_engine_stage_ms": (I, [P, P, I]),
+    "dee_store_create": (I, [ctypes.POINTER(P)]),
+    "dee_store_destroy": (None, [P]),
+    "dee_store_open": (I, [P, ctypes.c_char_p, I, I]),
+    "dee_store_close": (None, [P]),
+    "dee_store_last_error": (ctypes.c_char_p, [P]),
+    "dee_store_backend": (ctypes.c_char_p, [P]),
+    "dee_store_identity": (ctypes.c_char_p, [P]),
+    "dee_store_get_info": (I, [P, ctypes.POINTER(DeeStoreInfo)]),
+    "dee_store_stats": (I, [P, ctypes.POINTER(ctypes.c_uint64)]),
+    "dee_store_lookup": (I, [P, I, I, ctypes.POINTER(ctypes.c_uint64)]),
+    "dee_store_materialize": (I, [P, I, I, P, SZ, ctypes.POINTER(DeeStoreReadStats)]),
+    "dee_store_read_layers": (I, [P, I, I, I, I, P, SZ, I, ctypes.POINTER(DeeStoreReadStats)]),
+    "dee_store_upload_layers_device": (I, [P, I, I, I, I, P, SZ, SZ, I, P, ctypes.POINTER(DeeStoreReadStats)]),
+    "dee_sha256_hex": (I, [P, SZ, ctypes.c_char_p]),
 }
 
 STAGES = ("route", "permute", "gather", "gate_up", "down", "combine")

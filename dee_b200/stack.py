@@ -43,7 +43,8 @@ class SyntheticStack:
     """One rank's share of the stack (world = 1: the whole stack on one GPU)."""
 
     def __init__(self, torch, spec: StackSpec, *, tokens: int, rank: int = 0, world: int = 1,
-                 transport: str = "p2p", offload_slots: int = 0):
+                 transport: str = "p2p", offload_slots: int = 0, store: str | None = None,
+                 verify_store: bool = True):
         self.torch, self.spec, self.rank, self.world = torch, spec, rank, world
         self.tokens = tokens  # sequences decoded by this rank
         S = spec
@@ -60,6 +61,49 @@ class SyntheticStack:
                                               device_id=dev.index))
         layout = RecordLayout(S.hidden, S.inter)
         first = rank * self.epr
+        self.offload = offload_slots > 0
+        if self.offload and world > 1:
+            raise ValueError("the offload tier runs on one GPU")
+        self.store = None
+        self.store_fill = None
+        self.cold_reads = 0
+        if store is not None:
+            self._records_from_store(store, verify_store, layout, first, dev, offload_slots)
+        else:
+            self._synthetic_records(layout, first, dev, offload_slots)
+        self._dense(dev, tokens, rank, world, transport)
+
+    def _records_from_store(self, path, verify, layout, first, dev, offload_slots):
+        """Every layer's records of this rank's experts from a DEE4 store on
+        disk: straight into HBM through pinned staging buffers (resident), or
+        into the offload tier's pinned host block."""
+        from .store import Dee4Store, StoreError
+        torch, S = self.torch, self.spec
+        st = Dee4Store(path, verify_segment_hashes=verify)
+        st.check_layout(layout)
+        if st.start_layer != 0 or st.num_layers < S.layers or st.experts_per_layer != S.experts:
+            raise StoreError(f"store holds layers [{st.start_layer}, {st.start_layer + st.num_layers}) x "
+                             f"{st.experts_per_layer} experts; the stack needs {S.layers} x {S.experts}")
+        self.store = st
+        n = S.layers * self.epr
+        if not self.offload:
+            block = torch.empty((n, layout.bytes), dtype=torch.uint8, device=dev)
+            self.store_fill = st.upload_layers(0, S.layers, block.data_ptr(), block.numel(),
+                                               torch.cuda.current_stream(), first_expert=first,
+                                               experts=self.epr)
+            self.banks = [block[l * self.epr:(l + 1) * self.epr] for l in range(S.layers)]
+            for layer, b in enumerate(self.banks):
+                self.engine.attach_bank(layer, b)
+        else:
+            self.host = pinned_host_tensor(torch, n, layout.bytes)
+            self.store_fill = st.read_layers(0, S.layers, self.host.data_ptr(), self.host.numel(),
+                                             first_expert=first, experts=self.epr)
+            self.pool = torch.empty((offload_slots, layout.bytes), dtype=torch.uint8, device=dev)
+            self.engine.offload_attach(self.host, S.layers, self.pool, offload_slots)
+            self.banks = [self.pool]
+
+    def _synthetic_records(self, layout, first, dev, offload_slots):
+        torch, S = self.torch, self.spec
         base = synthetic_bank(layout, self.epr, seed=S.seed, first_expert=first)
         packed = S.hidden * S.inter * 3 // 2  # w1, w3, w2 packed bytes lead the record
         stream = torch.cuda.current_stream().cuda_stream
@@ -74,7 +118,6 @@ class SyntheticStack:
             if rc != 0:
                 raise RuntimeError(f"dee_records_scramble_device failed ({rc})")
 
-        self.offload = offload_slots > 0
         if not self.offload:
             self.banks = [base]
             for layer in range(1, S.layers):
@@ -85,8 +128,6 @@ class SyntheticStack:
                 self.engine.attach_bank(layer, b)
         else:
             # every layer's records in pinned host memory, a shared device pool
-            if world > 1:
-                raise ValueError("the offload tier runs on one GPU")
             self.host = pinned_host_tensor(torch, S.layers * self.epr, layout.bytes)
             tmp = torch.empty_like(base)
             for layer in range(S.layers):
@@ -96,7 +137,9 @@ class SyntheticStack:
             self.pool = torch.empty((offload_slots, layout.bytes), dtype=torch.uint8, device=dev)
             self.engine.offload_attach(self.host, S.layers, self.pool, offload_slots)
             self.banks = [self.pool]
-        self.cold_reads = 0
+
+    def _dense(self, dev, tokens, rank, world, transport):
+        torch, S = self.torch, self.spec
         g = torch.Generator(device=dev)
         g.manual_seed(S.seed)
         self.embed = torch.randn((S.vocab, S.hidden), generator=g, device=dev).to(torch.float16)
@@ -125,6 +168,21 @@ class SyntheticStack:
                 self.ep = ExpertParallelMoE(torch, rank, world, self.epr, T, S.topk, H, "cuda",
                                             engine=self.engine)
                 self.transport = "nccl"
+
+    def layer_records_host(self, layer: int):
+        """uint8 numpy [experts of this rank, record_bytes] of one layer."""
+        if self.offload:
+            return self.host[layer * self.epr:(layer + 1) * self.epr].numpy()
+        return self.banks[layer].cpu().numpy()
+
+    def export_store(self, path: str, fmt: str = "dee4-v4-segmented") -> dict:
+        """Write every layer's records as a DEE4 store (one GPU's full stack)."""
+        from .store import write_store
+        if self.world != 1:
+            raise ValueError("export the stack from a one-GPU instance (a rank holds a share of the experts)")
+        S = self.spec
+        return write_store(path, RecordLayout(S.hidden, S.inter), S.layers, S.experts, self.layer_records_host,
+                           fmt=fmt)
 
     def _h_ptr(self, t):
         return ctypes.c_void_p(t.data_ptr())

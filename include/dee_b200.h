@@ -350,6 +350,91 @@ DEE_API int dee_engine_set_profiling(dee_engine* engine, int enable);
  * of entries written. */
 DEE_API int dee_engine_stage_ms(dee_engine* engine, float* out_ms, int n);
 
+/* ---- DEE4 expert store on disk -------------------------------------------
+ * Dee4ExpertStore (dee.cpp/include/dee/expert_store.h:286-409,
+ * dee.cpp/src/expert_store.cpp:786-1230): formats dee4-v2 (one fixed-stride
+ * file, dense index (layer - start_layer) * experts_per_layer + expert),
+ * dee4-v3-trace (one file with a sorted (layer, expert) record table) and
+ * dee4-v4-segmented (one sha256-sealed file per layer bucket).  open() takes
+ * a store directory or its metadata.json and fails closed, with the
+ * reference's messages, on malformed metadata, missing or mis-sized files,
+ * segment paths that leave the store, and (verify_segment_hashes != 0)
+ * segments whose sha256 does not match their seal.  Records are read with
+ * pread() by `threads` host threads straight into caller memory. */
+typedef struct dee_store dee_store;
+
+/* The geometry and component table (Dee4ExpertStore accessors,
+ * expert_store.h:349-358, and the per-component views of get()). */
+typedef struct dee_store_info {
+    int start_layer;
+    int num_layers;
+    int experts_per_layer;
+    int segmented;
+    int trace_indexed;
+    size_t record_bytes;
+    size_t stored_records;
+    size_t file_count;
+    size_t weight_offsets[3];
+    size_t weight_nbytes[3];
+    size_t weight_out[3];
+    size_t weight_stored_in[3];
+    size_t scale_offsets[3];
+    size_t scale_nbytes[3];
+    size_t scale_out[3];
+    size_t scale_in[3];
+} dee_store_info;
+
+/* Per-fill accounting (MaterializeResult, expert_store.h:48-61). */
+typedef struct dee_store_read_stats {
+    uint64_t bytes_read;
+    uint64_t pread_calls;
+    uint64_t short_reads;
+    uint64_t records;
+    double seconds;
+} dee_store_read_stats;
+
+/* Dee4ExpertStore() / ~Dee4ExpertStore(). */
+DEE_API int dee_store_create(dee_store** out);
+DEE_API void dee_store_destroy(dee_store* store);
+/* Dee4ExpertStore::open(path, Dee4OpenOptions{verify_segment_hashes})
+ * (expert_store.h:286-306, expert_store.cpp:790).  DEE_ERR_INVALID on any
+ * failure; the reason is dee_store_last_error(). */
+DEE_API int dee_store_open(dee_store* store, const char* directory_or_metadata, int verify_segment_hashes,
+                           int threads);
+DEE_API void dee_store_close(dee_store* store);
+DEE_API const char* dee_store_last_error(const dee_store* store);
+/* backend_name() ("dee4", "dee4_trace", "dee4_segmented") and
+ * integrity_identity() (data_sha256, or for a segmented store the sha256 of
+ * the concatenated segment seals). */
+DEE_API const char* dee_store_backend(const dee_store* store);
+DEE_API const char* dee_store_identity(const dee_store* store);
+DEE_API int dee_store_get_info(const dee_store* store, dee_store_info* out);
+/* {lookups, lookup failures, records read, bytes read} since open. */
+DEE_API int dee_store_stats(const dee_store* store, uint64_t* out4);
+/* get() (expert_store.cpp:1176-1215): the record index of (layer, expert);
+ * DEE_ERR_RANGE outside the store or, for a trace store, for a pair it does
+ * not hold. */
+DEE_API int dee_store_lookup(dee_store* store, int layer, int expert, uint64_t* record_index);
+/* materialize_ex() (expert_store.h:341-347): one record into dst (nbytes must
+ * equal record_bytes). */
+DEE_API int dee_store_materialize(dee_store* store, int layer, int expert, void* dst, size_t nbytes,
+                                  dee_store_read_stats* stats);
+/* Experts [first_expert, first_expert + experts) of layers [first_layer,
+ * first_layer + layers) into host memory dst as [layer][expert][record_bytes]
+ * (the offload tier's pinned record block; an expert-parallel rank's share),
+ * by `threads` parallel preads. */
+DEE_API int dee_store_read_layers(dee_store* store, int first_layer, int layers, int first_expert, int experts,
+                                  void* dst, size_t dst_bytes, int threads, dee_store_read_stats* stats);
+/* The same records into device memory d_dst (a resident expert bank),
+ * through 2 * threads pinned staging buffers of staging_bytes / (2 * threads)
+ * each: every reader thread preads into one buffer while its other buffer's
+ * H2D copy runs on `stream`.  Returns after the copies completed. */
+DEE_API int dee_store_upload_layers_device(dee_store* store, int first_layer, int layers, int first_expert,
+                                           int experts, void* d_dst, size_t dst_bytes, size_t staging_bytes,
+                                           int threads, void* stream, dee_store_read_stats* stats);
+/* SHA-256 of n bytes as 64 lowercase hex digits + NUL (the seal function). */
+DEE_API int dee_sha256_hex(const void* data, size_t n, char* out65);
+
 #ifdef __cplusplus
 }
 #endif
