@@ -67,6 +67,7 @@ class DeeStoreReadStats(ctypes.Structure):
         ("pread_calls", ctypes.c_uint64),
         ("short_reads", ctypes.c_uint64),
         ("records", ctypes.c_uint64),
+        ("files_verified", ctypes.c_uint64),
         ("seconds", ctypes.c_double),
     ]
 
@@ -125,8 +126,9 @@ SIGNATURES = {
     "dee_store_stats": (I, [P, ctypes.POINTER(ctypes.c_uint64)]),
     "dee_store_lookup": (I, [P, I, I, ctypes.POINTER(ctypes.c_uint64)]),
     "dee_store_materialize": (I, [P, I, I, P, SZ, ctypes.POINTER(DeeStoreReadStats)]),
-    "dee_store_read_layers": (I, [P, I, I, I, I, P, SZ, I, ctypes.POINTER(DeeStoreReadStats)]),
-    "dee_store_upload_layers_device": (I, [P, I, I, I, I, P, SZ, SZ, I, P, ctypes.POINTER(DeeStoreReadStats)]),
+    "dee_store_read_layers": (I, [P, I, I, I, I, P, SZ, I, I, ctypes.POINTER(DeeStoreReadStats)]),
+    "dee_store_upload_layers_device": (I, [P, I, I, I, I, P, SZ, SZ, I, I, P,
+                                           ctypes.POINTER(DeeStoreReadStats)]),
     "dee_sha256_hex": (I, [P, SZ, ctypes.c_char_p]),
 }
 

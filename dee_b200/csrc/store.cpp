@@ -20,6 +20,10 @@
 // syscall at a time.  No record is mapped into the address space.
 #include <cuda_runtime.h>
 #include <fcntl.h>
+#if defined(__x86_64__)
+#include <cpuid.h>
+#include <immintrin.h>
+#endif
 #include <sys/stat.h>
 #include <unistd.h>
 
@@ -263,12 +267,124 @@ private:
 
 // ---------------------------------------------------------------------------
 // SHA-256 (FIPS 180-4, sections 4.2.2, 5.3.3 and 6.2): the segment seals and
-// the segmented store's identity.  Scalar; a store opens with one hashing
-// thread per segment in flight.
+// the segmented store's identity.  Two compressions of whole 64-byte blocks:
+// the portable one, and one on the x86 SHA extensions (SHA256RNDS2 runs two
+// rounds on the state held as ABEF/CDGH, SHA256MSG1/MSG2 extend the message
+// schedule four words at a time), chosen once from CPUID leaf 7 (EBX bit 29).
+// DEE_SHA256_PORTABLE=1 in the environment forces the portable one.
 // ---------------------------------------------------------------------------
+
+// K: the first 32 bits of the fractional parts of the cube roots of the
+// first 64 primes (FIPS 180-4, 4.2.2).
+alignas(16) const uint32_t kSha256K[64] = {
+    0x428a2f98u, 0x71374491u, 0xb5c0fbcfu, 0xe9b5dba5u, 0x3956c25bu, 0x59f111f1u, 0x923f82a4u, 0xab1c5ed5u,
+    0xd807aa98u, 0x12835b01u, 0x243185beu, 0x550c7dc3u, 0x72be5d74u, 0x80deb1feu, 0x9bdc06a7u, 0xc19bf174u,
+    0xe49b69c1u, 0xefbe4786u, 0x0fc19dc6u, 0x240ca1ccu, 0x2de92c6fu, 0x4a7484aau, 0x5cb0a9dcu, 0x76f988dau,
+    0x983e5152u, 0xa831c66du, 0xb00327c8u, 0xbf597fc7u, 0xc6e00bf3u, 0xd5a79147u, 0x06ca6351u, 0x14292967u,
+    0x27b70a85u, 0x2e1b2138u, 0x4d2c6dfcu, 0x53380d13u, 0x650a7354u, 0x766a0abbu, 0x81c2c92eu, 0x92722c85u,
+    0xa2bfe8a1u, 0xa81a664bu, 0xc24b8b70u, 0xc76c51a3u, 0xd192e819u, 0xd6990624u, 0xf40e3585u, 0x106aa070u,
+    0x19a4c116u, 0x1e376c08u, 0x2748774cu, 0x34b0bcb5u, 0x391c0cb3u, 0x4ed8aa4au, 0x5b9cca4fu, 0x682e6ff3u,
+    0x748f82eeu, 0x78a5636fu, 0x84c87814u, 0x8cc70208u, 0x90befffau, 0xa4506cebu, 0xbef9a3f7u, 0xc67178f2u};
+
+inline uint32_t rotr32(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
+
+void sha256_blocks_portable(uint32_t h[8], const uint8_t* p, size_t blocks) {
+    for (; blocks; --blocks, p += 64) {
+        uint32_t w[64];
+        for (int t = 0; t < 16; ++t)
+            w[t] = (static_cast<uint32_t>(p[4 * t]) << 24) | (static_cast<uint32_t>(p[4 * t + 1]) << 16) |
+                   (static_cast<uint32_t>(p[4 * t + 2]) << 8) | static_cast<uint32_t>(p[4 * t + 3]);
+        for (int t = 16; t < 64; ++t) {
+            const uint32_t s0 = rotr32(w[t - 15], 7) ^ rotr32(w[t - 15], 18) ^ (w[t - 15] >> 3);
+            const uint32_t s1 = rotr32(w[t - 2], 17) ^ rotr32(w[t - 2], 19) ^ (w[t - 2] >> 10);
+            w[t] = w[t - 16] + s0 + w[t - 7] + s1;
+        }
+        uint32_t a = h[0], b = h[1], c = h[2], d = h[3], e = h[4], f = h[5], g = h[6], hh = h[7];
+        for (int t = 0; t < 64; ++t) {
+            const uint32_t t1 =
+                hh + (rotr32(e, 6) ^ rotr32(e, 11) ^ rotr32(e, 25)) + ((e & f) ^ (~e & g)) + kSha256K[t] + w[t];
+            const uint32_t t2 = (rotr32(a, 2) ^ rotr32(a, 13) ^ rotr32(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
+            hh = g;
+            g = f;
+            f = e;
+            e = d + t1;
+            d = c;
+            c = b;
+            b = a;
+            a = t1 + t2;
+        }
+        h[0] += a; h[1] += b; h[2] += c; h[3] += d;
+        h[4] += e; h[5] += f; h[6] += g; h[7] += hh;
+    }
+}
+
+#if defined(__x86_64__)
+__attribute__((target("sha,sse4.1,ssse3"))) void sha256_blocks_shani(uint32_t h[8], const uint8_t* p,
+                                                                       size_t blocks) {
+    // big-endian word loads
+    const __m128i bswap = _mm_set_epi64x(0x0c0d0e0f08090a0bLL, 0x0405060700010203LL);
+    // state words a..h -> the ABEF / CDGH register pair the round instruction uses
+    __m128i dcba = _mm_loadu_si128(reinterpret_cast<const __m128i*>(h));
+    __m128i hgfe = _mm_loadu_si128(reinterpret_cast<const __m128i*>(h + 4));
+    __m128i cdab = _mm_shuffle_epi32(dcba, 0xB1);
+    __m128i efgh = _mm_shuffle_epi32(hgfe, 0x1B);
+    __m128i abef = _mm_alignr_epi8(cdab, efgh, 8);
+    __m128i cdgh = _mm_blend_epi16(efgh, cdab, 0xF0);
+    for (; blocks; --blocks, p += 64) {
+        const __m128i abef0 = abef, cdgh0 = cdgh;
+        __m128i m[4];
+        for (int g = 0; g < 16; ++g) {
+            __m128i w;
+            if (g < 4) {
+                w = _mm_shuffle_epi8(_mm_loadu_si128(reinterpret_cast<const __m128i*>(p + 16 * g)), bswap);
+            } else {
+                // W[t..t+3] = MSG2(MSG1(W[t-16..], W[t-12..]) + W[t-7..t-4], W[t-4..t-1])
+                const __m128i x = _mm_add_epi32(_mm_sha256msg1_epu32(m[g & 3], m[(g + 1) & 3]),
+                                                _mm_alignr_epi8(m[(g + 3) & 3], m[(g + 2) & 3], 4));
+                w = _mm_sha256msg2_epu32(x, m[(g + 3) & 3]);
+            }
+            m[g & 3] = w;
+            __m128i k = _mm_add_epi32(w, _mm_load_si128(reinterpret_cast<const __m128i*>(kSha256K + 4 * g)));
+            cdgh = _mm_sha256rnds2_epu32(cdgh, abef, k);
+            k = _mm_shuffle_epi32(k, 0x0E);
+            abef = _mm_sha256rnds2_epu32(abef, cdgh, k);
+        }
+        abef = _mm_add_epi32(abef, abef0);
+        cdgh = _mm_add_epi32(cdgh, cdgh0);
+    }
+    const __m128i feba = _mm_shuffle_epi32(abef, 0x1B);
+    const __m128i dchg = _mm_shuffle_epi32(cdgh, 0xB1);
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(h), _mm_blend_epi16(feba, dchg, 0xF0));
+    _mm_storeu_si128(reinterpret_cast<__m128i*>(h + 4), _mm_alignr_epi8(dchg, feba, 8));
+}
+
+bool cpu_has_sha() {
+    unsigned a = 0, b = 0, c = 0, d = 0;
+    if (!__get_cpuid_count(7, 0, &a, &b, &c, &d)) return false;
+    unsigned a1 = 0, b1 = 0, c1 = 0, d1 = 0;
+    if (!__get_cpuid(1, &a1, &b1, &c1, &d1)) return false;
+    const bool sse41 = (c1 >> 19) & 1u, ssse3 = (c1 >> 9) & 1u;
+    return ((b >> 29) & 1u) && sse41 && ssse3;
+}
+#endif
+
+using Sha256Blocks = void (*)(uint32_t*, const uint8_t*, size_t);
+
+Sha256Blocks sha256_blocks_impl() {
+    static const Sha256Blocks impl = []() -> Sha256Blocks {
+        const char* force = std::getenv("DEE_SHA256_PORTABLE");
+        if (force && force[0] == '1') return sha256_blocks_portable;
+#if defined(__x86_64__)
+        if (cpu_has_sha()) return sha256_blocks_shani;
+#endif
+        return sha256_blocks_portable;
+    }();
+    return impl;
+}
+
 class Sha256 {
 public:
-    Sha256() { reset(); }
+    Sha256() : blocks_(sha256_blocks_impl()) { reset(); }
 
     void reset() {
         static const uint32_t kInit[8] = {0x6a09e667u, 0xbb67ae85u, 0x3c6ef372u, 0xa54ff53au,
@@ -288,10 +404,14 @@ public:
             p += take;
             n -= take;
             if (fill_ < 64) return;
-            block(buf_);
+            blocks_(h_, buf_, 1);
             fill_ = 0;
         }
-        for (; n >= 64; p += 64, n -= 64) block(p);
+        if (n >= 64) {
+            blocks_(h_, p, n / 64);
+            p += n & ~size_t(63);
+            n &= 63;
+        }
         if (n) {
             std::memcpy(buf_, p, n);
             fill_ = n;
@@ -300,13 +420,10 @@ public:
 
     std::string hex() {
         const uint64_t bits = bits_;
-        const uint8_t one = 0x80;
-        update(&one, 1);
-        const uint8_t zero = 0;
-        while (fill_ != 56) update(&zero, 1);
-        uint8_t len[8];
-        for (int k = 0; k < 8; ++k) len[k] = static_cast<uint8_t>(bits >> (56 - 8 * k));
-        update(len, 8);
+        uint8_t pad[72] = {0x80};
+        const size_t padlen = (fill_ < 56 ? 56 : 120) - fill_;
+        for (int k = 0; k < 8; ++k) pad[padlen + k] = static_cast<uint8_t>(bits >> (56 - 8 * k));
+        update(pad, padlen + 8);
         static const char kHex[] = "0123456789abcdef";
         std::string out(64, '0');
         for (int w = 0; w < 8; ++w)
@@ -315,52 +432,11 @@ public:
     }
 
 private:
+    Sha256Blocks blocks_;
     uint32_t h_[8];
     uint64_t bits_ = 0;
     uint8_t buf_[64];
     size_t fill_ = 0;
-
-    static uint32_t rotr(uint32_t x, int n) { return (x >> n) | (x << (32 - n)); }
-
-    void block(const uint8_t* p) {
-        // K: the first 32 bits of the fractional parts of the cube roots of
-        // the first 64 primes (FIPS 180-4, 4.2.2).
-        static const uint32_t K[64] = {
-            0x428a2f98u, 0x71374491u, 0xb5c0fbcfu, 0xe9b5dba5u, 0x3956c25bu, 0x59f111f1u, 0x923f82a4u,
-            0xab1c5ed5u, 0xd807aa98u, 0x12835b01u, 0x243185beu, 0x550c7dc3u, 0x72be5d74u, 0x80deb1feu,
-            0x9bdc06a7u, 0xc19bf174u, 0xe49b69c1u, 0xefbe4786u, 0x0fc19dc6u, 0x240ca1ccu, 0x2de92c6fu,
-            0x4a7484aau, 0x5cb0a9dcu, 0x76f988dau, 0x983e5152u, 0xa831c66du, 0xb00327c8u, 0xbf597fc7u,
-            0xc6e00bf3u, 0xd5a79147u, 0x06ca6351u, 0x14292967u, 0x27b70a85u, 0x2e1b2138u, 0x4d2c6dfcu,
-            0x53380d13u, 0x650a7354u, 0x766a0abbu, 0x81c2c92eu, 0x92722c85u, 0xa2bfe8a1u, 0xa81a664bu,
-            0xc24b8b70u, 0xc76c51a3u, 0xd192e819u, 0xd6990624u, 0xf40e3585u, 0x106aa070u, 0x19a4c116u,
-            0x1e376c08u, 0x2748774cu, 0x34b0bcb5u, 0x391c0cb3u, 0x4ed8aa4au, 0x5b9cca4fu, 0x682e6ff3u,
-            0x748f82eeu, 0x78a5636fu, 0x84c87814u, 0x8cc70208u, 0x90befffau, 0xa4506cebu, 0xbef9a3f7u,
-            0xc67178f2u};
-        uint32_t w[64];
-        for (int t = 0; t < 16; ++t)
-            w[t] = (static_cast<uint32_t>(p[4 * t]) << 24) | (static_cast<uint32_t>(p[4 * t + 1]) << 16) |
-                   (static_cast<uint32_t>(p[4 * t + 2]) << 8) | static_cast<uint32_t>(p[4 * t + 3]);
-        for (int t = 16; t < 64; ++t) {
-            const uint32_t s0 = rotr(w[t - 15], 7) ^ rotr(w[t - 15], 18) ^ (w[t - 15] >> 3);
-            const uint32_t s1 = rotr(w[t - 2], 17) ^ rotr(w[t - 2], 19) ^ (w[t - 2] >> 10);
-            w[t] = w[t - 16] + s0 + w[t - 7] + s1;
-        }
-        uint32_t a = h_[0], b = h_[1], c = h_[2], d = h_[3], e = h_[4], f = h_[5], g = h_[6], h = h_[7];
-        for (int t = 0; t < 64; ++t) {
-            const uint32_t t1 = h + (rotr(e, 6) ^ rotr(e, 11) ^ rotr(e, 25)) + ((e & f) ^ (~e & g)) + K[t] + w[t];
-            const uint32_t t2 = (rotr(a, 2) ^ rotr(a, 13) ^ rotr(a, 22)) + ((a & b) ^ (a & c) ^ (b & c));
-            h = g;
-            g = f;
-            f = e;
-            e = d + t1;
-            d = c;
-            c = b;
-            b = a;
-            a = t1 + t2;
-        }
-        h_[0] += a; h_[1] += b; h_[2] += c; h_[3] += d;
-        h_[4] += e; h_[5] += f; h_[6] += g; h_[7] += h;
-    }
 };
 
 bool is_sha256_hex(const std::string& v) {
@@ -445,12 +521,17 @@ struct StoreFile {
     size_t size = 0;
 };
 
-// A contiguous byte range of one file bound for dst + dst_offset.
-struct Piece {
+// A contiguous byte range of one file bound for dst + dst_offset, read in
+// order in pieces of `chunk` bytes.  `seal`: the range is the whole file and
+// the file has a sha256 seal; the pieces are hashed as they arrive and the
+// task fails on a mismatch.
+struct Task {
     const StoreFile* file;
     size_t file_offset;
     size_t dst_offset;
     size_t bytes;
+    size_t chunk;
+    bool seal;
 };
 
 // Run fn(i) for i in [0, n) on up to `threads` host threads.
@@ -470,6 +551,50 @@ void parallel_for(size_t n, int threads, Fn fn) {
     for (size_t k = 1; k < workers; ++k) pool.emplace_back(body);
     body();
     for (auto& t : pool) t.join();
+}
+
+// Work through `tasks` on `workers` threads.  For every piece,
+// buf = acquire(w, task, offset_in_task) names where the bytes land (the
+// destination itself, or worker w's staging buffer), then commit(w, buf, dst
+// offset, bytes) hands them on; acquire/commit return false to stop.
+// Returns the first error ("" on success).
+template <class Acquire, class Commit>
+std::string run_tasks(const std::vector<Task>& tasks, int workers, ReadCounters* rc, std::atomic<uint64_t>* sealed,
+                      Acquire acquire, Commit commit) {
+    std::atomic<size_t> next{0};
+    std::atomic<bool> stop{false};
+    std::mutex mu;
+    std::string err;
+    auto fail = [&](const std::string& m) {
+        std::lock_guard<std::mutex> g(mu);
+        if (err.empty()) err = m;
+        stop.store(true);
+    };
+    auto body = [&](int w) {
+        for (size_t i = next.fetch_add(1); i < tasks.size() && !stop.load(); i = next.fetch_add(1)) {
+            const Task& t = tasks[i];
+            Sha256 h;
+            for (size_t off = 0; off < t.bytes && !stop.load(); off += t.chunk) {
+                const size_t n = std::min(t.chunk, t.bytes - off);
+                void* buf = acquire(w, t, off);
+                if (!buf) return fail("staging buffer wait failed");
+                if (!pread_full(t.file->fd, buf, n, t.file_offset + off, rc))
+                    return fail("DEE4 read of " + t.file->file + " failed");
+                if (t.seal) h.update(buf, n);
+                if (!commit(w, buf, t.dst_offset + off, n)) return fail("device copy failed");
+            }
+            if (t.seal && !stop.load()) {
+                if (h.hex() != t.file->sha256) return fail("DEE4 segment " + t.file->file + " sha256 mismatch");
+                sealed->fetch_add(1);
+            }
+        }
+    };
+    const int n = std::max(1, std::min<int>(workers, static_cast<int>(tasks.size())));
+    std::vector<std::thread> pool;
+    for (int w = 1; w < n; ++w) pool.emplace_back(body, w);
+    body(0);
+    for (auto& t : pool) t.join();
+    return err;
 }
 
 }  // namespace
@@ -496,7 +621,7 @@ public:
         return false;
     }
 
-    bool open(const std::string& path, bool verify, int threads);
+    bool open(const std::string& path, bool verify, bool drop_pages, int threads);
 
     // Dee4ExpertStore::get (expert_store.cpp:1176-1215): the record index of
     // (layer, expert), or false outside the store (a trace store also misses
@@ -547,21 +672,16 @@ public:
         return true;
     }
 
-    // Pieces of at most `chunk` bytes that fill dst with experts
-    // [first_expert, first_expert+experts) of layers [first_layer,
-    // first_layer+layers) as [layer][expert][record_bytes].
-    bool plan_layers(int first_layer, int layers, int first_expert, int experts, size_t chunk,
-                     std::vector<Piece>* pieces) {
-        pieces->clear();
+    // Tasks that fill dst with experts [first_expert, first_expert+experts)
+    // of layers [first_layer, first_layer+layers) as [layer][expert][record]:
+    // contiguous runs of one file, each split into independent pieces of at
+    // most `chunk` bytes -- or, with `verify`, kept whole (read in order and
+    // hashed) when the run is an entire sealed file.  Sealed runs go first:
+    // they are the longest tasks.
+    bool plan_layers(int first_layer, int layers, int first_expert, int experts, size_t chunk, bool verify,
+                     std::vector<Task>* tasks) {
+        std::vector<Task> runs;
         size_t dst = 0;
-        const StoreFile* run_file = nullptr;
-        size_t run_off = 0, run_dst = 0, run_bytes = 0;
-        auto flush = [&]() {
-            for (size_t done = 0; done < run_bytes; done += chunk)
-                pieces->push_back({run_file, run_off + done, run_dst + done, std::min(chunk, run_bytes - done)});
-            run_file = nullptr;
-            run_bytes = 0;
-        };
         for (int l = first_layer; l < first_layer + layers; ++l) {
             for (int e = first_expert; e < first_expert + experts; ++e) {
                 size_t idx = 0, off = 0;
@@ -571,19 +691,24 @@ public:
                                   ") is not in the store";
                     return false;
                 }
-                if (run_file == f && run_off + run_bytes == off) {
-                    run_bytes += record_bytes_;
-                } else {
-                    if (run_file) flush();
-                    run_file = f;
-                    run_off = off;
-                    run_dst = dst;
-                    run_bytes = record_bytes_;
-                }
+                if (!runs.empty() && runs.back().file == f && runs.back().file_offset + runs.back().bytes == off &&
+                    runs.back().dst_offset + runs.back().bytes == dst)
+                    runs.back().bytes += record_bytes_;
+                else
+                    runs.push_back({f, off, dst, record_bytes_, chunk, false});
                 dst += record_bytes_;
             }
         }
-        if (run_file) flush();
+        tasks->clear();
+        for (const Task& r : runs)
+            if (verify && r.file_offset == 0 && r.bytes == r.file->size && !r.file->sha256.empty())
+                tasks->push_back({r.file, 0, r.dst_offset, r.bytes, chunk, true});
+        for (const Task& r : runs) {
+            if (verify && r.file_offset == 0 && r.bytes == r.file->size && !r.file->sha256.empty()) continue;
+            for (size_t done = 0; done < r.bytes; done += chunk)
+                tasks->push_back(
+                    {r.file, r.file_offset + done, r.dst_offset + done, std::min(chunk, r.bytes - done), chunk, false});
+        }
         return true;
     }
 
@@ -669,7 +794,7 @@ private:
 
 // Dee4ExpertStore::open (expert_store.cpp:790-1172): the same keys, the same
 // checks in the same order, the same fail-closed outcomes.
-bool Dee4Store::open(const std::string& path, bool verify, int threads) {
+bool Dee4Store::open(const std::string& path, bool verify, bool drop_pages, int threads) {
     close();
     last_error_.clear();
     std::string meta_path = path;
@@ -826,7 +951,7 @@ bool Dee4Store::open(const std::string& path, bool verify, int threads) {
                     h.update(buf.data(), n);
                 }
 #ifdef POSIX_FADV_DONTNEED
-                ::posix_fadvise(f.fd, 0, 0, POSIX_FADV_DONTNEED);
+                if (drop_pages) ::posix_fadvise(f.fd, 0, 0, POSIX_FADV_DONTNEED);
 #endif
                 digest[s] = h.hex();
                 ok[s] = 1;
@@ -841,6 +966,7 @@ bool Dee4Store::open(const std::string& path, bool verify, int threads) {
         if (!checked_mul(total, record_bytes_, &expect)) return fail("DEE4 total size overflow");
         StoreFile f;
         f.file = data_file;
+        f.sha256 = lower(identity_);  // data_sha256 seals the whole file
         f.first_record = 0;
         f.record_count = total;
         if (!open_file(dir, &f)) {
@@ -871,8 +997,10 @@ struct dee_store {
 
 namespace {
 
-void fill_stats(dee_store_read_stats* out, const dee::store::ReadCounters& rc, uint64_t records, double seconds) {
+void fill_stats(dee_store_read_stats* out, const dee::store::ReadCounters& rc, uint64_t records, double seconds,
+                uint64_t files_verified = 0) {
     if (!out) return;
+    out->files_verified = files_verified;
     out->bytes_read = rc.bytes.load();
     out->pread_calls = rc.calls.load();
     out->short_reads = rc.short_reads.load();
@@ -892,14 +1020,16 @@ DEE_API int dee_store_create(dee_store** out) {
 
 DEE_API void dee_store_destroy(dee_store* store) { delete store; }
 
-DEE_API int dee_store_open(dee_store* store, const char* directory_or_metadata, int verify_segment_hashes,
-                           int threads) {
+DEE_API int dee_store_open(dee_store* store, const char* directory_or_metadata, int options, int threads) {
     if (!store) return DEE_ERR_INVALID;
     if (!directory_or_metadata) {
         store->s.last_error_ = "DEE4 metadata.json is missing";
         return DEE_ERR_INVALID;
     }
-    return store->s.open(directory_or_metadata, verify_segment_hashes != 0, threads) ? DEE_OK : DEE_ERR_INVALID;
+    return store->s.open(directory_or_metadata, (options & DEE_STORE_VERIFY_SEALS) != 0,
+                         (options & DEE_STORE_SEAL_DROP_PAGES) != 0, threads)
+               ? DEE_OK
+               : DEE_ERR_INVALID;
 }
 
 DEE_API void dee_store_close(dee_store* store) {
@@ -964,7 +1094,7 @@ DEE_API int dee_store_materialize(dee_store* store, int layer, int expert, void*
 }
 
 DEE_API int dee_store_read_layers(dee_store* store, int first_layer, int layers, int first_expert, int experts,
-                                  void* dst, size_t dst_bytes, int threads, dee_store_read_stats* stats) {
+                                  void* dst, size_t dst_bytes, int threads, int verify, dee_store_read_stats* stats) {
     if (!store || !dst) return DEE_ERR_INVALID;
     Dee4Store& s = store->s;
     if (!s.loaded() || !s.valid_range(first_layer, layers, first_expert, experts)) {
@@ -976,22 +1106,22 @@ DEE_API int dee_store_read_layers(dee_store* store, int first_layer, int layers,
         s.last_error_ = "destination smaller than the layers' records";
         return DEE_ERR_INVALID;
     }
-    std::vector<dee::store::Piece> pieces;
-    if (!s.plan_layers(first_layer, layers, first_expert, experts, size_t(16) << 20, &pieces)) return DEE_ERR_RANGE;
+    std::vector<dee::store::Task> tasks;
+    if (!s.plan_layers(first_layer, layers, first_expert, experts, size_t(16) << 20, verify != 0, &tasks))
+        return DEE_ERR_RANGE;
     dee::store::ReadCounters rc;
-    std::atomic<int> failed{0};
+    std::atomic<uint64_t> sealed{0};
     const auto t0 = std::chrono::steady_clock::now();
-    dee::store::parallel_for(pieces.size(), threads, [&](size_t i) {
-        const auto& p = pieces[i];
-        if (failed.load(std::memory_order_relaxed)) return;
-        if (!dee::store::pread_full(p.file->fd, static_cast<char*>(dst) + p.dst_offset, p.bytes, p.file_offset, &rc))
-            failed.store(1);
-    });
+    char* base = static_cast<char*>(dst);
+    const std::string err = dee::store::run_tasks(
+        tasks, std::max(1, threads), &rc, &sealed,
+        [&](int, const dee::store::Task& t, size_t off) -> void* { return base + t.dst_offset + off; },
+        [](int, void*, size_t, size_t) { return true; });
     const uint64_t records = static_cast<uint64_t>(layers) * experts;
     s.count_reads(records, rc.bytes.load());
-    fill_stats(stats, rc, failed.load() ? 0 : records, dee::store::seconds_since(t0));
-    if (failed.load()) {
-        s.last_error_ = "DEE4 read failed";
+    fill_stats(stats, rc, err.empty() ? records : 0, dee::store::seconds_since(t0), sealed.load());
+    if (!err.empty()) {
+        s.last_error_ = err;
         return DEE_ERR_INVALID;
     }
     return DEE_OK;
@@ -999,7 +1129,7 @@ DEE_API int dee_store_read_layers(dee_store* store, int first_layer, int layers,
 
 DEE_API int dee_store_upload_layers_device(dee_store* store, int first_layer, int layers, int first_expert,
                                            int experts, void* d_dst, size_t dst_bytes, size_t staging_bytes,
-                                           int threads, void* stream, dee_store_read_stats* stats) {
+                                           int threads, int verify, void* stream, dee_store_read_stats* stats) {
     if (!store || !d_dst) return DEE_ERR_INVALID;
     Dee4Store& s = store->s;
     if (!s.loaded() || !s.valid_range(first_layer, layers, first_expert, experts)) {
@@ -1015,17 +1145,19 @@ DEE_API int dee_store_upload_layers_device(dee_store* store, int first_layer, in
     // Each reader thread double-buffers: pread into one pinned half while the
     // copy engine drains the other.
     const size_t chunk = std::max<size_t>(size_t(1) << 20, (staging_bytes / (2 * threads)) & ~size_t(4095));
-    std::vector<dee::store::Piece> pieces;
-    if (!s.plan_layers(first_layer, layers, first_expert, experts, chunk, &pieces)) return DEE_ERR_RANGE;
-    threads = static_cast<int>(std::min<size_t>(static_cast<size_t>(threads), pieces.size()));
+    std::vector<dee::store::Task> tasks;
+    if (!s.plan_layers(first_layer, layers, first_expert, experts, chunk, verify != 0, &tasks)) return DEE_ERR_RANGE;
+    threads = static_cast<int>(std::min<size_t>(static_cast<size_t>(threads), tasks.size()));
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) {
         s.last_error_ = "no CUDA device";
         return DEE_ERR_CUDA;
     }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    std::vector<void*> bufs(2 * static_cast<size_t>(threads), nullptr);
-    std::vector<cudaEvent_t> evs(bufs.size(), nullptr);
+    const size_t nbuf = 2 * static_cast<size_t>(threads);
+    std::vector<void*> bufs(nbuf, nullptr);
+    std::vector<cudaEvent_t> evs(nbuf, nullptr);
+    std::vector<int> used(nbuf, 0), half(threads, 0), bound(threads, 0);
     std::string cuda_err;
     std::mutex err_mu;
     auto note = [&](cudaError_t e, const char* what) {
@@ -1035,62 +1167,51 @@ DEE_API int dee_store_upload_layers_device(dee_store* store, int first_layer, in
         return false;
     };
     bool ok = true;
-    for (size_t b = 0; b < bufs.size() && ok; ++b)
+    for (size_t b = 0; b < nbuf && ok; ++b)
         ok = note(cudaHostAlloc(&bufs[b], chunk, cudaHostAllocDefault), "cudaHostAlloc") &&
              note(cudaEventCreateWithFlags(&evs[b], cudaEventDisableTiming), "cudaEventCreate");
     dee::store::ReadCounters rc;
-    std::atomic<int> failed{ok ? 0 : 1};
-    std::atomic<size_t> next{0};
+    std::atomic<uint64_t> sealed{0};
+    std::string err;
     const auto t0 = std::chrono::steady_clock::now();
-    auto worker = [&](int w) {
-        if (cudaSetDevice(device) != cudaSuccess) {
-            failed.store(1);
-            return;
-        }
-        bool used[2] = {false, false};
-        int half = 0;
-        for (size_t i = next.fetch_add(1); i < pieces.size() && !failed.load(); i = next.fetch_add(1)) {
-            const size_t b = 2 * static_cast<size_t>(w) + half;
-            if (used[half] && !note(cudaEventSynchronize(evs[b]), "cudaEventSynchronize")) {
-                failed.store(1);
-                break;
-            }
-            const auto& p = pieces[i];
-            if (!dee::store::pread_full(p.file->fd, bufs[b], p.bytes, p.file_offset, &rc)) {
-                failed.store(1);
-                break;
-            }
-            if (!note(cudaMemcpyAsync(static_cast<char*>(d_dst) + p.dst_offset, bufs[b], p.bytes,
-                                      cudaMemcpyHostToDevice, st),
-                      "cudaMemcpyAsync") ||
-                !note(cudaEventRecord(evs[b], st), "cudaEventRecord")) {
-                failed.store(1);
-                break;
-            }
-            used[half] = true;
-            half ^= 1;
-        }
-    };
     if (ok) {
-        std::vector<std::thread> pool;
-        for (int w = 1; w < threads; ++w) pool.emplace_back(worker, w);
-        worker(0);
-        for (auto& t : pool) t.join();
+        err = dee::store::run_tasks(
+            tasks, threads, &rc, &sealed,
+            [&](int w, const dee::store::Task&, size_t) -> void* {
+                if (!bound[w]) {  // a worker thread's first piece: bind it to the device
+                    if (!note(cudaSetDevice(device), "cudaSetDevice")) return nullptr;
+                    bound[w] = 1;
+                }
+                const size_t b = 2 * static_cast<size_t>(w) + half[w];
+                if (used[b] && !note(cudaEventSynchronize(evs[b]), "cudaEventSynchronize")) return nullptr;
+                return bufs[b];
+            },
+            [&](int w, void* buf, size_t dst_off, size_t n) {
+                const size_t b = 2 * static_cast<size_t>(w) + half[w];
+                if (!note(cudaMemcpyAsync(static_cast<char*>(d_dst) + dst_off, buf, n, cudaMemcpyHostToDevice, st),
+                          "cudaMemcpyAsync") ||
+                    !note(cudaEventRecord(evs[b], st), "cudaEventRecord"))
+                    return false;
+                used[b] = 1;
+                half[w] ^= 1;
+                return true;
+            });
         note(cudaStreamSynchronize(st), "cudaStreamSynchronize");
     }
-    for (size_t b = 0; b < bufs.size(); ++b) {
+    for (size_t b = 0; b < nbuf; ++b) {
         if (evs[b]) cudaEventDestroy(evs[b]);
         if (bufs[b]) cudaFreeHost(bufs[b]);
     }
     const uint64_t records = static_cast<uint64_t>(layers) * experts;
     s.count_reads(records, rc.bytes.load());
-    fill_stats(stats, rc, failed.load() || !cuda_err.empty() ? 0 : records, dee::store::seconds_since(t0));
+    const bool good = err.empty() && cuda_err.empty();
+    fill_stats(stats, rc, good ? records : 0, dee::store::seconds_since(t0), sealed.load());
     if (!cuda_err.empty()) {
         s.last_error_ = cuda_err;
         return DEE_ERR_CUDA;
     }
-    if (failed.load()) {
-        s.last_error_ = "DEE4 read failed";
+    if (!err.empty()) {
+        s.last_error_ = err;
         return DEE_ERR_INVALID;
     }
     return DEE_OK;

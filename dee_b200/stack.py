@@ -76,10 +76,13 @@ class SyntheticStack:
     def _records_from_store(self, path, verify, layout, first, dev, offload_slots):
         """Every layer's records of this rank's experts from a DEE4 store on
         disk: straight into HBM through pinned staging buffers (resident), or
-        into the offload tier's pinned host block."""
+        into the offload tier's pinned host block.  With `verify` the seals
+        are checked: while the fill streams whole segments in (one GPU: one
+        pass over the disk), or at open when a rank reads a share of each."""
         from .store import Dee4Store, StoreError
         torch, S = self.torch, self.spec
-        st = Dee4Store(path, verify_segment_hashes=verify)
+        whole = self.world == 1
+        st = Dee4Store(path, verify_segment_hashes=verify and not whole)
         st.check_layout(layout)
         if st.start_layer != 0 or st.num_layers < S.layers or st.experts_per_layer != S.experts:
             raise StoreError(f"store holds layers [{st.start_layer}, {st.start_layer + st.num_layers}) x "
@@ -90,14 +93,14 @@ class SyntheticStack:
             block = torch.empty((n, layout.bytes), dtype=torch.uint8, device=dev)
             self.store_fill = st.upload_layers(0, S.layers, block.data_ptr(), block.numel(),
                                                torch.cuda.current_stream(), first_expert=first,
-                                               experts=self.epr)
+                                               experts=self.epr, verify=verify and whole)
             self.banks = [block[l * self.epr:(l + 1) * self.epr] for l in range(S.layers)]
             for layer, b in enumerate(self.banks):
                 self.engine.attach_bank(layer, b)
         else:
             self.host = pinned_host_tensor(torch, n, layout.bytes)
             self.store_fill = st.read_layers(0, S.layers, self.host.data_ptr(), self.host.numel(),
-                                             first_expert=first, experts=self.epr)
+                                             first_expert=first, experts=self.epr, verify=verify and whole)
             self.pool = torch.empty((offload_slots, layout.bytes), dtype=torch.uint8, device=dev)
             self.engine.offload_attach(self.host, S.layers, self.pool, offload_slots)
             self.banks = [self.pool]

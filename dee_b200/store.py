@@ -194,23 +194,35 @@ def write_store(out_dir: str, layout: RecordLayout, num_layers: int, experts_per
     return meta
 
 
+VERIFY_SEALS = 1
+SEAL_DROP_PAGES = 2
+
+
 class Dee4Store:
     """An open DEE4 store (Dee4ExpertStore, expert_store.h:316-409).
 
     Opening fails closed with StoreError carrying the reader's message.
     `verify_segment_hashes` re-hashes every segment of a segmented store at
-    open (Dee4OpenOptions::verify_segment_hashes, default true); `threads`
-    host threads hash segments and read records in parallel.
+    open (Dee4OpenOptions::verify_segment_hashes, default true);
+    `seal_reads_through_page_cache` drops each segment from the page cache
+    after hashing it (Dee4OpenOptions::seal_reads_through_page_cache).
+    `threads` host threads hash segments and read records in parallel.  A
+    fill with verify=True checks the seal of every file it reads whole as the
+    bytes stream in, so a store opened without verification and filled whole
+    is sealed in one pass over the disk.
     """
 
-    def __init__(self, path: str, *, verify_segment_hashes: bool = True, threads: int = 0):
+    def __init__(self, path: str, *, verify_segment_hashes: bool = True,
+                 seal_reads_through_page_cache: bool = False, threads: int = 0):
         self._lib = _native.load()
         self.threads = threads if threads > 0 else max(1, min(32, os.cpu_count() or 1))
         h = ctypes.c_void_p()
         if self._lib.dee_store_create(ctypes.byref(h)) != 0:
             raise StoreError("dee_store_create failed")
         self._h = h
-        rc = self._lib.dee_store_open(h, os.fsencode(path), int(verify_segment_hashes), self.threads)
+        options = (VERIFY_SEALS if verify_segment_hashes else 0) | \
+            (SEAL_DROP_PAGES if seal_reads_through_page_cache else 0)
+        rc = self._lib.dee_store_open(h, os.fsencode(path), options, self.threads)
         if rc != 0:
             msg = self.last_error()
             self.close()
@@ -299,27 +311,28 @@ class Dee4Store:
         return first_expert, (self.experts_per_layer - first_expert) if experts is None else experts
 
     def read_layers(self, first_layer: int, layers: int, dst_ptr: int, dst_bytes: int, *,
-                    first_expert: int = 0, experts: int | None = None) -> dict:
+                    first_expert: int = 0, experts: int | None = None, verify: bool = False) -> dict:
         """Experts [first_expert, first_expert+experts) (default: all) of
         layers [first_layer, first_layer+layers) into host memory at dst_ptr
         as [layer][expert][record_bytes]."""
         fe, ne = self._experts(first_expert, experts)
         st = _native.DeeStoreReadStats()
         rc = self._lib.dee_store_read_layers(self._h, first_layer, layers, fe, ne, ctypes.c_void_p(dst_ptr),
-                                             dst_bytes, self.threads, ctypes.byref(st))
+                                             dst_bytes, self.threads, int(verify), ctypes.byref(st))
         if rc != 0:
             raise StoreError(self.last_error())
         return _stats(st)
 
     def upload_layers(self, first_layer: int, layers: int, d_ptr: int, d_bytes: int, stream=None, *,
-                      first_expert: int = 0, experts: int | None = None, staging_bytes: int = 512 << 20) -> dict:
+                      first_expert: int = 0, experts: int | None = None, staging_bytes: int = 512 << 20,
+                      verify: bool = False) -> dict:
         """The same records into device memory at d_ptr through pinned
         staging buffers; returns after the copies completed."""
         fe, ne = self._experts(first_expert, experts)
         st = _native.DeeStoreReadStats()
         s = getattr(stream, "cuda_stream", stream)
         rc = self._lib.dee_store_upload_layers_device(self._h, first_layer, layers, fe, ne, ctypes.c_void_p(d_ptr),
-                                                      d_bytes, staging_bytes, self.threads,
+                                                      d_bytes, staging_bytes, self.threads, int(verify),
                                                       ctypes.c_void_p(s) if s else None, ctypes.byref(st))
         if rc != 0:
             raise StoreError(self.last_error())
@@ -329,7 +342,7 @@ class Dee4Store:
 def _stats(st) -> dict:
     gbs = st.bytes_read / st.seconds / 1e9 if st.seconds > 0 else 0.0
     return {"bytes_read": st.bytes_read, "pread_calls": st.pread_calls, "short_reads": st.short_reads,
-            "records": st.records, "seconds": st.seconds, "gb_per_s": gbs}
+            "records": st.records, "files_verified": st.files_verified, "seconds": st.seconds, "gb_per_s": gbs}
 
 
 def _buffer_ptr(buf):

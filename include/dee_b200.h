@@ -384,23 +384,32 @@ typedef struct dee_store_info {
     size_t scale_in[3];
 } dee_store_info;
 
-/* Per-fill accounting (MaterializeResult, expert_store.h:48-61). */
+/* Per-fill accounting (MaterializeResult, expert_store.h:48-61).
+ * files_verified: files whose seal a fill checked (verify != 0). */
 typedef struct dee_store_read_stats {
     uint64_t bytes_read;
     uint64_t pread_calls;
     uint64_t short_reads;
     uint64_t records;
+    uint64_t files_verified;
     double seconds;
 } dee_store_read_stats;
+
+/* dee_store_open options (Dee4OpenOptions, expert_store.h:286-306).
+ * VERIFY_SEALS: re-hash every segment at open and fail closed on a mismatch
+ * (verify_segment_hashes).  SEAL_DROP_PAGES: drop each segment from the page
+ * cache after hashing it (the effect of seal_reads_through_page_cache). */
+#define DEE_STORE_VERIFY_SEALS 1
+#define DEE_STORE_SEAL_DROP_PAGES 2
 
 /* Dee4ExpertStore() / ~Dee4ExpertStore(). */
 DEE_API int dee_store_create(dee_store** out);
 DEE_API void dee_store_destroy(dee_store* store);
-/* Dee4ExpertStore::open(path, Dee4OpenOptions{verify_segment_hashes})
- * (expert_store.h:286-306, expert_store.cpp:790).  DEE_ERR_INVALID on any
- * failure; the reason is dee_store_last_error(). */
-DEE_API int dee_store_open(dee_store* store, const char* directory_or_metadata, int verify_segment_hashes,
-                           int threads);
+/* Dee4ExpertStore::open(path, Dee4OpenOptions) (expert_store.h:286-306,
+ * expert_store.cpp:790); options = DEE_STORE_* bits, `threads` hash segments
+ * in parallel.  DEE_ERR_INVALID on any failure; the reason is
+ * dee_store_last_error(). */
+DEE_API int dee_store_open(dee_store* store, const char* directory_or_metadata, int options, int threads);
 DEE_API void dee_store_close(dee_store* store);
 DEE_API const char* dee_store_last_error(const dee_store* store);
 /* backend_name() ("dee4", "dee4_trace", "dee4_segmented") and
@@ -422,16 +431,19 @@ DEE_API int dee_store_materialize(dee_store* store, int layer, int expert, void*
 /* Experts [first_expert, first_expert + experts) of layers [first_layer,
  * first_layer + layers) into host memory dst as [layer][expert][record_bytes]
  * (the offload tier's pinned record block; an expert-parallel rank's share),
- * by `threads` parallel preads. */
+ * by `threads` parallel preads.  verify != 0: every file the call reads whole
+ * (a segment, or the data file of a single-file store) is hashed as it
+ * streams in and the call fails closed on a seal mismatch -- the seal check
+ * of open() without a second pass over the disk. */
 DEE_API int dee_store_read_layers(dee_store* store, int first_layer, int layers, int first_expert, int experts,
-                                  void* dst, size_t dst_bytes, int threads, dee_store_read_stats* stats);
+                                  void* dst, size_t dst_bytes, int threads, int verify, dee_store_read_stats* stats);
 /* The same records into device memory d_dst (a resident expert bank),
  * through 2 * threads pinned staging buffers of staging_bytes / (2 * threads)
  * each: every reader thread preads into one buffer while its other buffer's
  * H2D copy runs on `stream`.  Returns after the copies completed. */
 DEE_API int dee_store_upload_layers_device(dee_store* store, int first_layer, int layers, int first_expert,
                                            int experts, void* d_dst, size_t dst_bytes, size_t staging_bytes,
-                                           int threads, void* stream, dee_store_read_stats* stats);
+                                           int threads, int verify, void* stream, dee_store_read_stats* stats);
 /* SHA-256 of n bytes as 64 lowercase hex digits + NUL (the seal function). */
 DEE_API int dee_sha256_hex(const void* data, size_t n, char* out65);
 

@@ -45,6 +45,8 @@ def test_stack_from_store_matches_synthetic(torch_cuda, tmp_path, fmt):
     for layer in range(spec.layers):
         assert torch.equal(res.banks[layer], src.banks[layer]), layer
     assert res.store_fill["records"] == spec.layers * spec.experts
+    # one GPU reads every file whole: the seals are checked during the fill
+    assert res.store_fill["files_verified"] == (spec.layers if fmt == "dee4-v4-segmented" else 1)
     ids_s, tok_s = _decode(torch, res, spec, first, steps)
     assert np.array_equal(ids_s, ids_r) and np.array_equal(tok_s, tok_r)
 
@@ -71,7 +73,8 @@ def test_full_shape_store_upload(torch_cuda, tmp_path):
     with Dee4Store(path) as st:
         st.check_layout(layout)
         block = torch.empty((L * E, layout.bytes), dtype=torch.uint8, device="cuda")
-        fill = st.upload_layers(0, L, block.data_ptr(), block.numel(), torch.cuda.current_stream())
+        fill = st.upload_layers(0, L, block.data_ptr(), block.numel(), torch.cuda.current_stream(), verify=True)
+        assert fill["files_verified"] == L
         for l in range(L):
             assert torch.equal(block[l * E:(l + 1) * E], banks[l])
         print(f"store -> HBM: {fill['bytes_read'] / 1e9:.2f} GB in {fill['seconds']:.3f} s "

@@ -65,6 +65,23 @@ def test_sha256_known_answers():
         assert sha256_hex(data) == hashlib.sha256(data).hexdigest(), n
 
 
+def test_sha256_portable_path_matches():
+    """The portable compression (forced) agrees with the SHA-extension one."""
+    import subprocess
+    import sys
+    code = ("import hashlib, numpy as np\n"
+            "from dee_b200.store import sha256_hex\n"
+            "rng = np.random.default_rng(3)\n"
+            "for n in (0, 3, 64, 65, 1000, 65536 + 17):\n"
+            "    d = rng.integers(0, 256, n, dtype=np.uint8).tobytes()\n"
+            "    assert sha256_hex(d) == hashlib.sha256(d).hexdigest(), n\n"
+            "print('ok')\n")
+    env = dict(os.environ, DEE_SHA256_PORTABLE="1")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", code], env=env, cwd=root, capture_output=True, text=True)
+    assert out.returncode == 0 and "ok" in out.stdout, out.stderr
+
+
 # -- the three formats --------------------------------------------------------
 
 @pytest.mark.parametrize("fmt", ["dee4-v4-segmented", "dee4-v2"])
@@ -212,6 +229,41 @@ def test_segment_files_fail_closed(tmp_path):
     edit_meta(d, lambda m: m["segments"][2].__setitem__("sha256", m["segments"][2]["sha256"].upper()))
     with open_store(d) as s:
         assert s.stored_records == LAYERS * EXPERTS
+
+
+@pytest.mark.parametrize("fmt", ["dee4-v4-segmented", "dee4-v2"])
+def test_fill_checks_seals_in_one_pass(tmp_path, fmt):
+    """A store opened without the seal pass and filled whole with verify:
+    every file is hashed as it streams in; a flipped byte fails the fill;
+    a partial read (an expert-parallel share) verifies nothing."""
+    from dee_b200.store import StoreError
+    d, meta = write(tmp_path, fmt)
+    files = LAYERS if fmt == "dee4-v4-segmented" else 1
+    buf = np.zeros((LAYERS, EXPERTS, SMALL.bytes), dtype=np.uint8)
+    with open_store(d, verify_segment_hashes=False) as s:
+        st = s.read_layers(0, LAYERS, buf.ctypes.data, buf.nbytes, verify=True)
+        assert st["files_verified"] == files and st["records"] == LAYERS * EXPERTS
+        part = np.zeros((LAYERS, 2, SMALL.bytes), dtype=np.uint8)
+        st = s.read_layers(0, LAYERS, part.ctypes.data, part.nbytes, first_expert=2, experts=2, verify=True)
+        assert st["files_verified"] == 0
+    path = os.path.join(d, meta["segments"][3]["file"] if files > 1 else "experts.dee4")
+    data = bytearray(open(path, "rb").read())
+    data[-5] ^= 1
+    open(path, "wb").write(data)
+    with open_store(d, verify_segment_hashes=False) as s:
+        s.read_layers(0, LAYERS, buf.ctypes.data, buf.nbytes)           # unverified fill serves it
+        with pytest.raises(StoreError, match="sha256 mismatch"):
+            s.read_layers(0, LAYERS, buf.ctypes.data, buf.nbytes, verify=True)
+    if files > 1:
+        with open_store(d, verify_segment_hashes=False) as s:        # the sealed files before it pass
+            st = s.read_layers(0, 3, buf.ctypes.data, buf.nbytes, verify=True)
+            assert st["files_verified"] == 3
+
+
+def test_seal_pass_can_drop_pages(tmp_path):
+    d, _ = write(tmp_path)
+    with open_store(d, seal_reads_through_page_cache=True) as s:
+        assert s.num_layers == LAYERS
 
 
 def test_single_file_fails_closed(tmp_path):
