@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--store", default=None,
                     help="stack: read every layer's expert records from this DEE4 store (resident banks "
                          "or, with --offload-gib, the offload tier's pinned host block)")
+    ap.add_argument("--store-cold", action="store_true",
+                    help="drop the store's files from the page cache before the fill (a fill from the disk)")
     ap.add_argument("--export-store", default=None,
                     help="stack on one GPU: write its synthetic records as a DEE4 segmented store here first")
     ap.add_argument("--experts", type=int, default=E,
@@ -421,6 +423,18 @@ def run_reference(args):
 
 # ---------------------------------------------------------------------------
 
+def drop_page_cache(path):
+    """Write back and drop this store's own files from the page cache."""
+    for root, _, files in os.walk(path):
+        for name in files:
+            fd = os.open(os.path.join(root, name), os.O_RDONLY)
+            try:
+                os.fsync(fd)
+                os.posix_fadvise(fd, 0, 0, os.POSIX_FADV_DONTNEED)
+            finally:
+                os.close(fd)
+
+
 def run_stack(args):
     """Config 3: greedy decode of b sequences through the synthetic L-layer
     stack (dee_b200.stack), expert parallel over the launched ranks.  Times
@@ -460,6 +474,8 @@ def run_stack(args):
         torch.cuda.empty_cache()
         if args.store is None:
             args.store = args.export_store
+    if args.store and args.store_cold:
+        drop_page_cache(args.store)
     t0 = time.perf_counter()
     stack = SyntheticStack(torch, spec, tokens=t_local, rank=rank, world=world, transport=args.ep,
                            offload_slots=slots, store=args.store)
@@ -469,7 +485,9 @@ def run_stack(args):
     if stack.store is not None:
         f = stack.store_fill
         store_info = {"backend": stack.store.backend, "identity": stack.store.identity,
-                      "fill_target": "pinned host" if slots else "HBM", "bytes": f["bytes_read"],
+                      "fill_target": "pinned host" if slots else "HBM",
+                      "page_cache": "dropped" if args.store_cold else "as found",
+                      "files_verified": f["files_verified"], "bytes": f["bytes_read"],
                       "seconds": f["seconds"], "gb_per_s": f["gb_per_s"], "pread_calls": f["pread_calls"],
                       "export": export}
     first = torch.from_numpy(seed_tokens(spec, b)[rank * t_local:(rank + 1) * t_local]).cuda()
