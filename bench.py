@@ -55,9 +55,10 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ep", default="p2p", choices=["p2p", "nccl"],
                     help="multi-GPU transport: NVLink peer memory (default) or NCCL all-to-all")
-    ap.add_argument("--workload", default="layer", choices=["layer", "stack"],
-                    help="layer: the one-layer headline (configs 1-2); stack: the synthetic "
-                         "multi-layer greedy decode (config 3)")
+    ap.add_argument("--workload", default="layer", choices=["layer", "prefill", "stack"],
+                    help="layer: the one-layer decode headline (config 1, with the b=1/64 and prefill "
+                         "sweep); prefill: the 4096-token prefill layer alone (config 2); stack: the "
+                         "synthetic multi-layer greedy decode (configs 3-4)")
     ap.add_argument("--layers", type=int, default=43, help="stack layers (--workload stack)")
     ap.add_argument("--offload-gib", type=float, default=0.0,
                     help="stack with the offload tier (config 4): device pool of this many GiB of expert "
@@ -423,6 +424,62 @@ def run_reference(args):
 
 # ---------------------------------------------------------------------------
 
+def run_prefill(args):
+    """Config 2: one 4096-token prefill layer (Zipf(1.1) expert bias), all 256
+    experts resident, timed over `steps` steps with an L2 flush before each.
+    The roofline is the tensor pipe: the gate/up kernel's algorithmic FLOPs
+    over its stage-event time against the measured bf16 peak."""
+    import torch
+    from dee_b200.records import RecordLayout, synthetic_bank
+
+    rank, world, local = dist_env()
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"workload": "prefill", "unavailable": "the prefill layer runs on one GPU"}))
+        return
+    torch.cuda.set_device(local)
+    hbm_peak, tc_peak, peak_kind = load_peaks()
+    global E
+    E = args.experts
+    T = 4096
+    bank = synthetic_bank(RecordLayout(H, I), E, seed=11)
+    eng = build_engine(torch, bank, max_tokens=T)
+    stream = torch.cuda.Stream()
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    launches0 = eng.launch_count()
+    with ClockSampler(local) as clk:
+        times, stages, counts = prefill_point(torch, eng, args.steps, args.warmup, flush, stream, seed=4000)
+    launches = (eng.launch_count() - launches0) / (args.steps + args.warmup + 1)
+    ms = statistics.mean(times)
+    flops = T * K * 3 * 2 * H * I
+    gu_flops = T * K * 2 * 2 * H * I
+    gu_ms = stages.get("gate_up", float("nan"))
+    dn_ms = stages.get("down", float("nan"))
+    achieved = gu_flops / (gu_ms / 1000.0) / 1e12
+    result = {
+        "metric": "MoE-layer tokens/s (T=4096 prefill, Zipf(1.1) expert bias)",
+        "value": T / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "cfg2-prefill-t4096-zipf1.1", "hidden": H, "inter": I, "experts": E, "topk": K,
+                   "tokens_per_step": T, "weights": "fp4-e2m1+ue8m0/32", "parallelism": "single",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "max_expert_rows": int(counts.max()), "active_experts": int((counts > 0).sum())},
+        "tflops_layer": flops / (ms / 1000.0) / 1e12,
+        "tc_frac_layer": flops / (ms / 1000.0) / 1e12 / tc_peak,
+        "tflops_down": (T * K * 2 * H * I) / (dn_ms / 1000.0) / 1e12,
+        "stage_ms": stages,
+        "roofline": {"bound": "tensor", "kernel": "moe_gemm_kernel<gate_up>", "achieved": achieved,
+                     "peak": tc_peak, "unit": "TFLOP/s", "frac": achieved / tc_peak,
+                     "peak_source": f"{peak_kind} bf16_tflops", "traffic": None,
+                     "algorithmic_flops_per_launch": gu_flops},
+        "gpu_launches": int(round(launches * args.steps)),
+        "gpu_launches_per_step": launches,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(result))
+
+
 def drop_page_cache(path):
     """Write back and drop this store's own files from the page cache."""
     for root, _, files in os.walk(path):
@@ -581,6 +638,9 @@ def main():
         return
     if args.workload == "stack":
         run_stack(args)
+        return
+    if args.workload == "prefill":
+        run_prefill(args)
         return
     import torch
     import torch.distributed as dist

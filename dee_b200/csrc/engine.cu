@@ -197,7 +197,7 @@ struct dee_engine {
     float* d_sh_out = nullptr;
     cudaStream_t journal_stream = nullptr;
     size_t h_ids_count = 0;
-    CUtensorMap map_xperm, map_act;      // 16-row token boxes (tcgen05 kernel)
+    CUtensorMap map_xperm_t[4], map_act_t[4];  // token boxes of the tcgen05 kernel
     CUtensorMap map_xperm_dec, map_act_dec;  // token rows of the decode kernel
     uint64_t launches = 0;
     // Opt-in stage timing (the role of the reference's StageProfiler,
@@ -297,21 +297,10 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
     }
     e->cap_sel = cap;
     e->max_tiles = max_tiles;
-    {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), cap};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 2};
-        const cuuint32_t box[2] = {64, 16};
-        if (!encode(e, &e->map_xperm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_xperm, dims, strides,
-                    box, CU_TENSOR_MAP_SWIZZLE_128B, "X_perm"))
-            return DEE_ERR_CUDA;
-    }
-    {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(I), cap};
-        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(I) * 2};
-        const cuuint32_t box[2] = {64, 16};
-        if (!encode(e, &e->map_act, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, e->d_act, dims, strides,
-                    box, CU_TENSOR_MAP_SWIZZLE_128B, "act"))
-            return DEE_ERR_CUDA;
+    if (!encode_gemm_token_maps(get_encode_fn(), e->d_xperm, static_cast<int>(cap), H, e->map_xperm_t) ||
+        !encode_gemm_token_maps(get_encode_fn(), e->d_act, static_cast<int>(cap), I, e->map_act_t)) {
+        e->last_error = "cuTensorMapEncodeTiled failed for the GEMM token maps";
+        return DEE_ERR_CUDA;
     }
     if (!encode_decode_token_map(get_encode_fn(), e->d_act, static_cast<int>(cap), I,
                                  &e->map_act_dec) ||
@@ -362,11 +351,10 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     // Decode-sized calls use the register-dequant kernel (tiles of <= 8 token
     // rows); larger calls the tcgen05 kernel (tiles of <= 128 rows).
     const bool decode = sel <= static_cast<size_t>(kDecodeMaxSelections);
-    const bool large = !decode;
     if (ret && !decode)
         return fail(e, DEE_ERR_UNSUPPORTED, "the NVLink expert-parallel return needs <= " +
                                                 std::to_string(kDecodeMaxSelections) + " rows per rank");
-    const int n_max = decode ? kDecodeTileRows : gemm_n_max(large);
+    const int n_max = decode ? kDecodeTileRows : gemm_n_max();
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm,     e->d_row_of,
                   e->d_tiles,  e->d_n_tiles, write_journal ? e->d_journal : nullptr};
@@ -413,13 +401,13 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
         gm.b = e->map_xperm_dec;
     } else {
         gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3;
-        gm.b = e->map_xperm;
+        for (int i = 0; i < 4; ++i) gm.bt[i] = e->map_xperm_t[i];
     }
     a.k_total = H;
     a.m_tiles = I / 64;
     stage_begin(e, kStageGateUp, stream);
     err = decode ? launch_moe_decode(true, gm, a, e->num_sms, stream)
-                 : launch_moe_gemm(true, large, gm, a, e->num_sms, stream);
+                 : launch_moe_gemm(true, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
     stage_end(e, kStageGateUp, stream);
 
@@ -428,13 +416,13 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
         gm.b = e->map_act_dec;
     } else {
         gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
-        gm.b = e->map_act;
+        for (int i = 0; i < 4; ++i) gm.bt[i] = e->map_act_t[i];
     }
     a.k_total = I;
     a.m_tiles = H / 128;
     stage_begin(e, kStageDown, stream);
     err = decode ? launch_moe_decode(false, gm, a, e->num_sms, stream)
-                 : launch_moe_gemm(false, large, gm, a, e->num_sms, stream);
+                 : launch_moe_gemm(false, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "down GEMM launch");
     stage_end(e, kStageDown, stream);
     e->launches += 4;

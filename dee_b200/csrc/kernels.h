@@ -29,13 +29,14 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 struct GemmMaps {
     CUtensorMap w0, w1, s0, s1, b;
+    CUtensorMap bt[4];  // tcgen05 kernel: token boxes of 16/32/64/128 rows x 128 K
 };
 
-// Largest N (rows per expert tile) of the small / large GEMM configuration.
-int gemm_n_max(bool large);
+// Largest N (rows per expert tile) of the tcgen05 GEMM.
+int gemm_n_max();
 
-cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, const GemmArgs& args,
-                            int grid, cudaStream_t stream);
+cudaError_t launch_moe_gemm(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
+                            cudaStream_t stream);
 
 // Decode-sized groups (tiles of at most kDecodeTileRows token rows): register
 // dequant + mma.sync kernel of moe_decode.cu.  Its tensor maps come from the
@@ -61,6 +62,13 @@ bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t rec
 // stages, 4 for the shared expert's 256-wide ones).
 bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
                              CUtensorMap* map, int box_chunks = 8);
+// The general form: [rows, cols] FP16 viewed as {64, rows, cols/64}, boxes of
+// box_rows rows x box_chunks chunks landing as [chunk][row][128 B] (128-byte
+// swizzle).
+bool encode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols, int box_rows, int box_chunks,
+                      CUtensorMap* map);
+// The tcgen05 GEMM's four token maps (boxes of 16/32/64/128 rows x 128 K).
+bool encode_gemm_token_maps(EncodeTiledFn fn, const void* rows_base, int rows, int cols, CUtensorMap* maps);
 
 // The shared expert (moe_shared.cu): dense F8_E4M3 projections W1, W3
 // [inter, H] and W2 [H, inter] with E8M0 scales per 128 x 128 tile.

@@ -558,10 +558,15 @@ bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t rec
 // stage, landing as [chunk][row][128 B] with the 128-byte swizzle.
 bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols,
                              CUtensorMap* map, int box_chunks) {
+    return encode_token_map(fn, rows_base, rows, cols, 8, box_chunks, map);
+}
+
+bool encode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols, int box_rows, int box_chunks,
+                      CUtensorMap* map) {
     if (!fn) return false;
     const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(cols / 64)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(cols) * 2, 128};
-    const cuuint32_t box[3] = {64, 8, static_cast<cuuint32_t>(box_chunks)};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), static_cast<cuuint32_t>(box_chunks)};
     const cuuint32_t elem[3] = {1, 1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(rows_base), dims, strides, box,
               elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

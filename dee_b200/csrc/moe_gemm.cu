@@ -89,19 +89,24 @@ __device__ __forceinline__ bool load_item(const GemmArgs& a, int item, ItemInfo&
     return slot >= 0 && slot < a.num_slots && out.td.n_pad >= 16 && out.td.n_pad % 16 == 0;
 }
 
-template <class Cfg, GemmMode MODE>
+// Token box for a tile of n_pad rows: index into the 16/32/64/128-row maps.
+__device__ __forceinline__ int token_box(int n_pad) {
+    return n_pad <= 16 ? 0 : n_pad <= 32 ? 1 : n_pad <= 64 ? 2 : 3;
+}
+
+template <GemmMode MODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap map_w0,   // w1 (gate/up) or w2 (down)
                     const __grid_constant__ CUtensorMap map_w1,   // w3 (gate/up only)
                     const __grid_constant__ CUtensorMap map_s0,   // s1 or s2
                     const __grid_constant__ CUtensorMap map_s1,   // s3 (gate/up only)
-                    const __grid_constant__ CUtensorMap map_b,    // X_perm or act
+                    const __grid_constant__ CUtensorMap map_b16,  // X_perm or act, 16-row boxes
+                    const __grid_constant__ CUtensorMap map_b32,
+                    const __grid_constant__ CUtensorMap map_b64,
+                    const __grid_constant__ CUtensorMap map_b128,
                     const GemmArgs args) {
-    constexpr int NMAX = Cfg::kNMax;
-    constexpr int PK = Cfg::kPk;
-    constexpr int BS = Cfg::kB;
-    constexpr int AS = Cfg::kA;
     constexpr bool kGU = MODE == GemmMode::kGateUp;
+    constexpr int kPrefetch = 2;  // packed stages prefetched into L2 beyond the ring
 
     // The gate/up GEMM follows the kernels that write its tile list and
     // token rows, so it waits before reading anything.  The down GEMM
@@ -122,16 +127,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
     uint8_t* pk_smem = smem;
-    uint8_t* b_smem = pk_smem + PK * kPkStageBytes;
-    uint8_t* sc_smem = b_smem + BS * Cfg::kBStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sc_smem + PK * kScStageBytes);
-    uint64_t* pk_full = bars;
-    uint64_t* pk_empty = pk_full + PK;
-    uint64_t* b_full = pk_empty + PK;
-    uint64_t* b_empty = b_full + BS;
-    uint64_t* a_full = b_empty + BS;
-    uint64_t* a_empty = a_full + AS;
-    uint64_t* acc_full = a_empty + AS;
+    uint8_t* b_smem = pk_smem + kPkStages * kPkStageBytes;
+    uint8_t* sc_smem = b_smem + kBStages * kBStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sc_smem + kPkStages * kScStageBytes);
+    uint64_t* pk_full = bars;                  // packed weight stage landed (TMA)
+    uint64_t* pk_empty = pk_full + kPkStages;  // all 8 dequantiser warps done with it
+    uint64_t* full = pk_empty + kPkStages;     // 128-K step: A written (4 warps) + B landed (TMA)
+    uint64_t* empty = full + kAStages;         // 128-K step consumed by the MMAs (commit)
+    uint64_t* acc_full = empty + kAStages;
     uint64_t* acc_empty = acc_full + 2;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_empty + 2);
 
@@ -139,29 +142,33 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < PK; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 8); }
-        for (int i = 0; i < BS; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-        for (int i = 0; i < AS; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < kPkStages; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 8); }
+        for (int i = 0; i < kAStages; ++i) { mbar_init(&full[i], 5); mbar_init(&empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
         fence_barrier_init();
     }
     if (warp == 2) {
-        tmem_alloc(tmem_holder, Cfg::kTmemCols);
+        tmem_alloc(tmem_holder, kTmemCols);
         tmem_relinquish();
     }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&map_w0);
         prefetch_tmap(&map_s0);
-        prefetch_tmap(&map_b);
         if (kGU) { prefetch_tmap(&map_w1); prefetch_tmap(&map_s1); }
+    }
+    if (warp == 1 && lane == 0) {
+        prefetch_tmap(&map_b16);
+        prefetch_tmap(&map_b32);
+        prefetch_tmap(&map_b64);
+        prefetch_tmap(&map_b128);
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
-    const int k_stages = args.k_total / kKStage;
-    const int k_blocks = args.k_total / kKBlock;
+    const int k_stages = args.k_total / kKStage;  // packed weight stages per item
+    const int a_steps = args.k_total / kAK;       // 128-K steps per item (even)
     uint32_t* status = args.status;
     if (!kGU && warp != 0) pdl_wait();
     pdl_trigger();
@@ -173,7 +180,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             int ps = 0;
             uint32_t pphase = 0;
             bool ok = true;
-            // L2 prefetch cursor: runs Cfg::kPrefetch stages ahead of the loads
+            // L2 prefetch cursor: runs kPrefetch stages ahead of the loads
             int pf_item = blockIdx.x, pf_s = 0, pf_slot = 0, pf_m = 0;
             bool pf_valid = false;
             auto pf_advance = [&]() {
@@ -201,22 +208,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tma_prefetch_3d(&map_w0, xk + 128, pf_m * 128, pf_slot);
                 }
             };
-            if (Cfg::kPrefetch > 0) {
+            pf_advance();
+            for (int i = 0; i < kPkStages + kPrefetch && pf_valid; ++i) {
+                pf_issue();
                 pf_advance();
-                for (int i = 0; i < PK + Cfg::kPrefetch && pf_valid; ++i) {
-                    pf_issue();
-                    pf_advance();
-                }
             }
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 ItemInfo it;
                 if (!load_item(args, item, it)) { atomicOr(status, kStatusBadExpert); }
                 const int slot = (it.slot < 0 || it.slot >= args.num_slots) ? 0 : it.slot;
                 for (int s = 0; s < k_stages; ++s) {
-                    if (Cfg::kPrefetch > 0) {
-                        pf_issue();
-                        pf_advance();
-                    }
+                    pf_issue();
+                    pf_advance();
                     if (!mbar_wait(&pk_empty[ps], pphase ^ 1, status, kStatusTimeoutTma)) { ok = false; break; }
                     mbar_arrive_expect_tx(&pk_full[ps], kPkStageBytes + kScStageBytes);
                     uint8_t* dst = pk_smem + ps * kPkStageBytes;
@@ -236,71 +239,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         tma_load_3d(dst + 16384, &map_w0, &pk_full[ps], xk + 128, row, slot, pol);
                         tma_load_3d(sdst, &map_s0, &pk_full[ps], s * 16, row, slot, pol);
                     }
-                    if (++ps == PK) { ps = 0; pphase ^= 1; }
+                    if (++ps == kPkStages) { ps = 0; pphase ^= 1; }
                 }
             }
         }
     } else if (warp == 1) {
         // ---------------- token operand producer ----------------
+        // Step g (a CTA-wide count of 128-K steps) lands in buffer g % 3 and
+        // completes full[g % 4]; the buffer is free again once the MMAs of
+        // step g - 3 have completed, i.e. after empty[(g - 3) % 4] phase
+        // (g - 3) / 4.  (That barrier cannot run two phases ahead: its next
+        // phase needs step g + 1, whose tokens this thread has not loaded.)
         if (lane == 0) {
             const uint64_t pol = policy_evict_last();
-            int bs = 0;
-            uint32_t bphase = 0;
+            uint32_t g = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
                 ItemInfo it;
                 load_item(args, item, it);
-                const int n_pad = min(it.td.n_pad, NMAX);
-                for (int kb0 = 0; kb0 < k_blocks; kb0 += Cfg::kBKb) {
-                    if (!mbar_wait(&b_empty[bs], bphase ^ 1, status, kStatusTimeoutTma)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&b_full[bs], n_pad * 128 * Cfg::kBKb);
-                    uint8_t* dst = b_smem + bs * Cfg::kBStageBytes;
-                    for (int j = 0; j < Cfg::kBKb; ++j)
-                        for (int r = 0; r < n_pad; r += 16)
-                            tma_load_2d(dst + j * (NMAX * 128) + r * 128, &map_b, &b_full[bs],
-                                        (kb0 + j) * kKBlock, it.td.row_start + r, pol);
-                    if (++bs == BS) { bs = 0; bphase ^= 1; }
+                const int n_pad = min(it.td.n_pad, kNMax);
+                const int box = token_box(n_pad);
+                const int rows = 16 << box;
+                const CUtensorMap* map = box == 0 ? &map_b16 : box == 1 ? &map_b32 : box == 2 ? &map_b64 : &map_b128;
+                for (int st = 0; st < a_steps; ++st, ++g) {
+                    if (g >= static_cast<uint32_t>(kBStages)) {
+                        const uint32_t gp = g - kBStages;
+                        if (!mbar_wait(&empty[gp % kAStages], (gp / kAStages) & 1u, status, kStatusTimeoutTma)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    uint64_t* bar = &full[g % kAStages];
+                    mbar_arrive_expect_tx(bar, rows * 128 * (kAK / kKBlock));
+                    tma_load_3d(b_smem + (g % kBStages) * kBStageBytes, map, bar, 0, it.td.row_start,
+                                st * (kAK / kKBlock), pol);
                 }
             }
         }
     } else if (warp == 2) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int as = 0, bs = 0;
-            uint32_t aphase = 0, bphase = 0;
+            uint32_t g = 0;
             bool ok = true;
             int local = 0;
             for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
                 ItemInfo it;
                 load_item(args, item, it);
-                const int n_pad = min(it.td.n_pad, NMAX);
+                const int n_pad = min(it.td.n_pad, kNMax);
+                const uint32_t chunk_bytes = static_cast<uint32_t>(16 << token_box(n_pad)) * 128u;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, status, kStatusTimeoutMma)) break;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + Cfg::kAccBase + acc * NMAX;
+                const uint32_t d_tmem = tmem_base + kAccBase + acc * kNMax;
                 const uint32_t idesc = idesc_f16_f32(128, n_pad);
-                for (int kb = 0; kb < k_blocks; ++kb) {
-                    const int j = kb % Cfg::kBKb;  // K step within the token-operand stage
-                    if (!mbar_wait(&a_full[as], aphase, status, kStatusTimeoutMma) ||
-                        (j == 0 && !mbar_wait(&b_full[bs], bphase, status, kStatusTimeoutMma))) {
+                for (int st = 0; st < a_steps; ++st, ++g) {
+                    const uint32_t s = g % kAStages;
+                    if (!mbar_wait(&full[s], (g / kAStages) & 1u, status, kStatusTimeoutMma)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_tmem = tmem_base + as * 32;
-                    const uint32_t b_addr = smem_u32(b_smem + bs * Cfg::kBStageBytes + j * (NMAX * 128));
+                    const uint32_t a_tmem = tmem_base + s * (kAK / 2);
+                    const uint32_t b_addr = smem_u32(b_smem + (g % kBStages) * kBStageBytes);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        mma_f16_ts(d_tmem, a_tmem + q * 8, smem_desc_k128(b_addr + q * 32), idesc,
-                                   (kb | q) != 0 ? 1u : 0u);
+                    for (int c = 0; c < kAK / kKBlock; ++c) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            mma_f16_ts(d_tmem, a_tmem + c * 32 + q * 8,
+                                       smem_desc_k128(b_addr + c * chunk_bytes + q * 32), idesc,
+                                       (st | c | q) != 0 ? 1u : 0u);
+                        }
                     }
-                    mma_commit(&a_empty[as]);
-                    if (++as == AS) { as = 0; aphase ^= 1; }
-                    if (j == Cfg::kBKb - 1) {
-                        mma_commit(&b_empty[bs]);
-                        if (++bs == BS) { bs = 0; bphase ^= 1; }
-                    }
+                    mma_commit(&empty[s]);
                 }
                 if (!ok) break;
                 mma_commit(&acc_full[acc]);
@@ -308,9 +319,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp <= 10) {
         // ---------------- dequantisers (TMEM lane = thread's weight row) ----------------
-        // Two warpgroups split the eight 64-wide K steps of a packed stage
-        // (even steps: warps 3-6, odd steps: warps 7-10); each thread owns
-        // one weight row, i.e. one TMEM lane.
+        // Warpgroup wg takes the 128-K steps g with g % 2 == wg (two of the
+        // four in each packed stage); each thread owns one weight row, i.e.
+        // one TMEM lane, and writes its 128 FP16 weights to A stage g % 4.
         const int wg = (warp - 3) >> 2;
         const int quad = warp & 3;
         const int L = quad * 32 + lane;  // TMEM lane / A row
@@ -325,44 +336,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int ps = 0;
         uint32_t pphase = 0;
-        uint32_t g = 0;  // K steps issued so far by this CTA (both warpgroups)
+        uint32_t g = 0;  // 128-K steps so far in this CTA (both warpgroups)
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             for (int s = 0; s < k_stages && ok; ++s) {
                 ok = mbar_wait(&pk_full[ps], pphase, status, kStatusTimeoutDequant);
                 if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-                const uint8_t* st = pk_smem + ps * kPkStageBytes;
+                const uint8_t* stg = pk_smem + ps * kPkStageBytes;
                 const uint4 sc = *reinterpret_cast<const uint4*>(sc_smem + ps * kScStageBytes + srow * 16);
                 const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
-                const uint32_t sshift = 16u * static_cast<uint32_t>(wg);
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    const int j = 2 * jj + wg;  // K step within the stage
-                    const int c0 = (j & 3) * 2;
-                    const uint8_t* rowp = st + (jj >> 1) * 16384 + srow * 128;
-                    const uint4 q0 = *reinterpret_cast<const uint4*>(rowp + ((c0 ^ sw) << 4));
-                    const uint4 q1 = *reinterpret_cast<const uint4*>(rowp + (((c0 + 1) ^ sw) << 4));
-                    const uint32_t sb0 = (scw[jj] >> sshift) & 0xFFu;
-                    const uint32_t sb1 = (scw[jj] >> (sshift + 8)) & 0xFFu;
-                    uint32_t v[32];
-                    dequant_block32(q0, sb0, v);
-                    dequant_block32(q1, sb1, v + 16);
-                    const uint32_t gi = g + static_cast<uint32_t>(j);
-                    const int as = static_cast<int>(gi % AS);
-                    const uint32_t aphase = (gi / AS) & 1u;
-                    const bool got = mbar_wait(&a_empty[as], aphase ^ 1, status, kStatusTimeoutDequant);
+                for (int h = 0; h < 2; ++h) {
+                    const int a = 2 * h + wg;  // 128-K step within the packed stage
+                    const uint8_t* rowp = stg + (a >> 1) * 16384 + srow * 128;
+                    const int c0 = (a & 1) * 4;
+                    uint32_t v0[32], v1[32];
+#pragma unroll
+                    for (int b = 0; b < 4; ++b) {
+                        const uint4 q = *reinterpret_cast<const uint4*>(rowp + (((c0 + b) ^ sw) << 4));
+                        dequant_block32(q, (scw[a] >> (8 * b)) & 0xFFu, b < 2 ? v0 + 16 * b : v1 + 16 * (b - 2));
+                    }
+                    const uint32_t gi = g + static_cast<uint32_t>(a);
+                    const uint32_t as = gi % kAStages;
+                    const bool got = mbar_wait(&empty[as], ((gi / kAStages) & 1u) ^ 1u, status, kStatusTimeoutDequant);
                     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                     tc_fence_after();
-                    tmem_st_32x32b_x32(tmem_base + lane_addr + as * 32, v);
+                    const uint32_t col = tmem_base + lane_addr + as * (kAK / 2);
+                    tmem_st_32x32b_x32(col, v0);
+                    tmem_st_32x32b_x32(col + 32, v1);
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[as]);
+                    if (lane == 0) mbar_arrive(&full[as]);
                 }
-                g += 8;
+                g += kKStage / kAK;
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&pk_empty[ps]);
-                if (++ps == PK) { ps = 0; pphase ^= 1; }
+                if (++ps == kPkStages) { ps = 0; pphase ^= 1; }
             }
         }
     } else {
@@ -374,14 +384,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++local) {
             ItemInfo it;
             const bool valid = load_item(args, item, it);
-            const int n_rows = min(it.td.n_rows, NMAX);
-            const int n_pad = min(it.td.n_pad, NMAX);
+            const int n_rows = min(it.td.n_rows, kNMax);
+            const int n_pad = min(it.td.n_pad, kNMax);
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             const bool got = mbar_wait(&acc_full[acc], acc_phase, status, kStatusTimeoutEpilogue);
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
-            const uint32_t col0 = tmem_base + lane_addr + Cfg::kAccBase + acc * NMAX;
+            const uint32_t col0 = tmem_base + lane_addr + kAccBase + acc * kNMax;
             for (int c = 0; c < n_pad; c += 16) {
                 uint32_t v[16];
                 tmem_ld_32x32b_x16(col0 + c, v);
@@ -428,42 +438,37 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     if (warp == 2) {
         __syncwarp();
-        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
-template <class Cfg, GemmMode MODE>
+template <GemmMode MODE>
 cudaError_t launch_one(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
-    auto kern = moe_gemm_kernel<Cfg, MODE>;
+    auto kern = moe_gemm_kernel<MODE>;
     static bool configured = false;
     if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg::kSmemBytes);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), Cfg::kSmemBytes, stream, maps.w0,
-                      maps.w1, maps.s0, maps.s1, maps.b, args);
+    return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), kGemmSmemBytes, stream, maps.w0, maps.w1, maps.s0,
+                      maps.s1, maps.bt[0], maps.bt[1], maps.bt[2], maps.bt[3], args);
 }
-
-// Decode-sized tiles: token rows for a whole 512-wide K stage per load (the
-// token operand then costs one TMA round trip per eight K steps) and packed
-// weights prefetched into L2 four stages beyond the shared-memory ring.
-using CfgSmall = GemmConfig<16, 4, 4, 8, 8, 4>;
-using CfgLarge = GemmConfig<128, 3, 6, 1, 4, 2>;
 
 }  // namespace
 
-int gemm_n_max(bool large) { return large ? CfgLarge::kNMax : CfgSmall::kNMax; }
+int gemm_n_max() { return kNMax; }
 
-cudaError_t launch_moe_gemm(bool gate_up, bool large, const GemmMaps& maps, const GemmArgs& args,
-                            int grid, cudaStream_t stream) {
-    if (gate_up) {
-        return large ? launch_one<CfgLarge, GemmMode::kGateUp>(maps, args, grid, stream)
-                     : launch_one<CfgSmall, GemmMode::kGateUp>(maps, args, grid, stream);
-    }
-    return large ? launch_one<CfgLarge, GemmMode::kDown>(maps, args, grid, stream)
-                 : launch_one<CfgSmall, GemmMode::kDown>(maps, args, grid, stream);
+cudaError_t launch_moe_gemm(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
+    if (args.k_total % kKStage || (args.k_total / kAK) % 2) return cudaErrorInvalidValue;
+    return gate_up ? launch_one<GemmMode::kGateUp>(maps, args, grid, stream)
+                   : launch_one<GemmMode::kDown>(maps, args, grid, stream);
+}
+
+bool encode_gemm_token_maps(EncodeTiledFn fn, const void* rows_base, int rows, int cols, CUtensorMap* maps) {
+    for (int b = 0; b < kTokenBoxes; ++b)
+        if (!encode_token_map(fn, rows_base, rows, cols, 16 << b, kAK / kKBlock, &maps[b])) return false;
+    return true;
 }
 
 }  // namespace dee

@@ -11,11 +11,12 @@
 //
 // Roles (one CTA per SM, persistent over a static round-robin work list):
 //   warp 0      TMA producer of packed FP4 weight tiles + UE8M0 scale tiles
-//   warp 1      TMA producer of the token operand (X_perm or act) tiles
+//   warp 1      TMA producer of the token operand (X_perm or act): one 3-D
+//               box per 128-K step, 16/32/64/128 rows to fit the tile
 //   warp 2      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 3-10  dequantisers, two warpgroups taking alternate 64-wide K steps:
-//               each thread owns one weight row (one TMEM lane), turns 64
-//               packed nibbles into 64 FP16 weights per step and writes them
+//   warps 3-10  dequantisers, two warpgroups taking alternate 128-wide K steps:
+//               each thread owns one weight row (one TMEM lane), turns 128
+//               packed nibbles into 128 FP16 weights per step and writes them
 //               to a tensor-memory A buffer with tcgen05.st
 //   warps 11-14 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
 //               scatter, global stores
@@ -81,30 +82,26 @@ constexpr int kGemmThreads = 480;     // 15 warps
 constexpr int kPkStageBytes = 32768;  // 128 rows x 256 packed bytes (K = 512)
 constexpr int kScStageBytes = 2048;   // 128 rows x 16 scale bytes
 constexpr int kKStage = 512;          // K elements per packed stage
-constexpr int kKBlock = 64;           // K elements per A/B step (one 128B row of FP16)
+constexpr int kKBlock = 64;           // K elements per 128-byte row of FP16
 
-// N_MAX: largest MMA N (token rows per tile); PK_STAGES: packed-weight
-// stages in shared memory; B_STAGES x B_KB: token-operand stages, each
-// covering B_KB 64-wide K steps; A_STAGES: tensor-memory A buffers;
-// PREFETCH: packed stages prefetched into L2 ahead of the shared-memory ring.
-template <int N_MAX, int PK_STAGES, int B_STAGES, int B_KB, int A_STAGES, int PREFETCH>
-struct GemmConfig {
-    static constexpr int kNMax = N_MAX;
-    static constexpr int kPk = PK_STAGES;
-    static constexpr int kB = B_STAGES;
-    static constexpr int kBKb = B_KB;
-    static constexpr int kA = A_STAGES;
-    static constexpr int kPrefetch = PREFETCH;
-    static constexpr int kBStageBytes = N_MAX * 128 * B_KB;
-    static constexpr int kAccBase = A_STAGES * 32;
-    static constexpr int kTmemCols = 512;
-    static_assert(N_MAX % 16 == 0 && N_MAX <= 256, "N_MAX");
-    static_assert(kAccBase + 2 * N_MAX <= kTmemCols, "tensor memory budget");
-    static_assert(A_STAGES % 2 == 0, "each A stage must belong to one dequantiser warpgroup");
-    static constexpr int kSmemBytes = 1024 /*align slack*/ + PK_STAGES * kPkStageBytes +
-                                      B_STAGES * kBStageBytes + PK_STAGES * kScStageBytes +
-                                      1024 /*barriers*/;
-    static_assert(kSmemBytes <= 232448, "shared memory budget");
-};
+// The pipeline between the dequantisers, the token producer and the MMA
+// issuer moves in steps of kAK = 128 K: one full/empty handshake per eight
+// K = 16 MMAs.  (A handshake costs the single issuing thread one mbarrier
+// wait and one tcgen05.commit -- together ~150 cycles in which at most one
+// queued MMA keeps the tensor pipe busy -- so per-64-K handshakes idled the
+// pipe for over half the time at N <= 128.)
+constexpr int kAK = 128;
+constexpr int kAStages = 4;                  // tensor-memory A stages, 64 columns each
+constexpr int kBStages = 3;                  // token-operand stages in shared memory
+constexpr int kNMax = 128;                   // MMA N (token rows per tile)
+constexpr int kBStageBytes = kNMax * 128 * (kAK / kKBlock);  // 32 KB
+constexpr int kPkStages = 3;
+constexpr int kAccBase = kAStages * (kAK / 2);               // first accumulator column
+constexpr int kTmemCols = 512;
+constexpr int kTokenBoxes = 4;               // token boxes of 16, 32, 64 and 128 rows
+static_assert(kAccBase + 2 * kNMax <= kTmemCols, "tensor memory budget");
+constexpr int kGemmSmemBytes = 1024 /*align slack*/ + kPkStages * kPkStageBytes + kBStages * kBStageBytes +
+                               kPkStages * kScStageBytes + 1024 /*barriers*/;
+static_assert(kGemmSmemBytes <= 232448, "shared memory budget");
 
 }  // namespace dee

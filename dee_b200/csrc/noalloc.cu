@@ -215,6 +215,10 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
         ok = ok && enc(&dn.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base + sp.act, d, st, box,
                        CU_TENSOR_MAP_SWIZZLE_128B);
     }
+    if (!decode) {
+        ok = ok && encode_gemm_token_maps(encode_fn(), base + sp.xperm, static_cast<int>(sel), H, gu.bt);
+        ok = ok && encode_gemm_token_maps(encode_fn(), base + sp.act, static_cast<int>(sel), I, dn.bt);
+    }
     if (decode) {
         ok = ok && encode_decode_weight_maps(encode_fn(), rec, record_bytes, n_slots, H, I, &gu, &dn);
         ok = ok && encode_decode_token_map(encode_fn(), base + sp.xperm, static_cast<int>(sel), H, &gu.b);
@@ -228,7 +232,6 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     identity_slots_kernel<<<1, 256, 0, stream>>>(slots, E);
     if ((err = cudaGetLastError()) != cudaSuccess) return report(DEE_ERR_CUDA, cudaGetErrorString(err));
 
-    const bool large = !decode;
     PermuteOut po{reinterpret_cast<int32_t*>(base + sp.counts),
                   reinterpret_cast<int32_t*>(base + sp.offsets),
                   reinterpret_cast<int32_t*>(base + sp.perm),
@@ -236,7 +239,7 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
                   reinterpret_cast<TileDesc*>(base + sp.tiles),
                   reinterpret_cast<int32_t*>(base + sp.n_tiles),
                   nullptr};
-    err = launch_permute(d_ids, tokens, K, E, decode ? kDecodeTileRows : gemm_n_max(large),
+    err = launch_permute(d_ids, tokens, K, E, decode ? kDecodeTileRows : gemm_n_max(),
                          sp.max_tiles, po, status, stream);
     if (err == cudaSuccess)
         err = launch_gather_rows(static_cast<const __half*>(d_x_f16), po.perm, po.offsets + E,
@@ -265,12 +268,12 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     a.k_total = H;
     a.m_tiles = I / 64;
     err = decode ? launch_moe_decode(true, gu, a, num_sms, stream)
-                 : launch_moe_gemm(true, large, gu, a, num_sms, stream);
+                 : launch_moe_gemm(true, gu, a, num_sms, stream);
     if (err == cudaSuccess) {
         a.k_total = I;
         a.m_tiles = H / 128;
         err = decode ? launch_moe_decode(false, dn, a, num_sms, stream)
-                     : launch_moe_gemm(false, large, dn, a, num_sms, stream);
+                     : launch_moe_gemm(false, dn, a, num_sms, stream);
     }
     if (err == cudaSuccess)
         err = launch_combine_f32(a.raw, d_weights, tokens, K, H, d_out_f32, stream);

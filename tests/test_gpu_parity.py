@@ -139,6 +139,68 @@ def test_moe_raw_small_shape(torch_cuda, oracle_mod, T, dup):
     assert np.array_equal(eng.journal_ids(T), ids)
 
 
+def _skewed_ids(rng, T, E, K, s=1.3):
+    """Distinct per-token ids drawn with Zipf(s) expert popularity: a few
+    experts take many rows (several 128-row tiles), most take a handful."""
+    p = np.arange(1, E + 1, dtype=np.float64) ** -s
+    p /= p.sum()
+    perm = rng.permutation(E)
+    return np.stack([perm[rng.choice(E, size=K, replace=False, p=p)] for _ in range(T)]).astype(np.int32)
+
+
+@pytest.mark.parametrize("H,I,T", [(512, 1024, 400), (1024, 512, 700)])
+def test_moe_raw_skewed_groups(torch_cuda, oracle_mod, H, I, T):
+    """The tensor-memory grouped GEMM over ragged groups: tiles of every
+    token-box size (16, 32, 64 and 128 rows) and experts spanning several
+    tiles, against the oracle per selection."""
+    torch = torch_cuda
+    orc = oracle_mod
+    E, K = 48, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=H + I + T, kind="normal")
+    rng = np.random.default_rng(T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _skewed_ids(rng, T, E, K, s=1.5)
+    counts = np.bincount(ids.ravel(), minlength=E)
+    assert counts.max() > 256 and (counts[counts > 0] <= 16).any()
+    assert ((counts > 16) & (counts <= 32)).any() and ((counts > 32) & (counts <= 64)).any()
+    eng = _engine(H, I, E, K, max_tokens=T)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    raw = _run_layer(torch, eng, bank, x16, ids, None)
+    want = orc.moe_layer_raw(recs, layout, x16, ids)
+    assert np.isfinite(raw).all()
+    assert orc.rel_l2(raw, want) <= TOL_REL_L2
+    per = [orc.rel_l2(raw[t, r], want[t, r]) for t in range(T) for r in range(K)]
+    assert max(per) <= 5 * TOL_REL_L2
+
+
+def test_full_shape_prefill_rows_match_decode(torch_cuda):
+    """DeepSeek-V4 shapes, 4096 tokens with Zipf(1.1)-skewed routing through
+    the tensor-memory grouped GEMM: the raw rows of sampled tokens equal
+    (within the FP32-summation tolerance) the same tokens' rows from the
+    register-dequant decode kernel, itself checked against the oracle at these
+    shapes in test_full_shape_decode."""
+    torch = torch_cuda
+    from dee_b200.records import RecordLayout, synthetic_bank
+    H, I, E, K, T = 4096, 2048, 256, 6, 4096
+    bank = synthetic_bank(RecordLayout(H, I), E, seed=77)
+    eng = _engine(H, I, E, K, max_tokens=T)
+    eng.attach_bank(0, bank)
+    rng = np.random.default_rng(78)
+    ids = _skewed_ids(rng, T, E, K, s=1.1)
+    x16 = rng.standard_normal((T, H)).astype(np.float16).view(np.uint16)
+    raw = _run_layer(torch, eng, bank, x16, ids, None)
+    assert np.isfinite(raw).all()
+    sample = np.concatenate([rng.choice(T, 8, replace=False)])
+    dec = _run_layer(torch, eng, bank, x16[sample].copy(), ids[sample].copy(), None)
+    for i, t in enumerate(sample):
+        for r in range(K):
+            num = np.linalg.norm((raw[t, r] - dec[i, r]).astype(np.float64))
+            den = np.linalg.norm(dec[i, r].astype(np.float64))
+            assert num <= 1e-3 * den, (t, r, num / den)
+
+
 def _plant_edge_rows(layout, recs, rng, experts, frac=0.25):
     """Give a fraction of the W2 rows of `experts` one scale byte for the
     whole row, drawn from the limits of the exact-FP16 dequant range: 60, 100
