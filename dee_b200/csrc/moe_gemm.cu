@@ -278,44 +278,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else if (warp == 2) {
         // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            uint32_t g = 0;
-            bool ok = true;
-            int local = 0;
-            for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
-                ItemInfo it;
-                load_item(args, item, it);
-                const int n_pad = min(it.td.n_pad, kNMax);
-                const uint32_t chunk_bytes = static_cast<uint32_t>(16 << token_box(n_pad)) * 128u;
-                const int acc = local & 1;
-                const uint32_t acc_phase = (local >> 1) & 1;
-                if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, status, kStatusTimeoutMma)) break;
+        // The whole warp runs the loop, so descriptors and addresses are
+        // warp-uniform values; one elected lane issues the MMAs and commits.
+        uint32_t g = 0;
+        bool ok = true;
+        int local = 0;
+        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++local) {
+            ItemInfo it;
+            load_item(args, item, it);
+            const int n_pad = min(it.td.n_pad, kNMax);
+            const uint32_t chunk_bytes = static_cast<uint32_t>(16 << token_box(n_pad)) * 128u;
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            ok = mbar_wait(&acc_empty[acc], acc_phase ^ 1, status, kStatusTimeoutMma);
+            if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + kAccBase + acc * kNMax;
+            const uint32_t idesc = idesc_f16_f32(128, n_pad);
+            for (int st = 0; st < a_steps; ++st, ++g) {
+                const uint32_t s = g % kAStages;
+                ok = mbar_wait(&full[s], (g / kAStages) & 1u, status, kStatusTimeoutMma);
+                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + kAccBase + acc * kNMax;
-                const uint32_t idesc = idesc_f16_f32(128, n_pad);
-                for (int st = 0; st < a_steps; ++st, ++g) {
-                    const uint32_t s = g % kAStages;
-                    if (!mbar_wait(&full[s], (g / kAStages) & 1u, status, kStatusTimeoutMma)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t a_tmem = tmem_base + s * (kAK / 2);
-                    const uint32_t b_addr = smem_u32(b_smem + (g % kBStages) * kBStageBytes);
+                const uint32_t a_tmem = tmem_base + s * (kAK / 2);
+                const uint64_t desc0 = smem_desc_k128(smem_u32(b_smem + (g % kBStages) * kBStageBytes));
+                if (elect_one()) {
 #pragma unroll
                     for (int c = 0; c < kAK / kKBlock; ++c) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
-                            mma_f16_ts(d_tmem, a_tmem + c * 32 + q * 8,
-                                       smem_desc_k128(b_addr + c * chunk_bytes + q * 32), idesc,
-                                       (st | c | q) != 0 ? 1u : 0u);
+                            // +16-byte units in the descriptor's start-address field
+                            mma_f16_ts(d_tmem, a_tmem + c * 32 + q * 8, desc0 + ((c * chunk_bytes + q * 32) >> 4),
+                                       idesc, (st | c | q) != 0 ? 1u : 0u);
                         }
                     }
                     mma_commit(&empty[s]);
                 }
-                if (!ok) break;
-                mma_commit(&acc_full[acc]);
+                __syncwarp();
             }
+            if (!ok) break;
+            if (elect_one()) mma_commit(&acc_full[acc]);
+            __syncwarp();
         }
     } else if (warp <= 10) {
         // ---------------- dequantisers (TMEM lane = thread's weight row) ----------------
