@@ -395,38 +395,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const uint32_t col0 = tmem_base + lane_addr + kAccBase + acc * kNMax;
-            for (int c = 0; c < n_pad; c += 16) {
-                uint32_t v[16];
-                tmem_ld_32x32b_x16(col0 + c, v);
+            // 32 columns (token rows) per load; the accumulator holds kNMax
+            // columns, so a chunk past n_pad stays inside it.
+            for (int c = 0; c < n_pad; c += 32) {
+                uint32_t v[32];
+                tmem_ld_32x32b_x32(col0 + c, v);
                 tmem_wait_ld();
                 if (!valid) continue;
+                // lane j holds the grouped position of chunk row j
+                const int prow = c + lane < n_rows ? args.perm[it.td.row_start + c + lane] : 0;
                 if (kGU) {
+                    // Lanes 0-15 hold gate rows, 16-31 the matching up rows.
+                    // Per column pair (i, i+1) the gate lane finishes column i
+                    // and the up lane column i+1: one exchange, every lane busy.
                     const bool is_gate = lane < 16;
                     const int feat = it.m * 64 + 16 * quad + (lane & 15);
                     const float lim = args.swiglu_limit;
+                    const bool off = args.official != 0;
+                    const float wl = (off && args.route_w && c + lane < n_rows) ? args.route_w[prow] : 1.0f;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float mine = __uint_as_float(v[i]);
-                        const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-                        // columns alternate between the two half-warps
-                        if ((i & 1) != (is_gate ? 0 : 1)) continue;
-                        const int col = c + i;
-                        if (col >= n_rows) continue;
-                        const float w = (args.official && args.route_w)
-                                            ? args.route_w[args.perm[it.td.row_start + col]]
-                                            : 1.0f;
-                        args.act[static_cast<size_t>(it.td.row_start + col) * args.inter + feat] =
-                            swiglu_out(is_gate ? mine : other, is_gate ? other : mine, lim,
-                                       args.official != 0, w);
+                    for (int i = 0; i < 32; i += 2) {
+                        const float lo = __uint_as_float(v[i]), hi = __uint_as_float(v[i + 1]);
+                        const float recv = __shfl_xor_sync(0xffffffffu, is_gate ? hi : lo, 16);
+                        const int j = is_gate ? i : i + 1;  // column this lane finishes
+                        const float w = __shfl_sync(0xffffffffu, wl, j);
+                        const int col = c + j;
+                        if (col < n_rows)
+                            args.act[static_cast<size_t>(it.td.row_start + col) * args.inter + feat] =
+                                swiglu_out(is_gate ? lo : recv, is_gate ? recv : hi, lim, off, w);
                     }
                 } else {
                     const int feat = it.m * 128 + L;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int col = c + i;
-                        if (col >= n_rows) break;
-                        const int pos = args.perm[it.td.row_start + col];
-                        args.raw[static_cast<size_t>(pos) * args.hidden + feat] = __uint_as_float(v[i]);
+                    for (int i = 0; i < 32; ++i) {
+                        const int pos = __shfl_sync(0xffffffffu, prow, i);
+                        if (c + i < n_rows)
+                            args.raw[static_cast<size_t>(pos) * args.hidden + feat] = __uint_as_float(v[i]);
                     }
                 }
             }
