@@ -142,7 +142,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kPkStages; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 8); }
+        // pk_empty: each of the four warps of a step's warpgroup, per step
+        for (int i = 0; i < kPkStages; ++i) { mbar_init(&pk_full[i], 1); mbar_init(&pk_empty[i], 4 * (kKStage / kAK)); }
         for (int i = 0; i < kAStages; ++i) { mbar_init(&full[i], 5); mbar_init(&empty[i], 1); }
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
         fence_barrier_init();
@@ -320,11 +321,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (elect_one()) mma_commit(&acc_full[acc]);
             __syncwarp();
         }
-    } else if (warp <= 10) {
+    } else if (warp < kEpilogueWarp) {
         // ---------------- dequantisers (TMEM lane = thread's weight row) ----------------
-        // Warpgroup wg takes the 128-K steps g with g % 2 == wg (two of the
-        // four in each packed stage); each thread owns one weight row, i.e.
-        // one TMEM lane, and writes its 128 FP16 weights to A stage g % 4.
+        // Warpgroup wg takes the 128-K steps g with g % kDqGroups == wg; each
+        // thread owns one weight row, i.e. one TMEM lane, and writes its 128
+        // FP16 weights to A stage g % 4.
         const int wg = (warp - 3) >> 2;
         const int quad = warp & 3;
         const int L = quad * 32 + lane;  // TMEM lane / A row
@@ -339,42 +340,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int ps = 0;
         uint32_t pphase = 0;
-        uint32_t g = 0;  // 128-K steps so far in this CTA (both warpgroups)
+        uint32_t g = 0;  // 128-K steps so far in this CTA (all warpgroups)
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             for (int s = 0; s < k_stages && ok; ++s) {
                 ok = mbar_wait(&pk_full[ps], pphase, status, kStatusTimeoutDequant);
                 if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
                 const uint8_t* stg = pk_smem + ps * kPkStageBytes;
-                const uint4 sc = *reinterpret_cast<const uint4*>(sc_smem + ps * kScStageBytes + srow * 16);
-                const uint32_t scw[4] = {sc.x, sc.y, sc.z, sc.w};
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int a = 2 * h + wg;  // 128-K step within the packed stage
+#pragma unroll 1
+                for (int a = 0; a < kKStage / kAK; ++a) {
+                    const uint32_t gi = g + static_cast<uint32_t>(a);
+                    if (gi % kDqGroups != static_cast<uint32_t>(wg)) continue;
+                    // this step's packed bytes and scales, then the stage can be refilled
                     const uint8_t* rowp = stg + (a >> 1) * 16384 + srow * 128;
                     const int c0 = (a & 1) * 4;
-                    uint32_t v0[32], v1[32];
+                    uint4 q[4];
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const uint4 q = *reinterpret_cast<const uint4*>(rowp + (((c0 + b) ^ sw) << 4));
-                        dequant_block32(q, (scw[a] >> (8 * b)) & 0xFFu, b < 2 ? v0 + 16 * b : v1 + 16 * (b - 2));
-                    }
-                    const uint32_t gi = g + static_cast<uint32_t>(a);
+                    for (int b = 0; b < 4; ++b) q[b] = *reinterpret_cast<const uint4*>(rowp + (((c0 + b) ^ sw) << 4));
+                    const uint32_t scw = *reinterpret_cast<const uint32_t*>(sc_smem + ps * kScStageBytes + srow * 16 + 4 * a);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&pk_empty[ps]);
+                    uint32_t v[32];
+                    dequant_block32(q[0], scw & 0xFFu, v);
+                    dequant_block32(q[1], (scw >> 8) & 0xFFu, v + 16);
                     const uint32_t as = gi % kAStages;
                     const bool got = mbar_wait(&empty[as], ((gi / kAStages) & 1u) ^ 1u, status, kStatusTimeoutDequant);
                     if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t col = tmem_base + lane_addr + as * (kAK / 2);
-                    tmem_st_32x32b_x32(col, v0);
-                    tmem_st_32x32b_x32(col + 32, v1);
+                    tmem_st_32x32b_x32(col, v);
+                    dequant_block32(q[2], (scw >> 16) & 0xFFu, v);
+                    dequant_block32(q[3], scw >> 24, v + 16);
+                    tmem_st_32x32b_x32(col + 32, v);
                     tmem_wait_st();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&full[as]);
                 }
                 g += kKStage / kAK;
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&pk_empty[ps]);
                 if (++ps == kPkStages) { ps = 0; pphase ^= 1; }
             }
         }

@@ -14,11 +14,11 @@
 //   warp 1      TMA producer of the token operand (X_perm or act): one 3-D
 //               box per 128-K step, 16/32/64/128 rows to fit the tile
 //   warp 2      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 3-10  dequantisers, two warpgroups taking alternate 128-wide K steps:
+//   warps 3-14  dequantisers, three warpgroups taking 128-wide K steps in turn:
 //               each thread owns one weight row (one TMEM lane), turns 128
 //               packed nibbles into 128 FP16 weights per step and writes them
 //               to a tensor-memory A buffer with tcgen05.st
-//   warps 11-14 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
+//   warps 15-18 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
 //               scatter, global stores
 //
 // The MMA is tcgen05.mma.kind::f16 with A (weights, M = 128 rows) read from
@@ -78,7 +78,9 @@ struct GemmArgs {
     const float* route_w;
 };
 
-constexpr int kGemmThreads = 480;     // 15 warps
+constexpr int kDqGroups = 3;          // dequantiser warpgroups
+constexpr int kEpilogueWarp = 3 + 4 * kDqGroups;
+constexpr int kGemmThreads = 32 * (kEpilogueWarp + 4);  // producers, MMA, dequantisers, epilogue
 constexpr int kPkStageBytes = 32768;  // 128 rows x 256 packed bytes (K = 512)
 constexpr int kScStageBytes = 2048;   // 128 rows x 16 scale bytes
 constexpr int kKStage = 512;          // K elements per packed stage
