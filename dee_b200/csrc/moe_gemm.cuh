@@ -14,11 +14,11 @@
 //   warp 1      TMA producer of the token operand (X_perm or act): one 3-D
 //               box per 128-K step, 16/32/64/128 rows to fit the tile
 //   warp 2      TMEM allocator and single-thread tcgen05.mma issuer
-//   warps 3-14  dequantisers, three warpgroups taking 128-wide K steps in turn:
+//   warps 3-18  dequantisers, four warpgroups taking 128-wide K steps in turn:
 //               each thread owns one weight row (one TMEM lane), turns 128
 //               packed nibbles into 128 FP16 weights per step and writes them
 //               to a tensor-memory A buffer with tcgen05.st
-//   warps 15-18 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
+//   warps 19-22 epilogue: tcgen05.ld of the FP32 accumulator, SwiGLU or
 //               scatter, global stores
 //
 // The MMA is tcgen05.mma.kind::f16 with A (weights, M = 128 rows) read from
@@ -78,7 +78,7 @@ struct GemmArgs {
     const float* route_w;
 };
 
-constexpr int kDqGroups = 3;          // dequantiser warpgroups
+constexpr int kDqGroups = 4;          // dequantiser warpgroups
 constexpr int kEpilogueWarp = 3 + 4 * kDqGroups;
 constexpr int kGemmThreads = 32 * (kEpilogueWarp + 4);  // producers, MMA, dequantisers, epilogue
 constexpr int kPkStageBytes = 32768;  // 128 rows x 256 packed bytes (K = 512)
@@ -94,10 +94,10 @@ constexpr int kKBlock = 64;           // K elements per 128-byte row of FP16
 // pipe for over half the time at N <= 128.)
 constexpr int kAK = 128;
 constexpr int kAStages = 4;                  // tensor-memory A stages, 64 columns each
-constexpr int kBStages = 3;                  // token-operand stages in shared memory
+constexpr int kBStages = 4;                  // token-operand stages in shared memory
 constexpr int kNMax = 128;                   // MMA N (token rows per tile)
 constexpr int kBStageBytes = kNMax * 128 * (kAK / kKBlock);  // 32 KB
-constexpr int kPkStages = 3;
+constexpr int kPkStages = 2;
 constexpr int kAccBase = kAStages * (kAK / 2);               // first accumulator column
 constexpr int kTmemCols = 512;
 constexpr int kTokenBoxes = 4;               // token boxes of 16, 32, 64 and 128 rows
