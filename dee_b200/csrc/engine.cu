@@ -1249,6 +1249,16 @@ int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_
                : DEE_ERR_CUDA;
 }
 
+int dee_act_quant_device(const void* d_x_f16, int rows, int cols, int block, uint8_t* d_q, uint8_t* d_scales,
+                         void* stream) {
+    if (!d_x_f16 || !d_q || !d_scales || rows < 0 || cols <= 0 || cols % 256 != 0 || (block != 32 && block != 128))
+        return DEE_ERR_INVALID;
+    return launch_act_quant(static_cast<const __half*>(d_x_f16), rows, cols, block, nullptr, 1, nullptr, d_q,
+                            d_scales, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? DEE_OK
+               : DEE_ERR_CUDA;
+}
+
 uint64_t dee_engine_launch_count(const dee_engine* e) { return e ? e->launches : 0; }
 
 int dee_engine_set_profiling(dee_engine* e, int enable) {

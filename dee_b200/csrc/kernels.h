@@ -135,6 +135,12 @@ cudaError_t launch_stack_rowdot_f16(const __half* x, const __half* w, int tokens
                                     float* out, cudaStream_t stream);
 cudaError_t launch_stack_residual_add(float* x, const float* y, size_t n, cudaStream_t stream);
 cudaError_t launch_stack_argmax(const float* logits, int tokens, int vocab, int32_t* ids, cudaStream_t stream);
+// Block-wise E4M3 quantisation with UE8M0 scales (act_quant.cu): rows of x
+// [.., cols] FP16 (row r = perm[r] / topk when perm is given; *rows_dev, if
+// given, caps the rows) into q [rows, cols] and scales [rows, cols / block].
+cudaError_t launch_act_quant(const __half* x, int rows, int cols, int block, const int32_t* perm, int topk,
+                             const int32_t* rows_dev, uint8_t* q, uint8_t* scales, cudaStream_t stream);
+
 cudaError_t launch_records_scramble(const uint8_t* src, uint8_t* dst, int records, size_t record_bytes,
                                     size_t packed_bytes, uint64_t seed, int first_record, cudaStream_t stream);
 

@@ -315,6 +315,16 @@ DEE_API int dee_fp4_decode_device(const uint8_t* d_packed, const uint8_t* d_scal
 DEE_API int dee_fp4_quantize_device(const float* d_w, size_t out, size_t in, uint8_t* d_packed,
                             uint8_t* d_scale, void* stream);
 
+/* The official FP8 activation quantisation (act_quant with scale_fmt
+ * "ue8m0", official-source/inference/kernel.py:41-103; restated in
+ * dee.cpp/scripts/deepseek_v4_layer_common.py:213-240): per row and block of
+ * `block` (128 official, 32 MX) columns, amax = max(|x|, 1e-4), scale
+ * s = 2^ceil(log2(amax / 448)), q = E4M3(clamp(x / s, +-448)) round to
+ * nearest even.  x FP16 [rows, cols] -> q E4M3 bytes [rows, cols] and the
+ * UE8M0 scale bytes [rows, cols / block].  cols % 256 == 0. */
+DEE_API int dee_act_quant_device(const void* d_x_f16, int rows, int cols, int block, uint8_t* d_q,
+                                 uint8_t* d_scales, void* stream);
+
 /* The layer forward for callers that cannot allocate device memory (code
  * inside an allocator or memory-pool callback, or a host whose device memory
  * is entirely owned by its own caching allocator).  No counterpart in the

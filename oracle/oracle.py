@@ -353,6 +353,48 @@ def e4m3_table() -> np.ndarray:
     return val.astype(np.float32)
 
 
+def e4m3_encode(v: np.ndarray) -> np.ndarray:
+    """FP32 values already clamped to [-448, 448] -> F8_E4M3 (fn) codes,
+    round to nearest, ties to even mantissa (the cast of the official
+    act_quant kernel, official-source/inference/kernel.py:88-93)."""
+    v = np.asarray(v, dtype=np.float64)
+    a = np.abs(v)
+    sign = np.where(np.signbit(v), 0x80, 0).astype(np.int64)
+    out = np.zeros(a.shape, dtype=np.int64)
+    sub = a < 2.0 ** -6
+    # subnormals: multiples of 2^-9, rounded half to even (np.rint)
+    out[sub] = np.rint(a[sub] * 2.0 ** 9).astype(np.int64)  # 8 carries into the first normal code
+    norm = ~sub
+    e = np.floor(np.log2(a[norm])).astype(np.int64)
+    m = np.rint((a[norm] / 2.0 ** e - 1.0) * 8.0).astype(np.int64)
+    e = np.where(m == 8, e + 1, e)
+    m = np.where(m == 8, 0, m)
+    out[norm] = ((e + 7) << 3) | m
+    return (out | sign).astype(np.uint8)
+
+
+def act_quant(x_f16_bits: np.ndarray, block: int) -> tuple[np.ndarray, np.ndarray]:
+    """The official act_quant with UE8M0 scales (kernel.py:41-103, FP32
+    compute; restated in deepseek_v4_layer_common.py:213-240): per row and
+    block, amax = max(|x|, 1e-4); s = 2^ceil(log2(fp32(amax * fp32(1/448))));
+    q = E4M3(clamp(x / s, -448, 448)).  FP16 bits [rows, cols] -> (codes
+    [rows, cols] uint8, UE8M0 bytes [rows, cols / block] uint8)."""
+    x = np.asarray(x_f16_bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+    rows, cols = x.shape
+    xb = x.reshape(rows, cols // block, block)
+    amax = np.maximum(np.abs(xb).max(axis=2), np.float32(1e-4)).astype(np.float32)
+    prod = (amax * np.float32(1.0 / 448.0)).astype(np.float32)
+    bits = prod.view(np.uint32)
+    e = ((bits >> 23) & 0xFF).astype(np.int64) - 127 + ((bits & 0x7FFFFF) != 0)
+    q = np.clip(xb * np.ldexp(np.float32(1.0), -e)[:, :, None].astype(np.float32), -448.0, 448.0)
+    return e4m3_encode(q.reshape(rows, cols)), (e + 127).astype(np.uint8)
+
+
+def act_dequant_f32(q: np.ndarray, scales: np.ndarray, block: int) -> np.ndarray:
+    """E4M3 codes x UE8M0 block scales -> FP32."""
+    return e4m3_table()[q] * np.repeat(e8m0_f32(scales), block, axis=1)
+
+
 def dequant_fp4_f32(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
     """Packed E2M1 [out, in/2] (low nibble first) x UE8M0 per 32 -> FP32 [out, in]
     (dequantize_expert_weight, deepseek_v4_expert_reference.py:85-99)."""

@@ -25,6 +25,9 @@ sha256 before use.
 * ``official.npz`` -- ``moe_layer_forward`` with a shared expert (F8_E4M3
                      weights, E8M0 scales per 128 x 128 tile): routed outputs
                      weighted before w2, clamp 10, shared output added.
+* ``act_quant.npz`` -- ``act_quant_inplace`` (deepseek_v4_layer_common.py
+                     :213-240) with UE8M0 scales, blocks of 128 and 32, on FP16
+                     rows spanning seven decades of magnitude.
 * ``journal.jsonl`` -- ``RoutedExpertJournal`` (kaggle/deepseek-v4-flash-0731/
                      deepseek_v4_native_generate.py:452-622) for two forwards
                      of three layers with fixed route ids.
@@ -160,6 +163,18 @@ def make_official() -> None:
         shared_output=res["shared_output"].numpy(), moe_output=res["moe_output"].numpy())
 
 
+def make_act_quant() -> None:
+    rng = np.random.default_rng(2027)
+    rows, cols = 48, 512
+    mag = 10.0 ** rng.uniform(-3, 3, size=(rows, 1))
+    x = torch.from_numpy((rng.standard_normal((rows, cols)) * mag).astype(np.float16))
+    out = {"x": x.numpy().view(np.uint16)}
+    for block in (128, 32):
+        y = common.act_quant_inplace(x.clone(), block_size=block, scale_fmt="ue8m0")
+        out[f"y{block}"] = y.numpy().view(np.uint16)
+    np.savez_compressed(HERE / "act_quant.npz", **out)
+
+
 def make_journal() -> None:
     import deepseek_v4_native_generate as gen
     rng = np.random.default_rng(505)
@@ -180,12 +195,10 @@ def make_journal() -> None:
 
 def main() -> None:
     torch.manual_seed(0)
-    make_quant()
-    make_decode()
-    make_expert()
-    make_moe_layer()
-    make_official()
-    make_journal()
+    makers = {"quant": make_quant, "decode": make_decode, "expert": make_expert, "moe_layer": make_moe_layer,
+              "official": make_official, "act_quant": make_act_quant, "journal": make_journal}
+    for name in sys.argv[1:] or list(makers):  # default: all
+        makers[name]()
     for p in sorted(HERE.iterdir()):
         if p.suffix in (".npz", ".jsonl"):
             print(p.name, p.stat().st_size)

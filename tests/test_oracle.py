@@ -287,3 +287,28 @@ def test_official_layer_matches_reference_fixture(oracle_mod):
     moe, sh = orc.official_layer(recs, layout, g["x"], g["expert_ids"], g["routing_weights"], shared, 10.0)
     assert orc.rel_l2(sh, g["shared_output"]) < 1e-5
     assert orc.rel_l2(moe, g["moe_output"]) < 1e-5
+
+
+def test_e4m3_encoder_matches_torch():
+    """The oracle's round-to-nearest-even E4M3 encoder against torch's
+    float8_e4m3fn cast (an independent implementation), incl. subnormal ties."""
+    import torch
+    from oracle import oracle as orc
+    rng = np.random.default_rng(5)
+    v = np.concatenate([rng.standard_normal(50000) * 60, rng.standard_normal(50000) * 0.005,
+                        np.array([0.0, -0.0, 448.0, -448.0, 2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -11, 2.0 ** -6,
+                                  1.0625, 1.1875, 2.0 ** -6 * 15 / 16])])
+    v = np.clip(v, -448, 448).astype(np.float32)
+    ref = torch.from_numpy(v).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(orc.e4m3_encode(v), ref)
+
+
+@pytest.mark.parametrize("block", [128, 32])
+def test_act_quant_matches_reference_fixture(oracle_mod, block):
+    """act_quant_inplace of the reference (UE8M0 scales) vs the oracle's
+    restatement of the official kernel: identical FP16 round trips."""
+    orc = oracle_mod
+    g = _load("act_quant.npz")
+    q, s = orc.act_quant(g["x"], block)
+    y = orc.act_dequant_f32(q, s, block).astype(np.float16).view(np.uint16)
+    assert np.array_equal(y, g[f"y{block}"])
