@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--offload-gib", type=float, default=0.0,
                     help="stack with the offload tier (config 4): device pool of this many GiB of expert "
                          "records, the rest in pinned host memory")
+    ap.add_argument("--act-quant", type=int, default=0, choices=[0, 32, 128],
+                    help="prefill: 0 = W4A16 (FP16 activations); 32 / 128 = the MXFP8-activation variant with "
+                         "UE8M0 scales per 32 (MX) or 128 (official act_quant) columns")
     ap.add_argument("--store", default=None,
                     help="stack: read every layer's expert records from this DEE4 store (resident banks "
                          "or, with --offload-gib, the offload tier's pinned host block)")
@@ -324,10 +327,24 @@ def e2e_point(torch, eng, b, n_steps, warmup, flush, stream, seed, make_layer=No
     return times, h2d, d2h
 
 
-def prefill_point(torch, eng, n_steps, warmup, flush, stream, seed):
+class MxLayer(Layer):
+    """The same layer through the MXFP8-activation variant."""
+
+    def __init__(self, torch, eng, b, act_block):
+        super().__init__(torch, eng, b)
+        self.act_block = act_block
+
+    def __call__(self, x, logits, stream):
+        self.eng.route_topk_device(logits.data_ptr(), self.b, self.ids.data_ptr(), self.w.data_ptr(), stream)
+        self.eng.moe_forward_mxfp8_device(0, x.data_ptr(), self.b, self.ids.data_ptr(),
+                                          d_weights_ptr=self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),
+                                          act_block=self.act_block, stream=stream)
+
+
+def prefill_point(torch, eng, n_steps, warmup, flush, stream, seed, act_block=0):
     T = 4096
     xs, logits = make_inputs(torch, max(min(n_steps, 4), 1), T, seed, zipf=True)
-    layer = Layer(torch, eng, T)
+    layer = MxLayer(torch, eng, T, act_block) if act_block else Layer(torch, eng, T)
 
     def fn(i, s):
         layer(xs[i % len(xs)], logits[i % len(xs)], s)
@@ -448,7 +465,8 @@ def run_prefill(args):
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     launches0 = eng.launch_count()
     with ClockSampler(local) as clk:
-        times, stages, counts = prefill_point(torch, eng, args.steps, args.warmup, flush, stream, seed=4000)
+        times, stages, counts = prefill_point(torch, eng, args.steps, args.warmup, flush, stream, seed=4000,
+                                              act_block=args.act_quant)
     launches = (eng.launch_count() - launches0) / (args.steps + args.warmup + 1)
     ms = statistics.mean(times)
     flops = T * K * 3 * 2 * H * I
@@ -456,22 +474,29 @@ def run_prefill(args):
     gu_ms = stages.get("gate_up", float("nan"))
     dn_ms = stages.get("down", float("nan"))
     achieved = gu_flops / (gu_ms / 1000.0) / 1e12
+    # the MXFP8 kernels run at the FP8 dense rate, twice the bf16 one
+    peak = tc_peak * (2 if args.act_quant else 1)
+    peak_src = f"{'2 x ' if args.act_quant else ''}{peak_kind} bf16_tflops"
     result = {
-        "metric": "MoE-layer tokens/s (T=4096 prefill, Zipf(1.1) expert bias)",
+        "metric": "MoE-layer tokens/s (T=4096 prefill, Zipf(1.1) expert bias)" +
+                  (f", MXFP8 activations (UE8M0 per {args.act_quant})" if args.act_quant else ""),
         "value": T / (ms / 1000.0), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "cfg2-prefill-t4096-zipf1.1", "hidden": H, "inter": I, "experts": E, "topk": K,
+        "vs_baseline": None, "dtype": "e4m3xe2m1" if args.act_quant else "f16", "data": "synthetic",
+        "config": {"workload": "cfg2-prefill-t4096-zipf1.1" + (f"-mxfp8-b{args.act_quant}" if args.act_quant else ""),
+                   "hidden": H, "inter": I, "experts": E, "topk": K,
                    "tokens_per_step": T, "weights": "fp4-e2m1+ue8m0/32", "parallelism": "single",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "max_expert_rows": int(counts.max()), "active_experts": int((counts > 0).sum())},
         "tflops_layer": flops / (ms / 1000.0) / 1e12,
-        "tc_frac_layer": flops / (ms / 1000.0) / 1e12 / tc_peak,
+        "tc_frac_layer": flops / (ms / 1000.0) / 1e12 / peak,
         "tflops_down": (T * K * 2 * H * I) / (dn_ms / 1000.0) / 1e12,
         "stage_ms": stages,
-        "roofline": {"bound": "tensor", "kernel": "moe_gemm_kernel<gate_up>", "achieved": achieved,
-                     "peak": tc_peak, "unit": "TFLOP/s", "frac": achieved / tc_peak,
-                     "peak_source": f"{peak_kind} bf16_tflops", "traffic": None,
+        "roofline": {"bound": "tensor",
+                     "kernel": "moe_mxfp8_kernel<gate_up>" if args.act_quant else "moe_gemm_kernel<gate_up>",
+                     "achieved": achieved,
+                     "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                     "peak_source": peak_src, "traffic": None,
                      "algorithmic_flops_per_launch": gu_flops},
         "gpu_launches": int(round(launches * args.steps)),
         "gpu_launches_per_step": launches,

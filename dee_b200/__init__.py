@@ -192,6 +192,18 @@ class Engine:
             ctypes.c_void_p(d_raw_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_moe_forward_device")
 
+    def moe_forward_mxfp8_device(self, layer: int, d_x_ptr: int, tokens: int, d_ids_ptr: int, d_raw_ptr: int = 0,
+                                 *, d_weights_ptr: int = 0, d_out_ptr: int = 0, act_block: int = 32,
+                                 stream=None) -> None:
+        """The MXFP8-activation variant of moe_forward_device: E4M3 token rows
+        and SwiGLU output with UE8M0 scales per act_block (32 MX, 128 the
+        official act_quant), block-scaled tcgen05 GEMMs on the FP4 records."""
+        rc = self._lib.dee_moe_forward_mxfp8_device(
+            self._h, layer, ctypes.c_void_p(d_x_ptr), tokens, ctypes.c_void_p(d_ids_ptr), self.cfg.topk,
+            ctypes.c_void_p(d_weights_ptr or 0), ctypes.c_void_p(d_out_ptr or 0), ctypes.c_void_p(d_raw_ptr or 0),
+            act_block, ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_moe_forward_mxfp8_device")
+
     # -- official DeepSeek-V4 semantics ---------------------------------------
     def attach_shared_expert(self, layer: int, w1, w1_scale, w3, w3_scale, w2, w2_scale) -> None:
         """Device tensors: F8_E4M3 (uint8 view) W1, W3 [inter, H], W2 [H, inter]

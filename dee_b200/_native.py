@@ -113,6 +113,7 @@ SIGNATURES = {
     "dee_fp4_quantize_device": (I, [P, SZ, SZ, P, P, P]),
     "dee_engine_launch_count": (ctypes.c_uint64, [P]),
     "dee_act_quant_device": (I, [P, I, I, I, P, P, P]),
+    "dee_moe_forward_mxfp8_device": (I, [P, I, P, I, P, I, P, P, P, I, P]),
     "dee_moe_forward_noalloc": (I, [ctypes.POINTER(DeeConfig), P, SZ, I, P, I, P, P, P, P, P]),
     "dee_engine_set_profiling": (I, [P, I]),
     "dee_engine_stage_ms": (I, [P, P, I]),

@@ -27,7 +27,7 @@ namespace {
 template <int BLOCK>
 __global__ void act_quant_kernel(const __half* __restrict__ x, int rows, int cols, const int32_t* __restrict__ perm,
                                  int topk, const int32_t* __restrict__ rows_dev, uint8_t* __restrict__ q,
-                                 uint8_t* __restrict__ scales) {
+                                 uint8_t* __restrict__ scales, bool per32) {
     sm100::pdl_wait();
     sm100::pdl_trigger();
     constexpr int kLanes = BLOCK / 8;  // lanes per block
@@ -71,15 +71,19 @@ __global__ void act_quant_kernel(const __half* __restrict__ x, int rows, int col
             else packed[i >> 1] = pv;
         }
         *reinterpret_cast<uint2*>(q + static_cast<size_t>(row) * cols + col) = make_uint2(packed[0], packed[1]);
-        if ((lane % kLanes) == 0)
+        if (per32) {
+            // one byte per 32 columns (a block of 128 repeats its scale four times)
+            if ((lane & 3) == 0) scales[static_cast<size_t>(row) * (cols / 32) + col / 32] = static_cast<uint8_t>(e + 127);
+        } else if ((lane % kLanes) == 0) {
             scales[static_cast<size_t>(row) * (cols / BLOCK) + col / BLOCK] = static_cast<uint8_t>(e + 127);
+        }
     }
 }
 
 }  // namespace
 
 cudaError_t launch_act_quant(const __half* x, int rows, int cols, int block, const int32_t* perm, int topk,
-                             const int32_t* rows_dev, uint8_t* q, uint8_t* scales, cudaStream_t stream) {
+                             const int32_t* rows_dev, uint8_t* q, uint8_t* scales, cudaStream_t stream, bool per32) {
     if (rows < 0 || cols % 256 != 0 || (block != 32 && block != 128) || (perm && topk <= 0))
         return cudaErrorInvalidValue;
     if (rows == 0) return cudaSuccess;
@@ -87,9 +91,9 @@ cudaError_t launch_act_quant(const __half* x, int rows, int cols, int block, con
     const int grid = static_cast<int>(warps / 8 + 1 < 148 * 16 ? warps / 8 + 1 : 148 * 16);
     return block == 32
                ? launch_pdl(act_quant_kernel<32>, dim3(grid), dim3(256), 0, stream, x, rows, cols, perm, topk,
-                            rows_dev, q, scales)
+                            rows_dev, q, scales, per32)
                : launch_pdl(act_quant_kernel<128>, dim3(grid), dim3(256), 0, stream, x, rows, cols, perm, topk,
-                            rows_dev, q, scales);
+                            rows_dev, q, scales, per32);
 }
 
 }  // namespace dee

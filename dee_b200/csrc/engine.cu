@@ -68,6 +68,8 @@ struct Bank {
     int32_t* d_slot_of = nullptr;  // [E]
     CUtensorMap w1, w3, w2, s1, s3, s2;  // tcgen05 kernel
     GemmMaps dec_gu{}, dec_dn{};         // decode kernel (weight maps)
+    bool mx = false;                     // MXFP8 kernel maps encoded
+    MxMaps mx_gu{}, mx_dn{};
     // the layer's shared expert (F8_E4M3 + E8M0 per 128 x 128), if attached
     bool shared = false;
     int shared_inter = 0;
@@ -191,6 +193,10 @@ struct dee_engine {
     int32_t* h_ids = nullptr;      // pinned staging of host-given ids
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
     // shared-expert workspaces, capacity in tokens
+    // MXFP8 path workspaces (E4M3 rows and per-32 UE8M0 scales), capacity in rows
+    size_t cap_mx = 0;
+    uint8_t *d_xq = nullptr, *d_xs = nullptr, *d_aq = nullptr, *d_as = nullptr;
+    CUtensorMap map_xq_t[4], map_aq_t[4];
     size_t cap_sh = 0;
     int cap_sh_inter = 0;
     __half* d_sh_act = nullptr;
@@ -429,6 +435,92 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     return DEE_OK;
 }
 
+// The MXFP8 workspaces for `sel` rows (grown like the FP16 ones).
+int ensure_mx_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
+    if (sel <= e->cap_mx) return DEE_OK;
+    cudaError_t err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "cudaStreamSynchronize(workspace growth)");
+    cudaFree(e->d_xq); cudaFree(e->d_xs); cudaFree(e->d_aq); cudaFree(e->d_as);
+    e->d_xq = e->d_xs = e->d_aq = e->d_as = nullptr;
+    e->cap_mx = 0;
+    const size_t cap = ((sel + 255) / 256) * 256;
+    const size_t H = e->cfg.hidden, I = e->cfg.inter;
+    if ((err = dev_alloc(&e->d_xq, cap * H)) != cudaSuccess || (err = dev_alloc(&e->d_xs, cap * H / 32)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_aq, cap * I)) != cudaSuccess || (err = dev_alloc(&e->d_as, cap * I / 32)) != cudaSuccess)
+        return cuda_fail(e, err, "MXFP8 workspace allocation");
+    if (!encode_mx_token_maps(get_encode_fn(), e->d_xq, static_cast<int>(cap), static_cast<int>(H), e->map_xq_t) ||
+        !encode_mx_token_maps(get_encode_fn(), e->d_aq, static_cast<int>(cap), static_cast<int>(I), e->map_aq_t))
+        return fail(e, DEE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the MXFP8 token maps");
+    e->cap_mx = cap;
+    return DEE_OK;
+}
+
+// The layer with E4M3 activations (act_block-column UE8M0 blocks, 32 or
+// 128) against the records' E2M1 weights: permute, quantise-and-gather the
+// token rows, block-scaled gate/up GEMM (SwiGLU into FP16 act), quantise act,
+// block-scaled down GEMM into raw.
+int run_experts_mx(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32, float* raw,
+                   cudaStream_t stream, int K, int act_block) {
+    if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
+        return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
+    const dee::Bank& bank = e->banks[layer];
+    if (!bank.mx) return fail(e, DEE_ERR_UNSUPPORTED, "the MXFP8 weight maps are unavailable on this driver");
+    const int H = e->cfg.hidden, I = e->cfg.inter, E = e->cfg.num_experts;
+    if (H % 256 || I % 256) return fail(e, DEE_ERR_UNSUPPORTED, "MXFP8 path needs hidden and inter % 256 == 0");
+    const size_t sel = static_cast<size_t>(tokens) * K;
+    int rc = ensure_mx_capacity(e, sel, stream);
+    if (rc != DEE_OK) return rc;
+    PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles, e->d_journal};
+    stage_begin(e, kStagePermute, stream);
+    cudaError_t err = launch_permute(d_ids32, tokens, K, E, gemm_n_max(), e->max_tiles, po, e->d_status, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    stage_end(e, kStagePermute, stream);
+    stage_begin(e, kStageGather, stream);
+    err = launch_act_quant(d_x, static_cast<int>(sel), H, act_block, e->d_perm, K, e->d_offsets + E, e->d_xq, e->d_xs,
+                           stream, true);
+    if (err != cudaSuccess) return cuda_fail(e, err, "activation quantisation launch");
+    stage_end(e, kStageGather, stream);
+
+    GemmArgs a{};
+    a.hidden = H;
+    a.inter = I;
+    a.topk = K;
+    a.swiglu_limit = e->cfg.swiglu_limit;
+    a.tiles = e->d_tiles;
+    a.n_tiles = e->d_n_tiles;
+    a.slot_of = bank.d_slot_of;
+    a.num_slots = bank.n_slots;
+    a.records = bank.records;
+    a.record_bytes = bank.record_bytes;
+    a.num_experts = E;
+    a.perm = e->d_perm;
+    a.act = e->d_act;
+    a.raw = raw;
+    a.status = e->d_status;
+    MxMaps m = bank.mx_gu;
+    for (int i = 0; i < 4; ++i) m.bt[i] = e->map_xq_t[i];
+    a.k_total = H;
+    a.m_tiles = I / 64;
+    const int cap = static_cast<int>(e->cap_mx);
+    stage_begin(e, kStageGateUp, stream);
+    err = launch_moe_mxfp8(true, m, a, e->d_xs, cap, e->num_sms, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "MXFP8 gate/up GEMM launch");
+    err = launch_act_quant(e->d_act, static_cast<int>(sel), I, act_block, nullptr, 1, e->d_offsets + E, e->d_aq,
+                           e->d_as, stream, true);
+    if (err != cudaSuccess) return cuda_fail(e, err, "act quantisation launch");
+    stage_end(e, kStageGateUp, stream);
+    m = bank.mx_dn;
+    for (int i = 0; i < 4; ++i) m.bt[i] = e->map_aq_t[i];
+    a.k_total = I;
+    a.m_tiles = H / 128;
+    stage_begin(e, kStageDown, stream);
+    err = launch_moe_mxfp8(false, m, a, e->d_as, cap, e->num_sms, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "MXFP8 down GEMM launch");
+    stage_end(e, kStageDown, stream);
+    e->launches += 5;
+    return DEE_OK;
+}
+
 }  // namespace
 }  // namespace dee
 
@@ -479,6 +571,10 @@ void dee_engine_destroy(dee_engine* e) {
     free_workspace(e);
     cudaFree(e->d_sh_act);
     cudaFree(e->d_sh_out);
+    cudaFree(e->d_xq);
+    cudaFree(e->d_xs);
+    cudaFree(e->d_aq);
+    cudaFree(e->d_as);
     if (e->off.copy_stream) cudaStreamDestroy(e->off.copy_stream);
     if (e->off.copied) cudaEventDestroy(e->off.copied);
     if (e->off.h_ids) cudaFreeHost(e->off.h_ids);
@@ -567,6 +663,9 @@ int dee_expert_bank_attach(dee_engine* e, int layer, const void* d_records, int 
     if (!encode_decode_weight_maps(get_encode_fn(), base, record_bytes, n_slots, H, I, &b.dec_gu,
                                    &b.dec_dn))
         return fail(e, DEE_ERR_CUDA, "cuTensorMapEncodeTiled failed for the decode weight maps");
+    // the MXFP8 path's maps (E2M1 unpacked by the TMA); a driver without
+    // that tensor-map type leaves the path unavailable, the rest works
+    b.mx = encode_mx_weight_maps(get_encode_fn(), base, record_bytes, n_slots, H, I, &b.mx_gu, &b.mx_dn);
     b.records = base;
     b.n_slots = n_slots;
     b.record_bytes = record_bytes;
@@ -653,6 +752,34 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     if (d_out_f32) {
         stage_begin(e, kStageCombine, stream);
         err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
+        stage_end(e, kStageCombine, stream);
+        e->launches += 1;
+    }
+    e->journal_stream = stream;
+    return DEE_OK;
+}
+
+int dee_moe_forward_mxfp8_device(dee_engine* e, int layer, const void* d_x_f16, int tokens, const int32_t* d_ids,
+                                 int topk, const float* d_weights, float* d_out_f32, float* d_raw, int act_block,
+                                 void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_x_f16 || tokens <= 0 || topk != e->cfg.topk || !d_ids || (!d_out_f32 && !d_raw) ||
+        (d_out_f32 && !d_weights) || (act_block != 32 && act_block != 128))
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_mxfp8_device arguments");
+    const size_t sel = static_cast<size_t>(tokens) * topk;
+    if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    e->h_ids_count = sel;
+    float* raw = d_raw ? d_raw : e->d_raw;
+    if ((rc = run_experts_mx(e, layer, static_cast<const __half*>(d_x_f16), tokens, d_ids, raw, stream, topk,
+                             act_block)) != DEE_OK)
+        return rc;
+    if (d_out_f32) {
+        stage_begin(e, kStageCombine, stream);
+        cudaError_t err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
         stage_end(e, kStageCombine, stream);
         e->launches += 1;
@@ -1254,7 +1381,7 @@ int dee_act_quant_device(const void* d_x_f16, int rows, int cols, int block, uin
     if (!d_x_f16 || !d_q || !d_scales || rows < 0 || cols <= 0 || cols % 256 != 0 || (block != 32 && block != 128))
         return DEE_ERR_INVALID;
     return launch_act_quant(static_cast<const __half*>(d_x_f16), rows, cols, block, nullptr, 1, nullptr, d_q,
-                            d_scales, static_cast<cudaStream_t>(stream)) == cudaSuccess
+                            d_scales, static_cast<cudaStream_t>(stream), false) == cudaSuccess
                ? DEE_OK
                : DEE_ERR_CUDA;
 }

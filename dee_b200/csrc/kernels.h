@@ -32,6 +32,15 @@ struct GemmMaps {
     CUtensorMap bt[4];  // tcgen05 kernel: token boxes of 16/32/64/128 rows x 128 K
 };
 
+// The MXFP8-activation grouped GEMM (moe_mxfp8.cu): weights E2M1 unpacked by
+// the TMA (a), E4M3 token rows in boxes of 16/32/64/128 rows (bt).
+struct MxMaps {
+    CUtensorMap a;
+    CUtensorMap bt[4];
+};
+cudaError_t launch_moe_mxfp8(bool gate_up, const MxMaps& maps, const GemmArgs& args, const uint8_t* b_scales,
+                             int b_rows_cap, int grid, cudaStream_t stream);
+
 // Largest N (rows per expert tile) of the tcgen05 GEMM.
 int gemm_n_max();
 
@@ -67,6 +76,10 @@ bool encode_decode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, 
 // swizzle).
 bool encode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int cols, int box_rows, int box_chunks,
                       CUtensorMap* map);
+// The MXFP8 GEMM's maps: E2M1 weights over a bank of records, E4M3 token rows.
+bool encode_mx_weight_maps(EncodeTiledFn fn, const void* records, size_t record_bytes, int n_slots, int hidden,
+                           int inter, MxMaps* gu, MxMaps* dn);
+bool encode_mx_token_maps(EncodeTiledFn fn, const void* rows_base, int rows, int cols, CUtensorMap* maps);
 // The tcgen05 GEMM's four token maps (boxes of 16/32/64/128 rows x 128 K).
 bool encode_gemm_token_maps(EncodeTiledFn fn, const void* rows_base, int rows, int cols, CUtensorMap* maps);
 
@@ -137,9 +150,11 @@ cudaError_t launch_stack_residual_add(float* x, const float* y, size_t n, cudaSt
 cudaError_t launch_stack_argmax(const float* logits, int tokens, int vocab, int32_t* ids, cudaStream_t stream);
 // Block-wise E4M3 quantisation with UE8M0 scales (act_quant.cu): rows of x
 // [.., cols] FP16 (row r = perm[r] / topk when perm is given; *rows_dev, if
-// given, caps the rows) into q [rows, cols] and scales [rows, cols / block].
+// given, caps the rows) into q [rows, cols] and scales [rows, cols / block],
+// or with per32 one scale byte per 32 columns (the MMA's granularity).
 cudaError_t launch_act_quant(const __half* x, int rows, int cols, int block, const int32_t* perm, int topk,
-                             const int32_t* rows_dev, uint8_t* q, uint8_t* scales, cudaStream_t stream);
+                             const int32_t* rows_dev, uint8_t* q, uint8_t* scales, cudaStream_t stream,
+                             bool per32);
 
 cudaError_t launch_records_scramble(const uint8_t* src, uint8_t* dst, int records, size_t record_bytes,
                                     size_t packed_bytes, uint64_t seed, int first_record, cudaStream_t stream);

@@ -177,6 +177,17 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         : "memory");
 }
 
+// 5-D tiled load (x innermost).
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t x, int32_t y,
+                                            int32_t z, int32_t w, int32_t v, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(v),
+        "l"(policy)
+        : "memory");
+}
+
 // 4-D tiled load (x innermost).
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t x, int32_t y, int32_t z, int32_t w,
@@ -281,6 +292,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
         "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
         "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
+}
+
+// Each thread writes 4 consecutive 32-bit columns of its own lane.
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t v0, uint32_t v1, uint32_t v2,
+                                                  uint32_t v3) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v0), "r"(v1),
+                 "r"(v2), "r"(v3)
+                 : "memory");
 }
 
 // Each thread reads 32 consecutive 32-bit columns of its own lane.

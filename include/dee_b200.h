@@ -128,6 +128,18 @@ DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_
                            const int32_t* d_ids, const int32_t* h_ids, int topk,
                            const float* d_weights, float* d_out_f32, float* d_raw, void* stream);
 
+/* The MXFP8-activation variant of dee_moe_forward_device (device ids only):
+ * token rows and the SwiGLU output are quantised to E4M3 with UE8M0 scales
+ * per act_block columns (128: the official act_quant, 32: MX), and both
+ * grouped GEMMs run tcgen05 kind::mxf8f6f4 block-scaled MMAs straight on the
+ * records' E2M1 weights and UE8M0 scales (no dequantisation).  Numerics
+ * differ from the FP16 path by the activation quantisation; the tolerance
+ * is stated with its tests.  DEE_ERR_UNSUPPORTED if the driver cannot encode
+ * the unpacked-FP4 tensor maps. */
+DEE_API int dee_moe_forward_mxfp8_device(dee_engine* engine, int layer, const void* d_x_f16, int tokens,
+                                         const int32_t* d_ids, int topk, const float* d_weights, float* d_out_f32,
+                                         float* d_raw, int act_block, void* stream);
+
 /* Synchronise `stream`, read and clear the engine's device status word.
  * Returns DEE_ERR_DEVICE (and *status_out != 0) when a kernel flagged an
  * invalid expert id, a router failure or a pipeline timeout. */

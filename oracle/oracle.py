@@ -298,6 +298,37 @@ def moe_layer_raw(records: np.ndarray, layout: Layout, x_f16: np.ndarray, ids: n
     return raw
 
 
+def mxfp8_layer_raw(records: np.ndarray, layout: Layout, x_f16: np.ndarray, ids: np.ndarray, act_block: int,
+                    swiglu_limit: float = 0.0) -> np.ndarray:
+    """Raw FP32 [T, K, H] of the MXFP8-activation variant: x quantised by
+    act_quant (E4M3, UE8M0 per act_block), the records' E2M1 weights with
+    their UE8M0 scales, FP64 sums of the exact FP8 x FP4 products, the live
+    FP16 SwiGLU chain (swiglu_cuda.cu:46-59), the SwiGLU output quantised by
+    act_quant again, then the down projection."""
+    T, K = ids.shape
+    H, I = layout.hidden, layout.inter
+    xq, xs = act_quant(x_f16, act_block)
+    xd = act_dequant_f32(xq, xs, act_block).astype(np.float64)
+    raw = np.zeros((T, K, H), dtype=np.float32)
+    for e in np.unique(ids):
+        rec = split_record(layout, records[e])
+        w1 = dequant_fp4_f32(rec["w1.weight"], rec["w1.scale"]).astype(np.float64)
+        w3 = dequant_fp4_f32(rec["w3.weight"], rec["w3.scale"]).astype(np.float64)
+        w2 = dequant_fp4_f32(rec["w2.weight"], rec["w2.scale"]).astype(np.float64)
+        t, k = np.nonzero(ids == e)
+        g = (xd[t] @ w1.T).astype(np.float32).astype(np.float16).astype(np.float32)
+        u = (xd[t] @ w3.T).astype(np.float32).astype(np.float16).astype(np.float32)
+        if swiglu_limit > 0:
+            g = np.minimum(g, np.float32(swiglu_limit))
+            u = np.clip(u, -swiglu_limit, swiglu_limit).astype(np.float32)
+        sv = (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32).astype(np.float16).astype(np.float32)
+        act = (sv * u).astype(np.float32).astype(np.float16)
+        aq, as_ = act_quant(act.view(np.uint16), act_block)
+        ad = act_dequant_f32(aq, as_, act_block).astype(np.float64)
+        raw[t, k] = (ad @ w2.T).astype(np.float32)
+    return raw
+
+
 def combine_f32(raw: np.ndarray, weights: np.ndarray) -> np.ndarray:
     raw = np.ascontiguousarray(raw, dtype=np.float32)
     weights = np.ascontiguousarray(weights, dtype=np.float32)
