@@ -15,13 +15,18 @@
 //   warp 1     TMA producer of the E4M3 token rows (16/32/64/128-row boxes)
 //   warp 2     MMA issuer (whole warp, one elected lane): eight K = 32 MMAs
 //              per 256-K step
-//   warps 3-6  scale writers: the weights' and the tokens' UE8M0 bytes of
+//   warps 3-10 scale writers, two warpgroups taking alternate steps (a
+//              tcgen05.st + wait::st costs ~700 cycles under the MMAs' tensor
+//              memory traffic): the weights' and the tokens' UE8M0 bytes of
 //              the step into tensor memory (tcgen05.st), in the layout the
 //              block-scaled MMA reads: for 4 K blocks, lane l of column c
 //              holds row 32c + l, one byte per K block, replicated in the
 //              four lane quadrants
-//   warps 7-10 epilogue: as the W4A16 kernel (SwiGLU into FP16 act, or the
-//              FP32 scatter to the selections' rows)
+//   warps 11-18 epilogue, two warps per lane quadrant taking alternate
+//              32-column chunks: as the W4A16 kernel (SwiGLU into FP16 act,
+//              or the FP32 scatter to the selections' rows); a K step here
+//              is four times shorter than a W4A16 one, so the epilogue needs
+//              twice the warps to stay hidden
 #include "decode_common.cuh"
 #include "kernels.h"
 #include "moe_gemm.cuh"
@@ -31,7 +36,9 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kMxThreads = 352;                 // 11 warps
+constexpr int kMxSfGroups = 2;                  // scale-writer warpgroups, alternate steps
+constexpr int kMxEpiWarp = 3 + 4 * kMxSfGroups;  // first epilogue warp
+constexpr int kMxThreads = 32 * (kMxEpiWarp + 8);
 constexpr int kMxStepK = 256;                   // K per pipeline step: 8 MMAs of K = 32
 constexpr int kMxStages = 3;
 constexpr int kMxAStageBytes = 128 * kMxStepK;  // 128 rows x 256 E2M1 in byte containers
@@ -106,8 +113,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kMxStages; ++i) { mbar_init(&full[i], 6); mbar_init(&empty[i], 1); }
-        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+        for (int i = 0; i < kMxStages; ++i) { mbar_init(&full[i], 6); mbar_init(&empty[i], 1); }  // 2 TMA + 4 warps
+        for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }  // 8 epilogue warps
         fence_barrier_init();
     }
     if (warp == 2) {
@@ -221,18 +228,40 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             if (elect_one()) mma_commit(&acc_full[acc]);
             __syncwarp();
         }
-    } else if (warp <= 6) {
+    } else if (warp < kMxEpiWarp) {
         // ---------------- scale writers ----------------
         const int quad = warp & 3;
+        const int grp = (warp - 3) >> 2;  // takes the steps g with g % kMxSfGroups == grp
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         const size_t ih = static_cast<size_t>(args.hidden) * args.inter;
         const size_t s1 = ih + ih / 2, s3 = s1 + ih / 32, s2 = s3 + ih / 32;
         const int kb_row = args.k_total / 32;  // scale bytes per row
         uint32_t g = 0;
         bool ok = true;
+        // The scale rows of an item (weights: 128 rows, tokens: up to 128)
+        // are contiguous; one thread pulls the next item's into L2 while the
+        // current one runs, so the per-step loads below hit L2, not HBM.
+        auto prefetch_scales = [&](int item) {
+            if (item >= n_items || warp != 3 + 4 * grp || lane != 0) return;
+            MxItem pi;
+            mx_load_item(args, item, pi);
+            const int ps = (pi.slot < 0 || pi.slot >= args.num_slots) ? 0 : pi.slot;
+            const uint8_t* prec = args.records + static_cast<size_t>(ps) * args.record_bytes;
+            if (kGU) {
+                bulk_prefetch_l2(prec + s1 + static_cast<size_t>(pi.m * 64) * kb_row, 64 * kb_row);
+                bulk_prefetch_l2(prec + s3 + static_cast<size_t>(pi.m * 64) * kb_row, 64 * kb_row);
+            } else {
+                bulk_prefetch_l2(prec + s2 + static_cast<size_t>(pi.m * 128) * kb_row, 128 * kb_row);
+            }
+            const int r0 = min(pi.td.row_start, b_rows_cap - 1);
+            const int nr = min(min(pi.td.n_pad, kMxNMax), b_rows_cap - r0);
+            bulk_prefetch_l2(b_scales + static_cast<size_t>(r0) * kb_row, nr * kb_row);
+        };
+        if (grp == 0) prefetch_scales(blockIdx.x);
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             MxItem it;
             mx_load_item(args, item, it);
+            if (grp == 0) prefetch_scales(item + gridDim.x);
             const int slot = (it.slot < 0 || it.slot >= args.num_slots) ? 0 : it.slot;
             const uint8_t* rec = args.records + static_cast<size_t>(slot) * args.record_bytes;
             const uint8_t* arow[4];
@@ -249,16 +278,17 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                 const int trow = min(it.td.row_start + r, b_rows_cap - 1);
                 brow[c] = b_scales + static_cast<size_t>(trow) * kb_row;
             }
-            for (int st = 0; st < steps; ++st, ++g) {
-                const uint32_t s = g % kMxStages;
-                uint2 av[4], bv[4];
+            auto load = [&](uint2 (&av)[4], uint2 (&bv)[4], int st) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     av[c] = __ldg(reinterpret_cast<const uint2*>(arow[c] + st * 8));
                     bv[c] = __ldg(reinterpret_cast<const uint2*>(brow[c] + st * 8));
                 }
-                ok = mbar_wait(&empty[s], ((g / kMxStages) & 1u) ^ 1u, status, kStatusTimeoutDequant);
-                if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+            };
+            auto put = [&](const uint2 (&av)[4], const uint2 (&bv)[4], uint32_t gi) -> bool {
+                const uint32_t s = gi % kMxStages;
+                const bool got = mbar_wait(&empty[s], ((gi / kMxStages) & 1u) ^ 1u, status, kStatusTimeoutDequant);
+                if (!__all_sync(0xffffffffu, got)) return false;
                 tc_fence_after();
                 const uint32_t col = tmem_base + lane_addr + kMxSfBase + s * kMxSfCols;
                 tmem_st_32x32b_x4(col, av[0].x, av[1].x, av[2].x, av[3].x);
@@ -269,11 +299,30 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
+                return true;
+            };
+            // This group's steps of the item are st = grp + kMxSfGroups * k.
+            // Two register sets alternate over k, each loaded two of the
+            // group's steps ahead of its use.
+            const int n_my = (steps - grp + kMxSfGroups - 1) / kMxSfGroups;
+            auto step_of = [&](int k) { return grp + kMxSfGroups * k; };
+            uint2 a0[4], b0[4], a1[4], b1[4];
+            if (n_my > 0) load(a0, b0, step_of(0));
+            if (n_my > 1) load(a1, b1, step_of(1));
+            for (int k = 0; k < n_my && ok; k += 2) {
+                ok = put(a0, b0, g + step_of(k));
+                if (!ok) break;
+                if (k + 2 < n_my) load(a0, b0, step_of(k + 2));
+                if (k + 1 >= n_my) break;
+                ok = put(a1, b1, g + step_of(k + 1));
+                if (ok && k + 3 < n_my) load(a1, b1, step_of(k + 3));
             }
+            g += steps;
         }
     } else {
         // ---------------- epilogue ----------------
         const int quad = warp & 3;
+        const int half = (warp - kMxEpiWarp) >> 2;  // which of the quadrant's two warps
         const int L = quad * 32 + lane;
         const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
         int local = 0;
@@ -287,7 +336,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             if (!__all_sync(0xffffffffu, got)) break;
             tc_fence_after();
             const uint32_t col0 = tmem_base + lane_addr + acc * kMxNMax;
-            for (int c = 0; c < n_pad; c += 32) {
+            for (int c = 32 * half; c < n_pad; c += 64) {
                 uint32_t v[32];
                 tmem_ld_32x32b_x32(col0 + c, v);
                 tmem_wait_ld();
