@@ -13,16 +13,17 @@
 //              groups of 16 so the accumulator lanes pair gate and up rows
 //              the way the W4A16 epilogue expects
 //   warp 1     TMA producer of the E4M3 token rows (16/32/64/128-row boxes)
-//   warp 2     MMA issuer (whole warp, one elected lane): eight K = 32 MMAs
-//              per 256-K step
-//   warps 3-10 scale writers, two warpgroups taking alternate steps (a
-//              tcgen05.st + wait::st costs ~700 cycles under the MMAs' tensor
-//              memory traffic): the weights' and the tokens' UE8M0 bytes of
-//              the step into tensor memory (tcgen05.st), in the layout the
-//              block-scaled MMA reads: for 4 K blocks, lane l of column c
-//              holds row 32c + l, one byte per K block, replicated in the
-//              four lane quadrants
-//   warps 11-18 epilogue, two warps per lane quadrant taking alternate
+//   warp 2     MMA issuer (whole warp, one elected lane): per 256-K step,
+//              four tcgen05.cp of the step's scales from shared memory into
+//              tensor memory, then eight K = 32 MMAs, in issue order
+//   warps 3-4  scale stagers, taking alternate steps: the weights' and the
+//              tokens' UE8M0 bytes of the step, loaded from L2 two of the
+//              warp's steps ahead, stored to shared memory in the layout
+//              tcgen05.cp.32x128b.warpx4 turns into the one the block-scaled
+//              MMA reads (per 128 rows and 4 K blocks, 512 bytes: row
+//              32c + l at byte 16l + 4c, one byte per K block; in tensor
+//              memory lane l of column c, the same in all four quadrants)
+//   warps 5-12 epilogue, two warps per lane quadrant taking alternate
 //              32-column chunks: as the W4A16 kernel (SwiGLU into FP16 act,
 //              or the FP32 scatter to the selections' rows); a K step here
 //              is four times shorter than a W4A16 one, so the epilogue needs
@@ -36,17 +37,20 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kMxSfGroups = 2;                  // scale-writer warpgroups, alternate steps
-constexpr int kMxEpiWarp = 3 + 4 * kMxSfGroups;  // first epilogue warp
+constexpr int kMxSfWarps = 2;                   // scale stagers, alternate steps
+constexpr int kMxEpiWarp = 3 + kMxSfWarps;       // first epilogue warp
 constexpr int kMxThreads = 32 * (kMxEpiWarp + 8);
 constexpr int kMxStepK = 256;                   // K per pipeline step: 8 MMAs of K = 32
 constexpr int kMxStages = 3;
 constexpr int kMxAStageBytes = 128 * kMxStepK;  // 128 rows x 256 E2M1 in byte containers
 constexpr int kMxBStageBytes = 128 * kMxStepK;  // up to 128 token rows x 256 E4M3
+constexpr int kMxSfAtom = 512;                  // scales of 128 rows x 4 K blocks
+constexpr int kMxSfStageBytes = 4 * kMxSfAtom;  // weights and tokens, 2 atoms each
 constexpr int kMxNMax = 128;
 constexpr int kMxSfBase = 2 * kMxNMax;          // after the double-buffered accumulator
 constexpr int kMxSfCols = 16;                   // per stage: A scales 8 columns, token scales 8
-constexpr int kMxSmemBytes = 1024 + kMxStages * (kMxAStageBytes + kMxBStageBytes) + 1024;
+constexpr int kMxSmemBytes =
+    1024 + kMxStages * (kMxAStageBytes + kMxBStageBytes + kMxSfStageBytes) + 1024;
 static_assert(kMxSmemBytes <= 232448, "shared memory budget");
 static_assert(kMxSfBase + kMxStages * kMxSfCols <= 512, "tensor memory budget");
 
@@ -103,8 +107,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                                                ~static_cast<uintptr_t>(1023));
     uint8_t* a_smem = smem;
     uint8_t* b_smem = a_smem + kMxStages * kMxAStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(b_smem + kMxStages * kMxBStageBytes);
-    uint64_t* full = bars;                 // weights + tokens landed, scales written
+    uint8_t* sf_smem = b_smem + kMxStages * kMxBStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sf_smem + kMxStages * kMxSfStageBytes);
+    uint64_t* full = bars;                 // weights + tokens landed, scales staged
     uint64_t* empty = full + kMxStages;    // step consumed by the MMAs
     uint64_t* acc_full = empty + kMxStages;
     uint64_t* acc_empty = acc_full + 2;
@@ -113,7 +118,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kMxStages; ++i) { mbar_init(&full[i], 6); mbar_init(&empty[i], 1); }  // 2 TMA + 4 warps
+        for (int i = 0; i < kMxStages; ++i) { mbar_init(&full[i], 3); mbar_init(&empty[i], 1); }  // 2 TMA + 1 stager
         for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 8); }  // 8 epilogue warps
         fence_barrier_init();
     }
@@ -212,7 +217,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                 const uint64_t da = smem_desc_k128(smem_u32(a_smem + s * kMxAStageBytes));
                 const uint64_t db = smem_desc_k128(smem_u32(b_smem + s * kMxBStageBytes));
                 const uint32_t sf = tmem_base + kMxSfBase + s * kMxSfCols;
+                const uint32_t sf_src = smem_u32(sf_smem + s * kMxSfStageBytes);
                 if (elect_one()) {
+                    // weight scales to columns sf + 0..7, token scales to sf + 8..15
+#pragma unroll
+                    for (int a = 0; a < 4; ++a) tmem_cp_32x128b_x4(sf + 4 * a, smem_desc_plain(sf_src + a * kMxSfAtom, 128));
 #pragma unroll
                     for (int kb = 0; kb < kMxStepK / 32; ++kb) {
                         const uint32_t c = kb >> 2, id = kb & 3;
@@ -229,10 +238,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             __syncwarp();
         }
     } else if (warp < kMxEpiWarp) {
-        // ---------------- scale writers ----------------
-        const int quad = warp & 3;
-        const int grp = (warp - 3) >> 2;  // takes the steps g with g % kMxSfGroups == grp
-        const uint32_t lane_addr = static_cast<uint32_t>(quad * 32) << 16;
+        // ---------------- scale stagers ----------------
+        const int grp = warp - 3;  // takes the steps g with g % kMxSfWarps == grp
         const size_t ih = static_cast<size_t>(args.hidden) * args.inter;
         const size_t s1 = ih + ih / 2, s3 = s1 + ih / 32, s2 = s3 + ih / 32;
         const int kb_row = args.k_total / 32;  // scale bytes per row
@@ -242,7 +249,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         // are contiguous; one thread pulls the next item's into L2 while the
         // current one runs, so the per-step loads below hit L2, not HBM.
         auto prefetch_scales = [&](int item) {
-            if (item >= n_items || warp != 3 + 4 * grp || lane != 0) return;
+            if (item >= n_items || grp != 0 || lane != 0) return;
             MxItem pi;
             mx_load_item(args, item, pi);
             const int ps = (pi.slot < 0 || pi.slot >= args.num_slots) ? 0 : pi.slot;
@@ -257,11 +264,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const int nr = min(min(pi.td.n_pad, kMxNMax), b_rows_cap - r0);
             bulk_prefetch_l2(b_scales + static_cast<size_t>(r0) * kb_row, nr * kb_row);
         };
-        if (grp == 0) prefetch_scales(blockIdx.x);
+        prefetch_scales(blockIdx.x);
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             MxItem it;
             mx_load_item(args, item, it);
-            if (grp == 0) prefetch_scales(item + gridDim.x);
+            prefetch_scales(item + gridDim.x);
             const int slot = (it.slot < 0 || it.slot >= args.num_slots) ? 0 : it.slot;
             const uint8_t* rec = args.records + static_cast<size_t>(slot) * args.record_bytes;
             const uint8_t* arow[4];
@@ -285,27 +292,27 @@ __global__ void __launch_bounds__(kMxThreads, 1)
                     bv[c] = __ldg(reinterpret_cast<const uint2*>(brow[c] + st * 8));
                 }
             };
+            // Lane l writes the 16 bytes of rows l, 32 + l, 64 + l, 96 + l of
+            // each atom (four K blocks each): 512 contiguous bytes per atom.
             auto put = [&](const uint2 (&av)[4], const uint2 (&bv)[4], uint32_t gi) -> bool {
                 const uint32_t s = gi % kMxStages;
                 const bool got = mbar_wait(&empty[s], ((gi / kMxStages) & 1u) ^ 1u, status, kStatusTimeoutDequant);
                 if (!__all_sync(0xffffffffu, got)) return false;
-                tc_fence_after();
-                const uint32_t col = tmem_base + lane_addr + kMxSfBase + s * kMxSfCols;
-                tmem_st_32x32b_x4(col, av[0].x, av[1].x, av[2].x, av[3].x);
-                tmem_st_32x32b_x4(col + 4, av[0].y, av[1].y, av[2].y, av[3].y);
-                tmem_st_32x32b_x4(col + 8, bv[0].x, bv[1].x, bv[2].x, bv[3].x);
-                tmem_st_32x32b_x4(col + 12, bv[0].y, bv[1].y, bv[2].y, bv[3].y);
-                tmem_wait_st();
-                tc_fence_before();
+                uint4* dst = reinterpret_cast<uint4*>(sf_smem + s * kMxSfStageBytes) + lane;
+                dst[0] = make_uint4(av[0].x, av[1].x, av[2].x, av[3].x);
+                dst[32] = make_uint4(av[0].y, av[1].y, av[2].y, av[3].y);
+                dst[64] = make_uint4(bv[0].x, bv[1].x, bv[2].x, bv[3].x);
+                dst[96] = make_uint4(bv[0].y, bv[1].y, bv[2].y, bv[3].y);
+                fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&full[s]);
                 return true;
             };
-            // This group's steps of the item are st = grp + kMxSfGroups * k.
+            // This warp's steps of the item are st = grp + kMxSfWarps * k.
             // Two register sets alternate over k, each loaded two of the
-            // group's steps ahead of its use.
-            const int n_my = (steps - grp + kMxSfGroups - 1) / kMxSfGroups;
-            auto step_of = [&](int k) { return grp + kMxSfGroups * k; };
+            // warp's steps ahead of its use.
+            const int n_my = (steps - grp + kMxSfWarps - 1) / kMxSfWarps;
+            auto step_of = [&](int k) { return grp + kMxSfWarps * k; };
             uint2 a0[4], b0[4], a1[4], b1[4];
             if (n_my > 0) load(a0, b0, step_of(0));
             if (n_my > 1) load(a1, b1, step_of(1));

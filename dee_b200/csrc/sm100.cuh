@@ -344,6 +344,33 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
     return d;
 }
 
+// Shared-memory descriptor of a tile without swizzle: core matrices of 8 rows
+// x 16 bytes (128 contiguous bytes), the next 8 rows `sbo` bytes further on.
+// Used as the source of tcgen05.cp for 16-byte-wide tiles, so the leading
+// byte offset (between core matrices along the row) is never stepped over.
+__device__ __forceinline__ uint64_t smem_desc_plain(uint32_t smem_addr, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((128u >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= static_cast<uint64_t>(1u) << 46;
+    return d;
+}
+
+// tcgen05.cp of 32 rows x 128 bits from shared memory into tensor memory
+// columns taddr..taddr+3, row i to lane i of each of the four 32-lane
+// quadrants.  Asynchronous: it runs in issue order with this thread's later
+// tcgen05.mma, and tcgen05.commit tracks it.
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Make this thread's ordinary shared-memory stores visible to the async
+// proxy (TMA, tcgen05.mma and tcgen05.cp reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Instruction descriptor for kind::f16: D FP32 (bits 4-5 = 1), A and B FP16
 // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24.
 __host__ __device__ __forceinline__ constexpr uint32_t idesc_f16_f32(int M, int N) {
