@@ -80,6 +80,7 @@ SIGNATURES = {
     "dee_last_error": (ctypes.c_char_p, [P]),
     "dee_expert_bank_attach": (I, [P, I, P, I, SZ, P]),
     "dee_expert_bank_set_slots": (I, [P, I, P, P]),
+    "dee_group_by_expert_device": (I, [P, P, I, I, P, P, P, P]),
     "dee_route_topk_device": (I, [P, P, I, P, P, P]),
     "dee_route_dsv4_device": (I, [P, P, P, P, P, I, ctypes.c_float, P, P, P]),
     "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),

@@ -192,6 +192,8 @@ struct dee_engine {
     float* d_raw = nullptr;
     int32_t* h_ids = nullptr;      // pinned staging of host-given ids
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
+    int32_t* d_perm_chunks = nullptr;  // multi-CTA permutation: per-chunk expert counts
+    int32_t* d_perm_lrank = nullptr;   // multi-CTA permutation: rank within the chunk
     // shared-expert workspaces, capacity in tokens
     // MXFP8 path workspaces (E4M3 rows and per-32 UE8M0 scales), capacity in rows
     size_t cap_mx = 0;
@@ -264,6 +266,8 @@ void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
     cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
+    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank);
+    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr;
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
@@ -296,6 +300,8 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_act, cap * I)) != cudaSuccess ||
         (err = dev_alloc(&e->d_raw, cap * H)) != cudaSuccess ||
         (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_perm_chunks, ((cap + 1023) / 1024) * static_cast<size_t>(E))) != cudaSuccess ||
+        (err = dev_alloc(&e->d_perm_lrank, cap)) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
                              cudaHostAllocDefault)) != cudaSuccess) {
         free_workspace(e);
@@ -364,10 +370,14 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
 
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm,     e->d_row_of,
                   e->d_tiles,  e->d_n_tiles, write_journal ? e->d_journal : nullptr};
+    po.chunk_counts = e->d_perm_chunks;
+    po.lrank = e->d_perm_lrank;
+    po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream, skip_negative);
     if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    e->launches += permute_launch_count(tokens, K, po) - 1;
     stage_end(e, kStagePermute, stream);
     stage_begin(e, kStageGather, stream);
     err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H,
@@ -471,9 +481,13 @@ int run_experts_mx(dee_engine* e, int layer, const __half* d_x, int tokens, cons
     int rc = ensure_mx_capacity(e, sel, stream);
     if (rc != DEE_OK) return rc;
     PermuteOut po{e->d_counts, e->d_offsets, e->d_perm, e->d_row_of, e->d_tiles, e->d_n_tiles, e->d_journal};
+    po.chunk_counts = e->d_perm_chunks;
+    po.lrank = e->d_perm_lrank;
+    po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, gemm_n_max(), e->max_tiles, po, e->d_status, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    e->launches += permute_launch_count(tokens, K, po) - 1;
     stage_end(e, kStagePermute, stream);
     stage_begin(e, kStageGather, stream);
     err = launch_act_quant(d_x, static_cast<int>(sel), H, act_block, e->d_perm, K, e->d_offsets + E, e->d_xq, e->d_xs,
@@ -702,6 +716,27 @@ int dee_route_topk_device(dee_engine* e, const float* d_logits, int tokens, int3
     if (err != cudaSuccess) return cuda_fail(e, err, "router launch");
     stage_end(e, kStageRoute, static_cast<cudaStream_t>(stream));
     e->launches += 1;
+    return DEE_OK;
+}
+
+int dee_group_by_expert_device(dee_engine* e, const int32_t* d_ids, int tokens, int topk, int32_t* d_perm,
+                               int32_t* d_row_of, int32_t* d_offsets, void* stream) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    if (!d_ids || !d_perm || !d_row_of || !d_offsets || tokens <= 0 || topk <= 0 || topk > e->cfg.num_experts)
+        return fail(e, DEE_ERR_INVALID, "invalid grouping arguments");
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if ((rc = ensure_capacity(e, static_cast<size_t>(tokens) * topk, s)) != DEE_OK) return rc;
+    PermuteOut po{e->d_counts, d_offsets, d_perm, d_row_of, e->d_tiles, e->d_n_tiles, nullptr};
+    po.chunk_counts = e->d_perm_chunks;
+    po.lrank = e->d_perm_lrank;
+    po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
+    stage_begin(e, kStagePermute, s);
+    cudaError_t err = launch_permute(d_ids, tokens, topk, e->cfg.num_experts, gemm_n_max(), e->max_tiles, po,
+                                     e->d_status, s);
+    if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+    stage_end(e, kStagePermute, s);
+    e->launches += permute_launch_count(tokens, topk, po);
     return DEE_OK;
 }
 

@@ -180,9 +180,17 @@ struct PermuteOut {
     TileDesc* tiles;    // [max_tiles]
     int32_t* n_tiles;   // [1]
     int32_t* journal;   // [T*K] copy of the consumed ids, or null
+    // Scratch of the multi-CTA permutation (batches of more than two chunks
+    // of 1024 selections); without it one CTA does the whole batch.
+    int32_t* chunk_counts = nullptr;  // [max_chunks * E]
+    int32_t* lrank = nullptr;         // [T*K]
+    long long max_chunks = 0;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.
+// Kernels launch_permute issues for this batch: 1 (one CTA) or 2 (the
+// multi-CTA passes).
+int permute_launch_count(int tokens, int topk, const PermuteOut& out);
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
                            cudaStream_t stream, bool skip_negative = false);

@@ -346,6 +346,156 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     }
 }
 
+// The same permutation over many CTAs, for batches of more than two chunks
+// of kPermChunk selections.  Pass 1 (one CTA per chunk of the (rank, token)
+// enumeration): validation, the journal copy, each selection's stable rank
+// among the chunk's selections of its expert, and the chunk's per-expert
+// counts.  Pass 2 (one CTA per chunk): every CTA sums the chunk counts into
+// expert totals and the prefix over earlier chunks, scans the totals into
+// expert offsets and places its chunk; CTA 0 also writes counts, offsets and
+// the tile list.  Rows come out exactly as the single-CTA kernel places them.
+constexpr int kPermChunk = 1024;
+
+__global__ void __launch_bounds__(kPermChunk, 1)
+    permute_count_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts, PermuteOut out,
+                         uint32_t* status, bool skip_negative) {
+    __shared__ int wcnt[32][kPermMaxExperts];  // per-warp group sizes
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int sel = tokens * topk;
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    for (int i = tid; i < 32 * kPermMaxExperts; i += kPermChunk) (&wcnt[0][0])[i] = 0;
+    __syncthreads();
+    const int j = blockIdx.x * kPermChunk + tid;
+    int key = -1 - lane;  // unique per lane when not a valid selection
+    if (j < sel) {
+        const int r = j / tokens;
+        const int t = j - r * tokens;
+        const int p = t * topk + r;
+        const int e = ids[p];
+        if (out.journal) out.journal[p] = e;
+        if (e < 0 || e >= experts) {
+            if (!(skip_negative && e == -1)) atomicOr(status, kStatusBadExpert);
+            out.row_of[p] = -1;
+        } else {
+            key = e;
+        }
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, key);
+    const int rank_w = __popc(peers & ((1u << lane) - 1u));
+    if (key >= 0 && rank_w == 0) wcnt[warp][key] = __popc(peers);
+    __syncthreads();
+    if (key >= 0) {
+        int pre = 0;
+        for (int w = 0; w < warp; ++w) pre += wcnt[w][key];
+        out.lrank[j] = pre + rank_w;
+    }
+    for (int e = tid; e < experts; e += kPermChunk) {
+        int c = 0;
+#pragma unroll 8
+        for (int w = 0; w < 32; ++w) c += wcnt[w][e];
+        out.chunk_counts[static_cast<size_t>(blockIdx.x) * experts + e] = c;
+    }
+}
+
+__global__ void __launch_bounds__(kPermChunk, 1)
+    permute_place_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts, int n_tile_max,
+                         int max_tiles, PermuteOut out, uint32_t* status) {
+    __shared__ int tot[kPermMaxExperts];
+    __shared__ int before[kPermMaxExperts];  // this chunk's prefix over earlier chunks
+    __shared__ int off[kPermMaxExperts + 1];
+    __shared__ int ntile_off[kPermMaxExperts + 1];
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int sel = tokens * topk;
+    const int chunks = (sel + kPermChunk - 1) / kPermChunk;
+    const int me = blockIdx.x;
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    for (int e = tid; e < experts; e += kPermChunk) {
+        int s = 0, b = 0;
+        for (int k = 0; k < chunks; ++k) {
+            const int v = out.chunk_counts[static_cast<size_t>(k) * experts + e];
+            if (k < me) b += v;
+            s += v;
+        }
+        tot[e] = s;
+        before[e] = b;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scan of totals and of per-expert tile counts
+        const int per = (experts + 31) / 32;
+        int s = 0, st = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < experts) {
+                s += tot[e];
+                st += tot[e] > 0 ? (tot[e] + n_tile_max - 1) / n_tile_max : 0;
+            }
+        }
+        int incl = s, incl_t = st;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int a = __shfl_up_sync(0xffffffffu, incl, o);
+            const int b = __shfl_up_sync(0xffffffffu, incl_t, o);
+            if (lane >= o) { incl += a; incl_t += b; }
+        }
+        int run = incl - s, run_t = incl_t - st;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < experts) {
+                off[e] = run;
+                ntile_off[e] = run_t;
+                run += tot[e];
+                run_t += tot[e] > 0 ? (tot[e] + n_tile_max - 1) / n_tile_max : 0;
+            }
+        }
+        if (lane == 31) { off[experts] = incl; ntile_off[experts] = incl_t; }
+    }
+    __syncthreads();
+    const int j = me * kPermChunk + tid;
+    if (j < sel) {
+        const int r = j / tokens;
+        const int t = j - r * tokens;
+        const int p = t * topk + r;
+        const int e = ids[p];
+        if (e >= 0 && e < experts) {
+            const int row = off[e] + before[e] + out.lrank[j];
+            out.perm[row] = p;
+            out.row_of[p] = row;
+        }
+    }
+    if (me != 0) return;
+    for (int e = tid; e < experts; e += kPermChunk) {
+        out.counts[e] = tot[e];
+        out.offsets[e] = off[e];
+        const int c = tot[e];
+        if (c == 0) continue;
+        const int nt = (c + n_tile_max - 1) / n_tile_max;
+        const int sz = (c + nt - 1) / nt;
+        for (int i = 0; i < nt; ++i) {
+            const int slot = ntile_off[e] + i;
+            if (slot >= max_tiles) { atomicOr(status, kStatusBadShape); break; }
+            const int start = i * sz;
+            const int n = min(sz, c - start);
+            TileDesc td;
+            td.expert = e;
+            td.row_start = off[e] + start;
+            td.n_rows = n;
+            td.n_pad = (n + 15) & ~15;
+            out.tiles[slot] = td;
+        }
+    }
+    if (tid == 0) {
+        out.offsets[experts] = off[experts];
+        *out.n_tiles = min(ntile_off[experts], max_tiles);
+    }
+}
+
 __global__ void gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
                                    const int32_t* __restrict__ total_rows_dev, int max_rows,
                                    int topk, int hidden, __half* __restrict__ x_perm) {
@@ -510,11 +660,24 @@ cudaError_t launch_route_dsv4(const float* logits, const float* bias, const int6
                       tid2eid, input_ids, tokens, experts, topk, route_scale, ids, weights, status);
 }
 
+int permute_launch_count(int tokens, int topk, const PermuteOut& out) {
+    const long long chunks = (static_cast<long long>(tokens) * topk + kPermChunk - 1) / kPermChunk;
+    return chunks > 2 && out.chunk_counts && out.lrank && chunks <= out.max_chunks ? 2 : 1;
+}
+
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
                            cudaStream_t stream, bool skip_negative) {
     if (experts <= 0 || experts > kPermMaxExperts || tokens <= 0 || topk <= 0 || n_tile_max < 8)
         return cudaErrorInvalidValue;
+    if (permute_launch_count(tokens, topk, out) == 2) {
+        const long long chunks = (static_cast<long long>(tokens) * topk + kPermChunk - 1) / kPermChunk;
+        cudaError_t err = launch_pdl(permute_count_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kPermChunk), 0,
+                                     stream, ids, tokens, topk, experts, out, status, skip_negative);
+        if (err != cudaSuccess) return err;
+        return launch_pdl(permute_place_kernel, dim3(static_cast<unsigned>(chunks)), dim3(kPermChunk), 0, stream,
+                          ids, tokens, topk, experts, n_tile_max, max_tiles, out, status);
+    }
     return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), 0, stream, ids, tokens, topk,
                       experts, n_tile_max, max_tiles, out, status, skip_negative);
 }

@@ -83,6 +83,15 @@ DEE_API int dee_expert_bank_attach(dee_engine* engine, int layer, const void* d_
 DEE_API int dee_expert_bank_set_slots(dee_engine* engine, int layer, const int32_t* h_slot_of_expert,
                               void* stream);
 
+/* The engine's group-by-expert step on its own (Engine's grouping,
+ * engine.cpp:812-823): device ids [tokens, topk] int32 -> perm [T*K]
+ * (grouped row -> position t*K + r; the rows of one expert in (rank, token)
+ * order, experts by ascending id), row_of [T*K] (position -> grouped row, -1
+ * for an id outside [0, E)) and offsets [E + 1].  Ids outside [0, E) are
+ * reported by dee_engine_sync_status.  Asynchronous on `stream`. */
+DEE_API int dee_group_by_expert_device(dee_engine* engine, const int32_t* d_ids, int tokens, int topk,
+                                       int32_t* d_perm, int32_t* d_row_of, int32_t* d_offsets, void* stream);
+
 /* Softmax top-k with renormalised weights on device logits [T, E] FP32 ->
  * ids [T, K] int32 in rank order and weights [T, K] FP32.
  * Engine::route_topk_batch (engine.cpp:2604-2771). */

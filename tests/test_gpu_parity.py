@@ -398,3 +398,55 @@ def test_dsv4_router_large_matches_oracle(torch_cuda, oracle_mod):
     want_ids, want_w, _ = oracle_mod.route_dsv4(logits, 6, bias=bias)
     assert np.array_equal(ids.cpu().numpy(), want_ids)
     np.testing.assert_allclose(w.cpu().numpy(), want_w, rtol=2e-6)
+
+
+def _group_dev(torch, eng, lib, ids):
+    T, K = ids.shape
+    di = torch.from_numpy(np.ascontiguousarray(ids, dtype=np.int32)).cuda()
+    perm = torch.full((T * K,), -7, dtype=torch.int32, device="cuda")
+    row_of = torch.full((T * K,), -7, dtype=torch.int32, device="cuda")
+    offs = torch.full((eng.cfg.num_experts + 1,), -7, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream()
+    rc = lib.dee_group_by_expert_device(eng._h, ctypes.c_void_p(di.data_ptr()), T, K,
+                                        ctypes.c_void_p(perm.data_ptr()), ctypes.c_void_p(row_of.data_ptr()),
+                                        ctypes.c_void_p(offs.data_ptr()), ctypes.c_void_p(s.cuda_stream))
+    assert rc == 0
+    torch.cuda.synchronize()
+    return perm.cpu().numpy(), row_of.cpu().numpy(), offs.cpu().numpy(), eng.sync_status()
+
+
+@pytest.mark.parametrize("T,K,E,skew", [(1, 6, 256, 0.0), (8, 6, 256, 0.0), (300, 6, 64, 0.0), (341, 6, 16, 0.0),
+                                         (342, 6, 16, 0.0), (700, 6, 48, 1.5), (4096, 6, 256, 1.1),
+                                         (5000, 8, 256, 0.0), (3000, 1, 7, 0.0)])
+def test_group_by_expert_bitexact(torch_cuda, lib, oracle_mod, T, K, E, skew):
+    """The grouping (one CTA for up to 2048 selections, two multi-CTA passes
+    above) against the oracle's restatement of engine.cpp:812-823: perm,
+    row_of and offsets bit-exact, rows of an expert in (rank, token) order."""
+    rng = np.random.default_rng(T * 31 + E)
+    ids = _skewed_ids(rng, T, E, K, s=skew) if skew else _rand_ids(rng, T, E, K)
+    eng = _engine(512, 512, E, K, max_tokens=T)
+    perm, row_of, offs, status = _group_dev(torch_cuda, eng, lib, ids)
+    counts, w_offs, w_perm = oracle_mod.group(ids, E)
+    assert status == 0
+    assert np.array_equal(offs, w_offs)
+    assert np.array_equal(perm, w_perm)
+    assert np.array_equal(row_of[perm], np.arange(T * K, dtype=np.int32))
+
+
+@pytest.mark.parametrize("T", [10, 3000])
+def test_group_by_expert_rejects_bad_ids(torch_cuda, lib, T):
+    """An id outside [0, E) sets the bad-expert status bit and leaves that
+    position out (row_of = -1); the valid selections are still grouped."""
+    rng = np.random.default_rng(T)
+    E, K = 32, 6
+    ids = _rand_ids(rng, T, E, K)
+    ids[T // 2, 3] = E + 5
+    ids[T - 1, 0] = -3
+    eng = _engine(512, 512, E, K, max_tokens=T)
+    perm, row_of, offs, status = _group_dev(torch_cuda, eng, lib, ids)
+    assert status & (1 << 4)
+    bad = [(T // 2) * K + 3, (T - 1) * K + 0]
+    assert all(row_of[p] == -1 for p in bad)
+    n = offs[E]
+    assert n == T * K - 2
+    assert np.array_equal(np.sort(perm[:n]), np.setdiff1d(np.arange(T * K), bad))
