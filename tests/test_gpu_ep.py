@@ -163,3 +163,32 @@ def test_expert_parallel_peer_emulated_two_ranks(torch_cuda, oracle_mod, T):
             got, want = rk["out"].cpu().numpy(), ref.cpu().numpy()
             assert np.array_equal(got, want), float(np.abs(got - want).max())
             assert np.array_equal(rk["eng"].journal_ids(T), rk["ids"])
+
+
+def test_rows_forward_large_receive_buffer(torch_cuda, oracle_mod):
+    """A receive buffer of 2500 rows (the multi-CTA grouping) with a third of
+    the rows unused (expert -1): the unused rows are left as they were, the
+    others match the oracle's FP16 expert chain."""
+    torch = torch_cuda
+    orc = oracle_mod
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, EPR, seed=4242, kind="normal")
+    eng = _engine(EPR)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    rng = np.random.default_rng(2500)
+    n = 2500
+    x16 = orc.f16_bits(rng.standard_normal((n, H)))
+    exp_ = rng.integers(0, EPR, n).astype(np.int32)
+    exp_[rng.random(n) < 0.35] = -1
+    rows = torch.from_numpy(x16.view(np.float16)).cuda()
+    dexp = torch.from_numpy(exp_).cuda()
+    raw = torch.full((n, H), 7.0, dtype=torch.float32, device="cuda")
+    eng.moe_forward_rows_device(0, rows.data_ptr(), dexp.data_ptr(), n, raw.data_ptr())
+    torch.cuda.synchronize()
+    assert eng.sync_status() == 0
+    got = raw.cpu().numpy()
+    unused = exp_ < 0
+    assert (got[unused] == 7.0).all()
+    want = orc.moe_layer_raw(recs, layout, x16[~unused], exp_[~unused].reshape(-1, 1))[:, 0]
+    assert orc.rel_l2(got[~unused], want) <= TOL_REL_L2
