@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstdint>
 
 #include "moe_gemm.cuh"
@@ -25,6 +26,22 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Opt kernel Kern in to `bytes` of dynamic shared memory on the current
+// device, once per device (the attribute belongs to the device's context;
+// devices 64 and up set it at every call).
+template <auto Kern>
+cudaError_t ensure_smem_attr(int bytes) {
+    static std::atomic<uint64_t> done{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (uint64_t{1} << dev) : 0;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+    return e;
 }
 
 struct GemmMaps {

@@ -509,13 +509,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 template <GemmMode MODE, bool kOfficial>
 cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
     auto kern = moe_decode_kernel<MODE, kOfficial>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmemLimit));
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<MODE, kOfficial>>(static_cast<int>(kSmemLimit));
+    if (e != cudaSuccess) return e;
     const DecLayout L = dec_layout(args.k_total);
     if (L.stages < 2 || L.bytes > kSmemLimit) return cudaErrorInvalidValue;
     return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps.w0, maps.w1, maps.b,

@@ -455,12 +455,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 template <GemmMode MODE>
 cudaError_t launch_one(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
     auto kern = moe_gemm_kernel<MODE>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    const cudaError_t e = ensure_smem_attr<moe_gemm_kernel<MODE>>(kGemmSmemBytes);
+    if (e != cudaSuccess) return e;
     return launch_pdl(kern, dim3(grid), dim3(kGemmThreads), kGemmSmemBytes, stream, maps.w0, maps.w1, maps.s0,
                       maps.s1, maps.bt[0], maps.bt[1], maps.bt[2], maps.bt[3], args);
 }

@@ -395,12 +395,8 @@ template <GemmMode MODE>
 cudaError_t launch_mx(const MxMaps& maps, const GemmArgs& args, const uint8_t* b_scales, int b_rows_cap, int grid,
                       cudaStream_t stream) {
     auto kern = moe_mxfp8_kernel<MODE>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    const cudaError_t e = ensure_smem_attr<moe_mxfp8_kernel<MODE>>(kMxSmemBytes);
+    if (e != cudaSuccess) return e;
     return launch_pdl(kern, dim3(grid), dim3(kMxThreads), kMxSmemBytes, stream, maps.a, maps.bt[0], maps.bt[1],
                       maps.bt[2], maps.bt[3], args, b_scales, b_rows_cap);
 }

@@ -224,12 +224,8 @@ template <bool kGU>
 cudaError_t launch_sh(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& b,
                       const SharedArgs& args, int grid, cudaStream_t stream) {
     auto kern = shared_fp8_kernel<kGU>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kShSmem);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    const cudaError_t e = ensure_smem_attr<shared_fp8_kernel<kGU>>(kShSmem);
+    if (e != cudaSuccess) return e;
     return launch_pdl(kern, dim3(grid), dim3(kShThreads), kShSmem, stream, w0, w1, b, args);
 }
 

@@ -450,3 +450,40 @@ def test_group_by_expert_rejects_bad_ids(torch_cuda, lib, T):
     n = offs[E]
     assert n == T * K - 2
     assert np.array_equal(np.sort(perm[:n]), np.setdiff1d(np.arange(T * K), bad))
+
+
+def test_two_devices_one_process(torch_cuda, oracle_mod):
+    """One process drives engines on two GPUs (decode and prefill kernels on
+    each): every kernel's shared-memory opt-in is made per device, and both
+    devices return the same bits for the same inputs."""
+    torch = torch_cuda
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import dee_b200
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=61, kind="normal")
+    rng = np.random.default_rng(61)
+    outs = []
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            eng = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
+                                                            device_id=dev, max_tokens=300))
+            bank = torch.from_numpy(recs).to(f"cuda:{dev}")
+            eng.attach_bank(0, bank)
+            got = []
+            for T in (8, 300):  # the decode kernel, then the tcgen05 prefill kernel
+                r = np.random.default_rng(T)
+                x16 = orc.f16_bits(r.standard_normal((T, H)))
+                ids = _rand_ids(r, T, E, K)
+                dx = torch.from_numpy(x16.view(np.float16)).to(f"cuda:{dev}")
+                raw = torch.zeros((T, K, H), dtype=torch.float32, device=f"cuda:{dev}")
+                assert eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
+                torch.cuda.synchronize(dev)
+                assert eng.sync_status() == 0
+                got.append(raw.cpu().numpy())
+            outs.append(got)
+            del eng
+    for a, b in zip(outs[0], outs[1]):
+        assert np.array_equal(a, b)
