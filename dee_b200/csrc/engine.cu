@@ -764,7 +764,7 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     if (rc != DEE_OK) return rc;
     e->last_error.clear();
     auto stream = static_cast<cudaStream_t>(stream_v);
-    if (!d_x_f16 || tokens <= 0 || topk != e->cfg.topk || (!d_ids && !h_ids) ||
+    if (!d_x_f16 || tokens <= 0 || topk <= 0 || topk > e->cfg.topk || (!d_ids && !h_ids) ||
         (!d_out_f32 && !d_raw) || (d_out_f32 && !d_weights))
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_device arguments");
     const size_t sel = static_cast<size_t>(tokens) * topk;
@@ -802,7 +802,7 @@ int dee_moe_forward_mxfp8_device(dee_engine* e, int layer, const void* d_x_f16, 
     if (rc != DEE_OK) return rc;
     e->last_error.clear();
     auto stream = static_cast<cudaStream_t>(stream_v);
-    if (!d_x_f16 || tokens <= 0 || topk != e->cfg.topk || !d_ids || (!d_out_f32 && !d_raw) ||
+    if (!d_x_f16 || tokens <= 0 || topk <= 0 || topk > e->cfg.topk || !d_ids || (!d_out_f32 && !d_raw) ||
         (d_out_f32 && !d_weights) || (act_block != 32 && act_block != 128))
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_mxfp8_device arguments");
     const size_t sel = static_cast<size_t>(tokens) * topk;
@@ -827,7 +827,7 @@ int dee_moe_forward_batch_device(dee_engine* e, int layer, const void* d_h_in, i
                                  const int32_t* h_expert_ids, int topk, void* d_experts_out) {
     int rc = check_engine(e);
     if (rc != DEE_OK) return rc;
-    if (!d_h_in || !h_expert_ids || !d_experts_out || tokens <= 0 || topk != e->cfg.topk)
+    if (!d_h_in || !h_expert_ids || !d_experts_out || tokens <= 0 || topk <= 0 || topk > e->cfg.topk)
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_batch_device arguments");
     cudaError_t err = cudaMemsetAsync(e->d_status, 0, 4, e->stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "status reset");
@@ -847,7 +847,7 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     e->last_error.clear();
     auto stream = static_cast<cudaStream_t>(external_stream);
     if (!d_h_in || !d_expert_ids || !d_weights_f32 || !d_output_f16 || tokens <= 0 ||
-        topk != e->cfg.topk)
+        topk <= 0 || topk > e->cfg.topk)
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_combined_device arguments");
     const size_t sel = static_cast<size_t>(tokens) * topk;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;

@@ -112,7 +112,8 @@ DEE_API int dee_route_dsv4_device(dee_engine* engine, const float* d_logits, con
 
 /* Engine::moe_forward_batch_device (engine.h:312-314, pydee.cpp:430-467):
  * FP16 hidden [T, H] on device, host int32 ids [T, K] (validated on the
- * host, fail closed), FP32 raw expert outputs [T, K, H] on device.
+ * host, fail closed), FP32 raw expert outputs [T, K, H] on device;
+ * 1 <= K <= EngineConfig::topk, as the reference accepts (engine.cpp:780-781).
  * Runs on the engine's stream and synchronises it before returning. */
 DEE_API int dee_moe_forward_batch_device(dee_engine* engine, int layer, const void* d_h_in, int tokens,
                                  const int32_t* h_expert_ids, int topk, void* d_experts_out);

@@ -487,3 +487,28 @@ def test_two_devices_one_process(torch_cuda, oracle_mod):
             del eng
     for a, b in zip(outs[0], outs[1]):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("T,K", [(8, 4), (200, 2)])
+def test_batch_with_fewer_selections_than_configured(torch_cuda, oracle_mod, T, K):
+    """The reference accepts topk <= EngineConfig::topk (engine.cpp:780-781):
+    K = 4 or 2 on a top-6 engine, raw [T, K, H] against the oracle, and the
+    journal holds the call's [T, K] ids."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E = 512, 512, 16
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=T + K, kind="normal")
+    eng = _engine(H, I, E, 6, max_tokens=T)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    rng = np.random.default_rng(T * 7 + K)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = _rand_ids(rng, T, E, K)
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    raw = torch.zeros((T, K, H), dtype=torch.float32, device="cuda")
+    assert eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
+    want = orc.moe_layer_raw(recs, layout, x16, ids)
+    assert orc.rel_l2(raw.cpu().numpy(), want) <= TOL_REL_L2
+    assert np.array_equal(eng.journal_ids(T), ids)
+    with pytest.raises(RuntimeError):
+        eng.moe_forward_batch_device(0, dx.data_ptr(), T, _rand_ids(rng, T, E, 7)[:, :7], 7, raw.data_ptr())
