@@ -813,6 +813,17 @@ def main():
                                   "tflops_gemms": flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None,
                                   "stage_ms": psg, "max_expert_rows": int(counts.max()),
                                   "active_experts": int((counts > 0).sum())}
+        # the same layer through the MXFP8-activation variant (E4M3 tokens,
+        # UE8M0 per 32; its tensor-core peak is the FP8 rate, 2x bf16)
+        try:
+            mt, msg, _ = prefill_point(torch, eng, 5, 2, flush, stream, seed=4000 + rank, act_block=32)
+            mms = statistics.mean(mt)
+            sweep["prefill_t4096_mxfp8"] = {"tokens_per_s": 4096 / (mms / 1000.0), "ms": mms,
+                                            "tflops_layer": flops / (mms / 1000.0) / 1e12,
+                                            "tc_frac_layer_fp8": flops / (mms / 1000.0) / 1e12 / (2 * tc_peak),
+                                            "stage_ms": msg, "act_block": 32}
+        except Exception as exc:  # the variant needs a driver that encodes unpacked-FP4 maps
+            sweep["prefill_t4096_mxfp8"] = {"unavailable": str(exc)[:200]}
         result["sweep"] = sweep
 
     # ---- CPU baseline (rank 0, N=1): the reference executor on host cores ----
