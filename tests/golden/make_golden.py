@@ -1,7 +1,7 @@
 """Generate the golden fixtures in this directory from the reference itself.
 
-Run in a container where so-nerdyy/dee is checked out (default
-``/root/reference``; override with ``DEE_REFERENCE_ROOT``):
+Run where so-nerdyy/dee is checked out (its root in ``DEE_REFERENCE_ROOT``,
+else the default of ``REF`` below):
 
     python tests/golden/make_golden.py
 
