@@ -658,6 +658,10 @@ def run_stack(args):
 
 def main():
     args = parse()
+    # Rank 0's stdout carries exactly one JSON line: NCCL's own log lines
+    # (its version banner included, when a launcher enables NCCL_DEBUG) go to
+    # a per-process file unless the caller chose a destination.
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/dee_b200_nccl.%h.%p.log")
     if args.impl == "reference":
         run_reference(args)
         return
