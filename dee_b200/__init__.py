@@ -62,7 +62,6 @@ class Engine:
         self.cfg: EngineConfig | None = None
         self._banks: dict[int, object] = {}
         self._shared: dict[int, tuple] = {}
-        self._last_topk: int | None = None  # selections per token of the latest forward
 
     # -- lifecycle -------------------------------------------------------
     def init(self, cfg: EngineConfig) -> bool:
@@ -142,12 +141,13 @@ class Engine:
         ids = np.ascontiguousarray(expert_ids, dtype=np.int32)
         if ids.ndim != 2 or ids.shape[0] != tokens or ids.shape[1] != topk:
             raise RuntimeError("expert_ids must have shape [tokens, topk]")
-        if not 1 <= topk <= self.cfg.topk:
-            raise RuntimeError("topk must be in [1, EngineConfig.topk]")
+        # pydee's binding accepts only the configured topk (pydee.cpp:443-444);
+        # the C entry also takes fewer, as Engine::moe_forward_batch_device does
+        if topk != self.cfg.topk:
+            raise RuntimeError("expert_ids topk does not match EngineConfig.topk")
         rc = self._lib.dee_moe_forward_batch_device(
             self._h, layer, ctypes.c_void_p(d_h_in_ptr), tokens, ids.ctypes.data_as(ctypes.c_void_p),
             topk, ctypes.c_void_p(d_experts_out_ptr))
-        self._last_topk = topk
         return rc == _native.DEE_OK
 
     def moe_forward_combined_device(self, layer: int, d_h_in_ptr: int, tokens: int,
@@ -155,13 +155,12 @@ class Engine:
                                     d_output_ptr: int, d_raw_trace_ptr: int,
                                     external_stream_ptr: int) -> bool:
         """pydee.Engine.moe_forward_combined_device (pydee.cpp:468-509)."""
-        if not 1 <= topk <= self.cfg.topk:
-            raise RuntimeError("topk must be in [1, EngineConfig.topk]")
+        if topk != self.cfg.topk:  # pydee.cpp:479-482
+            raise RuntimeError("expert_ids topk does not match EngineConfig.topk")
         rc = self._lib.dee_moe_forward_combined_device(
             self._h, layer, ctypes.c_void_p(d_h_in_ptr), tokens, ctypes.c_void_p(d_expert_ids_ptr),
             topk, ctypes.c_void_p(d_weights_ptr), ctypes.c_void_p(d_output_ptr),
             ctypes.c_void_p(d_raw_trace_ptr or 0), ctypes.c_void_p(external_stream_ptr or 0))
-        self._last_topk = topk
         return rc == _native.DEE_OK
 
     # -- device-resident routing and the one-call layer ------------------
@@ -194,7 +193,6 @@ class Engine:
             ctypes.c_void_p(d_weights_ptr or 0), ctypes.c_void_p(d_out_ptr or 0),
             ctypes.c_void_p(d_raw_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_moe_forward_device")
-        self._last_topk = self.cfg.topk
 
     def moe_forward_mxfp8_device(self, layer: int, d_x_ptr: int, tokens: int, d_ids_ptr: int, d_raw_ptr: int = 0,
                                  *, d_weights_ptr: int = 0, d_out_ptr: int = 0, act_block: int = 32,
@@ -326,9 +324,8 @@ class Engine:
         return int(st.value)
 
     def journal_ids(self, tokens: int) -> np.ndarray:
-        """The int32 [tokens, topk] ids the last forward consumed (topk of
-        that call)."""
-        out = np.empty((tokens, self._last_topk or self.cfg.topk), dtype=np.int32)
+        """The int32 [tokens, topk] ids the last forward consumed."""
+        out = np.empty((tokens, self.cfg.topk), dtype=np.int32)
         n = self._lib.dee_journal_ids_host(self._h, out.ctypes.data_as(ctypes.c_void_p), out.size)
         if n != out.size:
             raise DeeError(f"journal ids unavailable ({n} of {out.size})")

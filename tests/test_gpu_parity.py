@@ -490,10 +490,12 @@ def test_two_devices_one_process(torch_cuda, oracle_mod):
 
 
 @pytest.mark.parametrize("T,K", [(8, 4), (200, 2)])
-def test_batch_with_fewer_selections_than_configured(torch_cuda, oracle_mod, T, K):
-    """The reference accepts topk <= EngineConfig::topk (engine.cpp:780-781):
-    K = 4 or 2 on a top-6 engine, raw [T, K, H] against the oracle, and the
-    journal holds the call's [T, K] ids."""
+def test_batch_with_fewer_selections_than_configured(torch_cuda, lib, oracle_mod, T, K):
+    """The C entry takes topk <= EngineConfig::topk like
+    Engine::moe_forward_batch_device (engine.cpp:780-781): K = 4 or 2 on a
+    top-6 engine, raw [T, K, H] against the oracle and the journal holding
+    the call's [T, K] ids; the Python method keeps pydee's binding rule
+    (pydee.cpp:443-444) and refuses a topk other than the configured one."""
     torch = torch_cuda
     orc = oracle_mod
     H, I, E = 512, 512, 16
@@ -506,9 +508,13 @@ def test_batch_with_fewer_selections_than_configured(torch_cuda, oracle_mod, T, 
     ids = _rand_ids(rng, T, E, K)
     dx = torch.from_numpy(x16.view(np.float16)).cuda()
     raw = torch.zeros((T, K, H), dtype=torch.float32, device="cuda")
-    assert eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
+    rc = lib.dee_moe_forward_batch_device(eng._h, 0, ctypes.c_void_p(dx.data_ptr()), T,
+                                          ids.ctypes.data_as(ctypes.c_void_p), K, ctypes.c_void_p(raw.data_ptr()))
+    assert rc == 0, eng.last_error_message()
     want = orc.moe_layer_raw(recs, layout, x16, ids)
     assert orc.rel_l2(raw.cpu().numpy(), want) <= TOL_REL_L2
-    assert np.array_equal(eng.journal_ids(T), ids)
-    with pytest.raises(RuntimeError):
-        eng.moe_forward_batch_device(0, dx.data_ptr(), T, _rand_ids(rng, T, E, 7)[:, :7], 7, raw.data_ptr())
+    journal = np.empty(T * K, dtype=np.int32)
+    assert lib.dee_journal_ids_host(eng._h, journal.ctypes.data_as(ctypes.c_void_p), T * K) == T * K
+    assert np.array_equal(journal.reshape(T, K), ids)
+    with pytest.raises(RuntimeError, match="does not match EngineConfig.topk"):
+        eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
