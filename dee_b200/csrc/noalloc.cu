@@ -2,13 +2,14 @@
 // device memory.
 //
 // Some callers cannot call cudaMalloc: code running inside an allocator or
-// memory-pool callback, a host that has handed all device memory to its own
-// caching allocator, or a process under a hard no-allocation policy while a
-// CUDA graph is being prepared.  For them dee_moe_forward_noalloc runs the
-// same kernels as dee_moe_forward_device, but every scratch buffer (grouped
-// row tables, the tile list, the gathered token rows, the SwiGLU activations
-// and the raw per-selection rows) lives in one statically sized device array
-// defined in this file.  The call itself allocates nothing.
+// memory-pool callback (allocating there would re-enter the allocator), or a
+// host that has handed all device memory to its own caching allocator (a
+// second allocator would fail or fragment it).  For them
+// dee_moe_forward_noalloc runs the same kernels as dee_moe_forward_device,
+// but every scratch buffer (grouped row tables, the tile list, the gathered
+// token rows, the SwiGLU activations and the raw per-selection rows) lives in
+// one statically sized device array defined in this file.  The call itself
+// allocates nothing.
 //
 // Limits and sharing:
 //   * kNoAllocScratchBytes (4 MiB) of device memory is reserved on every GPU
