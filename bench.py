@@ -413,7 +413,7 @@ def run_reference(args):
         pass
     res = cpu_reference_sample(b, seed=7, min_seconds=1.0, max_reps=1)
     if res is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built"}))
+        emit({"impl": "reference", "unavailable": "oracle/_ref not built"})
         return
     vals = []
     for i in range(args.warmup + args.steps):
@@ -436,7 +436,7 @@ def run_reference(args):
                                    f"random-byte FP4 records", "cpu": cpu_model},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    emit(line)
 
 
 # ---------------------------------------------------------------------------
@@ -452,7 +452,7 @@ def run_prefill(args):
     rank, world, local = dist_env()
     if world > 1:
         if rank == 0:
-            print(json.dumps({"workload": "prefill", "unavailable": "the prefill layer runs on one GPU"}))
+            emit({"workload": "prefill", "unavailable": "the prefill layer runs on one GPU"})
         return
     torch.cuda.set_device(local)
     hbm_peak, tc_peak, peak_kind = load_peaks()
@@ -502,7 +502,7 @@ def run_prefill(args):
         "gpu_launches_per_step": launches,
         "clocks": clk.summary(),
     }
-    print(json.dumps(result))
+    emit(result)
 
 
 def drop_page_cache(path):
@@ -653,15 +653,28 @@ def run_stack(args):
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result))
+        emit(result)
+
+
+_RESULT_OUT = None
+
+
+def emit(result):
+    """Print the result line on the process's original standard output."""
+    out = _RESULT_OUT if _RESULT_OUT is not None else sys.stdout
+    print(json.dumps(result), file=out, flush=True)
 
 
 def main():
+    global _RESULT_OUT
     args = parse()
-    # Rank 0's stdout carries exactly one JSON line: NCCL's own log lines
-    # (its version banner included, when a launcher enables NCCL_DEBUG) go to
-    # a per-process file unless the caller chose a destination.
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/dee_b200_nccl.%h.%p.log")
+    # Standard output carries exactly one JSON line.  Libraries write to file
+    # descriptor 1 on their own (NCCL prints its version banner there when a
+    # launcher enables NCCL_DEBUG), so descriptor 1 is pointed at standard
+    # error and the result line goes to a duplicate of the original.
+    _RESULT_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     if args.impl == "reference":
         run_reference(args)
         return
@@ -845,7 +858,7 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
-        print(json.dumps(result))
+        emit(result)
 
 
 if __name__ == "__main__":
