@@ -783,7 +783,8 @@ def main():
                    "tokens_per_step": b, "experts_resident": E, "weights": "fp4-e2m1+ue8m0/32",
                    "parallelism": (f"ep{world}-{transport}" if world > 1 else "single"),
                    "l2": "flushed (256 MiB write) before every timed step",
-                   "unique_experts_per_step": statistics.mean(uniq)},
+                   "unique_experts_per_step": statistics.mean(uniq),
+                   "unique_experts_steps": uniq[:32]},
         "hbm_gbs_layer": layer_gbs,
         "hbm_frac_layer": layer_gbs / hbm_peak,
         "stage_ms": stages,

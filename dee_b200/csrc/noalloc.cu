@@ -23,7 +23,15 @@
 //     race on the array and must be serialised by the caller.
 //   * The first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (once per device, with that device current).  Make
-//     that first call before any stream capture begins.
+//     that first call before any stream capture begins.  The address is kept
+//     for the life of the process, so a process that calls cudaDeviceReset
+//     must not call this entry point again afterwards (the reset unloads the
+//     module that holds the array).
+//   * Every argument is checked on the host before any CUDA call: the token
+//     rows and the output are read and written with 16-byte vector accesses
+//     and must be 16-byte aligned (a column slice of a wider tensor is not),
+//     ids, weights and the status word 4-byte aligned.  A request that fails
+//     a check returns an error without launching anything.
 #include "dee_b200.h"
 #include "kernels.h"
 
@@ -144,6 +152,13 @@ extern "C" DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void
     if (record_bytes < need_record || record_bytes % 16 != 0 ||
         (reinterpret_cast<uintptr_t>(d_records) & 15) != 0)
         return report(DEE_ERR_INVALID, "record_bytes too small or records not 16-byte aligned");
+    // gather_rows_kernel copies token rows and combine_f32_kernel writes the
+    // output with 16-byte vectors; ids, weights and the status are 4-byte words.
+    if (((reinterpret_cast<uintptr_t>(d_x_f16) | reinterpret_cast<uintptr_t>(d_out_f32)) & 15) != 0)
+        return report(DEE_ERR_INVALID, "token rows and output must be 16-byte aligned");
+    if (((reinterpret_cast<uintptr_t>(d_ids) | reinterpret_cast<uintptr_t>(d_weights) |
+          reinterpret_cast<uintptr_t>(d_status_out)) & 3) != 0)
+        return report(DEE_ERR_INVALID, "ids, weights and status must be 4-byte aligned");
     const size_t sel = static_cast<size_t>(tokens) * K;
     const ScratchPlan sp = plan(H, I, E, sel);
     if (sp.total > kNoAllocScratchBytes) {

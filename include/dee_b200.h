@@ -360,7 +360,11 @@ DEE_API int dee_act_quant_device(const void* d_x_f16, int rows, int cols, int bl
  * kernels' status word (0 = ok).  All calls share the static array: calls
  * that overlap on the GPU race, so serialise them.  The first call on a
  * device resolves the array's device address; make it before any stream
- * capture. */
+ * capture.  That address is kept for the life of the process: do not call
+ * this entry point after cudaDeviceReset.  d_x_f16 and d_out_f32 must be
+ * 16-byte aligned, d_ids, d_weights and d_status_out 4-byte aligned; every
+ * argument is checked before any CUDA call (DEE_ERR_INVALID, nothing
+ * launched). */
 DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void* d_records,
                                     size_t record_bytes, int n_slots, const void* d_x_f16,
                                     int tokens, const int32_t* d_ids, const float* d_weights,

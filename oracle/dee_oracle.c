@@ -167,6 +167,36 @@ void dee_ref_fp4_dequant_f32(const uint8_t* packed, const uint8_t* scale,
     }
 }
 
+/* dequantize_expert_weight (dee.cpp/scripts/deepseek_v4_expert_reference.py
+ * :85-99, decode_e8m0 :49-62): value * 2^(b - 127) in FP32 with no clamp,
+ * so byte 0 is the subnormal 2^-127 and byte 255 overflows to infinity. */
+static const float kE2m1Signed[16] = {  /* FP4_VALUES of the Python reference: code 8 is -0.0 */
+    0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+    -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f,
+};
+
+static float scale_e8m0_exact(uint8_t b) {
+    const uint32_t bits = b == 255 ? 0x7F800000u : b == 0 ? 0x00400000u : (uint32_t)b << 23;
+    float f; memcpy(&f, &bits, 4); return f;
+}
+
+void dee_ref_fp4_dequant_e8m0_f32(const uint8_t* packed, const uint8_t* scale,
+                                  size_t out, size_t in, float* dst) {
+    const size_t half_in = in >> 1, sstride = in >> 5;
+    for (size_t o = 0; o < out; ++o) {
+        const uint8_t* p = packed + o * half_in;
+        float* d = dst + o * in;
+        for (size_t blk = 0; blk < sstride; ++blk) {
+            const float s = scale_e8m0_exact(scale[o * sstride + blk]);
+            for (size_t j = 0; j < 16; ++j) {
+                const uint8_t byte = p[blk * 16 + j];
+                d[blk * 32 + 2 * j] = kE2m1Signed[byte & 0x0F] * s;
+                d[blk * 32 + 2 * j + 1] = kE2m1Signed[byte >> 4] * s;
+            }
+        }
+    }
+}
+
 /* ------------------------------------------------------------------ */
 /* Router: softmax top-k with renormalisation                          */
 /* ------------------------------------------------------------------ */

@@ -29,6 +29,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import threading
 from dataclasses import dataclass
 
 import numpy as np
@@ -66,6 +67,7 @@ def lib() -> ctypes.CDLL:
         L.dee_ref_scale_host.argtypes = [ctypes.c_uint8]
         L.dee_ref_fp4_decode_f16.argtypes = [P, P, P, ctypes.c_size_t, ctypes.c_size_t]
         L.dee_ref_fp4_dequant_f32.argtypes = [P, P, ctypes.c_size_t, ctypes.c_size_t, P]
+        L.dee_ref_fp4_dequant_e8m0_f32.argtypes = [P, P, ctypes.c_size_t, ctypes.c_size_t, P]
         L.dee_ref_route_topk.restype = ctypes.c_int
         L.dee_ref_route_topk.argtypes = [P, ctypes.c_int, ctypes.c_int, ctypes.c_int, P, P]
         L.dee_ref_group.restype = ctypes.c_int
@@ -310,11 +312,18 @@ def mxfp8_layer_raw(records: np.ndarray, layout: Layout, x_f16: np.ndarray, ids:
     xq, xs = act_quant(x_f16, act_block)
     xd = act_dequant_f32(xq, xs, act_block).astype(np.float64)
     raw = np.zeros((T, K, H), dtype=np.float32)
-    for e in np.unique(ids):
+
+    def w64(rec, name, slot):
+        w = rec[name + ".weight"]
+        f32 = dequant_fp4_f32(w, rec[name + ".scale"], _scratch("f32" + slot, (w.shape[0], w.shape[1] * 2),
+                                                                  np.float32))
+        f64 = _scratch("f64" + slot, f32.shape, np.float64)
+        np.copyto(f64, f32)
+        return f64
+
+    def one(e):
         rec = split_record(layout, records[e])
-        w1 = dequant_fp4_f32(rec["w1.weight"], rec["w1.scale"]).astype(np.float64)
-        w3 = dequant_fp4_f32(rec["w3.weight"], rec["w3.scale"]).astype(np.float64)
-        w2 = dequant_fp4_f32(rec["w2.weight"], rec["w2.scale"]).astype(np.float64)
+        w1, w3, w2 = w64(rec, "w1", "a"), w64(rec, "w3", "b"), w64(rec, "w2", "c")
         t, k = np.nonzero(ids == e)
         g = (xd[t] @ w1.T).astype(np.float32).astype(np.float16).astype(np.float32)
         u = (xd[t] @ w3.T).astype(np.float32).astype(np.float16).astype(np.float32)
@@ -326,6 +335,8 @@ def mxfp8_layer_raw(records: np.ndarray, layout: Layout, x_f16: np.ndarray, ids:
         aq, as_ = act_quant(act.view(np.uint16), act_block)
         ad = act_dequant_f32(aq, as_, act_block).astype(np.float64)
         raw[t, k] = (ad @ w2.T).astype(np.float32)
+
+    _per_expert(np.unique(ids), one)
     return raw
 
 
@@ -426,14 +437,47 @@ def act_dequant_f32(q: np.ndarray, scales: np.ndarray, block: int) -> np.ndarray
     return e4m3_table()[q] * np.repeat(e8m0_f32(scales), block, axis=1)
 
 
-def dequant_fp4_f32(packed: np.ndarray, scale: np.ndarray) -> np.ndarray:
+_TLS = threading.local()
+
+
+def _scratch(name: str, shape: tuple, dtype) -> np.ndarray:
+    """A per-thread buffer reused across calls (large fresh allocations cost a
+    page fault per 4 KB; the per-expert oracles reuse theirs)."""
+    buf = getattr(_TLS, name, None)
+    if buf is None or buf.shape != shape or buf.dtype != np.dtype(dtype):
+        buf = np.empty(shape, dtype=dtype)
+        setattr(_TLS, name, buf)
+    return buf
+
+
+def dequant_fp4_f32(packed: np.ndarray, scale: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
     """Packed E2M1 [out, in/2] (low nibble first) x UE8M0 per 32 -> FP32 [out, in]
-    (dequantize_expert_weight, deepseek_v4_expert_reference.py:85-99)."""
-    p = np.asarray(packed, dtype=np.uint8)
-    vals = np.empty((p.shape[0], p.shape[1] * 2), dtype=np.float32)
-    vals[:, 0::2] = _FP4_VALUES[p & 0x0F]
-    vals[:, 1::2] = _FP4_VALUES[p >> 4]
-    return vals * np.repeat(e8m0_f32(scale), 32, axis=1)
+    (dequantize_expert_weight, deepseek_v4_expert_reference.py:85-99): each
+    value times 2^(b - 127) in FP32, byte 255 giving infinity.  Computed by
+    dee_ref_fp4_dequant_e8m0_f32 (C), into `out` when given."""
+    p = np.ascontiguousarray(packed, dtype=np.uint8)
+    s = np.ascontiguousarray(scale, dtype=np.uint8)
+    rows, half = p.shape
+    if out is None:
+        out = np.empty((rows, half * 2), dtype=np.float32)
+    assert out.shape == (rows, half * 2) and out.dtype == np.float32 and out.flags.c_contiguous
+    lib().dee_ref_fp4_dequant_e8m0_f32(_p(p), _p(s), rows, half * 2, _p(out))
+    return out
+
+
+def _per_expert(experts, fn, threads: int = 0) -> None:
+    """Run fn(e) for every expert on a thread pool (numpy releases the GIL in
+    its array work); fn writes disjoint outputs."""
+    from concurrent.futures import ThreadPoolExecutor
+    experts = list(experts)
+    n = threads if threads > 0 else min(len(experts), os.cpu_count() or 1, 16)
+    if n <= 1:
+        for e in experts:
+            fn(e)
+        return
+    with ThreadPoolExecutor(max_workers=n) as pool:
+        for f in [pool.submit(fn, e) for e in experts]:
+            f.result()
 
 
 def dequant_fp8_f32(w: np.ndarray, scale: np.ndarray) -> np.ndarray:
@@ -466,19 +510,23 @@ def official_layer(records: np.ndarray, layout: Layout, x: np.ndarray, ids: np.n
     s3, w2, s2: F8_E4M3 bytes and E8M0 scales).  Returns (moe, shared_out)."""
     x = np.asarray(x, dtype=np.float32)
     T, K = ids.shape
-    moe = np.zeros((T, x.shape[1]), dtype=np.float32)
-    cache = {}
-    for t in range(T):
-        for r in range(K):
-            e = int(ids[t, r])
-            if e not in cache:
-                parts = split_record(layout, records[e])
-                cache[e] = (dequant_fp4_f32(parts["w1.weight"], parts["w1.scale"]),
-                            dequant_fp4_f32(parts["w3.weight"], parts["w3.scale"]),
-                            dequant_fp4_f32(parts["w2.weight"], parts["w2.scale"]))
-            w1, w3, w2 = cache[e]
+    # each selection's FP32 output, then summed in rank order per token
+    routed = np.zeros((T, K, x.shape[1]), dtype=np.float32)
+
+    def one(e):
+        parts = split_record(layout, records[e])
+        w1, w3, w2 = (dequant_fp4_f32(parts[n + ".weight"], parts[n + ".scale"],
+                                      _scratch("f32" + n, (parts[n + ".weight"].shape[0],
+                                                           parts[n + ".weight"].shape[1] * 2), np.float32))
+                      for n in ("w1", "w3", "w2"))
+        for t, r in zip(*np.nonzero(ids == e)):
             h = _swiglu_f32(x[t:t + 1], w1, w3, swiglu_limit) * np.float32(weights[t, r])
-            moe[t] += (h @ w2.T)[0]
+            routed[t, r] = (h @ w2.T)[0]
+
+    _per_expert(np.unique(ids), one)
+    moe = np.zeros((T, x.shape[1]), dtype=np.float32)
+    for r in range(K):
+        moe += routed[:, r]
     sh = np.zeros_like(moe)
     if shared is not None:
         w1 = dequant_fp8_f32(shared["w1"], shared["s1"])
