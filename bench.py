@@ -85,6 +85,27 @@ def dist_env():
     return rank, world, local
 
 
+def profiled_traffic(profile: str, key: str):
+    """DRAM bytes (read + write) per launch of a kernel and the algorithmic
+    bytes of the same launch, from a committed ncu summary under profiles/
+    (lines `traffic_bytes_per_launch_<key>: N` and
+    `traffic_algorithmic_bytes_<key>: N`).  None when the summary is absent."""
+    path = os.path.join(ROOT, "profiles", profile)
+    vals = {}
+    try:
+        with open(path) as f:
+            for ln in f:
+                for name in ("traffic_bytes_per_launch_", "traffic_algorithmic_bytes_"):
+                    if ln.startswith(name + key + ":"):
+                        vals[name] = int(ln.split(":", 1)[1])
+    except OSError:
+        return None
+    if len(vals) != 2:
+        return None
+    t, a = vals["traffic_bytes_per_launch_"], vals["traffic_algorithmic_bytes_"]
+    return {"traffic": t, "traffic_ratio": t / a, "traffic_source": f"profiles/{profile}"}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -795,6 +816,11 @@ def main():
         "gpu_launches": int(round(per_step_launches * args.steps)),
         "gpu_launches_per_step": per_step_launches,
     }
+    if world == 1 and b == 8 and E == 256:
+        # ncu capture of this workload's gate/up launch (cold cache)
+        tr = profiled_traffic("traffic_decode_b8.md", "gate_up")
+        if tr:
+            result["roofline"].update(tr)
     result["clocks"] = clk.summary()
 
     # ---- e2e through the C ABI with host buffers ----
