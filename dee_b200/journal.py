@@ -23,7 +23,7 @@ class RouteJournal:
 
     def __init__(self, path, *, run_id: str, n_layers: int, topk: int, fsync: bool = True) -> None:
         if n_layers <= 0 or topk <= 0:
-            raise ValueError("route journal n_layers/topk must be positive")
+            raise ValueError(f"a journal needs at least one layer and one selection per token (got {n_layers} layers, top-{topk})")
         self.path = Path(path)
         self.run_id = str(run_id)
         self.n_layers = int(n_layers)
@@ -42,21 +42,21 @@ class RouteJournal:
 
     def append_layer(self, *, step: int, start_pos: int, layer: int, device: str, expert_ids) -> dict:
         if self._closed:
-            raise RuntimeError("route journal is closed")
+            raise RuntimeError(f"{self.path} was already closed; open a new journal to record more layers")
         if int(step) != self.completed_forwards or int(layer) != self.record_count % self.n_layers:
             raise RuntimeError(
-                f"non-canonical route journal order: got step={step} layer={layer}, expected "
-                f"step={self.completed_forwards} layer={self.record_count % self.n_layers}")
+                f"layers must be recorded forward by forward, layer by layer: next expected is forward "
+                f"{self.completed_forwards} layer {self.record_count % self.n_layers}, got forward {step} layer {layer}")
         raw = expert_ids.tolist() if hasattr(expert_ids, "tolist") else expert_ids
         if not isinstance(raw, (list, tuple)) or not raw:
-            raise ValueError("route journal expert_ids must be a non-empty matrix")
+            raise ValueError("expert ids must be given as a non-empty [tokens, topk] matrix")
         rows = []
         for i, r in enumerate(raw):
             row = [int(v) for v in r]
             if len(row) != self.topk:
-                raise ValueError(f"route journal row {i} topk={len(row)}; expected {self.topk}")
+                raise ValueError(f"token {i} carries {len(row)} expert ids, this journal records top-{self.topk}")
             if any(v < 0 for v in row):
-                raise ValueError(f"route journal row {i} has negative expert id")
+                raise ValueError(f"token {i} carries a negative expert id")
             rows.append(row)
         payload = {
             "schema_version": self.SCHEMA_VERSION,

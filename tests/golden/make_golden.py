@@ -46,7 +46,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF = Path(os.environ.get("DEE_REFERENCE_ROOT", "/root/reference")) / "dee.cpp"
+REF = Path(os.environ.get("DEE_REFERENCE_ROOT", Path(__file__).resolve().parents[3] / "reference")) / "dee.cpp"
 sys.path.insert(0, str(REF))
 sys.path.insert(0, str(REF / "kaggle" / "deepseek-v4-flash-0731"))
 sys.path.insert(0, str(REPO))
