@@ -103,6 +103,13 @@ class Engine:
     def launch_count(self) -> int:
         return int(self._lib.dee_engine_launch_count(self._h))
 
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of this engine's waits on other ranks' flags (100 us .. 2 s):
+        a rank that never arrives is reported by sync_status (bit 6) instead
+        of stalling the stream."""
+        self._check(self._lib.dee_engine_set_wait_limit_ns(self._h, int(seconds * 1e9)),
+                    "dee_engine_set_wait_limit_ns")
+
     def set_profiling(self, enable: bool) -> None:
         self._check(self._lib.dee_engine_set_profiling(self._h, int(bool(enable))),
                     "dee_engine_set_profiling")

@@ -169,6 +169,8 @@ struct Offload {
 struct dee_engine {
     dee_config cfg{};
     dee::EpP2P ep;
+    // limit of the waits on other ranks' flags (dee_engine_set_wait_limit_ns)
+    uint64_t wait_limit_ns = dee::sm100::kWaitLimitNs;
     dee::Offload off;
     std::string last_error;
     int num_sms = 148;
@@ -192,6 +194,7 @@ struct dee_engine {
     float* d_raw = nullptr;
     int32_t* h_ids = nullptr;      // pinned staging of host-given ids
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
+    int32_t* d_comb_cnt = nullptr;     // fused decode combine: [kDecodeMaxSelections, H / 128] counters
     int32_t* d_perm_chunks = nullptr;  // multi-CTA permutation: per-chunk expert counts
     int32_t* d_perm_lrank = nullptr;   // multi-CTA permutation: rank within the chunk
     // shared-expert workspaces, capacity in tokens
@@ -219,6 +222,8 @@ struct dee_engine {
 
 namespace dee {
 namespace {
+
+constexpr uint64_t kMinWaitLimitNs = 100000;  // 100 us
 
 int fail(dee_engine* e, int code, const std::string& msg) {
     if (e) e->last_error = msg;
@@ -266,8 +271,8 @@ void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
     cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
-    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank);
-    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr;
+    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank); cudaFree(e->d_comb_cnt);
+    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr; e->d_comb_cnt = nullptr;
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
@@ -302,6 +307,7 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_chunks, ((cap + 1023) / 1024) * static_cast<size_t>(E))) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_lrank, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_comb_cnt, static_cast<size_t>(kDecodeMaxSelections) * (H / 128))) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
                              cudaHostAllocDefault)) != cudaSuccess) {
         free_workspace(e);
@@ -352,9 +358,15 @@ struct EpReturn {
     int capacity, rank;
 };
 
+// fuse_out / fuse_w (may be null): the caller wants the rank-order FP32
+// combine of the raw rows into fuse_out; for decode-sized one-GPU calls the
+// down GEMM's epilogue does it and *fused is set, otherwise the caller
+// launches the combine.
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
-                const EpReturn* ret = nullptr, const float* official_route_w = nullptr) {
+                const EpReturn* ret = nullptr, const float* official_route_w = nullptr,
+                const float* fuse_w = nullptr, float* fuse_out = nullptr, bool* fused = nullptr) {
+    if (fused) *fused = false;
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -373,6 +385,12 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     po.chunk_counts = e->d_perm_chunks;
     po.lrank = e->d_perm_lrank;
     po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
+    const bool fuse = decode && fuse_out && fuse_w && !ret && !official_route_w && H % 128 == 0 &&
+                      (reinterpret_cast<uintptr_t>(fuse_out) & 15) == 0;
+    if (fuse) {  // the permutation (one CTA at this size) clears the combine counters
+        po.zero = e->d_comb_cnt;
+        po.zero_n = tokens * (H / 128);
+    }
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream, skip_negative);
@@ -436,6 +454,12 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     }
     a.k_total = I;
     a.m_tiles = H / 128;
+    if (fuse) {
+        a.combine_out = fuse_out;
+        a.combine_w = fuse_w;
+        a.combine_cnt = e->d_comb_cnt;
+        if (fused) *fused = true;
+    }
     stage_begin(e, kStageDown, stream);
     err = decode ? launch_moe_decode(false, gm, a, e->num_sms, stream)
                  : launch_moe_gemm(false, gm, a, e->num_sms, stream);
@@ -781,10 +805,12 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     }
     e->h_ids_count = sel;
     float* raw = d_raw ? d_raw : e->d_raw;
+    bool fused = false;
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, ids32, raw,
-                          stream, topk, false, true)) != DEE_OK)
+                          stream, topk, false, true, nullptr, nullptr, d_out_f32 ? d_weights : nullptr,
+                          d_out_f32, &fused)) != DEE_OK)
         return rc;
-    if (d_out_f32) {
+    if (d_out_f32 && !fused) {
         stage_begin(e, kStageCombine, stream);
         err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
@@ -1113,7 +1139,7 @@ int dee_ep_p2p_experts_device(dee_engine* e, int layer, void* stream_v) {
     if (!p.connected || p.epoch == 0)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_experts before any dispatch");
     cudaError_t err = launch_ep_wait(p.peers.recv_flag[p.rank], p.ranks, p.epoch, e->d_status,
-                                     sm100::kStatusTimeoutFlag, stream);
+                                     sm100::kStatusTimeoutFlag, e->wait_limit_ns, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep wait launch");
     const EpReturn ret{p.d_back_peers, p.capacity, p.rank};
     if ((rc = run_experts(e, layer, p.peers.recv_rows[p.rank], p.ranks * p.capacity,
@@ -1133,7 +1159,7 @@ int dee_ep_p2p_combine_device(dee_engine* e, const float* d_weights, float* d_ou
     if (!p.connected || p.epoch == 0 || !d_weights || !d_out_f32)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_combine needs a dispatched layer, weights and out");
     cudaError_t err = launch_ep_wait(p.peers.back_flag[p.rank], p.ranks, p.epoch, e->d_status,
-                                     sm100::kStatusTimeoutFlag, stream);
+                                     sm100::kStatusTimeoutFlag, e->wait_limit_ns, stream);
     if (err == cudaSuccess)
         err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
                                 e->cfg.topk, e->cfg.hidden, d_out_f32, stream);
@@ -1352,6 +1378,23 @@ int dee_records_scramble_device(const void* d_src, void* d_dst, int records, siz
     return err == cudaSuccess ? DEE_OK : DEE_ERR_CUDA;
 }
 
+int dee_engine_set_wait_limit_ns(dee_engine* e, uint64_t limit_ns) {
+    if (!e) return DEE_ERR_INVALID;
+    if (limit_ns < kMinWaitLimitNs || limit_ns > sm100::kWaitLimitNs)
+        return fail(e, DEE_ERR_INVALID, "wait limit must lie in [100 us, 2 s]");
+    e->wait_limit_ns = limit_ns;
+    return DEE_OK;
+}
+
+int dee_wait_selftest(uint64_t limit_ns, uint32_t* d_status, void* stream) {
+    if (!d_status || (reinterpret_cast<uintptr_t>(d_status) & 3) != 0 || limit_ns < kMinWaitLimitNs ||
+        limit_ns > sm100::kWaitLimitNs)
+        return DEE_ERR_INVALID;
+    const cudaError_t err =
+        launch_wait_selftest(limit_ns, d_status, sm100::kStatusTimeoutTma, static_cast<cudaStream_t>(stream));
+    return err == cudaSuccess ? DEE_OK : DEE_ERR_CUDA;
+}
+
 int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
     int rc = check_engine(e);
     if (rc != DEE_OK) return rc;
@@ -1367,7 +1410,8 @@ int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
         char buf[160];
         std::snprintf(buf, sizeof(buf),
                       "device status 0x%08x (bit0-3: pipeline wait timeout, bit4: expert id out "
-                      "of range or not resident, bit5: tile overflow, bit7: router failure)",
+                      "of range or not resident, bit5: tile overflow, bit6: a peer rank's flag "
+                      "did not arrive in time, bit7: router failure)",
                       st);
         e->last_error = buf;
         return DEE_ERR_DEVICE;

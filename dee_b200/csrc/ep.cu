@@ -187,7 +187,7 @@ __global__ void ep_signal_kernel(EpPeers peers, bool back, int ranks, int rank, 
 // array; on timeout set `code` in the status word and return, so the context
 // stays usable and the host sees the failure.
 __global__ void ep_wait_kernel(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                               uint32_t code) {
+                               uint32_t code, uint64_t limit_ns) {
     sm100::pdl_wait();
     sm100::pdl_trigger();
     const int s = threadIdx.x;
@@ -197,7 +197,7 @@ __global__ void ep_wait_kernel(const uint32_t* flags, int ranks, uint32_t epoch,
         uint32_t v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
         if (static_cast<int32_t>(v - epoch) >= 0) break;
-        if (sm100::global_ns() - t0 > sm100::kWaitLimitNs) {
+        if (sm100::global_ns() - t0 > limit_ns) {
             atomicOr(status, code);
             break;
         }
@@ -254,9 +254,28 @@ cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int ran
 }
 
 cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                           uint32_t code, cudaStream_t stream) {
+                           uint32_t code, uint64_t limit_ns, cudaStream_t stream) {
     if (ranks <= 0 || ranks > kEpMaxRanks) return cudaErrorInvalidValue;
-    return launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, stream, flags, ranks, epoch, status, code);
+    return launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, stream, flags, ranks, epoch, status, code, limit_ns);
+}
+
+namespace {
+// One thread waits on an mbarrier that nothing arrives on: the bounded wait
+// every pipeline kernel uses must give up after limit_ns and report `code`.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, uint32_t* status, uint32_t code) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        sm100::mbar_init(&bar, 1);
+        sm100::fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) sm100::mbar_wait_for(&bar, 0, status, code, limit_ns);
+}
+}  // namespace
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* status, uint32_t code, cudaStream_t stream) {
+    wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, status, code);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,

@@ -47,6 +47,9 @@ cudaError_t ensure_smem_attr(int bytes) {
 struct GemmMaps {
     CUtensorMap w0, w1, s0, s1, b;
     CUtensorMap bt[4];  // tcgen05 kernel: token boxes of 16/32/64/128 rows x 128 K
+    // decode kernel: s0 / s1 are swizzled scale-row maps (else its scale rows
+    // come in by bulk copies)
+    int scale_swz = 0;
 };
 
 // The MXFP8-activation grouped GEMM (moe_mxfp8.cu): weights E2M1 unpacked by
@@ -149,9 +152,12 @@ cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tok
 // return (back = true) flags, after the stream's earlier kernels.
 cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int rank, uint32_t epoch,
                              cudaStream_t stream);
-// Bounded wait until all `ranks` flags reached `epoch` (timeout: `code` in status).
+// Bounded wait until all `ranks` flags reached `epoch` (after limit_ns: `code`
+// in status).
 cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                           uint32_t code, cudaStream_t stream);
+                           uint32_t code, uint64_t limit_ns, cudaStream_t stream);
+// A wait on an mbarrier nothing arrives on, bounded by limit_ns (sets `code`).
+cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* status, uint32_t code, cudaStream_t stream);
 
 // The synthetic stack's dense glue (stack.cu), every per-token result in a
 // fixed order independent of the batch.
@@ -202,6 +208,10 @@ struct PermuteOut {
     int32_t* chunk_counts = nullptr;  // [max_chunks * E]
     int32_t* lrank = nullptr;         // [T*K]
     long long max_chunks = 0;
+    // Zeroed by the (one-CTA) permutation before it groups: the fused
+    // combine's counters of the forward that follows.
+    int32_t* zero = nullptr;
+    int zero_n = 0;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.

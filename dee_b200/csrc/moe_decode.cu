@@ -161,6 +161,58 @@ __device__ __forceinline__ DecItem finish_item(const GemmArgs& a, int item, cons
     return d;
 }
 
+// The live combine out[t] = sum_r w[t, r] * raw[t, r] (rank order, each
+// multiply and add rounded to FP32; deepseek_v4_layer_candidate.py:616-629)
+// fused into the down GEMM.  A 128-feature block of token t is complete once
+// all K of its selections have passed through the eight pair-leader warps
+// that write it; every such warp counts itself on the block's counter after
+// its stores (fenced), and the warp whose count completes the block sums the
+// K raw rows in rank order -- the same arithmetic as combine_f32_kernel, so
+// the result does not depend on which warp finishes.  No warp waits on
+// another: a warp that has left on a timeout only leaves blocks incomplete.
+struct CombineArgs {
+    const int* perm;
+    const float* raw;
+    const float* w;
+    float* out;
+    int* cnt;
+    int topk, hidden;
+};
+
+__device__ __noinline__ void combine_block(const CombineArgs a, int row_start, int n_rows, int m, int lane) {
+    const int K = a.topk;
+    const int blocks = a.hidden / 128;
+    const int target = 8 * K;  // 8 leader warps x K selections
+    __threadfence();           // this warp's raw stores before its count
+    __syncwarp();
+    int t = -1;
+    bool last = false;
+    if (lane < n_rows) {
+        t = a.perm[row_start + lane] / K;
+        last = atomicAdd(&a.cnt[t * blocks + m], 1) == target - 1;
+    }
+    unsigned done = __ballot_sync(0xffffffffu, last);
+    if (!done) return;
+    __threadfence();  // every other warp's raw stores before the reads below
+    while (done) {
+        const int src = __ffs(done) - 1;
+        done &= done - 1;
+        const int tok = __shfl_sync(0xffffffffu, t, src);
+        const size_t f = static_cast<size_t>(m) * 128 + 4 * lane;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < K; ++r) {
+            const size_t s = static_cast<size_t>(tok) * K + r;
+            const float w = a.w[s];
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.raw + s * a.hidden + f));
+            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
+            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
+            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
+            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
+        }
+        *reinterpret_cast<float4*>(a.out + static_cast<size_t>(tok) * a.hidden + f) = acc;
+    }
+}
+
 // What the consumers need of an item, handed over in shared memory with the
 // item's scale rows.
 struct ItemRec {
@@ -170,7 +222,8 @@ struct ItemRec {
 template <GemmMode MODE, bool kOfficial>
 __global__ void __launch_bounds__(kDecThreads, 1)
     moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
-                      const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_s0,
+                      const __grid_constant__ CUtensorMap map_s1, const GemmArgs args) {
     constexpr bool kGU = MODE == GemmMode::kGateUp;
     // The tile list comes from the permutation kernel, which has completed
     // whenever this kernel runs: its predecessor (gather or gate/up) only
@@ -213,6 +266,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         prefetch_tmap(&map_w0);
         prefetch_tmap(&map_b);
         if (kGU) prefetch_tmap(&map_w1);
+        if (args.scale_swz) {
+            prefetch_tmap(&map_s0);
+            if (kGU) prefetch_tmap(&map_s1);
+        }
     }
     __syncthreads();
     if (warp != 0) pdl_wait();
@@ -230,9 +287,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         const uint64_t pol_b = policy_evict_last();
         const size_t ih = static_cast<size_t>(args.hidden) * args.inter;
         const size_t off_s1 = ih + ih / 2, off_s3 = off_s1 + ih / 32, off_s2 = off_s3 + ih / 32;
-        // Scale rows of one item are contiguous in the record: one bulk copy
-        // per projection into the item's slot, after the item's record for
-        // the consumers.
+        // Scale rows of one item are contiguous in the record: one copy per
+        // projection into the item's slot, after the item's record for the
+        // consumers.  With scale maps (rows of 32, 64 or 128 bytes) the copy
+        // is a tensor load whose swizzle span is the row length, so the
+        // 16-byte chunk j of row r lands at chunk j ^ f(r) and the
+        // consumers' per-stage reads of eight rows hit distinct banks;
+        // otherwise a plain bulk copy.
         auto issue_scales = [&](const DecItem& d, int li) -> bool {
             const int slot = li % kDecScSlots;
             if (!mbar_wait(&sempty[slot], ((li / kDecScSlots) & 1) ^ 1, status, kStatusTimeoutTma))
@@ -244,7 +305,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             mbar_arrive_expect_tx(&sfull[slot], sc_item);
             uint8_t* dst = smem + L.sc_off + slot * L.sc_slot;
             const uint8_t* rec = args.records + static_cast<size_t>(d.slot) * args.record_bytes;
-            if (kGU) {
+            if (args.scale_swz) {
+                if (kGU) {
+                    tma_load_3d(dst, &map_s0, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
+                    tma_load_3d(dst + 64 * rb, &map_s1, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
+                } else {
+                    tma_load_3d(dst, &map_s0, &sfull[slot], 0, d.m * 128, d.slot, pol_w);
+                }
+            } else if (kGU) {
                 const size_t r0 = static_cast<size_t>(d.m) * 64 * rb;
                 bulk_load(dst, rec + off_s1 + r0, 64 * rb, &sfull[slot]);
                 bulk_load(dst + 64 * rb, rec + off_s3 + r0, 64 * rb, &sfull[slot]);
@@ -369,9 +437,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const uint32_t w_off = kh * kHalf + row_lo * 128 + (g << 4) + q * 4;
     const uint32_t b_off0 = kDecPkBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
     const uint32_t b_off1 = kDecPkBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
-    // this thread's scale bytes of stage s: row_lo * rb + s * 16 + kh * 8 in the slot
+    // this thread's scale bytes of stage s: row_lo * rb + s * 16 + kh * 8 in
+    // the slot, the 16-byte chunk s moved to s ^ sw when the rows came in
+    // swizzled (sw from the row's address bits 7 and up, as the tensor copy
+    // placed them; the hi row, 64 or 8 rows on, has the same sw)
     const uint32_t s_off = L.sc_off + row_lo * rb + kh * 8;
     const uint32_t s_hi = kHiRows * rb;
+    const uint32_t s_sw = args.scale_swz ? ((row_lo * rb) >> 7) & (rb / 16 - 1) : 0u;
     float* red = reinterpret_cast<float*>(smem + L.red_off);
     int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
     int st = 0, parity = 0, li = 0;
@@ -393,8 +465,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
             if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
             const uint32_t sb = smem_base + st * kDecStageBytes;
-            const uint2 slo = lds_v2(sc_base + s * 16);
-            const uint2 shi = lds_v2(sc_base + s * 16 + s_hi);
+            const uint32_t s_chunk = (static_cast<uint32_t>(s) ^ s_sw) << 4;
+            const uint2 slo = lds_v2(sc_base + s_chunk);
+            const uint2 shi = lds_v2(sc_base + s_chunk + s_hi);
             const uint32_t wb = sb + w_off;
             const uint32_t bb0 = sb + b_off0, bb1 = sb + b_off1;
             if (fast) {
@@ -502,6 +575,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 dst[f_lo] = c[h];
                 dst[f_lo + 8] = c[2 + h];
             }
+            if (args.combine_out)
+                combine_block(CombineArgs{args.perm, args.raw, args.combine_w, args.combine_out, args.combine_cnt,
+                                          args.topk, args.hidden},
+                              it_row_start, n_rows, it_m, lane);
         }
     }
 }
@@ -513,8 +590,10 @@ cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cud
     if (e != cudaSuccess) return e;
     const DecLayout L = dec_layout(args.k_total);
     if (L.stages < 2 || L.bytes > kSmemLimit) return cudaErrorInvalidValue;
-    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps.w0, maps.w1, maps.b,
-                      args);
+    GemmArgs a = args;
+    a.scale_swz = maps.scale_swz;
+    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps.w0, maps.w1, maps.b, maps.s0,
+                      maps.s1, a);
 }
 
 }  // namespace
@@ -545,6 +624,30 @@ bool encode_decode_weight_maps(EncodeTiledFn fn, const void* records, size_t rec
         !enc(&dn->w0, rec + ih, hidden, inter, 128))
         return false;
     dn->w1 = dn->w0;
+    // Scale rows [rows, K/32 bytes] of every record as {K/32, rows, slot},
+    // boxes of a work item's 64 (gate/up) or 128 (down) rows, swizzled with
+    // the span of one row when that is 32, 64 or 128 bytes.
+    auto enc_sc = [&](CUtensorMap* m, const uint8_t* base, int rows, int k, cuuint32_t box_rows) {
+        const cuuint32_t rbytes = static_cast<cuuint32_t>(k / 32);
+        const CUtensorMapSwizzle swz = rbytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : rbytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                      : CU_TENSOR_MAP_SWIZZLE_32B;
+        const cuuint64_t dims[3] = {rbytes, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(n_slots)};
+        const cuuint64_t strides[2] = {rbytes, static_cast<cuuint64_t>(record_bytes)};
+        const cuuint32_t box[3] = {rbytes, box_rows, 1};
+        return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<uint8_t*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    auto swizzles = [](int k) { return k / 32 == 32 || k / 32 == 64 || k / 32 == 128; };
+    const size_t off_s1 = ih + ih / 2, off_s3 = off_s1 + ih / 32, off_s2 = off_s3 + ih / 32;
+    if (swizzles(hidden) && record_bytes % 16 == 0 && enc_sc(&gu->s0, rec + off_s1, inter, hidden, 64) &&
+        enc_sc(&gu->s1, rec + off_s3, inter, hidden, 64))
+        gu->scale_swz = 1;
+    if (swizzles(inter) && record_bytes % 16 == 0 && enc_sc(&dn->s0, rec + off_s2, hidden, inter, 128)) {
+        dn->s1 = dn->s0;
+        dn->scale_swz = 1;
+    }
     return true;
 }
 

@@ -103,12 +103,13 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t pari
 // body costs the tensor-core issuer ~50 cycles per wait even when the phase
 // is already complete (measured: 120 vs 84 cycles per M=128, N=128 MMA with
 // one wait per four MMAs), enough to starve the MMA pipe between K steps.
-static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code) {
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code,
+                                                   uint64_t limit_ns) {
     const uint64_t t0 = global_ns();
     for (;;) {
         for (int i = 0; i < 16; ++i)
             if (mbar_try_wait_sleep(bar, parity)) return true;
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit_ns) {
             atomicOr(status, code);
             return false;
         }
@@ -120,7 +121,14 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status,
                                           uint32_t code) {
     if (__builtin_expect(mbar_try_wait(bar, parity), 1)) return true;
-    return mbar_wait_slow(bar, parity, status, code);
+    return mbar_wait_slow(bar, parity, status, code, kWaitLimitNs);
+}
+
+// The same wait with an explicit limit.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint32_t* status, uint32_t code,
+                                              uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, status, code, limit_ns);
 }
 
 // ---------------------------------------------------------------- PDL

@@ -370,6 +370,25 @@ DEE_API int dee_moe_forward_noalloc(const dee_config* cfg, const void* d_records
                                     int tokens, const int32_t* d_ids, const float* d_weights,
                                     float* d_out_f32, uint32_t* d_status_out, void* stream);
 
+/* Failure detection.  Every device wait is bounded: a wait that runs out
+ * sets a bit in the engine's status word, the kernel unwinds, the context
+ * stays usable and dee_engine_sync_status reports DEE_ERR_DEVICE (the
+ * fail-closed convention of Engine::last_error_message, engine.h:434-436).
+ *
+ * Limit of this engine's waits on other ranks' flags (the NVLink expert-
+ * parallel phases), in nanoseconds, 100 us .. 2 s (default 2 s): a rank that
+ * never dispatches or never returns its rows is reported after this long
+ * (status bit 6).  No counterpart in the reference's single-GPU engine. */
+DEE_API int dee_engine_set_wait_limit_ns(dee_engine* engine, uint64_t limit_ns);
+
+/* Self-test of the bounded pipeline wait on the current device: one kernel
+ * waits on an mbarrier that nothing ever arrives on; after limit_ns (100 us
+ * .. 2 s) the wait gives up and ORs bit 0 (a pipeline wait timeout) into
+ * *d_status (device memory, 4-byte aligned).  Queued on `stream`.  No
+ * counterpart in the reference (its host-side equivalent is the prefetcher's
+ * debug_fail_next_submit, include/dee/async_prefetcher.h:232). */
+DEE_API int dee_wait_selftest(uint64_t limit_ns, uint32_t* d_status, void* stream);
+
 /* Kernel launches issued by this engine since creation (for the bench's
  * launch accounting). */
 DEE_API uint64_t dee_engine_launch_count(const dee_engine* engine);

@@ -223,15 +223,18 @@ def _plant_edge_rows(layout, recs, rng, experts, frac=0.25):
     return planted
 
 
-@pytest.mark.parametrize("T", [8, 100])
-def test_moe_raw_edge_scales(torch_cuda, oracle_mod, T):
+@pytest.mark.parametrize("T,H,I", [(8, 512, 512), (100, 512, 512), (48, 1024, 2048), (48, 4096, 2048)])
+def test_moe_raw_edge_scales(torch_cuda, oracle_mod, T, H, I):
     """Scale bytes outside the exact-FP16 range take the FP16-rounded dequant
     path; rows without them take the fast one.  Every output feature is
-    compared at its own magnitude.  T=8 runs the decode kernel, T=100 the
-    tensor-memory grouped GEMM; both projections share the dequant code."""
+    compared at its own magnitude.  T <= 64 runs the decode kernel, T=100 the
+    tensor-memory grouped GEMM; both projections share the dequant code.
+    The decode kernel copies scale rows of 32, 64 or 128 bytes (K = 1024,
+    2048, 4096) with swizzled tensor loads and shorter ones with bulk
+    copies: H, I = 512 / 1024 and 2048 / 4096 and 2048 cover each kind."""
     torch = torch_cuda
     orc = oracle_mod
-    H, I, E, K = 512, 512, 16, 6
+    E, K = 16, 6
     layout = orc.Layout(H, I)
     recs = orc.synthetic_records(layout, E, seed=404, kind="normal")
     rng = np.random.default_rng(405)
@@ -518,3 +521,37 @@ def test_batch_with_fewer_selections_than_configured(torch_cuda, lib, oracle_mod
     assert np.array_equal(journal.reshape(T, K), ids)
     with pytest.raises(RuntimeError, match="does not match EngineConfig.topk"):
         eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
+
+
+@pytest.mark.parametrize("T,dup", [(1, False), (8, True), (64, False)])
+def test_fused_decode_combine_bitexact_over_calls(torch_cuda, oracle_mod, T, dup):
+    """Decode-sized calls (T * K <= 384) combine inside the down GEMM's
+    epilogue: per (token, 128-feature block) a counter, the warp that
+    completes it sums the K rows in rank order.  Three calls in a row on one
+    engine (the counters are cleared by each call's permutation), with
+    repeated expert ids in a token and at the 384-selection boundary: out is
+    bit-identical to the oracle's rank-order combine of the same raw rows."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 1024, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=818, kind="normal")
+    eng = _engine(H, I, E, K, max_tokens=64)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    rng = np.random.default_rng(819 + T)
+    for call in range(3):
+        x16 = orc.f16_bits(rng.standard_normal((T, H)))
+        ids = _rand_ids(rng, T, E, K, allow_dup=dup)
+        w = rng.random((T, K)).astype(np.float32)
+        w /= w.sum(1, keepdims=True)
+        dx = torch.from_numpy(x16.view(np.float16)).cuda()
+        dids = torch.from_numpy(ids).cuda()
+        dw = torch.from_numpy(w).cuda()
+        out = torch.full((T, H), float("nan"), dtype=torch.float32, device="cuda")
+        raw = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+        eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=dw.data_ptr(),
+                               d_out_ptr=out.data_ptr(), d_raw_ptr=raw.data_ptr())
+        assert eng.sync_status() == 0
+        raw_np = raw.cpu().numpy()
+        assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw_np, w)), f"call {call}"
+        assert orc.rel_l2(raw_np, orc.moe_layer_raw(recs, layout, x16, ids)) <= TOL_REL_L2
