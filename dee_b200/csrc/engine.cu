@@ -1407,7 +1407,7 @@ int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
     if (st != 0) {
         cudaMemsetAsync(e->d_status, 0, 4, s);
         cudaStreamSynchronize(s);
-        char buf[160];
+        char buf[320];
         std::snprintf(buf, sizeof(buf),
                       "device status 0x%08x (bit0-3: pipeline wait timeout, bit4: expert id out "
                       "of range or not resident, bit5: tile overflow, bit6: a peer rank's flag "

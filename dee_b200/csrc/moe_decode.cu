@@ -46,7 +46,7 @@ constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 5
 constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
 constexpr int kDecStageBytes = kDecPkBytes + kDecBBytes;
 constexpr int kDecBarBytes = 256;  // stage and scale-slot barriers, per-slot flags and item records
-constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
+constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
 constexpr uint32_t kSmemLimit = 232448;
 constexpr int kDecScSlots = 3;  // per-item scale rows: the consumed item, the next, the one after
 
@@ -166,7 +166,8 @@ __device__ __forceinline__ DecItem finish_item(const GemmArgs& a, int item, cons
 // fused into the down GEMM.  A 128-feature block of token t is complete once
 // all K of its selections have passed through the eight pair-leader warps
 // that write it; every such warp counts itself on the block's counter after
-// its stores (fenced), and the warp whose count completes the block sums the
+// its stores (fenced; the kernel makes the count one item later), and the
+// warp whose count completes the block sums the
 // K raw rows in rank order -- the same arithmetic as combine_f32_kernel, so
 // the result does not depend on which warp finishes.  No warp waits on
 // another: a warp that has left on a timeout only leaves blocks incomplete.
@@ -448,6 +449,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
     int st = 0, parity = 0, li = 0;
     uint32_t ph = 0;
+    // fused combine (down, pair leaders): the item whose raw rows this warp
+    // stored last, counted one item later, when those stores are long done
+    // and the fence before the count is cheap
+    const bool fuse_combine = !kGU && args.combine_out != nullptr;
+    const CombineArgs comb{args.perm, args.raw, args.combine_w, args.combine_out, args.combine_cnt, args.topk,
+                           args.hidden};
+    int pend_row = 0, pend_n = 0, pend_m = 0;
+    bool pend = false;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
         const int slot = li % kDecScSlots;
         float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -519,25 +528,30 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty[slot]);
-        // Pair reduction.  The buffer is double buffered by item parity: the
-        // second warp can only write it again after passing the next item's
-        // barrier, which the first warp reaches after reading this one.  The
-        // flag carries a timeout of the second warp, so neither warp waits on
-        // a partner that has left.
+        // Pair reduction: the second warp (kh == 1) hands its partial sums to
+        // the first through a slot double buffered by item parity.  Both warps
+        // wait on the pair's named barrier once per item, so neither runs an
+        // item ahead of the other.  (A second warp that only arrived could,
+        // when an item has fewer K stages than the ring holds, reach the
+        // barrier twice while its partner was in an epilogue, complete a
+        // phase on its own and leave the partner's last wait unmatched.)
+        // Each warp publishes whether its waits succeeded before the barrier;
+        // after it both read the partner's flag and leave together, so no
+        // barrier ever waits on a warp that has gone.
         float* rslot = red + ((parity * 8 + cw) * 32 + lane) * 4;
-        if (kh == 1) {
-            *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
-            if (lane == 0) red_ok[parity * 8 + cw] = ok ? 1 : 0;
-            named_bar_arrive(1 + cw, 64);
-            parity ^= 1;
-            if (!ok) break;
-            continue;
-        }
+        if (kh == 1) *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
+        if (lane == 0) red_ok[(parity * 2 + kh) * 8 + cw] = ok ? 1 : 0;
         named_bar_sync(1 + cw, 64);
-        const float4 o = *reinterpret_cast<const float4*>(rslot);
-        const bool ok_pair = red_ok[parity * 8 + cw] != 0;
+        const bool ok_pair = red_ok[(parity * 2 + (kh ^ 1)) * 8 + cw] != 0;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kh == 0) o = *reinterpret_cast<const float4*>(rslot);
         parity ^= 1;
         if (!ok || !ok_pair) break;
+        if (kh == 1) continue;
+        if (fuse_combine && pend) {
+            combine_block(comb, pend_row, pend_n, pend_m, lane);
+            pend = false;
+        }
         c[0] += o.x;
         c[1] += o.y;
         c[2] += o.z;
@@ -575,12 +589,15 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 dst[f_lo] = c[h];
                 dst[f_lo + 8] = c[2 + h];
             }
-            if (args.combine_out)
-                combine_block(CombineArgs{args.perm, args.raw, args.combine_w, args.combine_out, args.combine_cnt,
-                                          args.topk, args.hidden},
-                              it_row_start, n_rows, it_m, lane);
+            if (fuse_combine) {
+                pend = true;
+                pend_row = it_row_start;
+                pend_n = n_rows;
+                pend_m = it_m;
+            }
         }
     }
+    if (fuse_combine && pend) combine_block(comb, pend_row, pend_n, pend_m, lane);
 }
 
 template <GemmMode MODE, bool kOfficial>

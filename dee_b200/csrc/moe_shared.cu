@@ -26,7 +26,7 @@ constexpr int kShWBytes = 32768;              // 128 rows x 256 FP8
 constexpr int kShBBytes = 4096;               // 8 token rows x 256 FP16 (4 chunks of 8 x 128 B)
 constexpr int kShStageBytes = kShWBytes + kShBBytes;
 constexpr int kShStages = 5;
-constexpr int kShRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 8 * 4;
+constexpr int kShRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 2 * 8 * 4;
 constexpr int kShSmem = 1024 + kShStages * kShStageBytes + 256 + kShRedBytes;
 static_assert(kShSmem <= 232448, "shared memory budget");
 
@@ -175,21 +175,26 @@ __global__ void __launch_bounds__(kShThreads, 1)
             if (lane == 0) mbar_arrive(&empty[st]);
             if (++st == kShStages) { st = 0; ph ^= 1; }
         }
-        // pair reduction (double-buffered slot, partner timeout flag), as in moe_decode.cu
+        // Pair reduction: the second warp (kh == 1) hands its partial sums to
+        // the first through a slot double buffered by item parity.  Both warps
+        // wait on the pair's named barrier once per item, so neither runs an
+        // item ahead of the other.  (A second warp that only arrived could,
+        // when an item has fewer K stages than the ring holds, reach the
+        // barrier twice while its partner was in an epilogue, complete a
+        // phase on its own and leave the partner's last wait unmatched.)
+        // Each warp publishes whether its waits succeeded before the barrier;
+        // after it both read the partner's flag and leave together, so no
+        // barrier ever waits on a warp that has gone.
         float* rslot = red + ((parity * 8 + cw) * 32 + lane) * 4;
-        if (kh == 1) {
-            *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
-            if (lane == 0) red_ok[parity * 8 + cw] = ok ? 1 : 0;
-            named_bar_arrive(1 + cw, 64);
-            parity ^= 1;
-            if (!ok) break;
-            continue;
-        }
+        if (kh == 1) *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
+        if (lane == 0) red_ok[(parity * 2 + kh) * 8 + cw] = ok ? 1 : 0;
         named_bar_sync(1 + cw, 64);
-        const float4 o = *reinterpret_cast<const float4*>(rslot);
-        const bool ok_pair = red_ok[parity * 8 + cw] != 0;
+        const bool ok_pair = red_ok[(parity * 2 + (kh ^ 1)) * 8 + cw] != 0;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kh == 0) o = *reinterpret_cast<const float4*>(rslot);
         parity ^= 1;
         if (!ok || !ok_pair) break;
+        if (kh == 1) continue;
         c[0] += o.x;
         c[1] += o.y;
         c[2] += o.z;
