@@ -194,7 +194,6 @@ struct dee_engine {
     float* d_raw = nullptr;
     int32_t* h_ids = nullptr;      // pinned staging of host-given ids
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
-    int32_t* d_comb_cnt = nullptr;     // fused decode combine: [kDecodeMaxSelections, H / 128] counters
     int32_t* d_perm_chunks = nullptr;  // multi-CTA permutation: per-chunk expert counts
     int32_t* d_perm_lrank = nullptr;   // multi-CTA permutation: rank within the chunk
     // shared-expert workspaces, capacity in tokens
@@ -271,8 +270,8 @@ void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
     cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
-    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank); cudaFree(e->d_comb_cnt);
-    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr; e->d_comb_cnt = nullptr;
+    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank);
+    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr;
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
@@ -307,7 +306,6 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_chunks, ((cap + 1023) / 1024) * static_cast<size_t>(E))) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_lrank, cap)) != cudaSuccess ||
-        (err = dev_alloc(&e->d_comb_cnt, static_cast<size_t>(kDecodeMaxSelections) * (H / 128))) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
                              cudaHostAllocDefault)) != cudaSuccess) {
         free_workspace(e);
@@ -358,15 +356,9 @@ struct EpReturn {
     int capacity, rank;
 };
 
-// fuse_out / fuse_w (may be null): the caller wants the rank-order FP32
-// combine of the raw rows into fuse_out; for decode-sized one-GPU calls the
-// down GEMM's epilogue does it and *fused is set, otherwise the caller
-// launches the combine.
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
-                const EpReturn* ret = nullptr, const float* official_route_w = nullptr,
-                const float* fuse_w = nullptr, float* fuse_out = nullptr, bool* fused = nullptr) {
-    if (fused) *fused = false;
+                const EpReturn* ret = nullptr, const float* official_route_w = nullptr) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -385,12 +377,6 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     po.chunk_counts = e->d_perm_chunks;
     po.lrank = e->d_perm_lrank;
     po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
-    const bool fuse = decode && fuse_out && fuse_w && !ret && !official_route_w && H % 128 == 0 &&
-                      (reinterpret_cast<uintptr_t>(fuse_out) & 15) == 0;
-    if (fuse) {  // the permutation (one CTA at this size) clears the combine counters
-        po.zero = e->d_comb_cnt;
-        po.zero_n = tokens * (H / 128);
-    }
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream, skip_negative);
@@ -454,12 +440,6 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     }
     a.k_total = I;
     a.m_tiles = H / 128;
-    if (fuse) {
-        a.combine_out = fuse_out;
-        a.combine_w = fuse_w;
-        a.combine_cnt = e->d_comb_cnt;
-        if (fused) *fused = true;
-    }
     stage_begin(e, kStageDown, stream);
     err = decode ? launch_moe_decode(false, gm, a, e->num_sms, stream)
                  : launch_moe_gemm(false, gm, a, e->num_sms, stream);
@@ -805,12 +785,10 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     }
     e->h_ids_count = sel;
     float* raw = d_raw ? d_raw : e->d_raw;
-    bool fused = false;
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, ids32, raw,
-                          stream, topk, false, true, nullptr, nullptr, d_out_f32 ? d_weights : nullptr,
-                          d_out_f32, &fused)) != DEE_OK)
+                          stream, topk, false, true)) != DEE_OK)
         return rc;
-    if (d_out_f32 && !fused) {
+    if (d_out_f32) {
         stage_begin(e, kStageCombine, stream);
         err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");

@@ -208,10 +208,6 @@ struct PermuteOut {
     int32_t* chunk_counts = nullptr;  // [max_chunks * E]
     int32_t* lrank = nullptr;         // [T*K]
     long long max_chunks = 0;
-    // Zeroed by the (one-CTA) permutation before it groups: the fused
-    // combine's counters of the forward that follows.
-    int32_t* zero = nullptr;
-    int zero_n = 0;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.

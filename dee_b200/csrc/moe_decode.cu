@@ -161,59 +161,6 @@ __device__ __forceinline__ DecItem finish_item(const GemmArgs& a, int item, cons
     return d;
 }
 
-// The live combine out[t] = sum_r w[t, r] * raw[t, r] (rank order, each
-// multiply and add rounded to FP32; deepseek_v4_layer_candidate.py:616-629)
-// fused into the down GEMM.  A 128-feature block of token t is complete once
-// all K of its selections have passed through the eight pair-leader warps
-// that write it; every such warp counts itself on the block's counter after
-// its stores (fenced; the kernel makes the count one item later), and the
-// warp whose count completes the block sums the
-// K raw rows in rank order -- the same arithmetic as combine_f32_kernel, so
-// the result does not depend on which warp finishes.  No warp waits on
-// another: a warp that has left on a timeout only leaves blocks incomplete.
-struct CombineArgs {
-    const int* perm;
-    const float* raw;
-    const float* w;
-    float* out;
-    int* cnt;
-    int topk, hidden;
-};
-
-__device__ __noinline__ void combine_block(const CombineArgs a, int row_start, int n_rows, int m, int lane) {
-    const int K = a.topk;
-    const int blocks = a.hidden / 128;
-    const int target = 8 * K;  // 8 leader warps x K selections
-    __threadfence();           // this warp's raw stores before its count
-    __syncwarp();
-    int t = -1;
-    bool last = false;
-    if (lane < n_rows) {
-        t = a.perm[row_start + lane] / K;
-        last = atomicAdd(&a.cnt[t * blocks + m], 1) == target - 1;
-    }
-    unsigned done = __ballot_sync(0xffffffffu, last);
-    if (!done) return;
-    __threadfence();  // every other warp's raw stores before the reads below
-    while (done) {
-        const int src = __ffs(done) - 1;
-        done &= done - 1;
-        const int tok = __shfl_sync(0xffffffffu, t, src);
-        const size_t f = static_cast<size_t>(m) * 128 + 4 * lane;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int r = 0; r < K; ++r) {
-            const size_t s = static_cast<size_t>(tok) * K + r;
-            const float w = a.w[s];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.raw + s * a.hidden + f));
-            acc.x = __fadd_rn(acc.x, __fmul_rn(w, v.x));
-            acc.y = __fadd_rn(acc.y, __fmul_rn(w, v.y));
-            acc.z = __fadd_rn(acc.z, __fmul_rn(w, v.z));
-            acc.w = __fadd_rn(acc.w, __fmul_rn(w, v.w));
-        }
-        *reinterpret_cast<float4*>(a.out + static_cast<size_t>(tok) * a.hidden + f) = acc;
-    }
-}
-
 // What the consumers need of an item, handed over in shared memory with the
 // item's scale rows.
 struct ItemRec {
@@ -449,14 +396,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
     int st = 0, parity = 0, li = 0;
     uint32_t ph = 0;
-    // fused combine (down, pair leaders): the item whose raw rows this warp
-    // stored last, counted one item later, when those stores are long done
-    // and the fence before the count is cheap
-    const bool fuse_combine = !kGU && args.combine_out != nullptr;
-    const CombineArgs comb{args.perm, args.raw, args.combine_w, args.combine_out, args.combine_cnt, args.topk,
-                           args.hidden};
-    int pend_row = 0, pend_n = 0, pend_m = 0;
-    bool pend = false;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
         const int slot = li % kDecScSlots;
         float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -548,10 +487,6 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         parity ^= 1;
         if (!ok || !ok_pair) break;
         if (kh == 1) continue;
-        if (fuse_combine && pend) {
-            combine_block(comb, pend_row, pend_n, pend_m, lane);
-            pend = false;
-        }
         c[0] += o.x;
         c[1] += o.y;
         c[2] += o.z;
@@ -589,15 +524,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 dst[f_lo] = c[h];
                 dst[f_lo + 8] = c[2 + h];
             }
-            if (fuse_combine) {
-                pend = true;
-                pend_row = it_row_start;
-                pend_n = n_rows;
-                pend_m = it_m;
-            }
         }
     }
-    if (fuse_combine && pend) combine_block(comb, pend_row, pend_n, pend_m, lane);
 }
 
 template <GemmMode MODE, bool kOfficial>

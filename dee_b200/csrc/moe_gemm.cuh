@@ -79,12 +79,6 @@ struct GemmArgs {
     // Decode kernel: the scale rows arrive by swizzled tensor copies (set by
     // the launcher from GemmMaps::scale_swz).
     int scale_swz;
-    // Decode down GEMM, one-GPU path: the rank-order FP32 combine fused into
-    // the epilogue (combine_out null: raw rows only).  combine_cnt holds one
-    // counter per (token, 128-feature block), zero when the kernel starts.
-    float* combine_out;          // [T, H]
-    const float* combine_w;      // [T, K] routing weights
-    int* combine_cnt;            // [T, H / 128]
 };
 
 constexpr int kDqGroups = 4;          // dequantiser warpgroups

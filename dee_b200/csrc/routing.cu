@@ -245,7 +245,6 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     sm100::pdl_wait();
     sm100::pdl_trigger();
     for (int e = tid; e < experts; e += kPermThreads) { cnt[e] = 0; cursor[e] = 0; }
-    for (int i = tid; i < out.zero_n; i += kPermThreads) out.zero[i] = 0;
     for (int i = tid; i < 32 * kPermMaxExperts; i += kPermThreads) (&wcnt[0][0])[i] = 0;
     __syncthreads();
     for (int p = tid; p < sel; p += kPermThreads) {

@@ -524,13 +524,14 @@ def test_batch_with_fewer_selections_than_configured(torch_cuda, lib, oracle_mod
 
 
 @pytest.mark.parametrize("T,dup", [(1, False), (8, True), (64, False)])
-def test_fused_decode_combine_bitexact_over_calls(torch_cuda, oracle_mod, T, dup):
-    """Decode-sized calls (T * K <= 384) combine inside the down GEMM's
-    epilogue: per (token, 128-feature block) a counter, the warp that
-    completes it sums the K rows in rank order.  Three calls in a row on one
-    engine (the counters are cleared by each call's permutation), with
-    repeated expert ids in a token and at the 384-selection boundary: out is
-    bit-identical to the oracle's rank-order combine of the same raw rows."""
+def test_decode_combine_bitexact_over_calls(torch_cuda, oracle_mod, T, dup):
+    """Decode-sized calls (T * K <= 384, the register-dequant kernel) three
+    times in a row on one engine, with repeated expert ids in a token and at
+    the 384-selection boundary: out is bit-identical to the oracle's
+    rank-order combine of the same raw rows, and the raw rows match the
+    oracle's FP16 chain.  At H = 1024 the gate/up items have two K stages, so
+    the pair of consumer warps of an item goes through its reduction barrier
+    many times per CTA."""
     torch = torch_cuda
     orc = oracle_mod
     H, I, E, K = 1024, 512, 16, 6
