@@ -523,6 +523,11 @@ def run_prefill(args):
         "gpu_launches_per_step": launches,
         "clocks": clk.summary(),
     }
+    if E == 256 and not args.act_quant:
+        # ncu capture of this workload's gate/up launch (cold cache)
+        tr = profiled_traffic("moe_gemm_prefill_t4096.md", "prefill_gate_up")
+        if tr:
+            result["roofline"].update(tr)
     emit(result)
 
 
@@ -857,6 +862,10 @@ def main():
                                   "tflops_gemms": flops / (gemm_ms / 1000.0) / 1e12 if gemm_ms else None,
                                   "stage_ms": psg, "max_expert_rows": int(counts.max()),
                                   "active_experts": int((counts > 0).sum())}
+        if E == 256:
+            tr = profiled_traffic("moe_gemm_prefill_t4096.md", "prefill_gate_up")
+            if tr:
+                sweep["prefill_t4096"]["gate_up_traffic"] = tr
         # the same layer through the MXFP8-activation variant (E4M3 tokens,
         # UE8M0 per 32; its tensor-core peak is the FP8 rate, 2x bf16)
         try:
