@@ -98,6 +98,7 @@ struct EpP2P {
     std::vector<void*> opened;        // peer blocks opened from IPC handles
     float** d_back_peers = nullptr;   // device copy of peers.back_rows
     int32_t* d_slot_of_pos = nullptr; // [tokens * K]
+    uint32_t* d_done = nullptr;       // dispatch rows kernel's completion counter (in the same allocation)
     uint32_t epoch = 0;
     bool connected = false;
 };
@@ -356,9 +357,19 @@ struct EpReturn {
     int capacity, rank;
 };
 
+// The senders' dispatch flags the permutation waits for (bounded) before it
+// reads an expert-parallel receive buffer.
+struct EpWait {
+    const uint32_t* flags;
+    int ranks;
+    uint32_t epoch;
+    uint64_t limit_ns;
+};
+
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
-                const EpReturn* ret = nullptr, const float* official_route_w = nullptr) {
+                const EpReturn* ret = nullptr, const float* official_route_w = nullptr,
+                const EpWait* wait = nullptr) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -377,6 +388,12 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     po.chunk_counts = e->d_perm_chunks;
     po.lrank = e->d_perm_lrank;
     po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
+    if (wait) {
+        po.wait_flags = wait->flags;
+        po.wait_ranks = wait->ranks;
+        po.wait_epoch = wait->epoch;
+        po.wait_limit_ns = wait->limit_ns;
+    }
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
                                      stream, skip_negative);
@@ -1031,8 +1048,12 @@ int dee_ep_p2p_init(dee_engine* e, int ranks, int rank, int tokens, void* ipc_ha
     p.bytes = up(p.off_back_flag + static_cast<size_t>(ranks) * 4);
     cudaError_t err = cudaMalloc(reinterpret_cast<void**>(&p.block), p.bytes);
     if (err == cudaSuccess) err = cudaMemset(p.block, 0, p.bytes);  // flags start below epoch 1
-    if (err == cudaSuccess)
-        err = cudaMalloc(reinterpret_cast<void**>(&p.d_slot_of_pos), sizeof(int32_t) * cap);
+    const size_t sop_bytes = up(sizeof(int32_t) * cap);
+    if (err == cudaSuccess) err = cudaMalloc(reinterpret_cast<void**>(&p.d_slot_of_pos), sop_bytes + 256);
+    if (err == cudaSuccess) {
+        p.d_done = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(p.d_slot_of_pos) + sop_bytes);
+        err = cudaMemset(p.d_done, 0, 256);
+    }
     if (err == cudaSuccess)
         err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle_out), p.block);
     if (err != cudaSuccess) {
@@ -1101,9 +1122,9 @@ int dee_ep_p2p_dispatch_device(dee_engine* e, const void* d_x_f16, const int32_t
     cudaError_t err = launch_ep_peer_dispatch(d_ids, static_cast<const __half*>(d_x_f16), p.tokens,
                                               e->cfg.topk, e->cfg.hidden, p.ranks, p.rank,
                                               e->cfg.num_experts, p.capacity, p.peers, p.d_slot_of_pos,
-                                              e->d_journal, e->d_status, p.epoch, stream);
+                                              e->d_journal, e->d_status, p.d_done, p.epoch, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep peer dispatch launch");
-    e->launches += 3;
+    e->launches += 2;
     e->h_ids_count = sel;
     e->journal_stream = stream;
     return DEE_OK;
@@ -1116,16 +1137,16 @@ int dee_ep_p2p_experts_device(dee_engine* e, int layer, void* stream_v) {
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!p.connected || p.epoch == 0)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_experts before any dispatch");
-    cudaError_t err = launch_ep_wait(p.peers.recv_flag[p.rank], p.ranks, p.epoch, e->d_status,
-                                     sm100::kStatusTimeoutFlag, e->wait_limit_ns, stream);
-    if (err != cudaSuccess) return cuda_fail(e, err, "ep wait launch");
+    // the permutation waits (bounded) for every sender's dispatch flag
     const EpReturn ret{p.d_back_peers, p.capacity, p.rank};
+    const EpWait wait{p.peers.recv_flag[p.rank], p.ranks, p.epoch, e->wait_limit_ns};
     if ((rc = run_experts(e, layer, p.peers.recv_rows[p.rank], p.ranks * p.capacity,
-                          p.peers.recv_expert[p.rank], e->d_raw, stream, 1, true, false, &ret)) != DEE_OK)
+                          p.peers.recv_expert[p.rank], e->d_raw, stream, 1, true, false, &ret, nullptr,
+                          &wait)) != DEE_OK)
         return rc;
-    err = launch_ep_signal(p.peers, true, p.ranks, p.rank, p.epoch, stream);
+    cudaError_t err = launch_ep_signal(p.peers, true, p.ranks, p.rank, p.epoch, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep signal launch");
-    e->launches += 2;
+    e->launches += 1;
     return DEE_OK;
 }
 
@@ -1136,13 +1157,13 @@ int dee_ep_p2p_combine_device(dee_engine* e, const float* d_weights, float* d_ou
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!p.connected || p.epoch == 0 || !d_weights || !d_out_f32)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_combine needs a dispatched layer, weights and out");
-    cudaError_t err = launch_ep_wait(p.peers.back_flag[p.rank], p.ranks, p.epoch, e->d_status,
-                                     sm100::kStatusTimeoutFlag, e->wait_limit_ns, stream);
-    if (err == cudaSuccess)
-        err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
-                                e->cfg.topk, e->cfg.hidden, d_out_f32, stream);
+    // every combine CTA waits (bounded) for every owner's return flag
+    const cudaError_t err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
+                                              e->cfg.topk, e->cfg.hidden, d_out_f32, stream,
+                                              p.peers.back_flag[p.rank], p.ranks, p.epoch, e->d_status,
+                                              e->wait_limit_ns);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
-    e->launches += 2;
+    e->launches += 1;
     return DEE_OK;
 }
 

@@ -119,11 +119,18 @@ __global__ void ep_pack_rows_kernel(const __half* __restrict__ x, const int32_t*
 // The live combine (deepseek_v4_layer_candidate.py:616-629) over rows that
 // came back from the expert owners: out = 0, then for each rank in order
 // out += w * row, the multiply and the add each rounded to FP32.
+// With `flags` set (the NVLink path) every CTA first waits (bounded) for each
+// expert owner's return flag to reach `epoch`.
 __global__ void ep_combine_kernel(const float* __restrict__ back, const int32_t* __restrict__ slot_of_pos,
                                   const float* __restrict__ w, int tokens, int topk, int hidden,
-                                  float* __restrict__ out) {
+                                  float* __restrict__ out, const uint32_t* flags, int ranks, uint32_t epoch,
+                                  uint32_t* status, uint64_t limit_ns) {
     sm100::pdl_wait();
     sm100::pdl_trigger();
+    if (flags) {
+        sm100::wait_flags_bounded(flags, ranks, epoch, limit_ns, status, sm100::kStatusTimeoutFlag);
+        __syncthreads();
+    }
     const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
     for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
          i += static_cast<size_t>(gridDim.x) * blockDim.x) {
@@ -151,8 +158,13 @@ __global__ void ep_combine_kernel(const float* __restrict__ back, const int32_t*
 // over NVLink (peer pointers from CUDA IPC); block `rank` of every owner's
 // buffer belongs to this rank.
 
+// The rows, then the dispatch flags: every CTA fences its stores and counts
+// itself on `done`; the CTA that completes the count resets it and raises
+// `epoch` in slot `rank` of every owner's flag array (what ep_signal_kernel
+// does as a launch of its own).
 __global__ void ep_peer_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ slot_of_pos,
-                                    int sel, int topk, int hidden, int rank, int capacity, EpPeers peers) {
+                                    int sel, int topk, int hidden, int rank, int capacity, EpPeers peers,
+                                    int ranks, uint32_t* done, uint32_t epoch) {
     sm100::pdl_wait();
     sm100::pdl_trigger();
     const int warps_total = gridDim.x * (blockDim.x >> 5);
@@ -167,6 +179,14 @@ __global__ void ep_peer_rows_kernel(const __half* __restrict__ x, const int32_t*
                                               static_cast<size_t>(rank * capacity + (s - d * capacity)) * hidden);
         for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
     }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x != 0) return;
+    if (atomicAdd(done, 1u) != gridDim.x - 1) return;
+    *done = 0;
+    __threadfence_system();
+    for (int d = 0; d < ranks; ++d)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(peers.recv_flag[d] + rank), "r"(epoch) : "memory");
 }
 
 // After the kernels before it on the stream have completed: make their
@@ -180,28 +200,6 @@ __global__ void ep_signal_kernel(EpPeers peers, bool back, int ranks, int rank, 
     for (int d = 0; d < ranks; ++d) {
         uint32_t* f = (back ? peers.back_flag[d] : peers.recv_flag[d]) + rank;
         asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
-    }
-}
-
-// Wait (bounded) until every peer has published `epoch` in this rank's flag
-// array; on timeout set `code` in the status word and return, so the context
-// stays usable and the host sees the failure.
-__global__ void ep_wait_kernel(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                               uint32_t code, uint64_t limit_ns) {
-    sm100::pdl_wait();
-    sm100::pdl_trigger();
-    const int s = threadIdx.x;
-    if (s >= ranks) return;
-    const uint64_t t0 = sm100::global_ns();
-    for (;;) {
-        uint32_t v;
-        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + s) : "memory");
-        if (static_cast<int32_t>(v - epoch) >= 0) break;
-        if (sm100::global_ns() - t0 > limit_ns) {
-            atomicOr(status, code);
-            break;
-        }
-        __nanosleep(200);
     }
 }
 
@@ -232,7 +230,7 @@ cudaError_t launch_ep_pack(const int32_t* ids, const __half* x, int tokens, int 
 cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tokens, int topk, int hidden,
                                     int ranks, int rank, int epr, int capacity, const EpPeers& peers,
                                     int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
-                                    uint32_t epoch, cudaStream_t stream) {
+                                    uint32_t* done, uint32_t epoch, cudaStream_t stream) {
     if (tokens <= 0 || topk <= 0 || ranks <= 0 || ranks > kEpMaxRanks || rank < 0 || rank >= ranks ||
         epr <= 0 || capacity <= 0 || hidden % 8 != 0)
         return cudaErrorInvalidValue;
@@ -241,22 +239,14 @@ cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tok
                                  ranks, rank, epr, capacity, static_cast<int32_t*>(nullptr), peers,
                                  slot_of_pos, journal, status);
     if (err != cudaSuccess) return err;
-    err = launch_pdl(ep_peer_rows_kernel, dim3(grid_cap(static_cast<size_t>(sel), 8, 148 * 8)), dim3(256), 0,
-                     stream, x, static_cast<const int32_t*>(slot_of_pos), sel, topk, hidden, rank, capacity,
-                     peers);
-    if (err != cudaSuccess) return err;
-    return launch_ep_signal(peers, false, ranks, rank, epoch, stream);
+    return launch_pdl(ep_peer_rows_kernel, dim3(grid_cap(static_cast<size_t>(sel), 8, 148 * 8)), dim3(256), 0,
+                      stream, x, static_cast<const int32_t*>(slot_of_pos), sel, topk, hidden, rank, capacity,
+                      peers, ranks, done, epoch);
 }
 
 cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int rank, uint32_t epoch,
                              cudaStream_t stream) {
     return launch_pdl(ep_signal_kernel, dim3(1), dim3(32), 0, stream, peers, back, ranks, rank, epoch);
-}
-
-cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                           uint32_t code, uint64_t limit_ns, cudaStream_t stream) {
-    if (ranks <= 0 || ranks > kEpMaxRanks) return cudaErrorInvalidValue;
-    return launch_pdl(ep_wait_kernel, dim3(1), dim3(32), 0, stream, flags, ranks, epoch, status, code, limit_ns);
 }
 
 namespace {
@@ -279,11 +269,14 @@ cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* status, uint32_t c
 }
 
 cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,
-                              int tokens, int topk, int hidden, float* out, cudaStream_t stream) {
-    if (tokens <= 0 || topk <= 0 || hidden % 4 != 0) return cudaErrorInvalidValue;
+                              int tokens, int topk, int hidden, float* out, cudaStream_t stream,
+                              const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
+                              uint64_t limit_ns) {
+    if (tokens <= 0 || topk <= 0 || hidden % 4 != 0 || (flags && (ranks <= 0 || ranks > 256)))
+        return cudaErrorInvalidValue;
     const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
     return launch_pdl(ep_combine_kernel, dim3(grid_cap(n4, 256, 148 * 4)), dim3(256), 0, stream, back,
-                      slot_of_pos, weights, tokens, topk, hidden, out);
+                      slot_of_pos, weights, tokens, topk, hidden, out, flags, ranks, epoch, status, limit_ns);
 }
 
 }  // namespace dee

@@ -128,9 +128,13 @@ cudaError_t launch_ep_pack(const int32_t* ids, const __half* x, int tokens, int 
                            int ranks, int epr, int capacity, __half* send_rows, int32_t* send_expert,
                            int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
                            cudaStream_t stream);
-// Rank-order FP32 combine of rows returned by the expert owners.
+// Rank-order FP32 combine of rows returned by the expert owners; with `flags`
+// each CTA first waits (bounded by limit_ns, status bit kStatusTimeoutFlag)
+// for every owner's return flag to reach `epoch`.
 cudaError_t launch_ep_combine(const float* back, const int32_t* slot_of_pos, const float* weights,
-                              int tokens, int topk, int hidden, float* out, cudaStream_t stream);
+                              int tokens, int topk, int hidden, float* out, cudaStream_t stream,
+                              const uint32_t* flags = nullptr, int ranks = 0, uint32_t epoch = 0,
+                              uint32_t* status = nullptr, uint64_t limit_ns = 0);
 
 // Peer (NVLink) expert parallelism: every rank's exchange buffers, indexed by
 // rank (this rank's own entries are local pointers).  Block s of rank d's
@@ -143,19 +147,17 @@ struct EpPeers {
     float* back_rows[kEpMaxRanks];       // [ranks * capacity, H] FP32
     uint32_t* back_flag[kEpMaxRanks];    // [ranks] return epoch per expert owner
 };
-// Index + row stores into the owners' receive buffers, then the dispatch flags.
+// Index + row stores into the owners' receive buffers, then the dispatch flags
+// (raised by the rows kernel's last CTA; `done` is its completion counter,
+// zero between calls).
 cudaError_t launch_ep_peer_dispatch(const int32_t* ids, const __half* x, int tokens, int topk, int hidden,
                                     int ranks, int rank, int epr, int capacity, const EpPeers& peers,
                                     int32_t* slot_of_pos, int32_t* journal, uint32_t* status,
-                                    uint32_t epoch, cudaStream_t stream);
+                                    uint32_t* done, uint32_t epoch, cudaStream_t stream);
 // Publish `epoch` in slot `rank` of every rank's dispatch (back = false) or
 // return (back = true) flags, after the stream's earlier kernels.
 cudaError_t launch_ep_signal(const EpPeers& peers, bool back, int ranks, int rank, uint32_t epoch,
                              cudaStream_t stream);
-// Bounded wait until all `ranks` flags reached `epoch` (after limit_ns: `code`
-// in status).
-cudaError_t launch_ep_wait(const uint32_t* flags, int ranks, uint32_t epoch, uint32_t* status,
-                           uint32_t code, uint64_t limit_ns, cudaStream_t stream);
 // A wait on an mbarrier nothing arrives on, bounded by limit_ns (sets `code`).
 cudaError_t launch_wait_selftest(uint64_t limit_ns, uint32_t* status, uint32_t code, cudaStream_t stream);
 
@@ -208,6 +210,12 @@ struct PermuteOut {
     int32_t* chunk_counts = nullptr;  // [max_chunks * E]
     int32_t* lrank = nullptr;         // [T*K]
     long long max_chunks = 0;
+    // Expert-parallel receive buffers: before reading ids, wait (bounded)
+    // for wait_ranks senders' flags to reach wait_epoch.
+    const uint32_t* wait_flags = nullptr;
+    int wait_ranks = 0;
+    uint32_t wait_epoch = 0;
+    uint64_t wait_limit_ns = 0;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.

@@ -244,6 +244,12 @@ __global__ void __launch_bounds__(kPermThreads, 1)
 
     sm100::pdl_wait();
     sm100::pdl_trigger();
+    // expert-parallel receive buffer: the senders' rows and ids have landed
+    // once their flags reach the epoch (the __syncthreads below orders every
+    // thread's reads after the acquires)
+    if (out.wait_flags)
+        sm100::wait_flags_bounded(out.wait_flags, out.wait_ranks, out.wait_epoch, out.wait_limit_ns, status,
+                                  sm100::kStatusTimeoutFlag);
     for (int e = tid; e < experts; e += kPermThreads) { cnt[e] = 0; cursor[e] = 0; }
     for (int i = tid; i < 32 * kPermMaxExperts; i += kPermThreads) (&wcnt[0][0])[i] = 0;
     __syncthreads();
@@ -366,6 +372,9 @@ __global__ void __launch_bounds__(kPermChunk, 1)
     const int sel = tokens * topk;
     sm100::pdl_wait();
     sm100::pdl_trigger();
+    if (out.wait_flags)  // as in permute_kernel; the place pass runs after this one completes
+        sm100::wait_flags_bounded(out.wait_flags, out.wait_ranks, out.wait_epoch, out.wait_limit_ns, status,
+                                  sm100::kStatusTimeoutFlag);
     for (int i = tid; i < 32 * kPermMaxExperts; i += kPermChunk) (&wcnt[0][0])[i] = 0;
     __syncthreads();
     const int j = blockIdx.x * kPermChunk + tid;

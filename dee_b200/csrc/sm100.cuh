@@ -131,6 +131,28 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ui
     return mbar_wait_slow(bar, parity, status, code, limit_ns);
 }
 
+// Bounded wait of thread i < n for flags[i] to reach `epoch` (system-scope
+// acquire: the flags are raised by kernels on other GPUs after their
+// stores).  A flag that has not arrived after limit_ns sets `code` in
+// *status and the thread goes on.  Callers follow it with a CTA barrier, so
+// every thread of the CTA is ordered after the acquires.
+__device__ __forceinline__ void wait_flags_bounded(const uint32_t* flags, int n, uint32_t epoch,
+                                                   uint64_t limit_ns, uint32_t* status, uint32_t code) {
+    const int i = threadIdx.x;
+    if (i >= n) return;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + i) : "memory");
+        if (static_cast<int32_t>(v - epoch) >= 0) return;
+        if (global_ns() - t0 > limit_ns) {
+            atomicOr(status, code);
+            return;
+        }
+        __nanosleep(200);
+    }
+}
+
 // ---------------------------------------------------------------- PDL
 
 // Programmatic dependent launch.  A kernel launched with programmatic stream
