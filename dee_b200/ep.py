@@ -9,8 +9,12 @@ not depend on the GPU count.  A layer call on this rank's T tokens:
 
   1. pack: selections sorted by owner rank into `capacity` rows per rank
      (FP16 hidden row + the owner's local expert id, -1 unused);
-  2. all-to-all of the rows and the expert ids (equal blocks, so no host
-     synchronisation and no split sizes);
+  2. all-to-all of the rows and the expert ids: either equal blocks of
+     `capacity` rows per rank pair (no host synchronisation, no split
+     sizes: the choice for decode-sized layers, where the padded bytes cost
+     less than a host round trip), or -- above `counts_rows` padded rows --
+     an all-to-all of the per-destination counts, one host read of them, and
+     all-to-alls of the occupied rows only;
   3. the grouped expert GEMMs over the received rows;
   4. all-to-all of the FP32 output rows back to their tokens' owners;
   5. the rank-order FP32 combine.
@@ -69,7 +73,8 @@ class ExpertParallelMoE:
 
     def __init__(self, torch_mod, rank: int, world: int, experts_per_rank: int, tokens: int,
                  topk: int, hidden: int, device, *, engine=None, layer: int = 0,
-                 capacity: int | None = None, group=None, ops: EpOps | None = None):
+                 capacity: int | None = None, group=None, ops: EpOps | None = None,
+                 exchange: str = "auto", counts_rows: int = 4096):
         self.torch = torch_mod
         self.dist = torch_mod.distributed
         self.rank, self.world, self.epr = rank, world, experts_per_rank
@@ -94,6 +99,10 @@ class ExpertParallelMoE:
         self.raw = t.zeros((n, hidden), dtype=t.float32, device=device)
         self.back = t.empty((n, hidden), dtype=t.float32, device=device)
         self.out = t.empty((tokens, hidden), dtype=t.float32, device=device)
+        if exchange not in ("auto", "fixed", "counts"):
+            raise ValueError(f"exchange must be auto, fixed or counts, not {exchange!r}")
+        self.counts_mode = exchange == "counts" or (exchange == "auto" and n >= counts_rows)
+        self.device = device
 
     def forward(self, x, ids, weights, layer: int | None = None):
         """x FP16 [T, H], ids int32 [T, K] (global expert ids), weights FP32
@@ -106,15 +115,58 @@ class ExpertParallelMoE:
             raise ValueError(f"expected x [{self.tokens}, {self.hidden}] and ids [{self.tokens}, "
                              f"{self.topk}], got {tuple(x.shape)} and {tuple(ids.shape)}")
         self.ops.pack(ids, x, self.send_rows, self.send_expert, self.slot_of_pos)
-        # FP16 rows travel as int32 pairs: a bitwise view every backend moves
-        i32 = self.torch.int32
-        self.dist.all_to_all_single(self.recv_rows.view(i32), self.send_rows.view(i32),
-                                    group=self.group)
-        self.dist.all_to_all_single(self.recv_expert, self.send_expert, group=self.group)
-        self.ops.compute(self.recv_rows, self.recv_expert, self.raw, self.layer if layer is None else layer)
-        self.dist.all_to_all_single(self.back, self.raw, group=self.group)
+        lyr = self.layer if layer is None else layer
+        if self.counts_mode:
+            self._exchange_counts(lyr)
+        else:
+            # FP16 rows travel as int32 pairs: a bitwise view every backend moves
+            i32 = self.torch.int32
+            self.dist.all_to_all_single(self.recv_rows.view(i32), self.send_rows.view(i32),
+                                        group=self.group)
+            self.dist.all_to_all_single(self.recv_expert, self.send_expert, group=self.group)
+            self.ops.compute(self.recv_rows, self.recv_expert, self.raw, lyr)
+            self.dist.all_to_all_single(self.back, self.raw, group=self.group)
         self.ops.combine(self.back, self.slot_of_pos, weights, self.out)
         return self.out
+
+    def _exchange_counts(self, layer) -> None:
+        """Occupied rows only.  Pack fills each destination's block from its
+        start, so block d's first send_n[d] rows are the ones to send; they
+        land at the start of this rank's block on the owner, the rest of the
+        owner's block is marked unused (-1), and the returned rows land where
+        the fixed exchange would put them, so slot_of_pos and the combine are
+        unchanged."""
+        t, dist, W, C = self.torch, self.dist, self.world, self.capacity
+        i32, i64 = t.int32, t.int64
+        send_n = (self.send_expert.view(W, C) >= 0).sum(dim=1).to(i64)
+        recv_n = t.empty_like(send_n)
+        dist.all_to_all_single(recv_n, send_n, group=self.group)
+        s_list, r_list = send_n.tolist(), recv_n.tolist()  # the one host read of the layer
+
+        def rows_index(counts):
+            idx = [d * C + i for d, k in enumerate(counts) for i in range(k)]
+            return t.tensor(idx, dtype=i64, device=self.device)
+
+        s_idx, r_idx = rows_index(s_list), rows_index(r_list)
+        rows32 = self.send_rows.view(i32)
+        recv32 = self.recv_rows.view(i32)
+        send_c = rows32.index_select(0, s_idx)
+        recv_c = t.empty((len(r_idx), rows32.shape[1]), dtype=i32, device=self.device)
+        dist.all_to_all_single(recv_c, send_c, output_split_sizes=r_list, input_split_sizes=s_list,
+                               group=self.group)
+        exp_c = self.send_expert.index_select(0, s_idx)
+        recv_e = t.empty(len(r_idx), dtype=i32, device=self.device)
+        dist.all_to_all_single(recv_e, exp_c, output_split_sizes=r_list, input_split_sizes=s_list,
+                               group=self.group)
+        self.recv_expert.fill_(-1)
+        recv32.index_copy_(0, r_idx, recv_c)
+        self.recv_expert.index_copy_(0, r_idx, recv_e)
+        self.ops.compute(self.recv_rows, self.recv_expert, self.raw, layer)
+        raw_c = self.raw.index_select(0, r_idx)
+        back_c = t.empty((len(s_idx), self.hidden), dtype=self.raw.dtype, device=self.device)
+        dist.all_to_all_single(back_c, raw_c, output_split_sizes=s_list, input_split_sizes=r_list,
+                               group=self.group)
+        self.back.index_copy_(0, s_idx, back_c)
 
 
 class ExpertParallelPeer:

@@ -71,7 +71,7 @@ def _np_ops(orc, layout, recs_local, capacity):
     return EpOps(pack, compute, combine)
 
 
-def _rank_main(rank, port, q):
+def _rank_main(rank, port, q, exchange="fixed"):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
@@ -85,7 +85,8 @@ def _rank_main(rank, port, q):
         layout, recs, x16, ids, w = _inputs(orc, rank)
         recs_local = recs[rank * EPR:(rank + 1) * EPR]
         ep = ExpertParallelMoE(torch, rank, WORLD, EPR, T, K, H, "cpu",
-                               ops=_np_ops(orc, layout, recs_local, T * K))
+                               ops=_np_ops(orc, layout, recs_local, T * K), exchange=exchange)
+        assert ep.counts_mode == (exchange == "counts")
         out = ep.forward(torch.from_numpy(x16.view(np.float16)), torch.from_numpy(ids),
                          torch.from_numpy(w)).numpy().copy()
         want = orc.combine_f32(orc.moe_layer_raw(recs, layout, x16, ids), w)
@@ -96,12 +97,15 @@ def _rank_main(rank, port, q):
         q.put((rank, False, repr(exc)))
 
 
-def test_expert_parallel_two_ranks_match_single_process():
+@pytest.mark.parametrize("exchange", ["fixed", "counts"])
+def test_expert_parallel_two_ranks_match_single_process(exchange):
+    """Both exchanges: equal blocks of capacity rows per rank pair, and the
+    counts all-to-all followed by all-to-alls of the occupied rows only."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_rank_main, args=(r, port, q, exchange)) for r in range(WORLD)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(WORLD)]

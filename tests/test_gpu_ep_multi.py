@@ -71,6 +71,11 @@ def _rank_main(rank, port, q):
         out2 = coll.forward(dx, dids, dw)
         torch.cuda.synchronize()
         results["nccl"] = bool(np.array_equal(out2.cpu().numpy(), ref.cpu().numpy()))
+        # the same over the counts exchange (occupied rows only)
+        coll_c = ExpertParallelMoE(torch, rank, WORLD, EPR, T, K, H, "cuda", engine=local2, exchange="counts")
+        out3 = coll_c.forward(dx, dids, dw)
+        torch.cuda.synchronize()
+        results["nccl_counts"] = bool(np.array_equal(out3.cpu().numpy(), ref.cpu().numpy()))
         results["journal"] = bool(np.array_equal(local.journal_ids(T), ids))
         dist.barrier()
         dist.destroy_process_group()
@@ -96,4 +101,5 @@ def test_expert_parallel_two_gpus_match_one_engine():
     for rank in range(WORLD):
         res = results[rank]
         assert "error" not in res, res
-        assert res["peer_status"] == 0 and res["peer"] and res["nccl"] and res["journal"], (rank, res)
+        assert res["peer_status"] == 0 and res["peer"] and res["nccl"] and res["nccl_counts"] and \
+            res["journal"], (rank, res)
