@@ -179,9 +179,11 @@ __global__ void ep_peer_rows_kernel(const __half* __restrict__ x, const int32_t*
                                               static_cast<size_t>(rank * capacity + (s - d * capacity)) * hidden);
         for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
     }
-    __threadfence_system();
+    // the CTA barrier orders every thread's stores before thread 0's fence,
+    // which is cumulative: one system fence per CTA, then its count
     __syncthreads();
     if (threadIdx.x != 0) return;
+    __threadfence_system();
     if (atomicAdd(done, 1u) != gridDim.x - 1) return;
     *done = 0;
     __threadfence_system();
