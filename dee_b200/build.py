@@ -61,12 +61,43 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     return LIB
 
 
+PYDEE_SRC = os.path.join(HERE, "pybind", "pydee.cpp")
+
+
+def pydee_path() -> str:
+    import sysconfig
+    return os.path.join(HERE, "_pydee" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_pydee(force: bool = False, verbose: bool = False) -> str:
+    """The pybind11 module dee_b200._pydee (pydee.Engine's methods over the
+    C ABI), linked against the in-tree libdee_b200.so through an $ORIGIN
+    rpath.  Needs the library built first."""
+    import sysconfig
+
+    import pybind11
+    out = pydee_path()
+    srcs = [PYDEE_SRC, os.path.join(ROOT, "include", "dee_b200.h"), LIB]
+    if not force and os.path.exists(out) and all(os.path.getmtime(p) <= os.path.getmtime(out) for p in srcs):
+        return out
+    cxx = os.environ.get("CXX") or shutil.which("g++") or "g++"
+    cmd = [cxx, "-O2", "-std=c++17", "-shared", "-fPIC", "-fvisibility=hidden",
+           "-I", pybind11.get_include(), "-I", sysconfig.get_paths()["include"], "-I", os.path.join(ROOT, "include"),
+           "-o", out + ".tmp", PYDEE_SRC, "-L", HERE, "-l:libdee_b200.so", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(out + ".tmp", out)
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
     args = ap.parse_args()
     print(build(force=args.force, verbose=True, ptxas_info=args.ptxas_info))
+    print(build_pydee(force=args.force, verbose=True))
 
 
 if __name__ == "__main__":
