@@ -531,6 +531,25 @@ def run_prefill(args):
     emit(result)
 
 
+def h2d_peak_gbs(torch, nbytes: int = 1 << 30, reps: int = 3) -> float:
+    """Host-to-device bandwidth of one plain copy from pinned memory, the
+    ceiling of the offload tier's copy stream (CUDA events, best of reps)."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    dst.copy_(src, non_blocking=True)
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = min(best, a.elapsed_time(b))
+    del src, dst
+    return nbytes / (best / 1000.0) / 1e9
+
+
 def drop_page_cache(path):
     """Write back and drop this store's own files from the page cache."""
     for root, _, files in os.walk(path):
@@ -623,11 +642,14 @@ def run_stack(args):
     if slots:
         stats1 = stack.engine.offload_stats()
         d = {k: stats1[k] - stats0[k] for k in stats1}
+        h2d = d["bytes"] / (ms / 1000.0) / 1e9
+        peak = h2d_peak_gbs(torch)
         offload = {"pool_gib": args.offload_gib, "pool_slots": slots,
                    "host_bytes": int(stack.host.numel()), "cold_reads": d["cold_reads"],
                    "cold_reads_per_token": d["cold_reads"] / (b * args.steps),
                    "hit_rate": d["hits"] / max(d["lookups"], 1),
-                   "h2d_gbs": d["bytes"] / (ms / 1000.0) / 1e9, "eviction": "next-use"}
+                   "h2d_gbs": h2d, "h2d_peak_gbs": peak, "copy_stream_busy_frac": h2d / peak,
+                   "eviction": "next-use"}
     if world > 1:
         t = torch.tensor([ms], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

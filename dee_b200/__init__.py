@@ -278,6 +278,11 @@ class Engine:
         self._check(rc, "dee_offload_prepare_device")
         return cold.value
 
+    def offload_debug_fail_next_copy(self) -> None:
+        """Test hook: the next cold record copy fails as if it could not be
+        queued (the reference's AsyncPrefetcher.debug_fail_next_submit)."""
+        self._check(self._lib.dee_offload_debug_fail_next_copy(self._h), "dee_offload_debug_fail_next_copy")
+
     def offload_stats(self) -> dict:
         out = (ctypes.c_uint64 * 4)()
         self._lib.dee_offload_stats(self._h, out)

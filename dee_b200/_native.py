@@ -120,6 +120,7 @@ SIGNATURES = {
     "dee_engine_stage_ms": (I, [P, P, I]),
     "dee_engine_set_wait_limit_ns": (I, [P, ctypes.c_uint64]),
     "dee_wait_selftest": (I, [ctypes.c_uint64, P, P]),
+    "dee_offload_debug_fail_next_copy": (I, [P]),
     "dee_store_create": (I, [ctypes.POINTER(P)]),
     "dee_store_destroy": (None, [P]),
     "dee_store_open": (I, [P, ctypes.c_char_p, I, I]),

@@ -135,6 +135,10 @@ struct Offload {
     int32_t* h_ids = nullptr;       // pinned staging of a layer's ids
     size_t h_ids_cap = 0;
     uint64_t lookups = 0, hits = 0, cold = 0, bytes = 0;
+    // one-shot test hook: the next cold copy's submission fails
+    // (AsyncPrefetcher::debug_fail_next_submit, include/dee/async_prefetcher.h:232)
+    bool fail_next_copy = false;
+    uint64_t submit_failures = 0;
 
     double probability(int64_t key) const {
         auto it = stats.find(key);
@@ -1270,6 +1274,7 @@ int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, i
         for (size_t i = 0; i < want; ++i) take.push_back(cand[i].second);
     }
     int cold = 0;
+    int failed_expert = -1;
     for (size_t i = 0; i < miss.size(); ++i) {
         const int64_t key = static_cast<int64_t>(layer) * E + miss[i];
         const int victim = take[i];
@@ -1278,10 +1283,25 @@ int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, i
         o.slot_key[static_cast<size_t>(victim)] = key;
         o.slot_of[static_cast<size_t>(key)] = victim;
         o.used_visit[static_cast<size_t>(victim)] = stamp;
-        err = cudaMemcpyAsync(o.pool + static_cast<size_t>(victim) * o.record_bytes,
-                              o.host + static_cast<size_t>(key) * o.record_bytes, o.record_bytes,
-                              cudaMemcpyHostToDevice, o.copy_stream);
-        if (err != cudaSuccess) return cuda_fail(e, err, "offload H2D");
+        err = cudaSuccess;
+        if (o.fail_next_copy) {
+            o.fail_next_copy = false;
+            err = cudaErrorLaunchFailure;  // as if the copy could not be queued
+        } else {
+            err = cudaMemcpyAsync(o.pool + static_cast<size_t>(victim) * o.record_bytes,
+                                  o.host + static_cast<size_t>(key) * o.record_bytes, o.record_bytes,
+                                  cudaMemcpyHostToDevice, o.copy_stream);
+        }
+        if (err != cudaSuccess) {
+            // the slot holds no valid record: invalidate it so no later lookup
+            // can hit it (a later call for the expert cold-loads again), and
+            // report the failure once this layer's table is consistent
+            o.slot_key[static_cast<size_t>(victim)] = -1;
+            o.slot_of[static_cast<size_t>(key)] = -1;
+            ++o.submit_failures;
+            if (failed_expert < 0) failed_expert = miss[i];
+            continue;
+        }
         ++cold;
         o.bytes += o.record_bytes;
     }
@@ -1294,6 +1314,16 @@ int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, i
     if (err == cudaSuccess) err = cudaStreamWaitEvent(stream, o.copied, 0);
     if (err != cudaSuccess) return cuda_fail(e, err, "offload slot table");
     if (cold_out) *cold_out = cold;
+    if (failed_expert >= 0)
+        return fail(e, DEE_ERR_CUDA, "offload H2D copy of layer " + std::to_string(layer) + " expert " +
+                                         std::to_string(failed_expert) +
+                                         " could not be queued; the expert is not resident");
+    return DEE_OK;
+}
+
+int dee_offload_debug_fail_next_copy(dee_engine* e) {
+    if (!e || !e->off.on) return DEE_ERR_INVALID;
+    e->off.fail_next_copy = true;
     return DEE_OK;
 }
 

@@ -280,6 +280,14 @@ DEE_API int dee_offload_attach(dee_engine* engine, const void* h_records, size_t
  * wait for the copies.  *cold_out (may be NULL) = experts copied. */
 DEE_API int dee_offload_prepare_device(dee_engine* engine, int layer, const int32_t* d_ids, int tokens,
                                        void* stream, int* cold_out);
+/* Test hook, one-shot: the next cold record copy of dee_offload_prepare_device
+ * fails as if it could not be queued (AsyncPrefetcher::debug_fail_next_submit,
+ * dee.cpp/include/dee/async_prefetcher.h:232).  That prepare call returns
+ * DEE_ERR_CUDA naming the expert, whose slot is invalidated (not resident:
+ * a forward run anyway reports it through the status word instead of
+ * reading the slot), and a later prepare for it cold-loads it again. */
+DEE_API int dee_offload_debug_fail_next_copy(dee_engine* engine);
+
 /* Exactly `bytes` of pinned host memory (for an offload tier's records;
  * allocators that round pinned requests up to powers of two cannot hold a
  * 140 GB stack on a 196 GB host). */

@@ -122,3 +122,46 @@ def test_wait_limit_is_range_checked(torch_cuda):
     with pytest.raises(dee_b200.DeeError):
         eng.set_wait_limit(5.0)
     eng.set_wait_limit(0.5)
+
+
+def test_offload_copy_failure_is_reported_not_computed(torch_cuda, oracle_mod):
+    """The offload tier's injected submit failure (the reference's
+    AsyncPrefetcher.debug_fail_next_submit, include/dee/async_prefetcher.h:232):
+    the prepare call reports it and names the expert, the expert is left not
+    resident, so a forward run anyway reports bit 4 (expert not resident)
+    rather than reading an unfilled slot; the next prepare cold-loads it and
+    the layer then matches the oracle."""
+    torch = torch_cuda
+    orc = oracle_mod
+    import dee_b200
+    layers, T = 2, 4
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, layers * E, seed=6060, kind="normal")
+    host = torch.from_numpy(recs).pin_memory()
+    pool = torch.empty((3 * K * T, recs.shape[1]), dtype=torch.uint8, device="cuda")
+    eng = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
+                                                    num_layers=layers, max_tokens=64))
+    eng.offload_attach(host, layers, pool, pool.shape[0])
+    rng = np.random.default_rng(6061)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    w = rng.random((T, K)).astype(np.float32)
+    w /= w.sum(axis=1, keepdims=True)
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    dids = torch.from_numpy(ids).cuda()
+    dw = torch.from_numpy(w).cuda()
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    layer = 1
+    eng.offload_debug_fail_next_copy()
+    with pytest.raises(dee_b200.DeeError, match="could not be queued"):
+        eng.offload_prepare_device(layer, dids.data_ptr(), T)
+    eng.moe_forward_device(layer, dx.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=dw.data_ptr(),
+                           d_out_ptr=out.data_ptr())
+    assert eng.sync_status() & (1 << 4)
+    cold = eng.offload_prepare_device(layer, dids.data_ptr(), T)
+    assert cold == 1  # only the expert whose copy failed
+    eng.moe_forward_device(layer, dx.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=dw.data_ptr(),
+                           d_out_ptr=out.data_ptr())
+    assert eng.sync_status() == 0
+    want = orc.combine_f32(orc.moe_layer_raw(recs[layer * E:(layer + 1) * E], layout, x16, ids), w)
+    assert orc.rel_l2(out.cpu().numpy(), want) <= 2e-3
