@@ -85,6 +85,44 @@ def lib() -> ctypes.CDLL:
     return _LIB
 
 
+_REF_CUDA = None
+
+
+def ref_cuda_lib() -> ctypes.CDLL | None:
+    """The reference's own GPU expert path (FP4 decode + cuBLAS SwiGLU,
+    oracle/ref_cuda_shim.cu), or None when oracle/_ref was not built with it."""
+    global _REF_CUDA
+    if _REF_CUDA is None:
+        path = os.path.join(_HERE, "_ref", "libdee_ref_cuda.so")
+        if not os.path.exists(path):
+            return None
+        L = ctypes.CDLL(path)
+        P = ctypes.c_void_p
+        L.dee_refcuda_moe_layer.restype = ctypes.c_int
+        L.dee_refcuda_moe_layer.argtypes = [P, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, P, ctypes.c_int, P, ctypes.c_float, P]
+        _REF_CUDA = L
+    return _REF_CUDA
+
+
+def ref_cuda_moe_layer_raw(d_records_ptr: int, record_bytes: int, experts: int, layout: "Layout",
+                           x_f16: np.ndarray, ids: np.ndarray, swiglu_limit: float = 0.0) -> np.ndarray:
+    """Raw FP32 [T, K, H] from the reference's own device path (records
+    already on the GPU at d_records_ptr)."""
+    L = ref_cuda_lib()
+    if L is None:
+        raise RuntimeError("oracle/_ref/libdee_ref_cuda.so not built")
+    x_f16 = np.ascontiguousarray(x_f16, dtype=np.uint16)
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    T, K = ids.shape
+    raw = np.zeros((T, K, layout.hidden), dtype=np.float32)
+    rc = L.dee_refcuda_moe_layer(ctypes.c_void_p(d_records_ptr), record_bytes, layout.hidden, layout.inter,
+                                 experts, K, _p(x_f16), T, _p(ids), swiglu_limit, _p(raw))
+    if rc != 0:
+        raise RuntimeError(f"reference device path failed ({rc})")
+    return raw
+
+
 def ref_lib() -> ctypes.CDLL | None:
     """The reference's own CPU code, or None when oracle/_ref was not built."""
     global _REF
