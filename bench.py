@@ -19,7 +19,11 @@ packs the selections by owner rank, exchanges rows with NCCL all-to-all,
 runs the grouped GEMMs over the rows it received, returns the FP32 rows and
 combines (dee_b200.ep).  Weak scaling: value = all ranks' tokens / the
 max-over-ranks time; the per-GPU weight traffic shrinks as the union of
-the N*b tokens' experts is spread over N GPUs.
+the N*b tokens' experts is spread over N GPUs.  Every line also carries a
+strong-scaling point ("strong_scaling": 64 tokens per step in total, 64/N
+per rank; at N=1 the b=64 decode point) and the sha256 of rank 0's route
+journal over 16 steps of its inputs, which are the same at every N, so the
+hash must not change with N.
 
 --impl reference times the reference's own CPU routed-expert executor
 (oracle/_ref, compiled from the reference sources) on the same workload.
@@ -315,6 +319,23 @@ def decode_point(torch, eng, b, n_steps, warmup, flush, stream, seed, profile=Tr
     if status:
         raise RuntimeError(f"device status {status:#x}: {eng.last_error_message()}")
     return times, uniq, stages
+
+
+def journal_point(torch, eng, b, n_steps, stream, seed, make_layer=None):
+    """sha256 of the route journal (the reference's JSONL format) of this
+    rank's first n_steps input batches, read back from the engine's device
+    journal after each step (the ids the path actually grouped by)."""
+    from dee_b200.stack import journal_bytes, sha256
+    xs, logits = make_inputs(torch, n_steps, b, seed)
+    layer = make_layer(b) if make_layer else Layer(torch, eng, b)
+    steps = []
+    for i in range(n_steps):
+        layer(xs[i], logits[i], stream)
+        stream.synchronize()
+        steps.append(eng.journal_ids(b))
+    import numpy as np
+    ids_all = np.stack(steps)[:, None, :, :]
+    return sha256(journal_bytes(ids_all, run_id="dee-b200-layer"))
 
 
 def layer_bytes(b, u):
@@ -766,18 +787,25 @@ def main():
         router = dee_b200.new_engine(dee_b200.EngineConfig(hidden=H, inter=I, num_experts=E, topk=K,
                                                            max_tokens=64, device_id=local))
         ep_cache = {}
+        extra_engines = []
         transport = args.ep
 
         def make_layer(bb):
             nonlocal transport
             if bb not in ep_cache:
-                if transport == "p2p" and bb != b:
-                    raise SystemExit("the peer path is set up for one batch size per engine")
                 ep = None
                 if transport == "p2p":
                     from dee_b200.ep import ExpertParallelPeer
+                    # the peer exchange blocks are sized for one batch: another
+                    # batch size gets its own engine over the same bank
+                    peer_eng = eng
+                    if ep_cache:
+                        peer_eng = dee_b200.new_engine(dee_b200.EngineConfig(
+                            hidden=H, inter=I, num_experts=epr, topk=K, max_tokens=64, device_id=local))
+                        peer_eng.attach_bank(0, bank)
+                        extra_engines.append(peer_eng)
                     try:
-                        ep = ExpertParallelPeer(torch, eng, rank, world, bb, H)
+                        ep = ExpertParallelPeer(torch, peer_eng, rank, world, bb, H)
                     except Exception as exc:  # no peer access: same layer over NCCL
                         print(f"rank {rank}: NVLink peer path unavailable ({exc}); using NCCL",
                               file=sys.stderr)
@@ -843,6 +871,11 @@ def main():
         "gpu_launches": int(round(per_step_launches * args.steps)),
         "gpu_launches_per_step": per_step_launches,
     }
+    gemm_ms = (stages or {}).get("gate_up", 0.0) + (stages or {}).get("down", 0.0)
+    result["split_ms"] = {"gemm": gemm_ms, "exchange_and_other": layer_ms - gemm_ms,
+                          "note": "gemm = gate/up + down stage events of a profiled pass; the rest of "
+                                  "ms_per_step is routing, grouping, the row exchange with its flag "
+                                  "waits, and the combine"}
     if world == 1 and b == 8 and E == 256:
         # ncu capture of this workload's gate/up launch (cold cache)
         tr = profiled_traffic("traffic_decode_b8.md", "gate_up")
@@ -860,6 +893,28 @@ def main():
         e_ms = float(t.item())
     result["e2e"] = {"value": world * b * args.steps / (e_ms / 1000.0), "unit": "tokens/s",
                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+
+    # ---- route journal of rank 0's inputs (identical at every N) ----
+    jh = journal_point(torch, eng, b, 16, stream, seed=1000 + rank, make_layer=make_layer)
+    if world > 1:
+        hs = [None] * world
+        dist.all_gather_object(hs, jh)
+        jh = hs[0]
+    result["route_journal_sha256"] = jh
+    result["route_journal"] = f"rank 0's {16} steps x {b} tokens (inputs seed 1000)"
+
+    # ---- strong scaling: 64 tokens per step over all ranks ----
+    if world > 1 and 64 % world == 0:
+        bb = 64 // world
+        st, _, _ = decode_point(torch, eng, bb, args.steps, args.warmup, flush, stream,
+                                seed=3064 + rank, profile=False, make_layer=make_layer)
+        s_ms = sum(st)
+        t = torch.tensor([s_ms], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        s_ms = float(t.item())
+        result["strong_scaling"] = {"total_tokens_per_step": 64, "tokens_per_rank": bb,
+                                    "value": 64 * args.steps / (s_ms / 1000.0), "unit": "tokens/s",
+                                    "ms_per_step": s_ms / args.steps}
 
     # ---- sweep: b = 1, 64 and the 4096-token prefill ----
     if not args.no_sweep and world == 1:
@@ -900,6 +955,10 @@ def main():
         except Exception as exc:  # the variant needs a driver that encodes unpacked-FP4 maps
             sweep["prefill_t4096_mxfp8"] = {"unavailable": str(exc)[:200]}
         result["sweep"] = sweep
+        if "decode_b64" in sweep:
+            result["strong_scaling"] = {"total_tokens_per_step": 64, "tokens_per_rank": 64,
+                                        "value": sweep["decode_b64"]["tokens_per_s"], "unit": "tokens/s",
+                                        "ms_per_step": sweep["decode_b64"]["ms"]}
 
     # ---- CPU baseline (rank 0, N=1): the reference executor on host cores ----
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

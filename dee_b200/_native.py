@@ -138,7 +138,7 @@ SIGNATURES = {
     "dee_sha256_hex": (I, [P, SZ, ctypes.c_char_p]),
 }
 
-STAGES = ("route", "permute", "gather", "gate_up", "down", "combine")
+STAGES = ("route", "permute", "gather", "gate_up", "down", "combine", "dispatch")
 
 _lib = None
 

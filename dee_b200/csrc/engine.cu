@@ -57,8 +57,10 @@ RecordLayout record_layout(int hidden, int inter) {
     return L;
 }
 
+// kStageDispatch: the expert-parallel send side (the peer rows kernel, or
+// the NCCL path's pack), recorded by the engine that owns the tokens.
 enum Stage : int { kStageRoute = 0, kStagePermute, kStageGather, kStageGateUp, kStageDown,
-                   kStageCombine, kStageCount };
+                   kStageCombine, kStageDispatch, kStageCount };
 
 struct Bank {
     bool attached = false;
@@ -911,11 +913,13 @@ int dee_ep_pack_device(dee_engine* e, const int32_t* d_ids, int tokens, const vo
     // rows forward does not regrow the workspace and drop the journal
     const size_t recv = static_cast<size_t>(ranks) * capacity;
     if ((rc = ensure_capacity(e, sel > recv ? sel : recv, stream)) != DEE_OK) return rc;
+    stage_begin(e, kStageDispatch, stream);
     cudaError_t err = launch_ep_pack(d_ids, static_cast<const __half*>(d_x_f16), tokens, e->cfg.topk,
                                      e->cfg.hidden, ranks, experts_per_rank, capacity,
                                      static_cast<__half*>(d_send_rows), d_send_expert, d_slot_of_pos,
                                      e->d_journal, e->d_status, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep pack launch");
+    stage_end(e, kStageDispatch, stream);
     e->launches += 2;
     e->h_ids_count = sel;
     e->journal_stream = stream;
@@ -942,9 +946,12 @@ int dee_ep_combine_device(dee_engine* e, const float* d_back, const int32_t* d_s
     e->last_error.clear();
     if (!d_back || !d_slot_of_pos || !d_weights || !d_out || tokens <= 0)
         return fail(e, DEE_ERR_INVALID, "invalid ep_combine arguments");
+    const auto stream = static_cast<cudaStream_t>(stream_v);
+    stage_begin(e, kStageCombine, stream);
     cudaError_t err = launch_ep_combine(d_back, d_slot_of_pos, d_weights, tokens, e->cfg.topk,
-                                        e->cfg.hidden, d_out, static_cast<cudaStream_t>(stream_v));
+                                        e->cfg.hidden, d_out, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
+    stage_end(e, kStageCombine, stream);
     e->launches += 1;
     return DEE_OK;
 }
@@ -1123,11 +1130,13 @@ int dee_ep_p2p_dispatch_device(dee_engine* e, const void* d_x_f16, const int32_t
     const size_t recv = static_cast<size_t>(p.ranks) * p.capacity;
     if ((rc = ensure_capacity(e, sel > recv ? sel : recv, stream)) != DEE_OK) return rc;
     ++p.epoch;
+    stage_begin(e, kStageDispatch, stream);
     cudaError_t err = launch_ep_peer_dispatch(d_ids, static_cast<const __half*>(d_x_f16), p.tokens,
                                               e->cfg.topk, e->cfg.hidden, p.ranks, p.rank,
                                               e->cfg.num_experts, p.capacity, p.peers, p.d_slot_of_pos,
                                               e->d_journal, e->d_status, p.d_done, p.epoch, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep peer dispatch launch");
+    stage_end(e, kStageDispatch, stream);
     e->launches += 2;
     e->h_ids_count = sel;
     e->journal_stream = stream;
@@ -1162,11 +1171,13 @@ int dee_ep_p2p_combine_device(dee_engine* e, const float* d_weights, float* d_ou
     if (!p.connected || p.epoch == 0 || !d_weights || !d_out_f32)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_combine needs a dispatched layer, weights and out");
     // every combine CTA waits (bounded) for every owner's return flag
+    stage_begin(e, kStageCombine, stream);
     const cudaError_t err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
                                               e->cfg.topk, e->cfg.hidden, d_out_f32, stream,
                                               p.peers.back_flag[p.rank], p.ranks, p.epoch, e->d_status,
                                               e->wait_limit_ns);
     if (err != cudaSuccess) return cuda_fail(e, err, "ep combine launch");
+    stage_end(e, kStageCombine, stream);
     e->launches += 1;
     return DEE_OK;
 }

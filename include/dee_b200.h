@@ -405,7 +405,8 @@ DEE_API uint64_t dee_engine_launch_count(const dee_engine* engine);
  * (dee.cpp/include/dee/profiling.h:31-46, GpuStage): when enabled every
  * stage of a forward is bracketed by CUDA events on its launch stream.
  * Stages: 0 route, 1 permute, 2 gather, 3 gate/up GEMM, 4 down GEMM,
- * 5 combine. */
+ * 5 combine, 6 expert-parallel dispatch (the peer rows kernel or the pack
+ * before an NCCL exchange). */
 DEE_API int dee_engine_set_profiling(dee_engine* engine, int enable);
 
 /* Milliseconds of each stage of the most recent profiled forward (-1 for a
