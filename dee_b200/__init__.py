@@ -188,6 +188,18 @@ class Engine:
             ctypes.c_void_p(_stream_handle(stream)))
         self._check(rc, "dee_route_dsv4_device")
 
+    def moe_forward_routed_device(self, layer: int, d_x_ptr: int, tokens: int, d_logits_ptr: int, d_ids_ptr: int,
+                                  d_weights_ptr: int, *, d_out_ptr: int = 0, d_raw_ptr: int = 0,
+                                  stream=None) -> None:
+        """Route (softmax top-k of device logits [T, E] into d_ids / d_weights)
+        and run the layer in one call; decode-sized batches route inside the
+        grouping kernel."""
+        rc = self._lib.dee_moe_forward_routed_device(
+            self._h, layer, ctypes.c_void_p(d_x_ptr), tokens, ctypes.c_void_p(d_logits_ptr),
+            ctypes.c_void_p(d_ids_ptr), ctypes.c_void_p(d_weights_ptr), ctypes.c_void_p(d_out_ptr or 0),
+            ctypes.c_void_p(d_raw_ptr or 0), ctypes.c_void_p(_stream_handle(stream)))
+        self._check(rc, "dee_moe_forward_routed_device")
+
     def moe_forward_device(self, layer: int, d_x_ptr: int, tokens: int, *, d_ids_ptr: int = 0,
                            h_ids: np.ndarray | None = None, d_weights_ptr: int = 0,
                            d_out_ptr: int = 0, d_raw_ptr: int = 0, stream=None) -> None:

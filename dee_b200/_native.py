@@ -86,6 +86,7 @@ SIGNATURES = {
     "dee_moe_forward_batch_device": (I, [P, I, P, I, P, I, P]),
     "dee_moe_forward_combined_device": (I, [P, I, P, I, P, I, P, P, P, P]),
     "dee_moe_forward_device": (I, [P, I, P, I, P, P, I, P, P, P, P]),
+    "dee_moe_forward_routed_device": (I, [P, I, P, I, P, P, P, P, P, P]),
     "dee_shared_expert_attach": (I, [P, I, P, P, P, P, P, P, I]),
     "dee_moe_forward_official_device": (I, [P, I, P, I, P, P, P, P, P]),
     "dee_ep_pack_device": (I, [P, P, I, P, I, I, I, P, P, P, P]),
@@ -138,7 +139,7 @@ SIGNATURES = {
     "dee_sha256_hex": (I, [P, SZ, ctypes.c_char_p]),
 }
 
-STAGES = ("route", "permute", "gather", "gate_up", "down", "combine", "dispatch")
+STAGES = ("route", "permute", "gather", "gate_up", "down", "combine", "dispatch", "experts")
 
 _lib = None
 

@@ -59,8 +59,10 @@ RecordLayout record_layout(int hidden, int inter) {
 
 // kStageDispatch: the expert-parallel send side (the peer rows kernel, or
 // the NCCL path's pack), recorded by the engine that owns the tokens.
+// kStageExperts: the one-launch decode layer (gate/up, down and, for the
+// live path, the combine in one kernel).
 enum Stage : int { kStageRoute = 0, kStagePermute, kStageGather, kStageGateUp, kStageDown,
-                   kStageCombine, kStageDispatch, kStageCount };
+                   kStageCombine, kStageDispatch, kStageExperts, kStageCount };
 
 struct Bank {
     bool attached = false;
@@ -203,6 +205,9 @@ struct dee_engine {
     int32_t* d_journal = nullptr;  // ids consumed by the latest forward (written by permute)
     int32_t* d_perm_chunks = nullptr;  // multi-CTA permutation: per-chunk expert counts
     int32_t* d_perm_lrank = nullptr;   // multi-CTA permutation: rank within the chunk
+    // one-launch decode layer: [max_tiles] gate/up items done per tile, then
+    // [kDecodeMaxSelections * H/128] rows written per (token, feature block)
+    uint32_t* d_sync = nullptr;
     // shared-expert workspaces, capacity in tokens
     // MXFP8 path workspaces (E4M3 rows and per-32 UE8M0 scales), capacity in rows
     size_t cap_mx = 0;
@@ -277,8 +282,8 @@ void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
     cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
-    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank);
-    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr;
+    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank); cudaFree(e->d_sync);
+    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr; e->d_sync = nullptr;
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
@@ -313,6 +318,8 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_chunks, ((cap + 1023) / 1024) * static_cast<size_t>(E))) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_lrank, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_sync, static_cast<size_t>(max_tiles) +
+                                         static_cast<size_t>(kDecodeMaxSelections) * (H / 128))) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
                              cudaHostAllocDefault)) != cudaSuccess) {
         free_workspace(e);
@@ -372,10 +379,26 @@ struct EpWait {
     uint64_t limit_ns;
 };
 
+// Routing fused into the permutation (decode-sized batches): the router
+// reads logits and writes the ids run_experts groups by, and the weights.
+struct FusedRoute {
+    const float* logits;
+    float* weights;
+};
+
+// The live combine fused into the decode layer launch: out[t] = sum_r
+// weights[t*K + r] * raw[t*K + r] (run_experts reports whether it ran it).
+struct FusedCombine {
+    const float* weights;
+    float* out;
+    bool* done;
+};
+
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
                 const EpReturn* ret = nullptr, const float* official_route_w = nullptr,
-                const EpWait* wait = nullptr) {
+                const EpWait* wait = nullptr, const FusedRoute* route = nullptr,
+                const FusedCombine* combine = nullptr) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
@@ -400,11 +423,25 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
         po.wait_epoch = wait->epoch;
         po.wait_limit_ns = wait->limit_ns;
     }
+    // the decode layer runs in one launch; its counters are zeroed by the
+    // (one-CTA) permutation
+    const bool fuse_combine = decode && combine && !ret && !official_route_w;
+    if (combine) *combine->done = fuse_combine;
+    if (decode) {
+        po.clear = e->d_sync;
+        po.clear_n = e->max_tiles + (fuse_combine ? tokens * (H / 128) : 0);
+    }
     stage_begin(e, kStagePermute, stream);
-    cudaError_t err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status,
-                                     stream, skip_negative);
-    if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
-    e->launches += permute_launch_count(tokens, K, po) - 1;
+    cudaError_t err;
+    if (route) {
+        err = launch_route_permute(route->logits, tokens, E, K, const_cast<int32_t*>(d_ids32), route->weights,
+                                   n_max, e->max_tiles, po, e->d_status, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "route+permute launch");
+    } else {
+        err = launch_permute(d_ids32, tokens, K, E, n_max, e->max_tiles, po, e->d_status, stream, skip_negative);
+        if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
+        e->launches += permute_launch_count(tokens, K, po) - 1;
+    }
     stage_end(e, kStagePermute, stream);
     stage_begin(e, kStageGather, stream);
     err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H,
@@ -438,34 +475,41 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
         a.ep_rank = ret->rank;
     }
 
-    GemmMaps gm{};
     if (decode) {
-        gm = bank.dec_gu;
-        gm.b = e->map_xperm_dec;
-    } else {
+        GemmMaps gu = bank.dec_gu, dn = bank.dec_dn;
+        gu.b = e->map_xperm_dec;
+        dn.b = e->map_act_dec;
+        a.tile_done = e->d_sync;
+        if (fuse_combine) {
+            a.comb_w = combine->weights;
+            a.comb_out = combine->out;
+            a.comb_cnt = e->d_sync + e->max_tiles;
+        }
+        stage_begin(e, kStageExperts, stream);
+        err = launch_moe_decode_layer(gu, dn, a, e->num_sms, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "decode layer launch");
+        stage_end(e, kStageExperts, stream);
+        e->launches += 3;
+        return DEE_OK;
+    }
+    GemmMaps gm{};
+    {
         gm.w0 = bank.w1; gm.w1 = bank.w3; gm.s0 = bank.s1; gm.s1 = bank.s3;
         for (int i = 0; i < 4; ++i) gm.bt[i] = e->map_xperm_t[i];
     }
     a.k_total = H;
     a.m_tiles = I / 64;
     stage_begin(e, kStageGateUp, stream);
-    err = decode ? launch_moe_decode(true, gm, a, e->num_sms, stream)
-                 : launch_moe_gemm(true, gm, a, e->num_sms, stream);
+    err = launch_moe_gemm(true, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gate/up GEMM launch");
     stage_end(e, kStageGateUp, stream);
 
-    if (decode) {
-        gm = bank.dec_dn;
-        gm.b = e->map_act_dec;
-    } else {
-        gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
-        for (int i = 0; i < 4; ++i) gm.bt[i] = e->map_act_t[i];
-    }
+    gm.w0 = bank.w2; gm.w1 = bank.w2; gm.s0 = bank.s2; gm.s1 = bank.s2;
+    for (int i = 0; i < 4; ++i) gm.bt[i] = e->map_act_t[i];
     a.k_total = I;
     a.m_tiles = H / 128;
     stage_begin(e, kStageDown, stream);
-    err = decode ? launch_moe_decode(false, gm, a, e->num_sms, stream)
-                 : launch_moe_gemm(false, gm, a, e->num_sms, stream);
+    err = launch_moe_gemm(false, gm, a, e->num_sms, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "down GEMM launch");
     stage_end(e, kStageDown, stream);
     e->launches += 4;
@@ -808,12 +852,47 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     }
     e->h_ids_count = sel;
     float* raw = d_raw ? d_raw : e->d_raw;
+    bool combined = false;
+    const FusedCombine fc{d_weights, d_out_f32, &combined};
     if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, ids32, raw,
-                          stream, topk, false, true)) != DEE_OK)
+                          stream, topk, false, true, nullptr, nullptr, nullptr, nullptr,
+                          d_out_f32 ? &fc : nullptr)) != DEE_OK)
         return rc;
-    if (d_out_f32) {
+    if (d_out_f32 && !combined) {
         stage_begin(e, kStageCombine, stream);
         err = launch_combine_f32(raw, d_weights, tokens, topk, e->cfg.hidden, d_out_f32, stream);
+        if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
+        stage_end(e, kStageCombine, stream);
+        e->launches += 1;
+    }
+    e->journal_stream = stream;
+    return DEE_OK;
+}
+
+int dee_moe_forward_routed_device(dee_engine* e, int layer, const void* d_x_f16, int tokens, const float* d_logits,
+                                  int32_t* d_ids, float* d_weights, float* d_out_f32, float* d_raw, void* stream_v) {
+    int rc = check_engine(e);
+    if (rc != DEE_OK) return rc;
+    e->last_error.clear();
+    auto stream = static_cast<cudaStream_t>(stream_v);
+    if (!d_x_f16 || !d_logits || !d_ids || !d_weights || tokens <= 0 || (!d_out_f32 && !d_raw))
+        return fail(e, DEE_ERR_INVALID, "invalid moe_forward_routed_device arguments");
+    const int K = e->cfg.topk;
+    const size_t sel = static_cast<size_t>(tokens) * K;
+    if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    const bool fuse = route_permute_fits(tokens, K, e->cfg.num_experts);
+    if (!fuse && (rc = dee_route_topk_device(e, d_logits, tokens, d_ids, d_weights, stream)) != DEE_OK) return rc;
+    e->h_ids_count = sel;
+    float* raw = d_raw ? d_raw : e->d_raw;
+    const FusedRoute fr{d_logits, d_weights};
+    bool combined = false;
+    const FusedCombine fc{d_weights, d_out_f32, &combined};
+    if ((rc = run_experts(e, layer, static_cast<const __half*>(d_x_f16), tokens, d_ids, raw, stream, K, false, true,
+                          nullptr, nullptr, nullptr, fuse ? &fr : nullptr, d_out_f32 ? &fc : nullptr)) != DEE_OK)
+        return rc;
+    if (d_out_f32 && !combined) {
+        stage_begin(e, kStageCombine, stream);
+        const cudaError_t err = launch_combine_f32(raw, d_weights, tokens, K, e->cfg.hidden, d_out_f32, stream);
         if (err != cudaSuccess) return cuda_fail(e, err, "combine launch");
         stage_end(e, kStageCombine, stream);
         e->launches += 1;

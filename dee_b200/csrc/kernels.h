@@ -76,6 +76,12 @@ constexpr int kDecodeMaxTokens = 64;
 constexpr int kDecodeMaxSelections = 384;  // selections (rows) the decode kernel takes
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream);
+// Both projections in one persistent launch: the gate/up items of every tile,
+// then the down items (each waits, bounded, for its tile's gate/up items),
+// and, with args.comb_out, the fused rank-order combine.  args.tile_done and
+// (with comb_out) args.comb_cnt must have been zeroed by the permutation.
+cudaError_t launch_moe_decode_layer(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args, int grid,
+                                    cudaStream_t stream);
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -216,6 +222,10 @@ struct PermuteOut {
     int wait_ranks = 0;
     uint32_t wait_epoch = 0;
     uint64_t wait_limit_ns = 0;
+    // Counters of the one-launch decode layer, zeroed before grouping
+    // (one-CTA permutation only).
+    uint32_t* clear = nullptr;
+    int clear_n = 0;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.
@@ -225,6 +235,17 @@ int permute_launch_count(int tokens, int topk, const PermuteOut& out);
 cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
                            int max_tiles, const PermuteOut& out, uint32_t* status,
                            cudaStream_t stream, bool skip_negative = false);
+
+// Softmax top-k routing and the permutation in one single-CTA launch, for
+// batches route_permute_fits accepts (T*K <= kDecodeMaxSelections, E <= 256):
+// the same ids, weights and grouping as launch_route_topk + launch_permute.
+inline bool route_permute_fits(int tokens, int topk, int experts) {
+    return tokens > 0 && topk > 0 && topk <= experts && experts <= 256 &&
+           static_cast<long long>(tokens) * topk <= kDecodeMaxSelections;
+}
+cudaError_t launch_route_permute(const float* logits, int tokens, int experts, int topk, int32_t* ids,
+                                 float* weights, int n_tile_max, int max_tiles, const PermuteOut& out,
+                                 uint32_t* status, cudaStream_t stream);
 
 // X_perm[row] = X[perm[row] / topk] (FP16 rows of H elements).
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,

@@ -40,12 +40,14 @@ using namespace sm100;
 
 constexpr int kDecConsumerWarps = 16;
 constexpr int kDecCheckerWarp = 1 + kDecConsumerWarps;
-constexpr int kDecThreads = 32 * (kDecCheckerWarp + 1);  // producer, 8 pairs of consumers, checker
+constexpr int kDecSignalWarp = kDecCheckerWarp + 1;
+constexpr int kDecDepWarp = kDecSignalWarp + 1;
+constexpr int kDecThreads = 32 * (kDecDepWarp + 1);  // producer, 8 pairs of consumers, checker, signal, dependency
 constexpr int kDecMaxStages = 4;
 constexpr int kDecPkBytes = 32768;         // 128 rows x 256 packed bytes (K = 512)
 constexpr int kDecBBytes = 8 * 1024;       // 8 token rows x 512 FP16 (8 boxes of 8 x 128 B)
 constexpr int kDecStageBytes = kDecPkBytes + kDecBBytes;
-constexpr int kDecBarBytes = 256;  // stage and scale-slot barriers, per-slot flags and item records
+constexpr int kDecBarBytes = 256;  // stage, scale-slot and signal barriers, per-slot flags and item records
 constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
 constexpr uint32_t kSmemLimit = 232448;
 constexpr int kDecScSlots = 3;  // per-item scale rows: the consumed item, the next, the one after
@@ -135,23 +137,59 @@ __device__ __forceinline__ uint32_t scale_bytes_exact(uint32_t w) {
     return y & ~z & 0x80808080u;
 }
 
-struct DecItem {
-    int m;
-    TileDesc td;
-    int slot;
-    bool valid;
+// The tensor maps of both projections.  A one-projection launch fills the
+// other projection's maps with copies it never uses.
+struct DecMaps {
+    CUtensorMap gw1, gw3, gx, gs1, gs3;  // gate/up: W1 and W3 rows, token rows, scale rows
+    CUtensorMap dw2, dact, ds2;          // down: W2 rows, SwiGLU rows, scale rows
 };
 
-__device__ __forceinline__ TileDesc load_tile(const GemmArgs& a, int item) {
-    return a.tiles[item / a.m_tiles];
+// The launch's work list: the gate/up items of every tile (tile-major, I/64
+// per tile), then the down items (tile-major, H/128 per tile), either part
+// empty when its phase bit is clear.
+struct DecPlan {
+    int n_gu, n_items, mg, md;
+};
+
+__device__ __forceinline__ DecPlan dec_plan(const GemmArgs& a) {
+    DecPlan p;
+    const int nt = *a.n_tiles;
+    p.mg = a.inter / 64;
+    p.md = a.hidden / 128;
+    p.n_gu = (a.phases & 1) ? nt * p.mg : 0;
+    p.n_items = p.n_gu + ((a.phases & 2) ? nt * p.md : 0);
+    return p;
+}
+
+// The layout's K: the longer reduction of the phases the launch runs.
+__host__ __device__ inline int dec_layout_k(const GemmArgs& a) {
+    int k = 0;
+    if (a.phases & 1) k = a.hidden;
+    if ((a.phases & 2) && a.inter > k) k = a.inter;
+    return k;
+}
+
+struct DecItem {
+    int m, tile;
+    TileDesc td;
+    int slot;
+    bool valid, gu;
+};
+
+__device__ __forceinline__ TileDesc load_tile(const GemmArgs& a, const DecPlan& p, int item) {
+    return item < p.n_gu ? a.tiles[item / p.mg] : a.tiles[(item - p.n_gu) / p.md];
 }
 
 // Completes an item from its tile descriptor: the expert's record slot and
 // whether the item can run (an expert id that is out of range or not
 // resident leaves the item's outputs unwritten and raises kStatusBadExpert).
-__device__ __forceinline__ DecItem finish_item(const GemmArgs& a, int item, const TileDesc& td) {
+__device__ __forceinline__ DecItem finish_item(const GemmArgs& a, const DecPlan& p, int item, const TileDesc& td) {
     DecItem d;
-    d.m = item % a.m_tiles;
+    d.gu = item < p.n_gu;
+    const int j = d.gu ? item : item - p.n_gu;
+    const int mt = d.gu ? p.mg : p.md;
+    d.tile = j / mt;
+    d.m = j - d.tile * mt;
     d.td = td;
     const int e = td.expert;
     int slot = -1;
@@ -167,199 +205,68 @@ struct ItemRec {
     int m, row_start, n_rows, valid;
 };
 
-template <GemmMode MODE, bool kOfficial>
-__global__ void __launch_bounds__(kDecThreads, 1)
-    moe_decode_kernel(const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1,
-                      const __grid_constant__ CUtensorMap map_b, const __grid_constant__ CUtensorMap map_s0,
-                      const __grid_constant__ CUtensorMap map_s1, const GemmArgs args) {
-    constexpr bool kGU = MODE == GemmMode::kGateUp;
-    // The tile list comes from the permutation kernel, which has completed
-    // whenever this kernel runs: its predecessor (gather or gate/up) only
-    // signals its dependents after its own griddepcontrol.wait.  Everything
-    // that reads weights or the tile list may therefore start before this
-    // kernel's wait; only the token rows (the predecessor's output) wait.
-    const int n_items = *args.n_tiles * args.m_tiles;
-    if (static_cast<int>(blockIdx.x) >= n_items) {
-        pdl_wait();
-        pdl_trigger();
-        return;
-    }
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~static_cast<uintptr_t>(1023));
-    const DecLayout L = dec_layout(args.k_total);
-    const int n_stages = L.stages;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [stages] TMA landed
-    uint64_t* empty = full + kDecMaxStages;                             // [stages] consumers done
-    uint64_t* sfull = empty + kDecMaxStages;      // [slots] scale rows landed
-    uint64_t* sready = sfull + kDecScSlots;        // [slots] scale rows checked
-    uint64_t* sempty = sready + kDecScSlots;       // [slots] item consumed
-    volatile int* fast_flag = reinterpret_cast<volatile int*>(sempty + kDecScSlots);  // [slots]
-    volatile ItemRec* item_rec = reinterpret_cast<volatile ItemRec*>(smem + L.bar_off + 160);  // [slots]
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < n_stages; ++i) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kDecConsumerWarps);
+// Bounded wait (gpu-scope acquire) for *p >= target; false and `code` in
+// *status when the limit expires.
+__device__ __forceinline__ bool wait_count_geq(const uint32_t* p, uint32_t target, uint32_t* status,
+                                               uint32_t code) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        uint32_t v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+        if (v >= target) return true;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicOr(status, code);
+            return false;
         }
-        for (int i = 0; i < kDecScSlots; ++i) {
-            mbar_init(&sfull[i], 1);
-            mbar_init(&sready[i], 1);
-            mbar_init(&sempty[i], kDecConsumerWarps);
-        }
-        fence_barrier_init();
+        __nanosleep(128);
     }
-    if (warp == 0 && lane == 0) {
-        prefetch_tmap(&map_w0);
-        prefetch_tmap(&map_b);
-        if (kGU) prefetch_tmap(&map_w1);
-        if (args.scale_swz) {
-            prefetch_tmap(&map_s0);
-            if (kGU) prefetch_tmap(&map_s1);
+}
+
+// Bounded wait (cta-scope acquire) for the shared word *p >= target.
+__device__ __forceinline__ bool wait_smem_geq(const uint32_t* p, uint32_t target, uint32_t* status,
+                                              uint32_t code) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+    if (v >= target) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        __nanosleep(64);
+        asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+        if (v >= target) return true;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicOr(status, code);
+            return false;
         }
     }
-    __syncthreads();
-    if (warp != 0) pdl_wait();
-    pdl_trigger();
-    const int k_stages = args.k_total / kKStage;
-    const uint32_t rb = static_cast<uint32_t>(args.k_total / 32);  // scale bytes per weight row
-    const uint32_t sc_item = 128 * rb;                              // scale bytes per item
+}
+
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Shared-memory handles of the consumers.
+struct DecSmem {
+    uint8_t* smem;
+    uint32_t base;
+    uint64_t *full, *empty, *sready, *sempty, *stored, *sfree;
+    volatile int* fast_flag;
+    volatile ItemRec* item_rec;
+    float* red;
+    int* red_ok;
+};
+
+// One work item of one consumer warp: the K stages, the pair reduction and
+// (first warp of the pair) the epilogue; with `signal`, the first warps then
+// hand the item to the signal warp.  Returns false when a wait gave up.
+template <bool kGU, bool kOfficial>
+__device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayout& L, const DecSmem& S, int li,
+                                             int& st, uint32_t& ph, int& parity, int n_stages, bool signal,
+                                             int warp, int lane) {
     uint32_t* status = args.status;
-    const uint32_t smem_base = smem_u32(smem);
-
-    if (warp == 0) {
-        // ---------------- producer ----------------
-        if (lane != 0) return;
-        const uint64_t pol_w = policy_evict_first();
-        const uint64_t pol_b = policy_evict_last();
-        const size_t ih = static_cast<size_t>(args.hidden) * args.inter;
-        const size_t off_s1 = ih + ih / 2, off_s3 = off_s1 + ih / 32, off_s2 = off_s3 + ih / 32;
-        // Scale rows of one item are contiguous in the record: one copy per
-        // projection into the item's slot, after the item's record for the
-        // consumers.  With scale maps (rows of 32, 64 or 128 bytes) the copy
-        // is a tensor load whose swizzle span is the row length, so the
-        // 16-byte chunk j of row r lands at chunk j ^ f(r) and the
-        // consumers' per-stage reads of eight rows hit distinct banks;
-        // otherwise a plain bulk copy.
-        auto issue_scales = [&](const DecItem& d, int li) -> bool {
-            const int slot = li % kDecScSlots;
-            if (!mbar_wait(&sempty[slot], ((li / kDecScSlots) & 1) ^ 1, status, kStatusTimeoutTma))
-                return false;
-            item_rec[slot].m = d.m;
-            item_rec[slot].row_start = d.td.row_start;
-            item_rec[slot].n_rows = d.td.n_rows;
-            item_rec[slot].valid = d.valid ? 1 : 0;
-            mbar_arrive_expect_tx(&sfull[slot], sc_item);
-            uint8_t* dst = smem + L.sc_off + slot * L.sc_slot;
-            const uint8_t* rec = args.records + static_cast<size_t>(d.slot) * args.record_bytes;
-            if (args.scale_swz) {
-                if (kGU) {
-                    tma_load_3d(dst, &map_s0, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
-                    tma_load_3d(dst + 64 * rb, &map_s1, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
-                } else {
-                    tma_load_3d(dst, &map_s0, &sfull[slot], 0, d.m * 128, d.slot, pol_w);
-                }
-            } else if (kGU) {
-                const size_t r0 = static_cast<size_t>(d.m) * 64 * rb;
-                bulk_load(dst, rec + off_s1 + r0, 64 * rb, &sfull[slot]);
-                bulk_load(dst + 64 * rb, rec + off_s3 + r0, 64 * rb, &sfull[slot]);
-            } else {
-                bulk_load(dst, rec + off_s2 + static_cast<size_t>(d.m) * 128 * rb, 128 * rb, &sfull[slot]);
-            }
-            return true;
-        };
-        // weights: {128 B, rows, two 128-byte K chunks, slot} per projection;
-        // tokens: {64, 8 rows, eight 64-wide K chunks}
-        auto issue_weights = [&](const DecItem& d, int s, int st) {
-            uint8_t* pk = smem + st * kDecStageBytes;
-            if (kGU) {
-                tma_load_4d(pk, &map_w0, &full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
-                tma_load_4d(pk + 16384, &map_w1, &full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
-            } else {
-                tma_load_4d(pk, &map_w0, &full[st], 0, d.m * 128, 2 * s, d.slot, pol_w);
-            }
-        };
-        auto issue_tokens = [&](const DecItem& d, int s, int st) {
-            tma_load_3d(smem + st * kDecStageBytes + kDecPkBytes, &map_b, &full[st], 0, d.td.row_start,
-                        8 * s, pol_b);
-        };
-        // The next item's scale rows are issued when an item starts, so they
-        // have a whole item's worth of stage traffic to land behind.  Item
-        // metadata is pipelined so that no dependent global load sits on the
-        // issue path: while item li is issued, the slot of item li+2 and the
-        // tile descriptor of item li+3 are in flight.
-        const int G = gridDim.x;
-        int item = blockIdx.x;
-        DecItem cur = finish_item(args, item, load_tile(args, item));
-        DecItem n1{};
-        if (item + G < n_items) n1 = finish_item(args, item + G, load_tile(args, item + G));
-        TileDesc td2{};
-        if (item + 2 * G < n_items) td2 = load_tile(args, item + 2 * G);
-        // Before the wait: the first two items' scale rows and the weights of
-        // the first ring's worth of stages.
-        if (!issue_scales(cur, 0)) return;
-        if (item + G < n_items && !issue_scales(n1, 1)) return;
-        const int pre = n_stages < k_stages ? n_stages : k_stages;
-        for (int s = 0; s < pre; ++s) {  // first use of ring slots 0..pre-1
-            mbar_arrive_expect_tx(&full[s], kDecStageBytes);
-            issue_weights(cur, s, s);
-        }
-        pdl_wait();
-        int st = 0;
-        uint32_t ph = 0;
-        for (int li = 0; item < n_items; item += G, ++li) {
-            if (li > 0 && item + G < n_items && !issue_scales(n1, li + 1)) return;
-            DecItem n2{};
-            if (item + 2 * G < n_items) n2 = finish_item(args, item + 2 * G, td2);
-            if (item + 3 * G < n_items) td2 = load_tile(args, item + 3 * G);
-            if (!cur.valid) atomicOr(status, kStatusBadExpert);
-            for (int s = 0; s < k_stages; ++s) {
-                if (li > 0 || s >= pre) {
-                    if (!mbar_wait(&empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
-                    mbar_arrive_expect_tx(&full[st], kDecStageBytes);
-                    issue_weights(cur, s, st);
-                }
-                issue_tokens(cur, s, st);
-                if (++st == n_stages) { st = 0; ph ^= 1; }
-            }
-            cur = n1;
-            n1 = n2;
-        }
-        return;
-    }
-
-    if (warp == kDecCheckerWarp) {
-        // ---------------- scale checker ----------------
-        // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
-        // finite binary16, so scaling a block's FP32 partial sum equals
-        // summing the reference's FP16-rounded weights.  Byte 103 rounds
-        // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.  The
-        // checker reads each item's scale rows once and publishes whether all
-        // of them are in range; the consumers start the item after that.
-        int li = 0;
-        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
-            const int slot = li % kDecScSlots;
-            const bool ok = mbar_wait(&sfull[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
-            if (!__all_sync(0xffffffffu, ok)) return;
-            const uint32_t sc = smem_base + L.sc_off + slot * L.sc_slot;
-            uint32_t acc = 0x80808080u;
-#pragma unroll 4
-            for (uint32_t i = lane; i < sc_item / 16; i += 32) {
-                const uint4 v = lds_v4(sc + i * 16);
-                acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
-                       scale_bytes_exact(v.w);
-            }
-            const bool fast = __all_sync(0xffffffffu, acc == 0x80808080u);
-            if (lane == 0) {
-                fast_flag[slot] = fast ? 1 : 0;
-                mbar_arrive(&sready[slot]);
-            }
-        }
-        return;
-    }
-
-    // ---------------- consumers ----------------
+    const int k_total = kGU ? args.hidden : args.inter;
+    const int k_stages = k_total / kKStage;
+    const uint32_t rb = static_cast<uint32_t>(k_total / 32);  // scale bytes per weight row
+    const int swz = kGU ? args.scale_swz : args.dn_scale_swz;
     // K inside each 32-wide scale block is assigned so that thread q owns
     // packed bytes 4q..4q+3 (K 8q..8q+7): its A fragments come from one
     // 32-bit word per row and its token fragments for both k16 steps from
@@ -391,107 +298,103 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // placed them; the hi row, 64 or 8 rows on, has the same sw)
     const uint32_t s_off = L.sc_off + row_lo * rb + kh * 8;
     const uint32_t s_hi = kHiRows * rb;
-    const uint32_t s_sw = args.scale_swz ? ((row_lo * rb) >> 7) & (rb / 16 - 1) : 0u;
-    float* red = reinterpret_cast<float*>(smem + L.red_off);
-    int* red_ok = reinterpret_cast<int*>(red + 2 * 8 * 32 * 4);
-    int st = 0, parity = 0, li = 0;
-    uint32_t ph = 0;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
-        const int slot = li % kDecScSlots;
-        float c[4] = {0.f, 0.f, 0.f, 0.f};
-        bool ok = mbar_wait(&sready[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
-        ok = __all_sync(0xffffffffu, ok);
-        // official semantics dequantise in FP32: the scaled FP32 partial sum
-        // is exact for every scale byte
-        const bool fast = ok && (kOfficial || fast_flag[slot] != 0);
-        const int it_m = item_rec[slot].m;
-        const int it_row_start = item_rec[slot].row_start;
-        const int it_n_rows = item_rec[slot].n_rows;
-        const bool it_valid = item_rec[slot].valid != 0;
-        const uint32_t sc_base = smem_base + s_off + slot * L.sc_slot;
-        for (int s = 0; s < k_stages && ok; ++s) {
-            ok = mbar_wait(&full[st], ph, status, kStatusTimeoutDequant);
-            if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-            const uint32_t sb = smem_base + st * kDecStageBytes;
-            const uint32_t s_chunk = (static_cast<uint32_t>(s) ^ s_sw) << 4;
-            const uint2 slo = lds_v2(sc_base + s_chunk);
-            const uint2 shi = lds_v2(sc_base + s_chunk + s_hi);
-            const uint32_t wb = sb + w_off;
-            const uint32_t bb0 = sb + b_off0, bb1 = sb + b_off1;
-            if (fast) {
+    const uint32_t s_sw = swz ? ((row_lo * rb) >> 7) & (rb / 16 - 1) : 0u;
+
+    const int slot = li % kDecScSlots;
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = mbar_wait(&S.sready[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
+    ok = __all_sync(0xffffffffu, ok);
+    // official semantics dequantise in FP32: the scaled FP32 partial sum
+    // is exact for every scale byte
+    const bool fast = ok && (kOfficial || S.fast_flag[slot] != 0);
+    const int it_m = S.item_rec[slot].m;
+    const int it_row_start = S.item_rec[slot].row_start;
+    const int it_n_rows = S.item_rec[slot].n_rows;
+    const bool it_valid = S.item_rec[slot].valid != 0;
+    const uint32_t sc_base = S.base + s_off + slot * L.sc_slot;
+    for (int s = 0; s < k_stages && ok; ++s) {
+        ok = mbar_wait(&S.full[st], ph, status, kStatusTimeoutDequant);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        const uint32_t sb = S.base + st * kDecStageBytes;
+        const uint32_t s_chunk = (static_cast<uint32_t>(s) ^ s_sw) << 4;
+        const uint2 slo = lds_v2(sc_base + s_chunk);
+        const uint2 shi = lds_v2(sc_base + s_chunk + s_hi);
+        const uint32_t wb = sb + w_off;
+        const uint32_t bb0 = sb + b_off0, bb1 = sb + b_off1;
+        if (fast) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
-                    const uint32_t wlo = lds_u32(wa);
-                    const uint32_t whi = lds_u32(wa + kHi);
-                    const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
-                    uint32_t a[8];  // [lo b0..b3, hi b0..b3] as f16x2
-                    cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
-                    cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
-                    float t[4];
-                    mma_16816_zero(t, a[0], a[4], a[1], a[5], bv.x, bv.y);
-                    mma_16816_acc(t, a[2], a[6], a[3], a[7], bv.z, bv.w);
-                    const uint32_t sl = ((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu;
-                    const uint32_t sh = ((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu;
-                    const float flo = kOfficial ? e8m0_value(sl) : __uint_as_float(sl << 23);
-                    const float fhi = kOfficial ? e8m0_value(sh) : __uint_as_float(sh << 23);
-                    c[0] = fmaf(flo, t[0], c[0]);
-                    c[1] = fmaf(flo, t[1], c[1]);
-                    c[2] = fmaf(fhi, t[2], c[2]);
-                    c[3] = fmaf(fhi, t[3], c[3]);
-                }
-            } else {
-#pragma unroll 1
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
-                    const uint32_t wlo = lds_u32(wa);
-                    const uint32_t whi = lds_u32(wa + kHi);
-                    const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
-                    const Scale s_lo = make_scale(((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu);
-                    const Scale s_hi = make_scale(((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu);
-                    uint32_t a[8];
-                    cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
-                    cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        a[i] = dequant_f16(a[i], s_lo);
-                        a[4 + i] = dequant_f16(a[4 + i], s_hi);
-                    }
-                    mma_16816_acc(c, a[0], a[4], a[1], a[5], bv.x, bv.y);
-                    mma_16816_acc(c, a[2], a[6], a[3], a[7], bv.z, bv.w);
-                }
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
+                const uint32_t wlo = lds_u32(wa);
+                const uint32_t whi = lds_u32(wa + kHi);
+                const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
+                uint32_t a[8];  // [lo b0..b3, hi b0..b3] as f16x2
+                cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
+                cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
+                float t[4];
+                mma_16816_zero(t, a[0], a[4], a[1], a[5], bv.x, bv.y);
+                mma_16816_acc(t, a[2], a[6], a[3], a[7], bv.z, bv.w);
+                const uint32_t sl = ((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu;
+                const uint32_t sh = ((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu;
+                const float flo = kOfficial ? e8m0_value(sl) : __uint_as_float(sl << 23);
+                const float fhi = kOfficial ? e8m0_value(sh) : __uint_as_float(sh << 23);
+                c[0] = fmaf(flo, t[0], c[0]);
+                c[1] = fmaf(flo, t[1], c[1]);
+                c[2] = fmaf(fhi, t[2], c[2]);
+                c[3] = fmaf(fhi, t[3], c[3]);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[st]);
-            if (++st == n_stages) { st = 0; ph ^= 1; }
+        } else {
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
+                const uint32_t wlo = lds_u32(wa);
+                const uint32_t whi = lds_u32(wa + kHi);
+                const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
+                const Scale s_lo = make_scale(((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu);
+                const Scale s_hi = make_scale(((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu);
+                uint32_t a[8];
+                cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
+                cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    a[i] = dequant_f16(a[i], s_lo);
+                    a[4 + i] = dequant_f16(a[4 + i], s_hi);
+                }
+                mma_16816_acc(c, a[0], a[4], a[1], a[5], bv.x, bv.y);
+                mma_16816_acc(c, a[2], a[6], a[3], a[7], bv.z, bv.w);
+            }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sempty[slot]);
-        // Pair reduction: the second warp (kh == 1) hands its partial sums to
-        // the first through a slot double buffered by item parity.  Both warps
-        // wait on the pair's named barrier once per item, so neither runs an
-        // item ahead of the other.  (A second warp that only arrived could,
-        // when an item has fewer K stages than the ring holds, reach the
-        // barrier twice while its partner was in an epilogue, complete a
-        // phase on its own and leave the partner's last wait unmatched.)
-        // Each warp publishes whether its waits succeeded before the barrier;
-        // after it both read the partner's flag and leave together, so no
-        // barrier ever waits on a warp that has gone.
-        float* rslot = red + ((parity * 8 + cw) * 32 + lane) * 4;
-        if (kh == 1) *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
-        if (lane == 0) red_ok[(parity * 2 + kh) * 8 + cw] = ok ? 1 : 0;
-        named_bar_sync(1 + cw, 64);
-        const bool ok_pair = red_ok[(parity * 2 + (kh ^ 1)) * 8 + cw] != 0;
-        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (kh == 0) o = *reinterpret_cast<const float4*>(rslot);
-        parity ^= 1;
-        if (!ok || !ok_pair) break;
-        if (kh == 1) continue;
-        c[0] += o.x;
-        c[1] += o.y;
-        c[2] += o.z;
-        c[3] += o.w;
-        if (!it_valid) continue;
+        if (lane == 0) mbar_arrive(&S.empty[st]);
+        if (++st == n_stages) { st = 0; ph ^= 1; }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.sempty[slot]);
+    // Pair reduction: the second warp (kh == 1) hands its partial sums to
+    // the first through a slot double buffered by item parity.  Both warps
+    // wait on the pair's named barrier once per item, so neither runs an
+    // item ahead of the other.  (A second warp that only arrived could,
+    // when an item has fewer K stages than the ring holds, reach the
+    // barrier twice while its partner was in an epilogue, complete a
+    // phase on its own and leave the partner's last wait unmatched.)
+    // Each warp publishes whether its waits succeeded before the barrier;
+    // after it both read the partner's flag and leave together, so no
+    // barrier ever waits on a warp that has gone.
+    float* rslot = S.red + ((parity * 8 + cw) * 32 + lane) * 4;
+    if (kh == 1) *reinterpret_cast<float4*>(rslot) = make_float4(c[0], c[1], c[2], c[3]);
+    if (lane == 0) S.red_ok[(parity * 2 + kh) * 8 + cw] = ok ? 1 : 0;
+    named_bar_sync(1 + cw, 64);
+    const bool ok_pair = S.red_ok[(parity * 2 + (kh ^ 1)) * 8 + cw] != 0;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (kh == 0) o = *reinterpret_cast<const float4*>(rslot);
+    parity ^= 1;
+    if (!ok || !ok_pair) return false;
+    if (kh == 1) return true;
+    c[0] += o.x;
+    c[1] += o.y;
+    c[2] += o.z;
+    c[3] += o.w;
+    if (it_valid) {
         const int n_rows = it_n_rows;
         const int n0 = q, n1 = 4 + q;  // tokens of MMA columns 2q and 2q+1
         if (kGU) {
@@ -515,9 +418,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 float* dst;
                 if (args.raw_peers) {  // straight into the token owner's return buffer
                     const int src = pos / args.ep_capacity;
-                    const int slot = pos - src * args.ep_capacity;
+                    const int rslot_ep = pos - src * args.ep_capacity;
                     dst = args.raw_peers[src] +
-                          static_cast<size_t>(args.ep_rank * args.ep_capacity + slot) * args.hidden;
+                          static_cast<size_t>(args.ep_rank * args.ep_capacity + rslot_ep) * args.hidden;
                 } else {
                     dst = args.raw + static_cast<size_t>(pos) * args.hidden;
                 }
@@ -526,19 +429,362 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
         }
     }
+    if (signal) {
+        // the item's stores are done in this warp; the signal warp publishes
+        // them (one arrival per first warp; a buffer is reused two items on,
+        // after the signal warp has released it)
+        __syncwarp();
+        bool sok = true;
+        if (lane == 0) {
+            const int b = li & 1;
+            if (li >= 2) sok = mbar_wait(&S.sfree[b], ((li >> 1) - 1) & 1, status, kStatusTimeoutEpilogue);
+            if (sok) mbar_arrive(&S.stored[b]);
+        }
+        if (!__shfl_sync(0xffffffffu, sok, 0)) return false;  // the whole warp leaves together
+    }
+    return true;
 }
 
-template <GemmMode MODE, bool kOfficial>
-cudaError_t launch_dec(const GemmMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
-    auto kern = moe_decode_kernel<MODE, kOfficial>;
-    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<MODE, kOfficial>>(static_cast<int>(kSmemLimit));
+template <bool kOfficial>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    moe_decode_kernel(const __grid_constant__ DecMaps maps, const GemmArgs args) {
+    // The tile list comes from the permutation kernel, which has completed
+    // whenever this kernel runs: its predecessor (gather or gate/up) only
+    // signals its dependents after its own griddepcontrol.wait.  Everything
+    // that reads weights or the tile list may therefore start before this
+    // kernel's wait; only the token rows (the predecessor's output) and the
+    // counters the permutation zeroed wait.
+    const DecPlan P = dec_plan(args);
+    const int n_items = P.n_items;
+    if (static_cast<int>(blockIdx.x) >= n_items) {
+        pdl_wait();
+        pdl_trigger();
+        return;
+    }
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    const DecLayout L = dec_layout(dec_layout_k(args));
+    const int n_stages = L.stages;
+    DecSmem S;
+    S.smem = smem;
+    S.base = smem_u32(smem);
+    S.full = reinterpret_cast<uint64_t*>(smem + L.bar_off);  // [stages] TMA landed
+    S.empty = S.full + kDecMaxStages;                         // [stages] consumers done
+    uint64_t* sfull = S.empty + kDecMaxStages;                // [slots] scale rows landed
+    S.sready = sfull + kDecScSlots;                           // [slots] scale rows checked
+    S.sempty = S.sready + kDecScSlots;                        // [slots] item consumed
+    S.fast_flag = reinterpret_cast<volatile int*>(S.sempty + kDecScSlots);            // [slots]
+    S.item_rec = reinterpret_cast<volatile ItemRec*>(smem + L.bar_off + 160);         // [slots]
+    S.stored = reinterpret_cast<uint64_t*>(smem + L.bar_off + 208);  // [2] an item's outputs stored
+    S.sfree = S.stored + 2;                                          // [2] signal warp done with it
+    // down items of this CTA whose tiles' gate/up items are all published
+    uint32_t* dep_ready = reinterpret_cast<uint32_t*>(smem + L.bar_off + 240);
+    S.red = reinterpret_cast<float*>(smem + L.red_off);
+    S.red_ok = reinterpret_cast<int*>(S.red + 2 * 8 * 32 * 4);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const bool gu_on = (args.phases & 1) != 0, dn_on = (args.phases & 2) != 0;
+    // the down items of a two-phase launch wait for their tile's gate/up items
+    const bool dep = gu_on && dn_on && args.tile_done != nullptr;
+    const bool signal = dep || args.comb_out != nullptr;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < n_stages; ++i) {
+            mbar_init(&S.full[i], 1);
+            mbar_init(&S.empty[i], kDecConsumerWarps);
+        }
+        for (int i = 0; i < kDecScSlots; ++i) {
+            mbar_init(&sfull[i], 1);
+            mbar_init(&S.sready[i], 1);
+            mbar_init(&S.sempty[i], kDecConsumerWarps);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&S.stored[i], kDecConsumerWarps / 2);
+            mbar_init(&S.sfree[i], 1);
+        }
+        *dep_ready = 0u;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        if (gu_on) {
+            prefetch_tmap(&maps.gw1);
+            prefetch_tmap(&maps.gw3);
+            prefetch_tmap(&maps.gx);
+            if (args.scale_swz) {
+                prefetch_tmap(&maps.gs1);
+                prefetch_tmap(&maps.gs3);
+            }
+        }
+        if (dn_on) {
+            prefetch_tmap(&maps.dw2);
+            prefetch_tmap(&maps.dact);
+            if (args.dn_scale_swz) prefetch_tmap(&maps.ds2);
+        }
+    }
+    __syncthreads();
+    if (warp != 0) pdl_wait();
+    pdl_trigger();
+    uint32_t* status = args.status;
+    const int H = args.hidden, I = args.inter;
+
+    if (warp == 0) {
+        // ---------------- producer ----------------
+        if (lane != 0) return;
+        const uint64_t pol_w = policy_evict_first();
+        const uint64_t pol_b = policy_evict_last();
+        const size_t ih = static_cast<size_t>(H) * I;
+        const size_t off_s1 = ih + ih / 2, off_s3 = off_s1 + ih / 32, off_s2 = off_s3 + ih / 32;
+        // Scale rows of one item are contiguous in the record: one copy per
+        // projection into the item's slot, after the item's record for the
+        // consumers.  With scale maps (rows of 32, 64 or 128 bytes) the copy
+        // is a tensor load whose swizzle span is the row length, so the
+        // 16-byte chunk j of row r lands at chunk j ^ f(r) and the
+        // consumers' per-stage reads of eight rows hit distinct banks;
+        // otherwise a plain bulk copy.
+        auto issue_scales = [&](const DecItem& d, int li) -> bool {
+            const int slot = li % kDecScSlots;
+            if (!mbar_wait(&S.sempty[slot], ((li / kDecScSlots) & 1) ^ 1, status, kStatusTimeoutTma))
+                return false;
+            S.item_rec[slot].m = d.m;
+            S.item_rec[slot].row_start = d.td.row_start;
+            S.item_rec[slot].n_rows = d.td.n_rows;
+            S.item_rec[slot].valid = d.valid ? 1 : 0;
+            const uint32_t rb = static_cast<uint32_t>((d.gu ? H : I) / 32);
+            mbar_arrive_expect_tx(&sfull[slot], 128 * rb);
+            uint8_t* dst = smem + L.sc_off + slot * L.sc_slot;
+            const uint8_t* rec = args.records + static_cast<size_t>(d.slot) * args.record_bytes;
+            if (d.gu) {
+                if (args.scale_swz) {
+                    tma_load_3d(dst, &maps.gs1, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
+                    tma_load_3d(dst + 64 * rb, &maps.gs3, &sfull[slot], 0, d.m * 64, d.slot, pol_w);
+                } else {
+                    const size_t r0 = static_cast<size_t>(d.m) * 64 * rb;
+                    bulk_load(dst, rec + off_s1 + r0, 64 * rb, &sfull[slot]);
+                    bulk_load(dst + 64 * rb, rec + off_s3 + r0, 64 * rb, &sfull[slot]);
+                }
+            } else if (args.dn_scale_swz) {
+                tma_load_3d(dst, &maps.ds2, &sfull[slot], 0, d.m * 128, d.slot, pol_w);
+            } else {
+                bulk_load(dst, rec + off_s2 + static_cast<size_t>(d.m) * 128 * rb, 128 * rb, &sfull[slot]);
+            }
+            return true;
+        };
+        // weights: {128 B, rows, two 128-byte K chunks, slot} per projection;
+        // tokens: {64, 8 rows, eight 64-wide K chunks}
+        auto issue_weights = [&](const DecItem& d, int s, int st) {
+            uint8_t* pk = smem + st * kDecStageBytes;
+            if (d.gu) {
+                tma_load_4d(pk, &maps.gw1, &S.full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
+                tma_load_4d(pk + 16384, &maps.gw3, &S.full[st], 0, d.m * 64, 2 * s, d.slot, pol_w);
+            } else {
+                tma_load_4d(pk, &maps.dw2, &S.full[st], 0, d.m * 128, 2 * s, d.slot, pol_w);
+            }
+        };
+        auto issue_tokens = [&](const DecItem& d, int s, int st) {
+            tma_load_3d(smem + st * kDecStageBytes + kDecPkBytes, d.gu ? &maps.gx : &maps.dact, &S.full[st], 0,
+                        d.td.row_start, 8 * s, pol_b);
+        };
+        auto stages_of = [&](const DecItem& d) { return (d.gu ? H : I) / kKStage; };
+        // The next item's scale rows are issued when an item starts, so they
+        // have a whole item's worth of stage traffic to land behind.  Item
+        // metadata is pipelined so that no dependent global load sits on the
+        // issue path: while item li is issued, the slot of item li+2 and the
+        // tile descriptor of item li+3 are in flight.
+        const int G = gridDim.x;
+        int item = blockIdx.x;
+        DecItem cur = finish_item(args, P, item, load_tile(args, P, item));
+        DecItem n1{};
+        if (item + G < n_items) n1 = finish_item(args, P, item + G, load_tile(args, P, item + G));
+        TileDesc td2{};
+        if (item + 2 * G < n_items) td2 = load_tile(args, P, item + 2 * G);
+        // Before the wait: the first two items' scale rows and the weights of
+        // the first ring's worth of stages.
+        if (!issue_scales(cur, 0)) return;
+        if (item + G < n_items && !issue_scales(n1, 1)) return;
+        const int k0 = stages_of(cur);
+        const int pre = n_stages < k0 ? n_stages : k0;
+        for (int s = 0; s < pre; ++s) {  // first use of ring slots 0..pre-1
+            mbar_arrive_expect_tx(&S.full[s], kDecStageBytes);
+            issue_weights(cur, s, s);
+        }
+        pdl_wait();
+        int st = 0;
+        uint32_t ph = 0;
+        uint32_t dk = 0;  // down items of this CTA issued so far
+        for (int li = 0; item < n_items; item += G, ++li) {
+            if (li > 0 && item + G < n_items && !issue_scales(n1, li + 1)) return;
+            DecItem n2{};
+            if (item + 2 * G < n_items) n2 = finish_item(args, P, item + 2 * G, td2);
+            if (item + 3 * G < n_items) td2 = load_tile(args, P, item + 3 * G);
+            if (!cur.valid) atomicOr(status, kStatusBadExpert);
+            const int ks = stages_of(cur);
+            for (int s = 0; s < ks; ++s) {
+                if (li > 0 || s >= pre) {
+                    if (!mbar_wait(&S.empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
+                    mbar_arrive_expect_tx(&S.full[st], kDecStageBytes);
+                    issue_weights(cur, s, st);
+                }
+                if (s == 0 && dep && !cur.gu) {
+                    // the SwiGLU rows of this tile: the dependency warp has
+                    // seen every gate/up item of the tile publish its stores
+                    // (generic proxy), which the tensor copies below read
+                    // through the async proxy
+                    if (!wait_smem_geq(dep_ready, ++dk, status, kStatusTimeoutTma)) return;
+                    fence_proxy_async_global();
+                }
+                issue_tokens(cur, s, st);
+                if (++st == n_stages) { st = 0; ph ^= 1; }
+            }
+            cur = n1;
+            n1 = n2;
+        }
+        return;
+    }
+
+    if (warp == kDecCheckerWarp) {
+        // ---------------- scale checker ----------------
+        // Scale bytes 104..140 make every E2M1 x 2^(s-127) product an exact,
+        // finite binary16, so scaling a block's FP32 partial sum equals
+        // summing the reference's FP16-rounded weights.  Byte 103 rounds
+        // 0.5 x 2^-24 and bytes >= 141 overflow in the reference dequant.  The
+        // checker reads each item's scale rows once and publishes whether all
+        // of them are in range; the consumers start the item after that.
+        int li = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
+            const int slot = li % kDecScSlots;
+            const uint32_t sc_item = 128u * static_cast<uint32_t>((item < P.n_gu ? H : I) / 32);
+            const bool ok = mbar_wait(&sfull[slot], (li / kDecScSlots) & 1, status, kStatusTimeoutDequant);
+            if (!__all_sync(0xffffffffu, ok)) return;
+            const uint32_t sc = S.base + L.sc_off + slot * L.sc_slot;
+            uint32_t acc = 0x80808080u;
+#pragma unroll 4
+            for (uint32_t i = lane; i < sc_item / 16; i += 32) {
+                const uint4 v = lds_v4(sc + i * 16);
+                acc &= scale_bytes_exact(v.x) & scale_bytes_exact(v.y) & scale_bytes_exact(v.z) &
+                       scale_bytes_exact(v.w);
+            }
+            const bool fast = __all_sync(0xffffffffu, acc == 0x80808080u);
+            if (lane == 0) {
+                S.fast_flag[slot] = fast ? 1 : 0;
+                mbar_arrive(&S.sready[slot]);
+            }
+        }
+        return;
+    }
+
+    if (warp == kDecDepWarp) {
+        // ---------------- dependency warp ----------------
+        // Walks this CTA's down items in order, waits (bounded, gpu-scope
+        // acquire) until each one's tile has all its gate/up items
+        // published and counts it in dep_ready (shared, release), so the
+        // producer's check is a shared-memory read and the global round
+        // trips run ahead of the TMA issue.
+        if (!dep || lane != 0) return;
+        uint32_t dk = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+            if (item < P.n_gu) continue;
+            const int tile = (item - P.n_gu) / P.md;
+            if (!wait_count_geq(&args.tile_done[tile], static_cast<uint32_t>(P.mg), status, kStatusTimeoutTma))
+                return;
+            ++dk;
+            asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(dep_ready)), "r"(dk)
+                         : "memory");
+        }
+        return;
+    }
+
+    if (warp == kDecSignalWarp) {
+        // ---------------- signal warp ----------------
+        // Publishes each item's stores to the grid once the item's first
+        // warps have stored them (mbarrier, CTA scope): a gpu-scope fence,
+        // then for a gate/up item one increment of its tile's count, for a
+        // down item (fused combine) one increment per row of its
+        // (token, feature block) count.  The row that completes a count --
+        // all K selections of the token written for this block -- runs the
+        // block's combine, reading the K rows in rank order.  Which CTA that
+        // is does not change the result.
+        if (!signal) return;
+        const int K = args.topk;
+        int li = 0;
+        for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
+            const int b = li & 1;
+            const bool ok = mbar_wait(&S.stored[b], (li >> 1) & 1, status, kStatusTimeoutEpilogue);
+            if (!__all_sync(0xffffffffu, ok)) return;
+            if (item < P.n_gu) {
+                if (dep && lane == 0) {
+                    fence_proxy_async_global();
+                    __threadfence();
+                    atomicAdd(&args.tile_done[item / P.mg], 1u);
+                }
+            } else if (args.comb_out) {
+                const int j = item - P.n_gu;
+                const int tile = j / P.md;
+                const int m = j - tile * P.md;
+                const TileDesc td = args.tiles[tile];
+                __threadfence();
+                int tok = 0;
+                bool last = false;
+                if (lane < td.n_rows) {
+                    tok = args.perm[td.row_start + lane] / K;
+                    last = atomicAdd(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
+                }
+                uint32_t mask = __ballot_sync(0xffffffffu, last);
+                if (mask) {
+                    __threadfence();  // the other CTAs' rows of these tokens
+                    const int h0 = m * 128 + lane * 4;
+                    while (mask) {
+                        const int n = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const int t = __shfl_sync(0xffffffffu, tok, n);
+                        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                        for (int r = 0; r < K; ++r) {
+                            const size_t sel = static_cast<size_t>(t) * K + r;
+                            const float wr = args.comb_w[sel];
+                            const float4 v = __ldcg(reinterpret_cast<const float4*>(args.raw + sel * H + h0));
+                            acc.x = __fadd_rn(acc.x, __fmul_rn(wr, v.x));
+                            acc.y = __fadd_rn(acc.y, __fmul_rn(wr, v.y));
+                            acc.z = __fadd_rn(acc.z, __fmul_rn(wr, v.z));
+                            acc.w = __fadd_rn(acc.w, __fmul_rn(wr, v.w));
+                        }
+                        *reinterpret_cast<float4*>(args.comb_out + static_cast<size_t>(t) * H + h0) = acc;
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&S.sfree[b]);
+        }
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    int st = 0, parity = 0, li = 0;
+    uint32_t ph = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
+        const bool go = item < P.n_gu
+                            ? consume_item<true, kOfficial>(args, L, S, li, st, ph, parity, n_stages, signal, warp,
+                                                            lane)
+                            : consume_item<false, kOfficial>(args, L, S, li, st, ph, parity, n_stages, signal,
+                                                             warp, lane);
+        if (!go) break;
+    }
+}
+
+template <bool kOfficial>
+cudaError_t launch_dec(const DecMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
+    auto kern = moe_decode_kernel<kOfficial>;
+    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<kOfficial>>(static_cast<int>(kSmemLimit));
     if (e != cudaSuccess) return e;
-    const DecLayout L = dec_layout(args.k_total);
-    if (L.stages < 2 || L.bytes > kSmemLimit) return cudaErrorInvalidValue;
-    GemmArgs a = args;
-    a.scale_swz = maps.scale_swz;
-    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps.w0, maps.w1, maps.b, maps.s0,
-                      maps.s1, a);
+    const DecLayout L = dec_layout(dec_layout_k(args));
+    if (L.stages < 2 || L.bytes > kSmemLimit || args.phases < 1 || args.phases > 3 || args.hidden % kKStage ||
+        args.inter % kKStage || args.inter % 64 || args.hidden % 128)
+        return cudaErrorInvalidValue;
+    if (args.comb_out && (!(args.phases & 2) || !args.comb_w || !args.comb_cnt || !args.raw || args.raw_peers))
+        return cudaErrorInvalidValue;
+    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps, args);
+}
+
+cudaError_t launch_decode(const DecMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
+    return args.official ? launch_dec<true>(maps, args, grid, stream) : launch_dec<false>(maps, args, grid, stream);
 }
 
 }  // namespace
@@ -618,11 +864,44 @@ bool encode_token_map(EncodeTiledFn fn, const void* rows_base, int rows, int col
 
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream) {
-    if (args.official)
-        return gate_up ? launch_dec<GemmMode::kGateUp, true>(maps, args, grid, stream)
-                       : launch_dec<GemmMode::kDown, true>(maps, args, grid, stream);
-    return gate_up ? launch_dec<GemmMode::kGateUp, false>(maps, args, grid, stream)
-                   : launch_dec<GemmMode::kDown, false>(maps, args, grid, stream);
+    // one projection: the other projection's map slots hold copies
+    DecMaps m;
+    m.gw1 = maps.w0;
+    m.gw3 = maps.w1;
+    m.gx = maps.b;
+    m.gs1 = maps.s0;
+    m.gs3 = maps.s1;
+    m.dw2 = maps.w0;
+    m.dact = maps.b;
+    m.ds2 = maps.s0;
+    GemmArgs a = args;
+    a.phases = gate_up ? 1 : 2;
+    a.scale_swz = gate_up ? maps.scale_swz : 0;
+    a.dn_scale_swz = gate_up ? 0 : maps.scale_swz;
+    a.tile_done = nullptr;
+    a.comb_out = nullptr;
+    a.comb_w = nullptr;
+    a.comb_cnt = nullptr;
+    return launch_decode(m, a, grid, stream);
+}
+
+cudaError_t launch_moe_decode_layer(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args, int grid,
+                                    cudaStream_t stream) {
+    if (!args.tile_done) return cudaErrorInvalidValue;
+    DecMaps m;
+    m.gw1 = gu.w0;
+    m.gw3 = gu.w1;
+    m.gx = gu.b;
+    m.gs1 = gu.s0;
+    m.gs3 = gu.s1;
+    m.dw2 = dn.w0;
+    m.dact = dn.b;
+    m.ds2 = dn.s0;
+    GemmArgs a = args;
+    a.phases = 3;
+    a.scale_swz = gu.scale_swz;
+    a.dn_scale_swz = dn.scale_swz;
+    return launch_decode(m, a, grid, stream);
 }
 
 }  // namespace dee

@@ -77,8 +77,21 @@ struct GemmArgs {
     int official;
     const float* route_w;
     // Decode kernel: the scale rows arrive by swizzled tensor copies (set by
-    // the launcher from GemmMaps::scale_swz).
+    // the launcher from GemmMaps::scale_swz of the gate/up and down maps).
     int scale_swz;
+    int dn_scale_swz;
+    // Decode kernel, both projections in one launch (launch_moe_decode_layer):
+    // tile_done[tile] counts the tile's finished gate/up items (zeroed by the
+    // permutation); a down item waits for its tile's count before it loads
+    // the SwiGLU rows.  With comb_out set, the kernel also runs the live
+    // combine comb_out[t] = sum_r comb_w[t*K + r] * raw[t*K + r] (rank order,
+    // FP32), per 128-feature block once the block's K rows are written;
+    // comb_cnt [tokens * H/128] counts them (zeroed by the permutation).
+    int phases;  // bit 0: gate/up items, bit 1: down items
+    uint32_t* tile_done;
+    const float* comb_w;
+    float* comb_out;
+    uint32_t* comb_cnt;
 };
 
 constexpr int kDqGroups = 4;          // dequantiser warpgroups

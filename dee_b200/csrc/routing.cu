@@ -36,20 +36,15 @@ __device__ __forceinline__ bool better(const Cand& a, const Cand& b) {
 // multiple of 2^(b-53) below 2^b, i.e. exactly representable in double, and
 // every addition is exact in any order.  A warp vote checks that; otherwise
 // lane 0 sums in expert order.
+//
+// route_token routes one token with one warp: l is the token's logits row,
+// sp a warp-private scratch of `experts` floats; rank k's id and weight go to
+// ids_row[k] / weights_row[k] (lane k) and, when s_ids_row is given, also to
+// s_ids_row[k].
 template <int NPER>
-__global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, int experts,
-                                  int topk, int32_t* __restrict__ ids, float* __restrict__ weights,
-                                  uint32_t* status) {
-    extern __shared__ float route_smem[];
-    sm100::pdl_wait();
-    sm100::pdl_trigger();
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (t >= tokens) return;
-    float* sp = route_smem + warp * experts;
-    const float* l = logits + static_cast<size_t>(t) * experts;
-
+__device__ __forceinline__ void route_token(const float* __restrict__ l, int experts, int topk, int lane,
+                                            float* sp, int32_t* ids_row, float* weights_row,
+                                            int32_t* s_ids_row, uint32_t* status) {
     float v[NPER];
     float m = -INFINITY;
 #pragma unroll
@@ -134,9 +129,26 @@ __global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, 
     if (lane == 0 && (bad || bad_sum)) atomicOr(status, kStatusBadRouter);
     if (lane < topk) {
         const bool ok = !(bad || bad_sum) && my_id >= 0 && my_id < experts;
-        ids[static_cast<size_t>(t) * topk + lane] = ok ? my_id : 0;
-        weights[static_cast<size_t>(t) * topk + lane] = ok ? __fdiv_rn(my_p, sum) : 0.0f;
+        ids_row[lane] = ok ? my_id : 0;
+        weights_row[lane] = ok ? __fdiv_rn(my_p, sum) : 0.0f;
+        if (s_ids_row) s_ids_row[lane] = ok ? my_id : 0;
     }
+}
+
+template <int NPER>
+__global__ void route_topk_kernel(const float* __restrict__ logits, int tokens, int experts,
+                                  int topk, int32_t* __restrict__ ids, float* __restrict__ weights,
+                                  uint32_t* status) {
+    extern __shared__ float route_smem[];
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (t >= tokens) return;
+    route_token<NPER>(logits + static_cast<size_t>(t) * experts, experts, topk, lane, route_smem + warp * experts,
+                      ids + static_cast<size_t>(t) * topk, weights + static_cast<size_t>(t) * topk, nullptr,
+                      status);
 }
 
 __global__ void route_dsv4_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
@@ -228,30 +240,23 @@ __global__ void route_dsv4_kernel(const float* __restrict__ logits, const float*
 constexpr int kPermThreads = 1024;
 constexpr int kPermMaxExperts = 256;
 
-__global__ void __launch_bounds__(kPermThreads, 1)
-    permute_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts,
-                   int n_tile_max, int max_tiles, PermuteOut out, uint32_t* status,
-                   bool skip_negative) {
+// The whole permutation in one CTA of kPermThreads threads.  ids may be in
+// global or shared memory; wcnt is a [32][kPermMaxExperts] shared scratch
+// (per-warp group sizes), which this function zeroes before use.
+__device__ void permute_block(const int32_t* ids, int tokens, int topk, int experts, int n_tile_max,
+                              int max_tiles, const PermuteOut& out, uint32_t* status, bool skip_negative,
+                              int (*wcnt)[kPermMaxExperts]) {
     __shared__ int cnt[kPermMaxExperts];
     __shared__ int off[kPermMaxExperts + 1];
     __shared__ int cursor[kPermMaxExperts];
     __shared__ int ntile_off[kPermMaxExperts + 1];
-    __shared__ int wcnt[32][kPermMaxExperts];  // per-warp group sizes, zero when unused
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const int sel = tokens * topk;
-
-    sm100::pdl_wait();
-    sm100::pdl_trigger();
-    // expert-parallel receive buffer: the senders' rows and ids have landed
-    // once their flags reach the epoch (the __syncthreads below orders every
-    // thread's reads after the acquires)
-    if (out.wait_flags)
-        sm100::wait_flags_bounded(out.wait_flags, out.wait_ranks, out.wait_epoch, out.wait_limit_ns, status,
-                                  sm100::kStatusTimeoutFlag);
     for (int e = tid; e < experts; e += kPermThreads) { cnt[e] = 0; cursor[e] = 0; }
     for (int i = tid; i < 32 * kPermMaxExperts; i += kPermThreads) (&wcnt[0][0])[i] = 0;
+    for (int i = tid; i < out.clear_n; i += kPermThreads) out.clear[i] = 0u;
     __syncthreads();
     for (int p = tid; p < sel; p += kPermThreads) {
         const int e = ids[p];
@@ -350,6 +355,47 @@ __global__ void __launch_bounds__(kPermThreads, 1)
         out.offsets[experts] = off[experts];
         *out.n_tiles = min(ntile_off[experts], max_tiles);
     }
+}
+
+__global__ void __launch_bounds__(kPermThreads, 1)
+    permute_kernel(const int32_t* __restrict__ ids, int tokens, int topk, int experts,
+                   int n_tile_max, int max_tiles, PermuteOut out, uint32_t* status,
+                   bool skip_negative) {
+    __shared__ int wcnt[32][kPermMaxExperts];
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    // expert-parallel receive buffer: the senders' rows and ids have landed
+    // once their flags reach the epoch (the __syncthreads in permute_block
+    // orders every thread's reads after the acquires)
+    if (out.wait_flags)
+        sm100::wait_flags_bounded(out.wait_flags, out.wait_ranks, out.wait_epoch, out.wait_limit_ns, status,
+                                  sm100::kStatusTimeoutFlag);
+    permute_block(ids, tokens, topk, experts, n_tile_max, max_tiles, out, status, skip_negative, wcnt);
+}
+
+// Router and permutation in one CTA, for decode-sized batches (T*K <= 384,
+// E <= 256): the warps route the tokens (one warp per token, as
+// route_topk_kernel) into ids/weights and a shared copy of the ids, and the
+// CTA then groups them exactly as permute_kernel does.  One launch and one
+// dependency instead of two.  The per-warp probability scratch of the router
+// and the permutation's per-warp counts share one buffer.
+__global__ void __launch_bounds__(kPermThreads, 1)
+    route_permute_kernel(const float* __restrict__ logits, int tokens, int experts, int topk,
+                         int32_t* __restrict__ ids, float* __restrict__ weights, int n_tile_max, int max_tiles,
+                         PermuteOut out, uint32_t* status) {
+    __shared__ int32_t s_ids[kDecodeMaxSelections];
+    __shared__ int scratch[32][kPermMaxExperts];
+    sm100::pdl_wait();
+    sm100::pdl_trigger();
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    float* sp = reinterpret_cast<float*>(&scratch[warp][0]);
+    for (int t = warp; t < tokens; t += kPermThreads / 32)
+        route_token<8>(logits + static_cast<size_t>(t) * experts, experts, topk, lane, sp,
+                       ids + static_cast<size_t>(t) * topk, weights + static_cast<size_t>(t) * topk,
+                       s_ids + t * topk, status);
+    __syncthreads();
+    permute_block(s_ids, tokens, topk, experts, n_tile_max, max_tiles, out, status, false, scratch);
 }
 
 // The same permutation over many CTAs, for batches of more than two chunks
@@ -689,6 +735,15 @@ cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts
     }
     return launch_pdl(permute_kernel, dim3(1), dim3(kPermThreads), 0, stream, ids, tokens, topk,
                       experts, n_tile_max, max_tiles, out, status, skip_negative);
+}
+
+cudaError_t launch_route_permute(const float* logits, int tokens, int experts, int topk, int32_t* ids,
+                                 float* weights, int n_tile_max, int max_tiles, const PermuteOut& out,
+                                 uint32_t* status, cudaStream_t stream) {
+    if (!route_permute_fits(tokens, topk, experts) || n_tile_max < 8 || topk > 32)
+        return cudaErrorInvalidValue;
+    return launch_pdl(route_permute_kernel, dim3(1), dim3(kPermThreads), 0, stream, logits, tokens, experts, topk,
+                      ids, weights, n_tile_max, max_tiles, out, status);
 }
 
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,

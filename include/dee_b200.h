@@ -138,6 +138,17 @@ DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_
                            const int32_t* d_ids, const int32_t* h_ids, int topk,
                            const float* d_weights, float* d_out_f32, float* d_raw, void* stream);
 
+/* Routing and the layer in one call: softmax top-k with renormalised weights
+ * on device logits [T, E] FP32 (dee_route_topk_device, Engine::route_topk_batch,
+ * engine.cpp:2604-2771) writes d_ids [T, K] int32 and d_weights [T, K] FP32,
+ * then the layer of dee_moe_forward_device runs on them (K = the engine's
+ * topk).  Decode-sized batches (T*K <= 384, E <= 256) route inside the
+ * grouping kernel, one launch and one kernel dependency fewer; results are
+ * identical to the two calls.  Queued on `stream`, no host sync. */
+DEE_API int dee_moe_forward_routed_device(dee_engine* engine, int layer, const void* d_x_f16, int tokens,
+                                          const float* d_logits, int32_t* d_ids, float* d_weights,
+                                          float* d_out_f32, float* d_raw, void* stream);
+
 /* The MXFP8-activation variant of dee_moe_forward_device (device ids only):
  * token rows and the SwiGLU output are quantised to E4M3 with UE8M0 scales
  * per act_block columns (128: the official act_quant, 32: MX), and both
@@ -406,7 +417,8 @@ DEE_API uint64_t dee_engine_launch_count(const dee_engine* engine);
  * stage of a forward is bracketed by CUDA events on its launch stream.
  * Stages: 0 route, 1 permute, 2 gather, 3 gate/up GEMM, 4 down GEMM,
  * 5 combine, 6 expert-parallel dispatch (the peer rows kernel or the pack
- * before an NCCL exchange). */
+ * before an NCCL exchange), 7 the one-launch decode layer (gate/up, down
+ * and the fused combine of decode-sized batches, in place of 3-5). */
 DEE_API int dee_engine_set_profiling(dee_engine* engine, int enable);
 
 /* Milliseconds of each stage of the most recent profiled forward (-1 for a

@@ -556,3 +556,49 @@ def test_decode_combine_bitexact_over_calls(torch_cuda, oracle_mod, T, dup):
         raw_np = raw.cpu().numpy()
         assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw_np, w)), f"call {call}"
         assert orc.rel_l2(raw_np, orc.moe_layer_raw(recs, layout, x16, ids)) <= TOL_REL_L2
+
+
+@pytest.mark.parametrize("T,E", [(1, 64), (8, 256), (33, 64), (64, 256), (65, 64), (100, 16)])
+def test_routed_forward_matches_route_then_forward(torch_cuda, oracle_mod, T, E):
+    """dee_moe_forward_routed_device against dee_route_topk_device followed
+    by dee_moe_forward_device: ids, weights, raw rows, the combined output
+    and the journal bit-identical.  T*K <= 384 with E <= 256 takes the fused
+    router+permutation kernel; (65, 64) and (100, 16) take the two-kernel
+    fallback inside the same entry point.  Ids also equal the oracle's."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, K = 512, 512, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=77 + E, kind="normal")
+    rng = np.random.default_rng(7000 + T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    logits = (rng.standard_normal((T, E)) * 2.0).astype(np.float32)
+    eng = _engine(H, I, E, K)
+    bank = torch.from_numpy(recs).cuda()
+    eng.attach_bank(0, bank)
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    dl = torch.from_numpy(logits).cuda()
+
+    def run(fused):
+        ids = torch.full((T, K), -7, dtype=torch.int32, device="cuda")
+        w = torch.full((T, K), -1.0, dtype=torch.float32, device="cuda")
+        out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        raw = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+        if fused:
+            eng.moe_forward_routed_device(0, dx.data_ptr(), T, dl.data_ptr(), ids.data_ptr(), w.data_ptr(),
+                                          d_out_ptr=out.data_ptr(), d_raw_ptr=raw.data_ptr())
+        else:
+            eng.route_topk_device(dl.data_ptr(), T, ids.data_ptr(), w.data_ptr())
+            eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=ids.data_ptr(), d_weights_ptr=w.data_ptr(),
+                                   d_out_ptr=out.data_ptr(), d_raw_ptr=raw.data_ptr())
+        assert eng.sync_status() == 0, eng.last_error_message()
+        return [t.cpu().numpy() for t in (ids, w, out, raw)] + [eng.journal_ids(T)]
+
+    a = run(True)
+    b = run(False)
+    for got, want in zip(a, b):
+        assert np.array_equal(got.view(np.uint32) if got.dtype == np.float32 else got,
+                              want.view(np.uint32) if want.dtype == np.float32 else want)
+    ids_ref, _ = orc.route_topk(logits, K)
+    assert np.array_equal(a[0], ids_ref)
+    assert np.array_equal(a[4], a[0])
