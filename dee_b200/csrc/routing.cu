@@ -551,21 +551,37 @@ __global__ void __launch_bounds__(kPermChunk, 1)
     }
 }
 
-__global__ void gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
-                                   const int32_t* __restrict__ total_rows_dev, int max_rows,
-                                   int topk, int hidden, __half* __restrict__ x_perm) {
+// One CTA per grouped row (grid-stride): every thread issues all of its
+// loads of the row before its stores, so a row costs one memory round trip
+// instead of one per 16 bytes of a thread.
+constexpr int kGatherThreads = 128;
+constexpr int kGatherUnroll = 4;
+
+__global__ void __launch_bounds__(kGatherThreads)
+    gather_rows_kernel(const __half* __restrict__ x, const int32_t* __restrict__ perm,
+                       const int32_t* __restrict__ total_rows_dev, int max_rows, int topk, int hidden,
+                       __half* __restrict__ x_perm) {
     sm100::pdl_wait();
     sm100::pdl_trigger();
     const int rows = min(*total_rows_dev, max_rows);
-    const int warps_total = gridDim.x * (blockDim.x >> 5);
-    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
     const int vec = hidden / 8;  // uint4 per row
-    for (int row = w; row < rows; row += warps_total) {
+    for (int row = blockIdx.x; row < rows; row += gridDim.x) {
         const int t = perm[row] / topk;
         const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<size_t>(t) * hidden);
         uint4* dst = reinterpret_cast<uint4*>(x_perm + static_cast<size_t>(row) * hidden);
-        for (int i = lane; i < vec; i += 32) dst[i] = __ldg(src + i);
+        for (int base = 0; base < vec; base += kGatherThreads * kGatherUnroll) {
+            uint4 v[kGatherUnroll];
+#pragma unroll
+            for (int k = 0; k < kGatherUnroll; ++k) {
+                const int i = base + k * kGatherThreads + threadIdx.x;
+                if (i < vec) v[k] = __ldg(src + i);
+            }
+#pragma unroll
+            for (int k = 0; k < kGatherUnroll; ++k) {
+                const int i = base + k * kGatherThreads + threadIdx.x;
+                if (i < vec) dst[i] = v[k];
+            }
+        }
     }
 }
 
@@ -749,9 +765,9 @@ cudaError_t launch_route_permute(const float* logits, int tokens, int experts, i
 cudaError_t launch_gather_rows(const __half* x, const int32_t* perm, const int32_t* total_rows_dev,
                                int max_rows, int topk, int hidden, __half* x_perm,
                                cudaStream_t stream) {
-    if (hidden % 8 != 0) return cudaErrorInvalidValue;
-    const int grid = grid_for(static_cast<size_t>(max_rows) * 32, 256, 148 * 8);
-    return launch_pdl(gather_rows_kernel, dim3(grid), dim3(256), 0, stream, x, perm, total_rows_dev,
+    if (hidden % 8 != 0 || max_rows <= 0) return cudaErrorInvalidValue;
+    const int grid = max_rows < 148 * 8 ? max_rows : 148 * 8;
+    return launch_pdl(gather_rows_kernel, dim3(grid), dim3(kGatherThreads), 0, stream, x, perm, total_rows_dev,
                       max_rows, topk, hidden, x_perm);
 }
 
