@@ -208,6 +208,11 @@ struct dee_engine {
     // one-launch decode layer: [max_tiles] gate/up items done per tile, then
     // [kDecodeMaxSelections * H/128] rows written per (token, feature block)
     uint32_t* d_sync = nullptr;
+    // one-launch decode front end: per-CTA grouping scratch and the
+    // epoch-tagged counters (zeroed once), with the epoch of the last launch
+    int32_t* d_front_scratch = nullptr;
+    unsigned long long* d_front_ctr = nullptr;
+    uint32_t front_epoch = 0;
     // shared-expert workspaces, capacity in tokens
     // MXFP8 path workspaces (E4M3 rows and per-32 UE8M0 scales), capacity in rows
     size_t cap_mx = 0;
@@ -656,6 +661,8 @@ void dee_engine_destroy(dee_engine* e) {
     free_workspace(e);
     cudaFree(e->d_sh_act);
     cudaFree(e->d_sh_out);
+    cudaFree(e->d_front_scratch);
+    cudaFree(e->d_front_ctr);
     cudaFree(e->d_xq);
     cudaFree(e->d_xs);
     cudaFree(e->d_aq);
@@ -869,6 +876,80 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     return DEE_OK;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The whole routed layer of a small decode batch in one launch
+// (launch_moe_decode_front): routing, grouping, token rows, both
+// projections and the combine.
+int forward_front(dee_engine* e, int layer, const void* d_x_f16, int tokens, const float* d_logits, int32_t* d_ids,
+                  float* d_weights, float* d_out_f32, float* d_raw, cudaStream_t stream) {
+    if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
+        return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
+    const dee::Bank& bank = e->banks[layer];
+    const int H = e->cfg.hidden, K = e->cfg.topk;
+    cudaError_t err;
+    if (!e->d_front_scratch) {
+        const size_t n_ctr = kFrontMaxTiles + static_cast<size_t>(kFrontMaxSel) * (H / 128);
+        if ((err = dev_alloc(&e->d_front_scratch, static_cast<size_t>(e->num_sms) * kFrontScratchInts)) !=
+                cudaSuccess ||
+            (err = dev_alloc(&e->d_front_ctr, n_ctr)) != cudaSuccess ||
+            (err = cudaMemsetAsync(e->d_front_ctr, 0, n_ctr * sizeof(unsigned long long), stream)) != cudaSuccess) {
+            cudaFree(e->d_front_scratch);
+            cudaFree(e->d_front_ctr);
+            e->d_front_scratch = nullptr;
+            e->d_front_ctr = nullptr;
+            return cuda_fail(e, err, "decode front-end workspace");
+        }
+    }
+    if (++e->front_epoch == 0) {
+        // after 2^32 launches the tags would repeat: start over from zeroed counters
+        const size_t n_ctr = kFrontMaxTiles + static_cast<size_t>(kFrontMaxSel) * (H / 128);
+        if ((err = cudaMemsetAsync(e->d_front_ctr, 0, n_ctr * sizeof(unsigned long long), stream)) != cudaSuccess)
+            return cuda_fail(e, err, "decode front-end counter reset");
+        e->front_epoch = 1;
+    }
+    GemmArgs a{};
+    a.hidden = H;
+    a.inter = e->cfg.inter;
+    a.topk = K;
+    a.swiglu_limit = e->cfg.swiglu_limit;
+    a.slot_of = bank.d_slot_of;
+    a.num_slots = bank.n_slots;
+    a.records = bank.records;
+    a.record_bytes = bank.record_bytes;
+    a.num_experts = e->cfg.num_experts;
+    a.act = e->d_act;
+    a.raw = d_raw ? d_raw : e->d_raw;
+    a.status = e->d_status;
+    a.comb_out = d_out_f32;
+    DecFront f{};
+    f.logits = d_logits;
+    f.x = static_cast<const __half*>(d_x_f16);
+    f.tokens = tokens;
+    f.ids_out = d_ids;
+    f.weights_out = d_weights;
+    f.journal = e->d_journal;
+    f.scratch = e->d_front_scratch;
+    f.ctr = e->d_front_ctr;
+    f.epoch = e->front_epoch;
+    GemmMaps gu = bank.dec_gu, dn = bank.dec_dn;
+    dn.b = e->map_act_dec;
+    stage_begin(e, kStageExperts, stream);
+    err = launch_moe_decode_front(gu, dn, a, f, e->num_sms, stream);
+    if (err != cudaSuccess) return cuda_fail(e, err, "decode front-end launch");
+    stage_end(e, kStageExperts, stream);
+    e->launches += 1;
+    e->h_ids_count = static_cast<size_t>(tokens) * K;
+    e->journal_stream = stream;
+    return DEE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
 int dee_moe_forward_routed_device(dee_engine* e, int layer, const void* d_x_f16, int tokens, const float* d_logits,
                                   int32_t* d_ids, float* d_weights, float* d_out_f32, float* d_raw, void* stream_v) {
     int rc = check_engine(e);
@@ -880,6 +961,9 @@ int dee_moe_forward_routed_device(dee_engine* e, int layer, const void* d_x_f16,
     const int K = e->cfg.topk;
     const size_t sel = static_cast<size_t>(tokens) * K;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
+    if (decode_front_fits(tokens, K, e->cfg.num_experts) && sel <= static_cast<size_t>(kFrontEngineMaxSel))
+        return forward_front(e, layer, d_x_f16, tokens, d_logits, d_ids,
+                                                                            d_weights, d_out_f32, d_raw, stream);
     const bool fuse = route_permute_fits(tokens, K, e->cfg.num_experts);
     if (!fuse && (rc = dee_route_topk_device(e, d_logits, tokens, d_ids, d_weights, stream)) != DEE_OK) return rc;
     e->h_ids_count = sel;
@@ -1525,6 +1609,15 @@ int dee_engine_sync_status(dee_engine* e, void* stream, uint32_t* status_out) {
     if (status_out) *status_out = st;
     if (st != 0) {
         cudaMemsetAsync(e->d_status, 0, 4, s);
+        // a launch that gave up may have left the decode front end's counters
+        // short of their per-launch totals: start them over
+        if (e->d_front_ctr) {
+            cudaMemsetAsync(e->d_front_ctr, 0,
+                            (kFrontMaxTiles + static_cast<size_t>(kFrontMaxSel) * (e->cfg.hidden / 128)) *
+                                sizeof(unsigned long long),
+                            s);
+            e->front_epoch = 0;
+        }
         cudaStreamSynchronize(s);
         char buf[320];
         std::snprintf(buf, sizeof(buf),

@@ -76,6 +76,40 @@ constexpr int kDecodeMaxTokens = 64;
 constexpr int kDecodeMaxSelections = 384;  // selections (rows) the decode kernel takes
 cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs& args, int grid,
                               cudaStream_t stream);
+// The whole decode layer in one launch, for batches decode_front_fits
+// accepts (T*K <= kFrontMaxSel, E <= 256; live semantics, one GPU): every
+// CTA routes the batch and groups it itself (the router of
+// launch_route_topk and the grouping of launch_permute, computed
+// redundantly per CTA), loads its token rows straight from x with bulk
+// copies, and runs the gate/up and down items and the combine of
+// launch_moe_decode_layer.  The counters between CTAs carry the launch's
+// epoch in their high 32 bits, so nothing is zeroed between calls.
+constexpr int kFrontMaxSel = 96;
+constexpr int kFrontMaxTiles = kFrontMaxSel;  // a tile holds at least one selection
+constexpr int kFrontScratchInts = 2 * kFrontMaxSel + 4 * kFrontMaxTiles;  // perm, weights, tiles per CTA
+struct DecFront {
+    const float* logits;      // [T, E] FP32 router logits
+    const __half* x;          // [T, H] token rows
+    int tokens;
+    int32_t* ids_out;         // [T, K]  (written by CTA 0)
+    float* weights_out;       // [T, K]  (written by CTA 0)
+    int32_t* journal;         // [T*K] or null (written by CTA 0)
+    int32_t* scratch;         // [grid * kFrontScratchInts]
+    unsigned long long* ctr;  // [kFrontMaxTiles + kFrontMaxSel * H/128], zeroed once at allocation
+    uint32_t epoch;           // > 0 and new for every launch on these counters
+};
+inline bool decode_front_fits(int tokens, int topk, int experts) {
+    return tokens > 0 && topk > 0 && topk <= experts && experts <= 256 &&
+           static_cast<long long>(tokens) * topk <= kFrontMaxSel;
+}
+// The engine takes the one-launch path for batches of at most this many
+// selections: measured on a B200 (DeepSeek-V4 layer, 256 experts), it saves
+// ~7 us of ~49 at one token but is ~1.5 us slower at eight tokens (48
+// selections), where every CTA routing all eight tokens costs more than the
+// separate router, grouping and gather kernels.
+constexpr int kFrontEngineMaxSel = 24;
+cudaError_t launch_moe_decode_front(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args,
+                                    const DecFront& front, int grid, cudaStream_t stream);
 // Both projections in one persistent launch: the gate/up items of every tile,
 // then the down items (each waits, bounded, for its tile's gate/up items),
 // and, with args.comb_out, the fused rank-order combine.  args.tile_done and

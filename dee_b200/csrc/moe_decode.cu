@@ -32,6 +32,7 @@
 // raw[token * K + rank] (engine.cpp:1080-1113).
 #include "decode_common.cuh"
 #include "kernels.h"
+#include "routing.cuh"
 
 namespace dee {
 namespace {
@@ -51,6 +52,15 @@ constexpr int kDecBarBytes = 256;  // stage, scale-slot and signal barriers, per
 constexpr int kDecRedBytes = 2 * 8 * 32 * 4 * 4 + 2 * 2 * 8 * 4;  // [parity][pair][lane][4] sums + flags
 constexpr uint32_t kSmemLimit = 232448;
 constexpr int kDecScSlots = 3;  // per-item scale rows: the consumed item, the next, the one after
+// The front end's tables in shared memory: per tile the token of each row
+// (u8), the tile (expert | row_start << 8 | n_rows << 16) and the expert's
+// record slot; per grouped row its position t*K + r (u8).
+constexpr int kFtTok = 0;
+constexpr int kFtTile = kFtTok + kFrontMaxTiles * 8;
+constexpr int kFtSlot = kFtTile + kFrontMaxTiles * 4;
+constexpr int kFtPerm = kFtSlot + kFrontMaxTiles * 4;
+constexpr int kDecTokBytes = (kFtPerm + kFrontMaxSel + 15) & ~15;
+static_assert(kFrontMaxSel <= 256 && kFrontMaxTiles <= 256, "front-end tables hold u8 rows and positions");
 
 // Shared-memory plan: a ring of 512-wide K stages (packed weights + token
 // rows), three slots of per-item scale rows (128 rows x K/32 bytes), the
@@ -65,13 +75,13 @@ struct DecLayout {
 __host__ __device__ inline DecLayout dec_layout(int k_total) {
     DecLayout L;
     L.sc_slot = (static_cast<uint32_t>(128 * (k_total / 32)) + 1023u) & ~1023u;
-    const uint32_t fixed = 1024 + kDecScSlots * L.sc_slot + kDecBarBytes + kDecRedBytes;
+    const uint32_t fixed = 1024 + kDecScSlots * L.sc_slot + kDecBarBytes + kDecRedBytes + kDecTokBytes;
     const uint32_t room = fixed < kSmemLimit ? (kSmemLimit - fixed) / kDecStageBytes : 0;
     L.stages = room < kDecMaxStages ? static_cast<int>(room) : kDecMaxStages;
     L.sc_off = L.stages * kDecStageBytes;
     L.bar_off = L.sc_off + kDecScSlots * L.sc_slot;
     L.red_off = L.bar_off + kDecBarBytes;
-    L.bytes = 1024 + L.red_off + kDecRedBytes;
+    L.bytes = 1024 + L.red_off + kDecRedBytes + kDecTokBytes;
     return L;
 }
 
@@ -151,9 +161,8 @@ struct DecPlan {
     int n_gu, n_items, mg, md;
 };
 
-__device__ __forceinline__ DecPlan dec_plan(const GemmArgs& a) {
+__device__ __forceinline__ DecPlan dec_plan(const GemmArgs& a, int nt) {
     DecPlan p;
-    const int nt = *a.n_tiles;
     p.mg = a.inter / 64;
     p.md = a.hidden / 128;
     p.n_gu = (a.phases & 1) ? nt * p.mg : 0;
@@ -176,8 +185,35 @@ struct DecItem {
     bool valid, gu;
 };
 
-__device__ __forceinline__ TileDesc load_tile(const GemmArgs& a, const DecPlan& p, int item) {
-    return item < p.n_gu ? a.tiles[item / p.mg] : a.tiles[(item - p.n_gu) / p.md];
+__device__ __forceinline__ TileDesc load_tile(const TileDesc* tiles, const DecPlan& p, int item) {
+    return item < p.n_gu ? tiles[item / p.mg] : tiles[(item - p.n_gu) / p.md];
+}
+
+// A tile from the front end's shared-memory table (n_pad is not used by
+// the decode kernel).
+__device__ __forceinline__ TileDesc front_tile(const uint8_t* ft, int tile) {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(ft + kFtTile)[tile];
+    TileDesc td;
+    td.expert = static_cast<int>(w & 0xFFu);
+    td.row_start = static_cast<int>((w >> 8) & 0xFFu);
+    td.n_rows = static_cast<int>((w >> 16) & 0xFFu);
+    td.n_pad = 0;
+    return td;
+}
+
+// The front end's item: tile and record slot from the shared-memory tables.
+__device__ __forceinline__ DecItem front_item(const GemmArgs& a, const DecPlan& p, const uint8_t* ft, int item) {
+    DecItem d;
+    d.gu = item < p.n_gu;
+    const int j = d.gu ? item : item - p.n_gu;
+    const int mt = d.gu ? p.mg : p.md;
+    d.tile = j / mt;
+    d.m = j - d.tile * mt;
+    d.td = front_tile(ft, d.tile);
+    const int slot = reinterpret_cast<const int32_t*>(ft + kFtSlot)[d.tile];
+    d.valid = slot >= 0 && slot < a.num_slots && d.td.n_rows > 0 && d.td.n_rows <= 8;
+    d.slot = d.valid ? slot : 0;
+    return d;
 }
 
 // Completes an item from its tile descriptor: the expert's record slot and
@@ -244,6 +280,34 @@ __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+// The front end's counters advance by a fixed amount per launch: a tile
+// counter by I/64 (its gate/up items, or one filler add for a tile the
+// launch does not have), a (token, feature block) counter by K (its rows, or
+// a filler add for a token beyond the batch).  After launch number `epoch`
+// they read epoch * I/64 and epoch * K, so nothing is zeroed between calls.
+// Bounded wait (gpu-scope acquire) for *p >= target.
+__device__ __forceinline__ bool wait_u64_geq(const unsigned long long* p, unsigned long long target,
+                                             uint32_t* status, uint32_t code) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        unsigned long long v;
+        asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+        if (v >= target) return true;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            atomicOr(status, code);
+            return false;
+        }
+        __nanosleep(128);
+    }
+}
+
+// Address of a thread's token slice j (see consume_item).
+template <bool kRowsB>
+__device__ __forceinline__ uint32_t b_addr(uint32_t bb0, uint32_t bb1, int j) {
+    if constexpr (kRowsB) return j == 7 ? bb1 : bb0 + (j >> 1) * 128 + (j & 1) * 64;
+    else return ((j & 1) ? bb1 : bb0) + (j >> 1) * 1024;
+}
+
 // Shared-memory handles of the consumers.
 struct DecSmem {
     uint8_t* smem;
@@ -258,10 +322,13 @@ struct DecSmem {
 // One work item of one consumer warp: the K stages, the pair reduction and
 // (first warp of the pair) the epilogue; with `signal`, the first warps then
 // hand the item to the signal warp.  Returns false when a wait gave up.
-template <bool kGU, bool kOfficial>
+// kRowsB: the gate/up token rows sit row-major in the stage (one 1 KB row
+// per token, rows 4-7 rotated by 64 bytes within their row) as the front
+// end's bulk copies place them, instead of the 128-byte-swizzled box.
+template <bool kGU, bool kOfficial, bool kRowsB>
 __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayout& L, const DecSmem& S, int li,
                                              int& st, uint32_t& ph, int& parity, int n_stages, bool signal,
-                                             int warp, int lane) {
+                                             int warp, int lane, const int* perm, const uint8_t* perm8) {
     uint32_t* status = args.status;
     const int k_total = kGU ? args.hidden : args.inter;
     const int k_stages = k_total / kKStage;
@@ -290,8 +357,21 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
     // (whose bits 4-6 are otherwise zero) the address of chunk j is
     // (stage + w_off) ^ (j * 16), for the lo and hi rows alike.
     const uint32_t w_off = kh * kHalf + row_lo * 128 + (g << 4) + q * 4;
-    const uint32_t b_off0 = kDecPkBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
-    const uint32_t b_off1 = kDecPkBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
+    // Token fragments: the 16-byte slice j of this thread's row.  Swizzled
+    // box: chunk (j>>1) of the half at b_off0 / b_off1 by the parity of j.
+    // Row-major rows: K offset kh*512 + (j>>1)*128 + (j&1)*64 + q*16 plus the
+    // row's rotation, which wraps (to q*16) only for j = 7 of the second half
+    // of a rotated row, so j = 7 gets its own base.  Rows brow and brow + 4
+    // of a shared-memory phase differ by 64 bytes: distinct banks.
+    uint32_t b_off0, b_off1;
+    if constexpr (kGU && kRowsB) {
+        const uint32_t rot = (brow & 4) ? 64u : 0u;
+        b_off0 = kDecPkBytes + brow * 1024 + kh * 512 + rot + q * 16;
+        b_off1 = kDecPkBytes + brow * 1024 + ((kh * 512 + 448 + q * 16 + rot) & 1023u);
+    } else {
+        b_off0 = kDecPkBytes + kh * 4096 + brow * 128 + ((q ^ brow) << 4);
+        b_off1 = kDecPkBytes + kh * 4096 + brow * 128 + (((4 + q) ^ brow) << 4);
+    }
     // this thread's scale bytes of stage s: row_lo * rb + s * 16 + kh * 8 in
     // the slot, the 16-byte chunk s moved to s ^ sw when the rows came in
     // swizzled (sw from the row's address bits 7 and up, as the tensor copy
@@ -327,7 +407,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
                 const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
                 const uint32_t wlo = lds_u32(wa);
                 const uint32_t whi = lds_u32(wa + kHi);
-                const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
+                const uint4 bv = lds_v4(b_addr<kGU && kRowsB>(bb0, bb1, j));
                 uint32_t a[8];  // [lo b0..b3, hi b0..b3] as f16x2
                 cvt_e2m1x8(wlo, a[0], a[1], a[2], a[3]);
                 cvt_e2m1x8(whi, a[4], a[5], a[6], a[7]);
@@ -349,7 +429,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
                 const uint32_t wa = wb ^ static_cast<uint32_t>(j << 4);
                 const uint32_t wlo = lds_u32(wa);
                 const uint32_t whi = lds_u32(wa + kHi);
-                const uint4 bv = lds_v4(((j & 1) ? bb1 : bb0) + (j >> 1) * 1024);
+                const uint4 bv = lds_v4(b_addr<kGU && kRowsB>(bb0, bb1, j));
                 const Scale s_lo = make_scale(((j < 4 ? slo.x : slo.y) >> (8 * (j & 3))) & 0xFFu);
                 const Scale s_hi = make_scale(((j < 4 ? shi.x : shi.y) >> (8 * (j & 3))) & 0xFFu);
                 uint32_t a[8];
@@ -404,7 +484,9 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                const float w = (kOfficial && args.route_w) ? args.route_w[args.perm[it_row_start + n]] : 1.0f;
+                const float w = (kOfficial && args.route_w)
+                                    ? args.route_w[kRowsB ? perm8[it_row_start + n] : perm[it_row_start + n]]
+                                    : 1.0f;
                 args.act[static_cast<size_t>(it_row_start + n) * args.inter + feat] =
                     swiglu_out(c[h], c[2 + h], lim, kOfficial, w);
             }
@@ -414,7 +496,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                const int pos = args.perm[it_row_start + n];
+                const int pos = kRowsB ? static_cast<int>(perm8[it_row_start + n]) : perm[it_row_start + n];
                 float* dst;
                 if (args.raw_peers) {  // straight into the token owner's return buffer
                     const int src = pos / args.ep_capacity;
@@ -445,26 +527,150 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
     return true;
 }
 
-template <bool kOfficial>
-__global__ void __launch_bounds__(kDecThreads, 1)
-    moe_decode_kernel(const __grid_constant__ DecMaps maps, const GemmArgs args) {
-    // The tile list comes from the permutation kernel, which has completed
-    // whenever this kernel runs: its predecessor (gather or gate/up) only
-    // signals its dependents after its own griddepcontrol.wait.  Everything
-    // that reads weights or the tile list may therefore start before this
-    // kernel's wait; only the token rows (the predecessor's output) and the
-    // counters the permutation zeroed wait.
-    const DecPlan P = dec_plan(args);
-    const int n_items = P.n_items;
-    if (static_cast<int>(blockIdx.x) >= n_items) {
-        pdl_wait();
-        pdl_trigger();
-        return;
+// The front end's router and grouping, run by every thread of every CTA on
+// the same inputs (so every CTA derives the same tile list without a grid
+// barrier).  The scratch lives in the stage ring, which nothing uses yet.
+// Routing: route_token per token (one warp each), as route_topk_kernel.
+// Grouping: selections enumerated j = rank * T + token and placed stably by
+// expert id (engine.cpp:812-823), tiles of at most kDecodeTileRows rows split
+// evenly, as permute_block.  Outputs go to this CTA's slice of the scratch
+// (grouped row -> position, weights by position, tiles); CTA 0 also writes
+// the caller's ids, weights and journal.  Returns the number of tiles.
+__device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* smem, uint8_t* ft) {
+    const int T = f.tokens, K = a.topk, E = a.num_experts, sel = T * K;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int32_t* s_ids = reinterpret_cast<int32_t*>(smem);              // [kFrontMaxSel] by position
+    float* s_w = reinterpret_cast<float*>(s_ids + kFrontMaxSel);    // [kFrontMaxSel] by position
+    int* s_ej = reinterpret_cast<int*>(s_w + kFrontMaxSel);         // [kFrontMaxSel] expert of selection j
+    int* cnt = s_ej + kFrontMaxSel;                                 // [256]
+    int* off = cnt + 256;                                           // [257]
+    int* toff = off + 257;                                          // [257]
+    float* sp = reinterpret_cast<float*>(smem + 8192);              // [warps][256] router scratch
+    for (int t = warp; t < T; t += kDecThreads / 32)
+        route_token<8>(f.logits + static_cast<size_t>(t) * E, E, K, lane, sp + warp * 256, s_ids + t * K,
+                       s_w + t * K, nullptr, a.status);
+    __syncthreads();
+    for (int j = tid; j < sel; j += kDecThreads) {
+        const int r = j / T, t = j - r * T;
+        s_ej[j] = s_ids[t * K + r];
     }
+    for (int e = tid; e < E; e += kDecThreads) {
+        int c = 0;
+        for (int p = 0; p < sel; ++p) c += s_ids[p] == e;
+        cnt[e] = c;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // exclusive scans of the group sizes and of the tiles per group
+        const int per = (E + 31) / 32;
+        int sum = 0, sum_t = 0;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < E) {
+                sum += cnt[e];
+                sum_t += (cnt[e] + kDecodeTileRows - 1) / kDecodeTileRows;
+            }
+        }
+        int incl = sum, incl_t = sum_t;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int x = __shfl_up_sync(0xffffffffu, incl, o);
+            const int y = __shfl_up_sync(0xffffffffu, incl_t, o);
+            if (lane >= o) { incl += x; incl_t += y; }
+        }
+        int run = incl - sum, run_t = incl_t - sum_t;
+        for (int i = 0; i < per; ++i) {
+            const int e = lane * per + i;
+            if (e < E) {
+                off[e] = run;
+                toff[e] = run_t;
+                run += cnt[e];
+                run_t += (cnt[e] + kDecodeTileRows - 1) / kDecodeTileRows;
+            }
+        }
+        if (lane == 31) { off[E] = incl; toff[E] = incl_t; }
+    }
+    __syncthreads();
+    // combine weights by position: this CTA's slice of the scratch
+    float* scr_w = reinterpret_cast<float*>(f.scratch + static_cast<size_t>(blockIdx.x) * kFrontScratchInts);
+    uint8_t* ft_tok = ft + kFtTok;
+    uint32_t* ft_tile = reinterpret_cast<uint32_t*>(ft + kFtTile);
+    int32_t* ft_slot = reinterpret_cast<int32_t*>(ft + kFtSlot);
+    uint8_t* ft_perm = ft + kFtPerm;
+    for (int j = tid; j < sel; j += kDecThreads) {
+        const int e = s_ej[j];
+        int rank = 0;
+        for (int j2 = 0; j2 < j; ++j2) rank += s_ej[j2] == e;
+        const int r = j / T, t = j - r * T;
+        ft_perm[off[e] + rank] = static_cast<uint8_t>(t * K + r);
+        scr_w[t * K + r] = s_w[t * K + r];
+        // the row's token, by tile and row within the tile (tiles split the
+        // expert's rows evenly, as below)
+        const int c = cnt[e];
+        const int ntl = (c + kDecodeTileRows - 1) / kDecodeTileRows;
+        const int sz = (c + ntl - 1) / ntl;
+        ft_tok[(toff[e] + rank / sz) * 8 + rank % sz] = static_cast<uint8_t>(t);
+    }
+    for (int e = tid; e < E; e += kDecThreads) {
+        const int c = cnt[e];
+        if (c == 0) continue;
+        const int ntl = (c + kDecodeTileRows - 1) / kDecodeTileRows;
+        const int sz = (c + ntl - 1) / ntl;
+        const int slot = a.slot_of[e];
+        for (int i = 0; i < ntl; ++i) {
+            const int n = min(sz, c - i * sz);
+            ft_tile[toff[e] + i] = static_cast<uint32_t>(e) | static_cast<uint32_t>(off[e] + i * sz) << 8 |
+                                   static_cast<uint32_t>(n) << 16;
+            ft_slot[toff[e] + i] = slot;
+        }
+    }
+    const int nt = toff[E];
+    if (blockIdx.x == 0) {
+        for (int p = tid; p < sel; p += kDecThreads) {
+            f.ids_out[p] = s_ids[p];
+            f.weights_out[p] = s_w[p];
+            if (f.journal) f.journal[p] = s_ids[p];
+        }
+        // filler adds: the counters of tiles and tokens this launch does not
+        // have advance like the others (relaxed; nothing waits on them in
+        // this launch, and the next launch starts after this one completes)
+        const int md = a.hidden / 128;
+        for (int t = nt + tid; t < kFrontMaxTiles; t += kDecThreads)
+            atomicAdd(f.ctr + t, static_cast<unsigned long long>(a.inter / 64));
+        for (int i = T * md + tid; i < kFrontMaxSel * md; i += kDecThreads)
+            atomicAdd(f.ctr + kFrontMaxTiles + i, static_cast<unsigned long long>(K));
+    }
+    __syncthreads();
+    return nt;
+}
+
+template <bool kOfficial, bool kFront>
+__global__ void __launch_bounds__(kDecThreads, 1)
+    moe_decode_kernel(const __grid_constant__ DecMaps maps, const GemmArgs args,
+                      const __grid_constant__ DecFront front) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
+    // The work list.  Without the front end the tile list comes from the
+    // permutation kernel, which has completed whenever this kernel runs: its
+    // predecessor (gather or gate/up) only signals its dependents after its
+    // own griddepcontrol.wait.  Everything that reads weights or the tile
+    // list may therefore start before this kernel's wait; only the token rows
+    // (the predecessor's output) and the counters the permutation zeroed
+    // wait.  The front end waits first and derives the list itself, into
+    // shared-memory tables (after the barriers are set up and the tensor
+    // maps prefetched, so that the first copies follow the grouping at once).
     const DecLayout L = dec_layout(dec_layout_k(args));
+    DecPlan P;
+    if constexpr (!kFront) {
+        P = dec_plan(args, *args.n_tiles);
+        if (static_cast<int>(blockIdx.x) >= P.n_items) {
+            pdl_wait();
+            pdl_trigger();
+            return;
+        }
+    }
+    uint8_t* ft = smem + L.red_off + kDecRedBytes;  // front-end tables
     const int n_stages = L.stages;
     DecSmem S;
     S.smem = smem;
@@ -486,7 +692,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     const int lane = threadIdx.x & 31;
     const bool gu_on = (args.phases & 1) != 0, dn_on = (args.phases & 2) != 0;
     // the down items of a two-phase launch wait for their tile's gate/up items
-    const bool dep = gu_on && dn_on && args.tile_done != nullptr;
+    const bool dep = gu_on && dn_on && (kFront || args.tile_done != nullptr);
     const bool signal = dep || args.comb_out != nullptr;
     if (threadIdx.x == 0) {
         for (int i = 0; i < n_stages; ++i) {
@@ -522,8 +728,22 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         }
     }
     __syncthreads();
-    if (warp != 0) pdl_wait();
-    pdl_trigger();
+    if constexpr (kFront) {
+        pdl_wait();
+        pdl_trigger();
+        P = dec_plan(args, front_route_group(args, front, smem, ft));
+        if (static_cast<int>(blockIdx.x) >= P.n_items) return;
+    } else {
+        if (warp != 0) pdl_wait();
+        pdl_trigger();
+    }
+    const int n_items = P.n_items;
+    const TileDesc* tiles = args.tiles;
+    const int* perm = args.perm;
+    const float* comb_w = kFront ? reinterpret_cast<const float*>(front.scratch + static_cast<size_t>(blockIdx.x) *
+                                                                                     kFrontScratchInts)
+                                 : args.comb_w;
+    const uint8_t* ft_perm = ft + kFtPerm;
     uint32_t* status = args.status;
     const int H = args.hidden, I = args.inter;
 
@@ -580,9 +800,31 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 tma_load_4d(pk, &maps.dw2, &S.full[st], 0, d.m * 128, 2 * s, d.slot, pol_w);
             }
         };
+        // front end, gate/up: each token row's 1 KB of the stage by bulk copy
+        // straight from x into row n of the stage (rows 4-7 rotated by 64
+        // bytes: two copies); otherwise one box of the grouped rows
         auto issue_tokens = [&](const DecItem& d, int s, int st) {
-            tma_load_3d(smem + st * kDecStageBytes + kDecPkBytes, d.gu ? &maps.gx : &maps.dact, &S.full[st], 0,
-                        d.td.row_start, 8 * s, pol_b);
+            uint8_t* bdst = smem + st * kDecStageBytes + kDecPkBytes;
+            if (kFront && d.gu) {
+                const uint8_t* x = reinterpret_cast<const uint8_t*>(front.x);
+                const uint8_t* toks = ft + kFtTok + d.tile * 8;
+                for (int n = 0; n < d.td.n_rows; ++n) {
+                    const int tok = toks[n];
+                    const uint8_t* src = x + (static_cast<size_t>(tok) * H + static_cast<size_t>(kKStage) * s) * 2;
+                    uint8_t* dst = bdst + n * 1024;
+                    if (n & 4) {
+                        bulk_load(dst + 64, src, 960, &S.full[st]);
+                        bulk_load(dst, src + 960, 64, &S.full[st]);
+                    } else {
+                        bulk_load(dst, src, 1024, &S.full[st]);
+                    }
+                }
+            } else {
+                tma_load_3d(bdst, d.gu ? &maps.gx : &maps.dact, &S.full[st], 0, d.td.row_start, 8 * s, pol_b);
+            }
+        };
+        auto stage_bytes = [&](const DecItem& d) -> uint32_t {
+            return (kFront && d.gu) ? static_cast<uint32_t>(kDecPkBytes + d.td.n_rows * 1024) : kDecStageBytes;
         };
         auto stages_of = [&](const DecItem& d) { return (d.gu ? H : I) / kKStage; };
         // The next item's scale rows are issued when an item starts, so they
@@ -592,19 +834,31 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // tile descriptor of item li+3 are in flight.
         const int G = gridDim.x;
         int item = blockIdx.x;
-        DecItem cur = finish_item(args, P, item, load_tile(args, P, item));
+        auto meta = [&](int it, const TileDesc& td) -> DecItem {
+            if constexpr (kFront) return front_item(args, P, ft, it);
+            else return finish_item(args, P, it, td);
+        };
+        auto ltile = [&](int it) -> TileDesc {
+            if constexpr (kFront) return TileDesc{};  // read with the item from shared memory
+            else return load_tile(tiles, P, it);
+        };
+        DecItem cur = meta(item, ltile(item));
         DecItem n1{};
-        if (item + G < n_items) n1 = finish_item(args, P, item + G, load_tile(args, P, item + G));
+        if (item + G < n_items) n1 = meta(item + G, ltile(item + G));
         TileDesc td2{};
-        if (item + 2 * G < n_items) td2 = load_tile(args, P, item + 2 * G);
+        if (item + 2 * G < n_items) td2 = ltile(item + 2 * G);
         // Before the wait: the first two items' scale rows and the weights of
-        // the first ring's worth of stages.
+        // the first ring's worth of stages.  (The front end has its token
+        // rows at hand too; issuing each stage's weights and tokens together
+        // instead landed the first stage sooner but made the layer slower:
+        // 138.5 against 132.7 us at b = 8, measured on one B200.)
         if (!issue_scales(cur, 0)) return;
         if (item + G < n_items && !issue_scales(n1, 1)) return;
         const int k0 = stages_of(cur);
         const int pre = n_stages < k0 ? n_stages : k0;
+        if (kFront) fence_proxy_async_smem();  // the ring held the front end's generic scratch
         for (int s = 0; s < pre; ++s) {  // first use of ring slots 0..pre-1
-            mbar_arrive_expect_tx(&S.full[s], kDecStageBytes);
+            mbar_arrive_expect_tx(&S.full[s], stage_bytes(cur));
             issue_weights(cur, s, s);
         }
         pdl_wait();
@@ -614,14 +868,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int li = 0; item < n_items; item += G, ++li) {
             if (li > 0 && item + G < n_items && !issue_scales(n1, li + 1)) return;
             DecItem n2{};
-            if (item + 2 * G < n_items) n2 = finish_item(args, P, item + 2 * G, td2);
-            if (item + 3 * G < n_items) td2 = load_tile(args, P, item + 3 * G);
+            if (item + 2 * G < n_items) n2 = meta(item + 2 * G, td2);
+            if (item + 3 * G < n_items) td2 = ltile(item + 3 * G);
             if (!cur.valid) atomicOr(status, kStatusBadExpert);
             const int ks = stages_of(cur);
             for (int s = 0; s < ks; ++s) {
                 if (li > 0 || s >= pre) {
                     if (!mbar_wait(&S.empty[st], ph ^ 1, status, kStatusTimeoutTma)) return;
-                    mbar_arrive_expect_tx(&S.full[st], kDecStageBytes);
+                    mbar_arrive_expect_tx(&S.full[st], stage_bytes(cur));
                     issue_weights(cur, s, st);
                 }
                 if (s == 0 && dep && !cur.gu) {
@@ -684,8 +938,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
             if (item < P.n_gu) continue;
             const int tile = (item - P.n_gu) / P.md;
-            if (!wait_count_geq(&args.tile_done[tile], static_cast<uint32_t>(P.mg), status, kStatusTimeoutTma))
-                return;
+            const bool ready =
+                kFront ? wait_u64_geq(front.ctr + tile, static_cast<unsigned long long>(front.epoch) * P.mg, status,
+                                      kStatusTimeoutTma)
+                       : wait_count_geq(&args.tile_done[tile], static_cast<uint32_t>(P.mg), status, kStatusTimeoutTma);
+            if (!ready) return;
             ++dk;
             asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(dep_ready)), "r"(dk)
                          : "memory");
@@ -714,19 +971,26 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                 if (dep && lane == 0) {
                     fence_proxy_async_global();
                     __threadfence();
-                    atomicAdd(&args.tile_done[item / P.mg], 1u);
+                    if (kFront)
+                        atomicAdd(front.ctr + item / P.mg, 1ull);
+                    else
+                        atomicAdd(&args.tile_done[item / P.mg], 1u);
                 }
             } else if (args.comb_out) {
                 const int j = item - P.n_gu;
                 const int tile = j / P.md;
                 const int m = j - tile * P.md;
-                const TileDesc td = args.tiles[tile];
+                const TileDesc td = kFront ? front_tile(ft, tile) : tiles[tile];
                 __threadfence();
                 int tok = 0;
                 bool last = false;
                 if (lane < td.n_rows) {
-                    tok = args.perm[td.row_start + lane] / K;
-                    last = atomicAdd(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
+                    tok = (kFront ? static_cast<int>(ft_perm[td.row_start + lane]) : perm[td.row_start + lane]) / K;
+                    if (kFront)
+                        last = atomicAdd(front.ctr + kFrontMaxTiles + tok * P.md + m, 1ull) + 1 ==
+                               static_cast<unsigned long long>(front.epoch) * K;
+                    else
+                        last = atomicAdd(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
                 }
                 uint32_t mask = __ballot_sync(0xffffffffu, last);
                 if (mask) {
@@ -739,7 +1003,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
                         for (int r = 0; r < K; ++r) {
                             const size_t sel = static_cast<size_t>(t) * K + r;
-                            const float wr = args.comb_w[sel];
+                            const float wr = comb_w[sel];
                             const float4 v = __ldcg(reinterpret_cast<const float4*>(args.raw + sel * H + h0));
                             acc.x = __fadd_rn(acc.x, __fmul_rn(wr, v.x));
                             acc.y = __fadd_rn(acc.y, __fmul_rn(wr, v.y));
@@ -761,30 +1025,34 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     uint32_t ph = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
         const bool go = item < P.n_gu
-                            ? consume_item<true, kOfficial>(args, L, S, li, st, ph, parity, n_stages, signal, warp,
-                                                            lane)
-                            : consume_item<false, kOfficial>(args, L, S, li, st, ph, parity, n_stages, signal,
-                                                             warp, lane);
+                            ? consume_item<true, kOfficial, kFront>(args, L, S, li, st, ph, parity, n_stages, signal,
+                                                                    warp, lane, perm, ft_perm)
+                            : consume_item<false, kOfficial, kFront>(args, L, S, li, st, ph, parity, n_stages,
+                                                                     signal, warp, lane, perm, ft_perm);
         if (!go) break;
     }
 }
 
-template <bool kOfficial>
-cudaError_t launch_dec(const DecMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
-    auto kern = moe_decode_kernel<kOfficial>;
-    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<kOfficial>>(static_cast<int>(kSmemLimit));
+template <bool kOfficial, bool kFront>
+cudaError_t launch_dec(const DecMaps& maps, const GemmArgs& args, const DecFront& front, int grid,
+                       cudaStream_t stream) {
+    auto kern = moe_decode_kernel<kOfficial, kFront>;
+    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<kOfficial, kFront>>(static_cast<int>(kSmemLimit));
     if (e != cudaSuccess) return e;
     const DecLayout L = dec_layout(dec_layout_k(args));
     if (L.stages < 2 || L.bytes > kSmemLimit || args.phases < 1 || args.phases > 3 || args.hidden % kKStage ||
         args.inter % kKStage || args.inter % 64 || args.hidden % 128)
         return cudaErrorInvalidValue;
-    if (args.comb_out && (!(args.phases & 2) || !args.comb_w || !args.comb_cnt || !args.raw || args.raw_peers))
+    if (!kFront && args.comb_out &&
+        (!(args.phases & 2) || !args.comb_w || !args.comb_cnt || !args.raw || args.raw_peers))
         return cudaErrorInvalidValue;
-    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps, args);
+    return launch_pdl(kern, dim3(grid), dim3(kDecThreads), L.bytes, stream, maps, args, front);
 }
 
 cudaError_t launch_decode(const DecMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
-    return args.official ? launch_dec<true>(maps, args, grid, stream) : launch_dec<false>(maps, args, grid, stream);
+    const DecFront none{};
+    return args.official ? launch_dec<true, false>(maps, args, none, grid, stream)
+                         : launch_dec<false, false>(maps, args, none, grid, stream);
 }
 
 }  // namespace
@@ -883,6 +1151,31 @@ cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs
     a.comb_w = nullptr;
     a.comb_cnt = nullptr;
     return launch_decode(m, a, grid, stream);
+}
+
+cudaError_t launch_moe_decode_front(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args,
+                                    const DecFront& front, int grid, cudaStream_t stream) {
+    if (args.official || args.raw_peers || !front.logits || !front.x || !front.scratch || !front.ctr ||
+        !front.ids_out || !front.weights_out || front.epoch == 0 ||
+        !decode_front_fits(front.tokens, args.topk, args.num_experts) || grid <= 0)
+        return cudaErrorInvalidValue;
+    if (args.comb_out && !args.raw) return cudaErrorInvalidValue;
+    DecMaps m;
+    m.gw1 = gu.w0;
+    m.gw3 = gu.w1;
+    m.gx = gu.w0;  // token rows come by bulk copy
+    m.gs1 = gu.s0;
+    m.gs3 = gu.s1;
+    m.dw2 = dn.w0;
+    m.dact = dn.b;
+    m.ds2 = dn.s0;
+    GemmArgs a = args;
+    a.phases = 3;
+    a.scale_swz = gu.scale_swz;
+    a.dn_scale_swz = dn.scale_swz;
+    a.tile_done = nullptr;
+    a.comb_cnt = nullptr;
+    return launch_dec<false, true>(m, a, front, grid, stream);
 }
 
 cudaError_t launch_moe_decode_layer(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args, int grid,

@@ -558,16 +558,21 @@ def test_decode_combine_bitexact_over_calls(torch_cuda, oracle_mod, T, dup):
         assert orc.rel_l2(raw_np, orc.moe_layer_raw(recs, layout, x16, ids)) <= TOL_REL_L2
 
 
-@pytest.mark.parametrize("T,E", [(1, 64), (8, 256), (33, 64), (64, 256), (65, 64), (100, 16)])
-def test_routed_forward_matches_route_then_forward(torch_cuda, oracle_mod, T, E):
+@pytest.mark.parametrize("T,E,H,I", [(1, 64, 512, 512), (3, 16, 512, 512), (4, 256, 512, 512), (8, 256, 512, 512),
+                                     (33, 64, 512, 512), (64, 256, 512, 512), (65, 64, 512, 512),
+                                     (100, 16, 512, 512), (1, 32, 4096, 2048), (4, 32, 4096, 2048)])
+def test_routed_forward_matches_route_then_forward(torch_cuda, oracle_mod, T, E, H, I):
     """dee_moe_forward_routed_device against dee_route_topk_device followed
     by dee_moe_forward_device: ids, weights, raw rows, the combined output
-    and the journal bit-identical.  T*K <= 384 with E <= 256 takes the fused
-    router+permutation kernel; (65, 64) and (100, 16) take the two-kernel
-    fallback inside the same entry point.  Ids also equal the oracle's."""
+    and the journal bit-identical.  T*K <= 24 takes the one-launch layer
+    (routing, grouping and token rows inside the decode kernel; (3, 16) puts
+    several rows in a tile, and the DeepSeek-V4 shape runs it at full size);
+    up to 384 selections with E <= 256 the fused router+permutation kernel;
+    (65, 64) and (100, 16) the two-kernel fallback inside the same entry
+    point.  Ids also equal the oracle's."""
     torch = torch_cuda
     orc = oracle_mod
-    H, I, K = 512, 512, 6
+    K = 6
     layout = orc.Layout(H, I)
     recs = orc.synthetic_records(layout, E, seed=77 + E, kind="normal")
     rng = np.random.default_rng(7000 + T)
