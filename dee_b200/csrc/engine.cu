@@ -399,6 +399,9 @@ struct FusedCombine {
     bool* done;
 };
 
+int forward_front(dee_engine* e, int layer, const void* d_x_f16, int tokens, int K, const float* d_logits,
+                  int32_t* d_ids, float* d_weights, float* d_out_f32, float* d_raw, cudaStream_t stream);
+
 int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const int32_t* d_ids32,
                 float* raw, cudaStream_t stream, int K, bool skip_negative, bool write_journal,
                 const EpReturn* ret = nullptr, const float* official_route_w = nullptr,
@@ -858,6 +861,9 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
         ids32 = e->d_ids;
     }
     e->h_ids_count = sel;
+    if (decode_front_fits(tokens, topk, e->cfg.num_experts) && sel <= static_cast<size_t>(kFrontEngineMaxSel))
+        return forward_front(e, layer, d_x_f16, tokens, topk, nullptr, const_cast<int32_t*>(ids32),
+                             const_cast<float*>(d_weights), d_out_f32, d_raw, stream);
     float* raw = d_raw ? d_raw : e->d_raw;
     bool combined = false;
     const FusedCombine fc{d_weights, d_out_f32, &combined};
@@ -878,17 +884,18 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
 
 }  // extern "C"
 
+namespace dee {
 namespace {
 
-// The whole routed layer of a small decode batch in one launch
-// (launch_moe_decode_front): routing, grouping, token rows, both
-// projections and the combine.
-int forward_front(dee_engine* e, int layer, const void* d_x_f16, int tokens, const float* d_logits, int32_t* d_ids,
-                  float* d_weights, float* d_out_f32, float* d_raw, cudaStream_t stream) {
+// A small decode batch's layer in one launch (launch_moe_decode_front):
+// grouping, token rows, both projections and the combine, and with d_logits
+// the routing too (else d_ids / d_weights are inputs).
+int forward_front(dee_engine* e, int layer, const void* d_x_f16, int tokens, int K, const float* d_logits,
+                  int32_t* d_ids, float* d_weights, float* d_out_f32, float* d_raw, cudaStream_t stream) {
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const dee::Bank& bank = e->banks[layer];
-    const int H = e->cfg.hidden, K = e->cfg.topk;
+    const int H = e->cfg.hidden;
     cudaError_t err;
     if (!e->d_front_scratch) {
         const size_t n_ctr = kFrontMaxTiles + static_cast<size_t>(kFrontMaxSel) * (H / 128);
@@ -947,6 +954,7 @@ int forward_front(dee_engine* e, int layer, const void* d_x_f16, int tokens, con
 }
 
 }  // namespace
+}  // namespace dee
 
 extern "C" {
 
@@ -962,8 +970,7 @@ int dee_moe_forward_routed_device(dee_engine* e, int layer, const void* d_x_f16,
     const size_t sel = static_cast<size_t>(tokens) * K;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
     if (decode_front_fits(tokens, K, e->cfg.num_experts) && sel <= static_cast<size_t>(kFrontEngineMaxSel))
-        return forward_front(e, layer, d_x_f16, tokens, d_logits, d_ids,
-                                                                            d_weights, d_out_f32, d_raw, stream);
+        return forward_front(e, layer, d_x_f16, tokens, K, d_logits, d_ids, d_weights, d_out_f32, d_raw, stream);
     const bool fuse = route_permute_fits(tokens, K, e->cfg.num_experts);
     if (!fuse && (rc = dee_route_topk_device(e, d_logits, tokens, d_ids, d_weights, stream)) != DEE_OK) return rc;
     e->h_ids_count = sel;

@@ -88,11 +88,11 @@ constexpr int kFrontMaxSel = 96;
 constexpr int kFrontMaxTiles = kFrontMaxSel;  // a tile holds at least one selection
 constexpr int kFrontScratchInts = 2 * kFrontMaxSel + 4 * kFrontMaxTiles;  // perm, weights, tiles per CTA
 struct DecFront {
-    const float* logits;      // [T, E] FP32 router logits
+    const float* logits;      // [T, E] FP32 router logits, or null: ids_out / weights_out are inputs
     const __half* x;          // [T, H] token rows
     int tokens;
-    int32_t* ids_out;         // [T, K]  (written by CTA 0)
-    float* weights_out;       // [T, K]  (written by CTA 0)
+    int32_t* ids_out;         // [T, K]  (written by CTA 0 when routing)
+    float* weights_out;       // [T, K]  (written by CTA 0 when routing; may be null without logits and combine)
     int32_t* journal;         // [T*K] or null (written by CTA 0)
     int32_t* scratch;         // [grid * kFrontScratchInts]
     unsigned long long* ctr;  // [kFrontMaxTiles + kFrontMaxSel * H/128], zeroed once at allocation
@@ -102,11 +102,14 @@ inline bool decode_front_fits(int tokens, int topk, int experts) {
     return tokens > 0 && topk > 0 && topk <= experts && experts <= 256 &&
            static_cast<long long>(tokens) * topk <= kFrontMaxSel;
 }
-// The engine takes the one-launch path for batches of at most this many
-// selections: measured on a B200 (DeepSeek-V4 layer, 256 experts), it saves
-// ~7 us of ~49 at one token but is ~1.5 us slower at eight tokens (48
-// selections), where every CTA routing all eight tokens costs more than the
-// separate router, grouping and gather kernels.
+// The engine takes the one-launch layer for batches of at most this many
+// selections.  Measured on a B200 (DeepSeek-V4 layer, 256 experts): with
+// routing inside it saves ~7 us of ~49 at one token; at eight tokens (48
+// selections) it is ~1.5 us slower than the router+grouping kernel, gather
+// and two-phase layer (every CTA routes all eight tokens), and on the
+// caller's ids ~3 us slower than grouping, gather and layer (the in-kernel
+// grouping holds back the first weight copies, which the two-phase layer
+// issues while the gather runs).
 constexpr int kFrontEngineMaxSel = 24;
 cudaError_t launch_moe_decode_front(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args,
                                     const DecFront& front, int grid, cudaStream_t stream);

@@ -546,9 +546,20 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
     int* off = cnt + 256;                                           // [257]
     int* toff = off + 257;                                          // [257]
     float* sp = reinterpret_cast<float*>(smem + 8192);              // [warps][256] router scratch
-    for (int t = warp; t < T; t += kDecThreads / 32)
-        route_token<8>(f.logits + static_cast<size_t>(t) * E, E, K, lane, sp + warp * 256, s_ids + t * K,
-                       s_w + t * K, nullptr, a.status);
+    if (f.logits) {
+        for (int t = warp; t < T; t += kDecThreads / 32)
+            route_token<8>(f.logits + static_cast<size_t>(t) * E, E, K, lane, sp + warp * 256, s_ids + t * K,
+                           s_w + t * K, nullptr, a.status);
+    } else {
+        // ids and weights from the caller (or a router kernel before this
+        // one); an id outside [0, E) is reported and its selection left out
+        for (int p = tid; p < sel; p += kDecThreads) {
+            const int e = f.ids_out[p];
+            if (e < 0 || e >= E) atomicOr(a.status, kStatusBadExpert);
+            s_ids[p] = (e < 0 || e >= E) ? -1 : e;
+            s_w[p] = f.weights_out ? f.weights_out[p] : 0.0f;
+        }
+    }
     __syncthreads();
     for (int j = tid; j < sel; j += kDecThreads) {
         const int r = j / T, t = j - r * T;
@@ -599,6 +610,7 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
     uint8_t* ft_perm = ft + kFtPerm;
     for (int j = tid; j < sel; j += kDecThreads) {
         const int e = s_ej[j];
+        if (e < 0) continue;  // a bad caller id: left out (reported above)
         int rank = 0;
         for (int j2 = 0; j2 < j; ++j2) rank += s_ej[j2] == e;
         const int r = j / T, t = j - r * T;
@@ -627,9 +639,11 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
     const int nt = toff[E];
     if (blockIdx.x == 0) {
         for (int p = tid; p < sel; p += kDecThreads) {
-            f.ids_out[p] = s_ids[p];
-            f.weights_out[p] = s_w[p];
-            if (f.journal) f.journal[p] = s_ids[p];
+            if (f.logits) {
+                f.ids_out[p] = s_ids[p];
+                f.weights_out[p] = s_w[p];
+            }
+            if (f.journal) f.journal[p] = f.logits ? s_ids[p] : f.ids_out[p];
         }
         // filler adds: the counters of tiles and tokens this launch does not
         // have advance like the others (relaxed; nothing waits on them in
@@ -639,6 +653,9 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
             atomicAdd(f.ctr + t, static_cast<unsigned long long>(a.inter / 64));
         for (int i = T * md + tid; i < kFrontMaxSel * md; i += kDecThreads)
             atomicAdd(f.ctr + kFrontMaxTiles + i, static_cast<unsigned long long>(K));
+        // a selection left out still counts for its token's blocks
+        for (int i = tid; i < sel * md; i += kDecThreads)
+            if (s_ids[i / md] < 0) atomicAdd(f.ctr + kFrontMaxTiles + (i / md / K) * md + i % md, 1ull);
     }
     __syncthreads();
     return nt;
@@ -1155,8 +1172,8 @@ cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs
 
 cudaError_t launch_moe_decode_front(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args,
                                     const DecFront& front, int grid, cudaStream_t stream) {
-    if (args.official || args.raw_peers || !front.logits || !front.x || !front.scratch || !front.ctr ||
-        !front.ids_out || !front.weights_out || front.epoch == 0 ||
+    if (args.official || args.raw_peers || !front.x || !front.scratch || !front.ctr || !front.ids_out ||
+        (front.logits && !front.weights_out) || (args.comb_out && !front.weights_out) || front.epoch == 0 ||
         !decode_front_fits(front.tokens, args.topk, args.num_experts) || grid <= 0)
         return cudaErrorInvalidValue;
     if (args.comb_out && !args.raw) return cudaErrorInvalidValue;
