@@ -276,6 +276,24 @@ __device__ __forceinline__ bool wait_smem_geq(const uint32_t* p, uint32_t target
     }
 }
 
+// gpu-scope release add (no result) and acquire-release add (old value).
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ unsigned long long atom_acq_rel_add(unsigned long long* p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -990,46 +1008,66 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             if (!__all_sync(0xffffffffu, ok)) return;
             if (item < P.n_gu) {
                 if (dep && lane == 0) {
+                    // release-add: publishes the stores this lane acquired
+                    // through the mbarrier (the act rows, read next through
+                    // the async proxy)
                     fence_proxy_async_global();
-                    __threadfence();
                     if (kFront)
-                        atomicAdd(front.ctr + item / P.mg, 1ull);
+                        red_release_add(front.ctr + item / P.mg, 1ull);
                     else
-                        atomicAdd(&args.tile_done[item / P.mg], 1u);
+                        red_release_add(&args.tile_done[item / P.mg], 1u);
                 }
             } else if (args.comb_out) {
                 const int j = item - P.n_gu;
                 const int tile = j / P.md;
                 const int m = j - tile * P.md;
                 const TileDesc td = kFront ? front_tile(ft, tile) : tiles[tile];
-                __threadfence();
                 int tok = 0;
                 bool last = false;
                 if (lane < td.n_rows) {
+                    // acquire-release add: publishes the rows this lane
+                    // acquired through the mbarrier, and the lane that
+                    // completes a block acquires every other CTA's rows of it
                     tok = (kFront ? static_cast<int>(ft_perm[td.row_start + lane]) : perm[td.row_start + lane]) / K;
                     if (kFront)
-                        last = atomicAdd(front.ctr + kFrontMaxTiles + tok * P.md + m, 1ull) + 1 ==
+                        last = atom_acq_rel_add(front.ctr + kFrontMaxTiles + tok * P.md + m, 1ull) + 1 ==
                                static_cast<unsigned long long>(front.epoch) * K;
                     else
-                        last = atomicAdd(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
+                        last = atom_acq_rel_add(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
                 }
                 uint32_t mask = __ballot_sync(0xffffffffu, last);
                 if (mask) {
-                    __threadfence();  // the other CTAs' rows of these tokens
+                    // the other lanes read rows the completing lane acquired:
+                    // the warp barrier orders their loads after its acquire
+                    __syncwarp();
                     const int h0 = m * 128 + lane * 4;
                     while (mask) {
                         const int n = __ffs(mask) - 1;
                         mask &= mask - 1;
                         const int t = __shfl_sync(0xffffffffu, tok, n);
+                        const size_t s0 = static_cast<size_t>(t) * K;
                         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                        for (int r = 0; r < K; ++r) {
-                            const size_t sel = static_cast<size_t>(t) * K + r;
-                            const float wr = comb_w[sel];
-                            const float4 v = __ldcg(reinterpret_cast<const float4*>(args.raw + sel * H + h0));
-                            acc.x = __fadd_rn(acc.x, __fmul_rn(wr, v.x));
-                            acc.y = __fadd_rn(acc.y, __fmul_rn(wr, v.y));
-                            acc.z = __fadd_rn(acc.z, __fmul_rn(wr, v.z));
-                            acc.w = __fadd_rn(acc.w, __fmul_rn(wr, v.w));
+                        for (int r0 = 0; r0 < K; r0 += 8) {
+                            // all loads of up to eight rows first (one round
+                            // trip), then the rank-order sum
+                            float wr[8];
+                            float4 v[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                if (r0 + i < K) {
+                                    wr[i] = comb_w[s0 + r0 + i];
+                                    v[i] = __ldcg(reinterpret_cast<const float4*>(args.raw + (s0 + r0 + i) * H + h0));
+                                }
+                            }
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                if (r0 + i < K) {
+                                    acc.x = __fadd_rn(acc.x, __fmul_rn(wr[i], v[i].x));
+                                    acc.y = __fadd_rn(acc.y, __fmul_rn(wr[i], v[i].y));
+                                    acc.z = __fadd_rn(acc.z, __fmul_rn(wr[i], v[i].z));
+                                    acc.w = __fadd_rn(acc.w, __fmul_rn(wr[i], v[i].w));
+                                }
+                            }
                         }
                         *reinterpret_cast<float4*>(args.comb_out + static_cast<size_t>(t) * H + h0) = acc;
                     }
