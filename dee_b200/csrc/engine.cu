@@ -208,6 +208,7 @@ struct dee_engine {
     // one-launch decode layer: [max_tiles] gate/up items done per tile, then
     // [kDecodeMaxSelections * H/128] rows written per (token, feature block)
     uint32_t* d_sync = nullptr;
+    int2* d_tile_grp = nullptr;      // [max_tiles] prefill: first tile and tile count of the tile's expert
     // one-launch decode front end: per-CTA grouping scratch and the
     // epoch-tagged counters (zeroed once), with the epoch of the last launch
     int32_t* d_front_scratch = nullptr;
@@ -287,8 +288,8 @@ void free_workspace(dee_engine* e) {
     cudaFree(e->d_ids); cudaFree(e->d_weights); cudaFree(e->d_perm); cudaFree(e->d_row_of);
     cudaFree(e->d_counts); cudaFree(e->d_offsets); cudaFree(e->d_tiles); cudaFree(e->d_n_tiles);
     cudaFree(e->d_xperm); cudaFree(e->d_act); cudaFree(e->d_raw); cudaFree(e->d_journal);
-    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank); cudaFree(e->d_sync);
-    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr; e->d_sync = nullptr;
+    cudaFree(e->d_perm_chunks); cudaFree(e->d_perm_lrank); cudaFree(e->d_sync); cudaFree(e->d_tile_grp);
+    e->d_perm_chunks = nullptr; e->d_perm_lrank = nullptr; e->d_sync = nullptr; e->d_tile_grp = nullptr;
     if (e->h_ids) cudaFreeHost(e->h_ids);
     e->d_ids = nullptr; e->d_weights = nullptr; e->d_perm = nullptr; e->d_row_of = nullptr;
     e->d_counts = nullptr; e->d_offsets = nullptr; e->d_tiles = nullptr; e->d_n_tiles = nullptr;
@@ -323,6 +324,7 @@ int ensure_capacity(dee_engine* e, size_t sel, cudaStream_t stream) {
         (err = dev_alloc(&e->d_journal, cap)) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_chunks, ((cap + 1023) / 1024) * static_cast<size_t>(E))) != cudaSuccess ||
         (err = dev_alloc(&e->d_perm_lrank, cap)) != cudaSuccess ||
+        (err = dev_alloc(&e->d_tile_grp, static_cast<size_t>(max_tiles))) != cudaSuccess ||
         (err = dev_alloc(&e->d_sync, static_cast<size_t>(max_tiles) +
                                          static_cast<size_t>(kDecodeMaxSelections) * (H / 128))) != cudaSuccess ||
         (err = cudaHostAlloc(reinterpret_cast<void**>(&e->h_ids), cap * sizeof(int32_t),
@@ -438,6 +440,8 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     if (decode) {
         po.clear = e->d_sync;
         po.clear_n = e->max_tiles + (fuse_combine ? tokens * (H / 128) : 0);
+    } else {
+        po.tile_grp = e->d_tile_grp;
     }
     stage_begin(e, kStagePermute, stream);
     cudaError_t err;
@@ -452,8 +456,7 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     }
     stage_end(e, kStagePermute, stream);
     stage_begin(e, kStageGather, stream);
-    err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H,
-                             e->d_xperm, stream);
+    err = launch_gather_rows(d_x, e->d_perm, e->d_offsets + E, static_cast<int>(sel), K, H, e->d_xperm, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "gather launch");
     stage_end(e, kStageGather, stream);
 
@@ -473,6 +476,7 @@ int run_experts(dee_engine* e, int layer, const __half* d_x, int tokens, const i
     a.act = e->d_act;
     a.raw = raw;
     a.status = e->d_status;
+    if (!decode) a.tile_grp = e->d_tile_grp;
     if (official_route_w) {
         a.official = 1;
         a.route_w = official_route_w;
@@ -563,6 +567,7 @@ int run_experts_mx(dee_engine* e, int layer, const __half* d_x, int tokens, cons
     po.chunk_counts = e->d_perm_chunks;
     po.lrank = e->d_perm_lrank;
     po.max_chunks = static_cast<long long>((e->cap_sel + 1023) / 1024);
+    po.tile_grp = e->d_tile_grp;
     stage_begin(e, kStagePermute, stream);
     cudaError_t err = launch_permute(d_ids32, tokens, K, E, gemm_n_max(), e->max_tiles, po, e->d_status, stream);
     if (err != cudaSuccess) return cuda_fail(e, err, "permute launch");
@@ -590,6 +595,7 @@ int run_experts_mx(dee_engine* e, int layer, const __half* d_x, int tokens, cons
     a.act = e->d_act;
     a.raw = raw;
     a.status = e->d_status;
+    a.tile_grp = e->d_tile_grp;
     MxMaps m = bank.mx_gu;
     for (int i = 0; i < 4; ++i) m.bt[i] = e->map_xq_t[i];
     a.k_total = H;

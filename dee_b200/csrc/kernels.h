@@ -263,6 +263,9 @@ struct PermuteOut {
     // (one-CTA permutation only).
     uint32_t* clear = nullptr;
     int clear_n = 0;
+    // Per tile: its expert's first tile and tile count (the prefill GEMMs'
+    // expert-local m-major item order).
+    int2* tile_grp = nullptr;
 };
 // skip_negative: ids of -1 mark unused rows (expert-parallel receive
 // buffers) and are left out without raising kStatusBadExpert.

@@ -341,9 +341,10 @@ struct DecSmem {
 // (first warp of the pair) the epilogue; with `signal`, the first warps then
 // hand the item to the signal warp.  Returns false when a wait gave up.
 // kRowsB: the gate/up token rows sit row-major in the stage (one 1 KB row
-// per token, rows 4-7 rotated by 64 bytes within their row) as the front
-// end's bulk copies place them, instead of the 128-byte-swizzled box.
-template <bool kGU, bool kOfficial, bool kRowsB>
+// per token, rows 4-7 rotated by 64 bytes within their row) as the bulk
+// copies from x place them, instead of the 128-byte-swizzled box.  kPerm8:
+// grouped positions come from the front end's shared-memory table.
+template <bool kGU, bool kOfficial, bool kRowsB, bool kPerm8>
 __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayout& L, const DecSmem& S, int li,
                                              int& st, uint32_t& ph, int& parity, int n_stages, bool signal,
                                              int warp, int lane, const int* perm, const uint8_t* perm8) {
@@ -503,7 +504,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
                 const float w = (kOfficial && args.route_w)
-                                    ? args.route_w[kRowsB ? perm8[it_row_start + n] : perm[it_row_start + n]]
+                                    ? args.route_w[kPerm8 ? perm8[it_row_start + n] : perm[it_row_start + n]]
                                     : 1.0f;
                 args.act[static_cast<size_t>(it_row_start + n) * args.inter + feat] =
                     swiglu_out(c[h], c[2 + h], lim, kOfficial, w);
@@ -514,7 +515,7 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
             for (int h = 0; h < 2; ++h) {
                 const int n = h ? n1 : n0;
                 if (n >= n_rows) continue;
-                const int pos = kRowsB ? static_cast<int>(perm8[it_row_start + n]) : perm[it_row_start + n];
+                const int pos = kPerm8 ? static_cast<int>(perm8[it_row_start + n]) : perm[it_row_start + n];
                 float* dst;
                 if (args.raw_peers) {  // straight into the token owner's return buffer
                     const int src = pos / args.ep_capacity;
@@ -679,10 +680,20 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
     return nt;
 }
 
-template <bool kOfficial, bool kFront>
+// Token rows of a launch: kModeBox, the grouped rows (gather kernel) by one
+// swizzled box per stage; kModeFront, the front end (routing and grouping
+// inside, token rows straight from x by bulk copies).  (Bulk copies from x
+// after the permutation kernel, without the gather, measured slower at
+// b = 8 -- 137.7 against 129.8 us on one B200, reproduced: eight 1 KB
+// copies per stage cost more than one 8 KB box -- and equal at b = 1.)
+constexpr int kModeBox = 0, kModeFront = 1;
+
+template <bool kOfficial, int kMode>
 __global__ void __launch_bounds__(kDecThreads, 1)
     moe_decode_kernel(const __grid_constant__ DecMaps maps, const GemmArgs args,
                       const __grid_constant__ DecFront front) {
+    constexpr bool kFront = kMode == kModeFront;
+    constexpr bool kRows = kMode != kModeBox;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -840,10 +851,12 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         // bytes: two copies); otherwise one box of the grouped rows
         auto issue_tokens = [&](const DecItem& d, int s, int st) {
             uint8_t* bdst = smem + st * kDecStageBytes + kDecPkBytes;
-            if (kFront && d.gu) {
+            if (kRows && d.gu) {
                 const uint8_t* x = reinterpret_cast<const uint8_t*>(front.x);
-                const uint8_t* toks = ft + kFtTok + d.tile * 8;
-                for (int n = 0; n < d.td.n_rows; ++n) {
+                const uint8_t* toks = ft + kFtTok + d.tile * 8;  // the tile rows' tokens
+#pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                    if (n >= d.td.n_rows) break;
                     const int tok = toks[n];
                     const uint8_t* src = x + (static_cast<size_t>(tok) * H + static_cast<size_t>(kKStage) * s) * 2;
                     uint8_t* dst = bdst + n * 1024;
@@ -859,7 +872,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             }
         };
         auto stage_bytes = [&](const DecItem& d) -> uint32_t {
-            return (kFront && d.gu) ? static_cast<uint32_t>(kDecPkBytes + d.td.n_rows * 1024) : kDecStageBytes;
+            return (kRows && d.gu) ? static_cast<uint32_t>(kDecPkBytes + d.td.n_rows * 1024) : kDecStageBytes;
         };
         auto stages_of = [&](const DecItem& d) { return (d.gu ? H : I) / kKStage; };
         // The next item's scale rows are issued when an item starts, so they
@@ -1084,19 +1097,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     uint32_t ph = 0;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x, ++li) {
         const bool go = item < P.n_gu
-                            ? consume_item<true, kOfficial, kFront>(args, L, S, li, st, ph, parity, n_stages, signal,
+                            ? consume_item<true, kOfficial, kRows, kFront>(args, L, S, li, st, ph, parity, n_stages, signal,
                                                                     warp, lane, perm, ft_perm)
-                            : consume_item<false, kOfficial, kFront>(args, L, S, li, st, ph, parity, n_stages,
+                            : consume_item<false, kOfficial, kRows, kFront>(args, L, S, li, st, ph, parity, n_stages,
                                                                      signal, warp, lane, perm, ft_perm);
         if (!go) break;
     }
 }
 
-template <bool kOfficial, bool kFront>
+template <bool kOfficial, int kMode>
 cudaError_t launch_dec(const DecMaps& maps, const GemmArgs& args, const DecFront& front, int grid,
                        cudaStream_t stream) {
-    auto kern = moe_decode_kernel<kOfficial, kFront>;
-    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<kOfficial, kFront>>(static_cast<int>(kSmemLimit));
+    constexpr bool kFront = kMode == kModeFront;
+    auto kern = moe_decode_kernel<kOfficial, kMode>;
+    const cudaError_t e = ensure_smem_attr<moe_decode_kernel<kOfficial, kMode>>(static_cast<int>(kSmemLimit));
     if (e != cudaSuccess) return e;
     const DecLayout L = dec_layout(dec_layout_k(args));
     if (L.stages < 2 || L.bytes > kSmemLimit || args.phases < 1 || args.phases > 3 || args.hidden % kKStage ||
@@ -1110,8 +1124,8 @@ cudaError_t launch_dec(const DecMaps& maps, const GemmArgs& args, const DecFront
 
 cudaError_t launch_decode(const DecMaps& maps, const GemmArgs& args, int grid, cudaStream_t stream) {
     const DecFront none{};
-    return args.official ? launch_dec<true, false>(maps, args, none, grid, stream)
-                         : launch_dec<false, false>(maps, args, none, grid, stream);
+    return args.official ? launch_dec<true, kModeBox>(maps, args, none, grid, stream)
+                         : launch_dec<false, kModeBox>(maps, args, none, grid, stream);
 }
 
 }  // namespace
@@ -1234,7 +1248,7 @@ cudaError_t launch_moe_decode_front(const GemmMaps& gu, const GemmMaps& dn, cons
     a.dn_scale_swz = dn.scale_swz;
     a.tile_done = nullptr;
     a.comb_cnt = nullptr;
-    return launch_dec<false, true>(m, a, front, grid, stream);
+    return launch_dec<false, kModeFront>(m, a, front, grid, stream);
 }
 
 cudaError_t launch_moe_decode_layer(const GemmMaps& gu, const GemmMaps& dn, const GemmArgs& args, int grid,

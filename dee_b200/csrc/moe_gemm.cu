@@ -79,8 +79,7 @@ struct ItemInfo {
 };
 
 __device__ __forceinline__ bool load_item(const GemmArgs& a, int item, ItemInfo& out) {
-    out.tile = item / a.m_tiles;
-    out.m = item - out.tile * a.m_tiles;
+    item_tile_m(a, item, out.tile, out.m);
     out.td = a.tiles[out.tile];
     const int e = out.td.expert;
     int slot = -1;

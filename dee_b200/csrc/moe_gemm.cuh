@@ -92,7 +92,29 @@ struct GemmArgs {
     const float* comb_w;
     float* comb_out;
     uint32_t* comb_cnt;
+    // Prefill GEMMs: per tile {first tile, tile count} of its expert.  With
+    // it the items of one expert run m-major -- all of its token tiles
+    // against one weight slice, then the next slice -- so the tiles sharing
+    // a weight slice run at the same time and its re-reads hit L2; without
+    // it items are tile-major.
+    const int2* tile_grp;
 };
+
+// Work item -> (tile, m).  The items of an expert's tiles [f, f + c) are
+// [f * M, (f + c) * M) in either order, so the tile-major tile of an item
+// names its expert group.
+__device__ __forceinline__ void item_tile_m(const GemmArgs& a, int item, int& tile, int& m) {
+    const int t0 = item / a.m_tiles;
+    if (a.tile_grp) {
+        const int2 g = a.tile_grp[t0];
+        const int j = item - g.x * a.m_tiles;
+        m = j / g.y;
+        tile = g.x + (j - m * g.y);
+    } else {
+        tile = t0;
+        m = item - t0 * a.m_tiles;
+    }
+}
 
 constexpr int kDqGroups = 4;          // dequantiser warpgroups
 constexpr int kEpilogueWarp = 3 + 4 * kDqGroups;

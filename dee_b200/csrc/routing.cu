@@ -224,6 +224,7 @@ __device__ void permute_block(const int32_t* ids, int tokens, int topk, int expe
             td.n_rows = n;
             td.n_pad = (n + 15) & ~15;
             out.tiles[slot] = td;
+            if (out.tile_grp) out.tile_grp[slot] = make_int2(ntile_off[e], nt);
         }
     }
     if (tid == 0) {
@@ -418,6 +419,7 @@ __global__ void __launch_bounds__(kPermChunk, 1)
             td.n_rows = n;
             td.n_pad = (n + 15) & ~15;
             out.tiles[slot] = td;
+            if (out.tile_grp) out.tile_grp[slot] = make_int2(ntile_off[e], nt);
         }
     }
     if (tid == 0) {
