@@ -277,10 +277,13 @@ cudaError_t launch_permute(const int32_t* ids, int tokens, int topk, int experts
                            cudaStream_t stream, bool skip_negative = false);
 
 // Softmax top-k routing and the permutation in one single-CTA launch, for
-// batches route_permute_fits accepts (T*K <= kDecodeMaxSelections, E <= 256):
-// the same ids, weights and grouping as launch_route_topk + launch_permute.
+// batches route_permute_fits accepts (at most 16 tokens, T*K <=
+// kDecodeMaxSelections, E <= 256): the same ids, weights and grouping as
+// launch_route_topk + launch_permute.  More tokens route faster spread over
+// SMs by the router kernel (one CTA routing 64 tokens cost ~13 us more on a
+// B200, measured at b = 64).
 inline bool route_permute_fits(int tokens, int topk, int experts) {
-    return tokens > 0 && topk > 0 && topk <= experts && experts <= 256 &&
+    return tokens > 0 && tokens <= 16 && topk > 0 && topk <= experts && experts <= 256 &&
            static_cast<long long>(tokens) * topk <= kDecodeMaxSelections;
 }
 cudaError_t launch_route_permute(const float* logits, int tokens, int experts, int topk, int32_t* ids,

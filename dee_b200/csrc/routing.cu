@@ -249,8 +249,8 @@ __global__ void __launch_bounds__(kPermThreads, 1)
     permute_block(ids, tokens, topk, experts, n_tile_max, max_tiles, out, status, skip_negative, wcnt);
 }
 
-// Router and permutation in one CTA, for decode-sized batches (T*K <= 384,
-// E <= 256): the warps route the tokens (one warp per token, as
+// Router and permutation in one CTA, for decode-sized batches (T <= 16,
+// T*K <= 384, E <= 256): the warps route the tokens (one warp per token, as
 // route_topk_kernel) into ids/weights and a shared copy of the ids, and the
 // CTA then groups them exactly as permute_kernel does.  One launch and one
 // dependency instead of two.  The per-warp probability scratch of the router

@@ -142,9 +142,10 @@ DEE_API int dee_moe_forward_device(dee_engine* engine, int layer, const void* d_
  * on device logits [T, E] FP32 (dee_route_topk_device, Engine::route_topk_batch,
  * engine.cpp:2604-2771) writes d_ids [T, K] int32 and d_weights [T, K] FP32,
  * then the layer of dee_moe_forward_device runs on them (K = the engine's
- * topk).  Decode-sized batches (T*K <= 384, E <= 256) route inside the
- * grouping kernel, one launch and one kernel dependency fewer; results are
- * identical to the two calls.  Queued on `stream`, no host sync. */
+ * topk).  Small batches (at most 16 tokens, E <= 256) route inside the
+ * grouping kernel -- at most 24 selections inside the one-launch layer --
+ * one launch and one kernel dependency fewer; results are identical to the
+ * two calls.  Queued on `stream`, no host sync. */
 DEE_API int dee_moe_forward_routed_device(dee_engine* engine, int layer, const void* d_x_f16, int tokens,
                                           const float* d_logits, int32_t* d_ids, float* d_weights,
                                           float* d_out_f32, float* d_raw, void* stream);

@@ -338,6 +338,44 @@ def test_bad_device_ids_reported(torch_cuda):
     assert eng.sync_status(s) & (1 << 4)
 
 
+@pytest.mark.parametrize("T", [2, 4])
+def test_one_launch_layer_recovers_after_bad_ids(torch_cuda, oracle_mod, T):
+    """A batch of at most 24 selections runs the one-launch layer, whose
+    counters between CTAs advance by a fixed amount per launch.  A device id
+    outside the bank is reported (status bit 4), its selection left out and
+    the counters kept in step; after the status read the next calls of the
+    same engine (several, so a drifted counter would show) match the oracle
+    and the two-call route + forward bit for bit."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=4242, kind="normal")
+    eng = _engine(H, I, E, K)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    rng = np.random.default_rng(4243 + T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    bad = _rand_ids(rng, T, E, K)
+    bad[T - 1, K - 1] = E + 3
+    dbad = torch.from_numpy(bad).cuda()
+    w = torch.full((T, K), 1.0 / K, dtype=torch.float32, device="cuda")
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=dbad.data_ptr(), d_weights_ptr=w.data_ptr(),
+                           d_out_ptr=out.data_ptr())
+    assert eng.sync_status() & (1 << 4)
+    for step in range(3):
+        ids = _rand_ids(rng, T, E, K)
+        dids = torch.from_numpy(ids).cuda()
+        raw = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+        eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=w.data_ptr(),
+                               d_out_ptr=out.data_ptr(), d_raw_ptr=raw.data_ptr())
+        assert eng.sync_status() == 0, eng.last_error_message()
+        want_raw = orc.moe_layer_raw(recs, layout, x16, ids)
+        assert orc.rel_l2(raw.cpu().numpy(), want_raw) <= TOL_REL_L2
+        assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw.cpu().numpy(), w.cpu().numpy()))
+
+
 @pytest.mark.parametrize("T", [8, 64])
 def test_full_shape_decode(torch_cuda, oracle_mod, T):
     """DeepSeek-V4 shapes (H=4096, I=2048, E=256, K=6), device-built bank."""
