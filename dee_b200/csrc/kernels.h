@@ -82,8 +82,10 @@ cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs
 // launch_route_topk and the grouping of launch_permute, computed
 // redundantly per CTA), loads its token rows straight from x with bulk
 // copies, and runs the gate/up and down items and the combine of
-// launch_moe_decode_layer.  The counters between CTAs carry the launch's
-// epoch in their high 32 bits, so nothing is zeroed between calls.
+// launch_moe_decode_layer.  No kernel runs before it to zero counters: the
+// tile counters advance by a fixed amount per launch (a launch waits for
+// epoch x target), the (token, block) counters are reset by the add that
+// completes them.
 constexpr int kFrontMaxSel = 96;
 constexpr int kFrontMaxTiles = kFrontMaxSel;  // a tile holds at least one selection
 constexpr int kFrontScratchInts = 2 * kFrontMaxSel + 4 * kFrontMaxTiles;  // perm, weights, tiles per CTA

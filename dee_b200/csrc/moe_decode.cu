@@ -664,17 +664,19 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
             }
             if (f.journal) f.journal[p] = f.logits ? s_ids[p] : f.ids_out[p];
         }
-        // filler adds: the counters of tiles and tokens this launch does not
-        // have advance like the others (relaxed; nothing waits on them in
-        // this launch, and the next launch starts after this one completes)
+        // filler adds: the counters of tiles this launch does not have
+        // advance like the others (relaxed; nothing waits on them in this
+        // launch, and the next launch starts after this one completes)
         const int md = a.hidden / 128;
         for (int t = nt + tid; t < kFrontMaxTiles; t += kDecThreads)
             atomicAdd(f.ctr + t, static_cast<unsigned long long>(a.inter / 64));
-        for (int i = T * md + tid; i < kFrontMaxSel * md; i += kDecThreads)
-            atomicAdd(f.ctr + kFrontMaxTiles + i, static_cast<unsigned long long>(K));
-        // a selection left out still counts for its token's blocks
-        for (int i = tid; i < sel * md; i += kDecThreads)
-            if (s_ids[i / md] < 0) atomicAdd(f.ctr + kFrontMaxTiles + (i / md / K) * md + i % md, 1ull);
+        // a selection left out still counts for its token's blocks; the add
+        // that completes a block resets it, as the combining one does
+        for (int i = tid; i < sel * md; i += kDecThreads) {
+            if (s_ids[i / md] >= 0) continue;
+            unsigned long long* c = f.ctr + kFrontMaxTiles + (i / md / K) * md + i % md;
+            if (atomicAdd(c, 1ull) + 1 == static_cast<unsigned long long>(K)) atomicExch(c, 0ull);
+        }
     }
     __syncthreads();
     return nt;
@@ -1042,10 +1044,13 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                     // acquired through the mbarrier, and the lane that
                     // completes a block acquires every other CTA's rows of it
                     tok = (kFront ? static_cast<int>(ft_perm[td.row_start + lane]) : perm[td.row_start + lane]) / K;
-                    if (kFront)
-                        last = atom_acq_rel_add(front.ctr + kFrontMaxTiles + tok * P.md + m, 1ull) + 1 ==
-                               static_cast<unsigned long long>(front.epoch) * K;
-                    else
+                    if (kFront) {
+                        // (token, block) counters start each launch at zero:
+                        // the add that completes a block resets it
+                        unsigned long long* c = front.ctr + kFrontMaxTiles + tok * P.md + m;
+                        last = atom_acq_rel_add(c, 1ull) + 1 == static_cast<unsigned long long>(K);
+                        if (last) atomicExch(c, 0ull);
+                    } else
                         last = atom_acq_rel_add(&args.comb_cnt[tok * P.md + m], 1u) == static_cast<uint32_t>(K - 1);
                 }
                 uint32_t mask = __ballot_sync(0xffffffffu, last);
