@@ -69,8 +69,8 @@ cudaError_t launch_moe_gemm(bool gate_up, const GemmMaps& maps, const GemmArgs& 
 
 // Decode-sized groups (tiles of at most kDecodeTileRows token rows): register
 // dequant + mma.sync kernel of moe_decode.cu.  Its tensor maps come from the
-// two encode_decode_* helpers below (maps.s0 / s1 are not used: scale rows
-// are copied per item straight from the records).
+// two encode_decode_* helpers below (maps.s0 / s1 are the swizzled scale-row
+// maps when scale_swz is set; otherwise scale rows come by bulk copies).
 constexpr int kDecodeTileRows = 8;
 constexpr int kDecodeMaxTokens = 64;
 constexpr int kDecodeMaxSelections = 384;  // selections (rows) the decode kernel takes

@@ -1,4 +1,4 @@
-// moe_decode.cu -- grouped W4A16 GEMM for decode-sized expert groups.
+// moe_decode.cu -- the routed-expert layer for decode-sized batches.
 //
 // For groups of at most 8 token rows per expert (decode), every packed
 // weight byte is used by only a handful of tokens, so the kernel is bound
@@ -6,14 +6,17 @@
 // Measured on B200, the tensor-memory A path of moe_gemm.cu pays about 110
 // cycles per 128x16 A slice whatever N is, and staging dequantised weights in
 // shared memory would need ~5 bytes of shared-memory traffic per weight.
-// Here the dequantised weights never leave registers:
+// Here the dequantised weights never leave registers.
 //
-//   warp 0       TMA producer: per 512-wide K stage, the packed FP4 rows
-//                (128 rows x 256 B) and the stage's token rows (8 rows x 1 KB,
-//                128-byte swizzled), one tensor copy per operand; per item,
-//                the rows' UE8M0 scales in one bulk copy per projection
-//   warp 17      scale checker: decides per stage whether every block scale
-//                allows the exact FP32 scaling below
+// One persistent kernel runs a work list of gate/up items (per tile: I/64
+// items of 64 gate + 64 up rows) and then down items (per tile: H/128 items
+// of 128 rows), or either part alone:
+//
+//   warp 0       producer: per 512-wide K stage, the packed FP4 rows
+//                (128 rows x 256 B) and the stage's token rows (8 rows x 1 KB)
+//                into a 4-deep ring, one tensor copy per operand (the front
+//                end: one bulk copy per token row, straight from x); per
+//                item, the rows' UE8M0 scales by a swizzled tensor copy
 //   warps 1-16   consumers: warp w owns the 16 weight rows (w-1)%8 of the
 //                128-row work item over one half of each stage's K (warps
 //                1-8 the first 256, warps 9-16 the second), reads its packed
@@ -24,12 +27,22 @@
 //                warp of each pair hands its sums to the first through shared
 //                memory (one fixed two-term add), and the first runs the
 //                epilogue.
+//   warp 17      scale checker: decides per item whether every block scale
+//                allows the exact FP32 scaling
+//   warp 18      signal: publishes each finished item to the grid (tile
+//                counters for the down items' dependency; with the fused
+//                combine, per (token, 128-feature block) counters, the
+//                completing row summing the block's K rows in rank order)
+//   warp 19      dependency: waits (bounded) for each down item's tile to
+//                have all of its gate/up items published
 //
 // Gate/up items pair 8 gate rows with the same 8 up rows in each 16-row MMA
 // tile, so one thread holds the gate and up accumulators of the same
 // (feature, token) and applies the reference's FP16 SwiGLU chain in
 // registers (swiglu_cuda.cu:46-59).  Down items scatter FP32 rows to
-// raw[token * K + rank] (engine.cpp:1080-1113).
+// raw[token * K + rank] (engine.cpp:1080-1113).  The "front end" form
+// (launch_moe_decode_front) also routes and groups the batch inside the
+// kernel, so a small decode layer is one launch.
 #include "decode_common.cuh"
 #include "kernels.h"
 #include "routing.cuh"
