@@ -204,17 +204,26 @@ class SyntheticStack:
                                              S.eps, T, self._h_ptr(self.h), st), "stack_rmsnorm")
             chk(lib.dee_stack_router_logits_device(e._h, self._h_ptr(self.h), self._h_ptr(self.w_r[layer]), T,
                                                    S.experts, self._h_ptr(self.logits), st), "router_logits")
-            self.router.route_topk_device(self.logits.data_ptr(), T, self.ids.data_ptr(), self.w.data_ptr(),
-                                          st.value)
-            if self.offload:
-                self.cold_reads += e.offload_prepare_device(layer, self.ids.data_ptr(), T, st.value)
-            if self.ep is None:
-                e.moe_forward_device(layer, self.h.data_ptr(), T, d_ids_ptr=self.ids.data_ptr(),
-                                     d_weights_ptr=self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),
-                                     stream=st.value)
+            if self.ep is None and not self.offload:
+                # every expert resident on this GPU: routing and the layer in
+                # one call (the router runs inside the grouping kernel or the
+                # one-launch layer; the same ids as the router engine's)
+                e.moe_forward_routed_device(layer, self.h.data_ptr(), T, self.logits.data_ptr(),
+                                            self.ids.data_ptr(), self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),
+                                            stream=st.value)
                 out = self.out
             else:
-                out = self.ep.forward(self.h, self.ids, self.w, layer=layer)
+                self.router.route_topk_device(self.logits.data_ptr(), T, self.ids.data_ptr(), self.w.data_ptr(),
+                                              st.value)
+                if self.offload:
+                    self.cold_reads += e.offload_prepare_device(layer, self.ids.data_ptr(), T, st.value)
+                if self.ep is None:
+                    e.moe_forward_device(layer, self.h.data_ptr(), T, d_ids_ptr=self.ids.data_ptr(),
+                                         d_weights_ptr=self.w.data_ptr(), d_out_ptr=self.out.data_ptr(),
+                                         stream=st.value)
+                    out = self.out
+                else:
+                    out = self.ep.forward(self.h, self.ids, self.w, layer=layer)
             if ids_log is not None:
                 ids_log[layer].copy_(self.ids)
             chk(lib.dee_stack_residual_add_device(e._h, self._h_ptr(self.x), self._h_ptr(out), T, st),
