@@ -530,7 +530,7 @@ def test_two_devices_one_process(torch_cuda, oracle_mod):
         assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("T,K", [(8, 4), (200, 2)])
+@pytest.mark.parametrize("T,K", [(3, 2), (5, 4), (8, 4), (200, 2)])
 def test_batch_with_fewer_selections_than_configured(torch_cuda, lib, oracle_mod, T, K):
     """The C entry takes topk <= EngineConfig::topk like
     Engine::moe_forward_batch_device (engine.cpp:780-781): K = 4 or 2 on a
@@ -559,6 +559,20 @@ def test_batch_with_fewer_selections_than_configured(torch_cuda, lib, oracle_mod
     assert np.array_equal(journal.reshape(T, K), ids)
     with pytest.raises(RuntimeError, match="does not match EngineConfig.topk"):
         eng.moe_forward_batch_device(0, dx.data_ptr(), T, ids, K, raw.data_ptr())
+    # device ids and weights with the combine (T * K <= 24 takes the
+    # one-launch layer): rank-order sum of the K rows, bit for bit
+    w = rng.random((T, K)).astype(np.float32)
+    dids = torch.from_numpy(ids).cuda()
+    dw = torch.from_numpy(w).cuda()
+    out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+    raw2 = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+    rc = lib.dee_moe_forward_device(eng._h, 0, ctypes.c_void_p(dx.data_ptr()), T, ctypes.c_void_p(dids.data_ptr()),
+                                    None, K, ctypes.c_void_p(dw.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                                    ctypes.c_void_p(raw2.data_ptr()), None)
+    assert rc == 0, eng.last_error_message()
+    assert eng.sync_status() == 0
+    assert np.array_equal(raw2.cpu().numpy(), raw.cpu().numpy())
+    assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw2.cpu().numpy(), w))
 
 
 @pytest.mark.parametrize("T,dup", [(1, False), (8, True), (64, False)])
