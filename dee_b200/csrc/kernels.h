@@ -88,7 +88,7 @@ cudaError_t launch_moe_decode(bool gate_up, const GemmMaps& maps, const GemmArgs
 // completes them.
 constexpr int kFrontMaxSel = 96;
 constexpr int kFrontMaxTiles = kFrontMaxSel;  // a tile holds at least one selection
-constexpr int kFrontScratchInts = 2 * kFrontMaxSel + 4 * kFrontMaxTiles;  // perm, weights, tiles per CTA
+constexpr int kFrontScratchInts = kFrontMaxSel;  // per CTA: the combine weights by position (FP32)
 struct DecFront {
     const float* logits;      // [T, E] FP32 router logits, or null: ids_out / weights_out are inputs
     const __half* x;          // [T, H] token rows

@@ -565,8 +565,9 @@ __device__ __forceinline__ bool consume_item(const GemmArgs& args, const DecLayo
 // Routing: route_token per token (one warp each), as route_topk_kernel.
 // Grouping: selections enumerated j = rank * T + token and placed stably by
 // expert id (engine.cpp:812-823), tiles of at most kDecodeTileRows rows split
-// evenly, as permute_block.  Outputs go to this CTA's slice of the scratch
-// (grouped row -> position, weights by position, tiles); CTA 0 also writes
+// evenly, as permute_block.  Outputs: the shared-memory tables (each tile,
+// its record slot and its rows' tokens; each grouped row's position) and the
+// combine weights by position in this CTA's slice of the scratch; CTA 0 also writes
 // the caller's ids, weights and journal.  Returns the number of tiles.
 __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* smem, uint8_t* ft) {
     const int T = f.tokens, K = a.topk, E = a.num_experts, sel = T * K;
