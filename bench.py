@@ -416,7 +416,7 @@ def prefill_point(torch, eng, n_steps, warmup, flush, stream, seed, act_block=0)
 # CPU baseline: the reference's own FP32 routed-expert executor
 # ---------------------------------------------------------------------------
 
-def cpu_reference_sample(b, seed, min_seconds=8.0, max_reps=50):
+def cpu_reference_sample(b, seed, min_seconds=10.0, max_reps=1000):
     """Time dee_refimpl_moe_layer (ReferenceCpuExecutor fanned out over every
     host thread) on one b-token decode layer.  Records are random-byte FP4
     with scale bytes in [0x7D, 0x83): the executor's cost does not depend on

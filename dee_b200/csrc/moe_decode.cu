@@ -685,8 +685,10 @@ __device__ int front_route_group(const GemmArgs& a, const DecFront& f, uint8_t* 
         for (int t = nt + tid; t < kFrontMaxTiles; t += kDecThreads)
             atomicAdd(f.ctr + t, static_cast<unsigned long long>(a.inter / 64));
         // a selection left out still counts for its token's blocks; the add
-        // that completes a block resets it, as the combining one does
-        for (int i = tid; i < sel * md; i += kDecThreads) {
+        // that completes a block resets it, as the combining one does.  (A
+        // launch without the combine adds nothing to these counters, so
+        // neither does its filler: a raw-only call leaves them at zero.)
+        for (int i = tid; a.comb_out && i < sel * md; i += kDecThreads) {
             if (s_ids[i / md] >= 0) continue;
             unsigned long long* c = f.ctr + kFrontMaxTiles + (i / md / K) * md + i % md;
             if (atomicAdd(c, 1ull) + 1 == static_cast<unsigned long long>(K)) atomicExch(c, 0ull);

@@ -376,6 +376,44 @@ def test_one_launch_layer_recovers_after_bad_ids(torch_cuda, oracle_mod, T):
         assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw.cpu().numpy(), w.cpu().numpy()))
 
 
+@pytest.mark.parametrize("T", [2, 4])
+def test_one_launch_layer_raw_only_call_leaves_combine_counters(torch_cuda, oracle_mod, T):
+    """A call of the one-launch layer without a combine output adds nothing
+    to the (token, feature block) counters of the fused combine -- a
+    selection left out for a bad id included.  Combined calls that follow it
+    on the same engine, with no status read in between, complete each block
+    only once all K of its rows are stored, so every output equals the
+    rank-order combine of that call's own rows bit for bit.  The status read
+    at the end still reports the first call's bad id."""
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K = 512, 512, 16, 6
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=4343, kind="normal")
+    eng = _engine(H, I, E, K)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    rng = np.random.default_rng(4344 + T)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    dx = torch.from_numpy(x16.view(np.float16)).cuda()
+    bad = _rand_ids(rng, T, E, K)
+    bad[0, 1] = E + 5
+    dbad = torch.from_numpy(bad).cuda()
+    raw0 = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+    eng.moe_forward_device(0, dx.data_ptr(), T, d_ids_ptr=dbad.data_ptr(), d_raw_ptr=raw0.data_ptr())
+    for step in range(3):
+        xs = orc.f16_bits(rng.standard_normal((T, H)))
+        dxs = torch.from_numpy(xs.view(np.float16)).cuda()
+        dids = torch.from_numpy(_rand_ids(rng, T, E, K)).cuda()
+        w = torch.from_numpy(rng.uniform(0.05, 1.0, (T, K)).astype(np.float32)).cuda()
+        out = torch.empty((T, H), dtype=torch.float32, device="cuda")
+        raw = torch.empty((T, K, H), dtype=torch.float32, device="cuda")
+        eng.moe_forward_device(0, dxs.data_ptr(), T, d_ids_ptr=dids.data_ptr(), d_weights_ptr=w.data_ptr(),
+                               d_out_ptr=out.data_ptr(), d_raw_ptr=raw.data_ptr())
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy(), orc.combine_f32(raw.cpu().numpy(), w.cpu().numpy())), step
+    assert eng.sync_status() & (1 << 4)
+
+
 @pytest.mark.parametrize("T", [8, 64])
 def test_full_shape_decode(torch_cuda, oracle_mod, T):
     """DeepSeek-V4 shapes (H=4096, I=2048, E=256, K=6), device-built bank."""
