@@ -16,6 +16,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -353,6 +354,27 @@ int check_engine(dee_engine* e) {
     if (!e) return DEE_ERR_INVALID;
     cudaError_t err = cudaSetDevice(e->cfg.device_id);
     if (err != cudaSuccess) return cuda_fail(e, err, "cudaSetDevice");
+    return DEE_OK;
+}
+
+// A caller's device pointer and the widest access the kernels make through
+// it: FP16 token rows by 16-byte vector loads, bulk copies or tensor maps,
+// FP32 rows (raw rows, outputs) by float4, ids, weights and logits by 4-byte
+// loads (int64 ids by 8).  A pointer off that alignment (a column slice of a
+// tensor, say) would raise a misaligned-address fault inside a kernel and
+// lose the context, so the entry points refuse it before any launch.  Null
+// passes: each entry checks the pointers it requires.
+struct PtrAlign {
+    const char* name;
+    const void* p;
+    uintptr_t align;
+};
+
+int check_aligned(dee_engine* e, const char* entry, std::initializer_list<PtrAlign> ptrs) {
+    for (const PtrAlign& q : ptrs)
+        if ((reinterpret_cast<uintptr_t>(q.p) & (q.align - 1)) != 0)
+            return fail(e, DEE_ERR_INVALID, std::string(entry) + ": " + q.name + " must be " +
+                                                std::to_string(q.align) + "-byte aligned");
     return DEE_OK;
 }
 
@@ -797,6 +819,9 @@ int dee_route_topk_device(dee_engine* e, const float* d_logits, int tokens, int3
     if (rc != DEE_OK) return rc;
     if (!d_logits || !d_ids || !d_weights || tokens <= 0)
         return fail(e, DEE_ERR_INVALID, "invalid router arguments");
+    if ((rc = check_aligned(e, "route_topk_device",
+                            {{"d_logits", d_logits, 4}, {"d_ids", d_ids, 4}, {"d_weights", d_weights, 4}})) != DEE_OK)
+        return rc;
     stage_begin(e, kStageRoute, static_cast<cudaStream_t>(stream));
     cudaError_t err = launch_route_topk(d_logits, tokens, e->cfg.num_experts, e->cfg.topk, d_ids,
                                         d_weights, e->d_status, static_cast<cudaStream_t>(stream));
@@ -812,6 +837,10 @@ int dee_group_by_expert_device(dee_engine* e, const int32_t* d_ids, int tokens, 
     if (rc != DEE_OK) return rc;
     if (!d_ids || !d_perm || !d_row_of || !d_offsets || tokens <= 0 || topk <= 0 || topk > e->cfg.num_experts)
         return fail(e, DEE_ERR_INVALID, "invalid grouping arguments");
+    if ((rc = check_aligned(e, "group_by_expert_device",
+                            {{"d_ids", d_ids, 4}, {"d_perm", d_perm, 4}, {"d_row_of", d_row_of, 4},
+                             {"d_offsets", d_offsets, 4}})) != DEE_OK)
+        return rc;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     if ((rc = ensure_capacity(e, static_cast<size_t>(tokens) * topk, s)) != DEE_OK) return rc;
     PermuteOut po{e->d_counts, d_offsets, d_perm, d_row_of, e->d_tiles, e->d_n_tiles, nullptr};
@@ -834,6 +863,11 @@ int dee_route_dsv4_device(dee_engine* e, const float* d_logits, const float* d_b
     if (rc != DEE_OK) return rc;
     if (!d_logits || !d_ids || !d_weights || tokens <= 0 || (d_tid2eid && !d_input_ids))
         return fail(e, DEE_ERR_INVALID, "invalid DSv4 router arguments");
+    if ((rc = check_aligned(e, "route_dsv4_device",
+                            {{"d_logits", d_logits, 4}, {"d_bias", d_bias, 4}, {"d_tid2eid", d_tid2eid, 8},
+                             {"d_input_ids", d_input_ids, 8}, {"d_ids", d_ids, 4}, {"d_weights", d_weights, 4}})) !=
+        DEE_OK)
+        return rc;
     stage_begin(e, kStageRoute, static_cast<cudaStream_t>(stream));
     cudaError_t err = launch_route_dsv4(d_logits, d_bias, d_tid2eid, d_input_ids, tokens,
                                         e->cfg.num_experts, e->cfg.topk, route_scale, d_ids,
@@ -854,6 +888,10 @@ int dee_moe_forward_device(dee_engine* e, int layer, const void* d_x_f16, int to
     if (!d_x_f16 || tokens <= 0 || topk <= 0 || topk > e->cfg.topk || (!d_ids && !h_ids) ||
         (!d_out_f32 && !d_raw) || (d_out_f32 && !d_weights))
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_device",
+                            {{"d_x_f16", d_x_f16, 16}, {"d_ids", d_ids, 4}, {"d_weights", d_weights, 4},
+                             {"d_out_f32", d_out_f32, 16}, {"d_raw", d_raw, 16}})) != DEE_OK)
+        return rc;
     const size_t sel = static_cast<size_t>(tokens) * topk;
     if (h_ids && !host_ids_valid(e, h_ids, sel)) return DEE_ERR_RANGE;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
@@ -972,6 +1010,11 @@ int dee_moe_forward_routed_device(dee_engine* e, int layer, const void* d_x_f16,
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!d_x_f16 || !d_logits || !d_ids || !d_weights || tokens <= 0 || (!d_out_f32 && !d_raw))
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_routed_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_routed_device",
+                            {{"d_x_f16", d_x_f16, 16}, {"d_logits", d_logits, 4}, {"d_ids", d_ids, 4},
+                             {"d_weights", d_weights, 4}, {"d_out_f32", d_out_f32, 16}, {"d_raw", d_raw, 16}})) !=
+        DEE_OK)
+        return rc;
     const int K = e->cfg.topk;
     const size_t sel = static_cast<size_t>(tokens) * K;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
@@ -1008,6 +1051,10 @@ int dee_moe_forward_mxfp8_device(dee_engine* e, int layer, const void* d_x_f16, 
     if (!d_x_f16 || tokens <= 0 || topk <= 0 || topk > e->cfg.topk || !d_ids || (!d_out_f32 && !d_raw) ||
         (d_out_f32 && !d_weights) || (act_block != 32 && act_block != 128))
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_mxfp8_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_mxfp8_device",
+                            {{"d_x_f16", d_x_f16, 16}, {"d_ids", d_ids, 4}, {"d_weights", d_weights, 4},
+                             {"d_out_f32", d_out_f32, 16}, {"d_raw", d_raw, 16}})) != DEE_OK)
+        return rc;
     const size_t sel = static_cast<size_t>(tokens) * topk;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
     e->h_ids_count = sel;
@@ -1052,6 +1099,11 @@ int dee_moe_forward_combined_device(dee_engine* e, int layer, const void* d_h_in
     if (!d_h_in || !d_expert_ids || !d_weights_f32 || !d_output_f16 || tokens <= 0 ||
         topk <= 0 || topk > e->cfg.topk)
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_combined_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_combined_device",
+                            {{"d_h_in", d_h_in, 16}, {"d_expert_ids", d_expert_ids, 8},
+                             {"d_weights_f32", d_weights_f32, 4}, {"d_output_f16", d_output_f16, 2},
+                             {"d_raw_trace_out", d_raw_trace_out, 16}})) != DEE_OK)
+        return rc;
     const size_t sel = static_cast<size_t>(tokens) * topk;
     if ((rc = ensure_capacity(e, sel, stream)) != DEE_OK) return rc;
     cudaError_t err = launch_ids_i64_to_i32(d_expert_ids, static_cast<int>(sel),
@@ -1084,6 +1136,10 @@ int dee_ep_pack_device(dee_engine* e, const int32_t* d_ids, int tokens, const vo
         return fail(e, DEE_ERR_INVALID,
                     "invalid ep_pack arguments (ranks 1..32, capacity > 0, experts_per_rank must "
                     "equal the engine's num_experts)");
+    if ((rc = check_aligned(e, "ep_pack_device",
+                            {{"d_ids", d_ids, 4}, {"d_x_f16", d_x_f16, 16}, {"d_send_rows", d_send_rows, 16},
+                             {"d_send_expert", d_send_expert, 4}, {"d_slot_of_pos", d_slot_of_pos, 4}})) != DEE_OK)
+        return rc;
     const size_t sel = static_cast<size_t>(tokens) * e->cfg.topk;
     // room for the rows this engine receives next (ranks x capacity), so the
     // rows forward does not regrow the workspace and drop the journal
@@ -1110,6 +1166,10 @@ int dee_moe_forward_rows_device(dee_engine* e, int layer, const void* d_rows_f16
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!d_rows_f16 || !d_expert || !d_raw || rows <= 0)
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_rows_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_rows_device",
+                            {{"d_rows_f16", d_rows_f16, 16}, {"d_expert", d_expert, 4}, {"d_raw", d_raw, 16}})) !=
+        DEE_OK)
+        return rc;
     if ((rc = ensure_capacity(e, static_cast<size_t>(rows), stream)) != DEE_OK) return rc;
     return run_experts(e, layer, static_cast<const __half*>(d_rows_f16), rows, d_expert, d_raw, stream,
                        1, true, false);
@@ -1122,6 +1182,10 @@ int dee_ep_combine_device(dee_engine* e, const float* d_back, const int32_t* d_s
     e->last_error.clear();
     if (!d_back || !d_slot_of_pos || !d_weights || !d_out || tokens <= 0)
         return fail(e, DEE_ERR_INVALID, "invalid ep_combine arguments");
+    if ((rc = check_aligned(e, "ep_combine_device",
+                            {{"d_back", d_back, 16}, {"d_slot_of_pos", d_slot_of_pos, 4},
+                             {"d_weights", d_weights, 4}, {"d_out", d_out, 16}})) != DEE_OK)
+        return rc;
     const auto stream = static_cast<cudaStream_t>(stream_v);
     stage_begin(e, kStageCombine, stream);
     cudaError_t err = launch_ep_combine(d_back, d_slot_of_pos, d_weights, tokens, e->cfg.topk,
@@ -1168,6 +1232,10 @@ int dee_moe_forward_official_device(dee_engine* e, int layer, const void* d_x_f1
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!d_x_f16 || tokens <= 0 || !d_ids || !d_weights || !d_out_f32)
         return fail(e, DEE_ERR_INVALID, "invalid moe_forward_official_device arguments");
+    if ((rc = check_aligned(e, "moe_forward_official_device",
+                            {{"d_x_f16", d_x_f16, 16}, {"d_ids", d_ids, 4}, {"d_weights", d_weights, 4},
+                             {"d_out_f32", d_out_f32, 16}, {"d_shared_out", d_shared_out, 16}})) != DEE_OK)
+        return rc;
     if (layer < 0 || layer >= static_cast<int>(e->banks.size()) || !e->banks[layer].attached)
         return fail(e, DEE_ERR_NO_BANK, "no expert bank attached for layer " + std::to_string(layer));
     const int K = e->cfg.topk, H = e->cfg.hidden;
@@ -1302,6 +1370,9 @@ int dee_ep_p2p_dispatch_device(dee_engine* e, const void* d_x_f16, const int32_t
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!p.connected || !d_x_f16 || !d_ids)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_dispatch needs a connected engine, x and ids");
+    if ((rc = check_aligned(e, "ep_p2p_dispatch_device", {{"d_x_f16", d_x_f16, 16}, {"d_ids", d_ids, 4}})) !=
+        DEE_OK)
+        return rc;
     const size_t sel = static_cast<size_t>(p.tokens) * e->cfg.topk;
     const size_t recv = static_cast<size_t>(p.ranks) * p.capacity;
     if ((rc = ensure_capacity(e, sel > recv ? sel : recv, stream)) != DEE_OK) return rc;
@@ -1346,6 +1417,9 @@ int dee_ep_p2p_combine_device(dee_engine* e, const float* d_weights, float* d_ou
     auto stream = static_cast<cudaStream_t>(stream_v);
     if (!p.connected || p.epoch == 0 || !d_weights || !d_out_f32)
         return fail(e, DEE_ERR_INVALID, "ep_p2p_combine needs a dispatched layer, weights and out");
+    if ((rc = check_aligned(e, "ep_p2p_combine_device", {{"d_weights", d_weights, 4}, {"d_out_f32", d_out_f32, 16}})) !=
+        DEE_OK)
+        return rc;
     // every combine CTA waits (bounded) for every owner's return flag
     stage_begin(e, kStageCombine, stream);
     const cudaError_t err = launch_ep_combine(p.peers.back_rows[p.rank], p.d_slot_of_pos, d_weights, p.tokens,
@@ -1406,6 +1480,7 @@ int dee_offload_prepare_device(dee_engine* e, int layer, const int32_t* d_ids, i
     const int E = o.experts, K = e->cfg.topk;
     if (!o.on || layer < 0 || layer >= o.layers || !d_ids || tokens <= 0)
         return fail(e, DEE_ERR_INVALID, "offload_prepare needs an attached offload tier and a layer's ids");
+    if ((rc = check_aligned(e, "offload_prepare_device", {{"d_ids", d_ids, 4}})) != DEE_OK) return rc;
     const size_t sel = static_cast<size_t>(tokens) * K;
     if (sel > o.h_ids_cap) {
         if (o.h_ids) cudaFreeHost(o.h_ids);

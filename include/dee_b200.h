@@ -9,7 +9,14 @@
  *     (dee.cpp/include/dee/engine.h:302-326);
  *   - failures return a negative status and record a message readable with
  *     dee_last_error() (Engine::last_error_message, engine.h:434-436);
- *   - one engine per CUDA device, driven from one host thread at a time.
+ *   - one engine per CUDA device, driven from one host thread at a time;
+ *   - device pointers are aligned to the widest access the kernels make:
+ *     FP16 token rows (x, h_in, rows) and FP32 row buffers (raw, outputs,
+ *     returned rows) 16 bytes, int64 ids 8, int32 ids, weights, logits and
+ *     index tables 4, FP16 outputs 2.  Rows of a contiguous tensor meet
+ *     this whenever its base does; a column slice need not.  An entry
+ *     point given a pointer off its alignment returns DEE_ERR_INVALID,
+ *     naming the pointer, before it launches anything.
  * No torch types cross this boundary: device pointers, host pointers,
  * sizes and CUDA stream handles (cudaStream_t passed as void*; NULL is the
  * legacy default stream, as in engine.cpp:2011-2013).

@@ -414,6 +414,67 @@ def test_one_launch_layer_raw_only_call_leaves_combine_counters(torch_cuda, orac
     assert eng.sync_status() & (1 << 4)
 
 
+def test_entry_points_refuse_misaligned_pointers(torch_cuda, oracle_mod):
+    """A device pointer off the alignment its kernels need -- offset the way
+    a column slice would be -- is refused with DEE_ERR_INVALID naming the
+    pointer, before anything is launched; the same engine then runs the
+    layer on the aligned pointers and matches the oracle."""
+    import dee_b200
+    torch = torch_cuda
+    orc = oracle_mod
+    H, I, E, K, T = 512, 512, 16, 6, 4
+    layout = orc.Layout(H, I)
+    recs = orc.synthetic_records(layout, E, seed=4545, kind="normal")
+    eng = _engine(H, I, E, K)
+    eng.attach_bank(0, torch.from_numpy(recs).cuda())
+    rng = np.random.default_rng(4546)
+    x16 = orc.f16_bits(rng.standard_normal((T, H)))
+    logits = rng.standard_normal((T, E)).astype(np.float32)
+    # every buffer has a spare 16 bytes, so base + offset stays inside it
+    dx = torch.zeros(T * H + 8, dtype=torch.float16, device="cuda")
+    dx[:T * H] = torch.from_numpy(x16.view(np.float16).reshape(-1)).cuda()
+    dl = torch.zeros(T * E + 4, dtype=torch.float32, device="cuda")
+    dl[:T * E] = torch.from_numpy(logits.reshape(-1)).cuda()
+    ids = torch.zeros(T * K + 4, dtype=torch.int32, device="cuda")
+    w = torch.zeros(T * K + 4, dtype=torch.float32, device="cuda")
+    out = torch.zeros(T * H + 4, dtype=torch.float32, device="cuda")
+    raw = torch.zeros(T * K * H + 4, dtype=torch.float32, device="cuda")
+    ids64 = torch.zeros(T * K + 2, dtype=torch.int64, device="cuda")
+    out16 = torch.zeros(T * H + 8, dtype=torch.float16, device="cuda")
+    x, lg, i, wp, o, r = (t.data_ptr() for t in (dx, dl, ids, w, out, raw))
+    torch.cuda.synchronize()
+    n0 = eng.launch_count()
+    cases = [
+        ("d_x_f16", lambda: eng.moe_forward_routed_device(0, x + 2, T, lg, i, wp, d_out_ptr=o)),
+        ("d_x_f16", lambda: eng.moe_forward_device(0, x + 8, T, d_ids_ptr=i, d_weights_ptr=wp, d_out_ptr=o)),
+        ("d_logits", lambda: eng.moe_forward_routed_device(0, x, T, lg + 2, i, wp, d_out_ptr=o)),
+        ("d_ids", lambda: eng.moe_forward_device(0, x, T, d_ids_ptr=i + 2, d_weights_ptr=wp, d_out_ptr=o)),
+        ("d_weights", lambda: eng.route_topk_device(lg, T, i, wp + 1)),
+        ("d_out_f32", lambda: eng.moe_forward_device(0, x, T, d_ids_ptr=i, d_weights_ptr=wp, d_out_ptr=o + 4)),
+        ("d_raw", lambda: eng.moe_forward_device(0, x, T, d_ids_ptr=i, d_raw_ptr=r + 8)),
+        ("d_raw", lambda: eng.moe_forward_mxfp8_device(0, x, T, i, r + 4)),
+    ]
+    for name, call in cases:
+        with pytest.raises(dee_b200.DeeError, match=name + " must be"):
+            call()
+    # the pydee-style entry answers False and keeps the reason
+    assert not eng.moe_forward_combined_device(0, x, T, ids64.data_ptr() + 4, K, wp, out16.data_ptr(), 0, 0)
+    assert "d_expert_ids must be 8-byte aligned" in eng.last_error_message()
+    assert not eng.moe_forward_combined_device(0, x, T, ids64.data_ptr(), K, wp, out16.data_ptr() + 1, 0, 0)
+    assert "d_output_f16 must be 2-byte aligned" in eng.last_error_message()
+    torch.cuda.synchronize()
+    assert eng.launch_count() == n0
+    assert eng.sync_status() == 0
+    eng.moe_forward_routed_device(0, x, T, lg, i, wp, d_out_ptr=o, d_raw_ptr=r)
+    assert eng.sync_status() == 0, eng.last_error_message()
+    ids_ref, _ = orc.route_topk(logits, K)
+    assert np.array_equal(ids[:T * K].cpu().numpy().reshape(T, K), ids_ref)
+    got_raw = raw[:T * K * H].cpu().numpy().reshape(T, K, H)
+    assert orc.rel_l2(got_raw, orc.moe_layer_raw(recs, layout, x16, ids_ref)) <= TOL_REL_L2
+    got_w = w[:T * K].cpu().numpy().reshape(T, K)
+    assert np.array_equal(out[:T * H].cpu().numpy().reshape(T, H), orc.combine_f32(got_raw, got_w))
+
+
 @pytest.mark.parametrize("T", [8, 64])
 def test_full_shape_decode(torch_cuda, oracle_mod, T):
     """DeepSeek-V4 shapes (H=4096, I=2048, E=256, K=6), device-built bank."""
