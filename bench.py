@@ -880,7 +880,8 @@ def main():
                                ", one launch)",
                      "achieved": achieved, "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
                      "peak_source": f"{peak_kind} hbm_gbs", "traffic": None,
-                     "algorithmic_bytes_per_launch": dec_bytes},
+                     "algorithmic_bytes_per_launch": dec_bytes,
+                     "unique_experts_per_launch": u_mean},
         "gpu_launches": int(round(per_step_launches * args.steps)),
         "gpu_launches_per_step": per_step_launches,
     }
