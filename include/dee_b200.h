@@ -10,6 +10,10 @@
  *   - failures return a negative status and record a message readable with
  *     dee_last_error() (Engine::last_error_message, engine.h:434-436);
  *   - one engine per CUDA device, driven from one host thread at a time;
+ *   - an engine's workspaces (grouped token rows, SwiGLU rows, internal raw
+ *     rows, the decode layer's counters) serve one call at a time: queue an
+ *     engine's calls on one stream, or order calls made on different streams
+ *     with events.  Separate engines share nothing;
  *   - device pointers are aligned to the widest access the kernels make:
  *     FP16 token rows (x, h_in, rows) and FP32 row buffers (raw, outputs,
  *     returned rows) 16 bytes, int64 ids 8, int32 ids, weights, logits and
