@@ -1,4 +1,4 @@
-"""CPU checks that pin the oracle to the reference before it judges the GPU.
+"""CPU checks that pin the oracle to the reference before it checks the GPU.
 
 Known answers come from the reference's own tests (cited per test); the
 fixtures in tests/golden come from the reference's Python semantics (see
